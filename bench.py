@@ -1,0 +1,367 @@
+"""Benchmark: 14B causal-fast DiT chunk-forward (one denoising step through all blocks) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4] [--impl lbw|reference]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N   (sequence parallel)
+
+Workload (the headline): 40 blocks of the 14B geometry (dim 5120, 40 heads,
+FFN 13824), one 720p chunk of 3 latent frames (45 x 80 tokens per frame, 10,800 query tokens) against a
+21-frame KV window (6 cached chunks + the destination chunk = 75,600 keys), 512 text tokens, hoisted
+camera FiLM, MXFP8 FFN. Synthetic seeded data with the benchmark distributions (no checkpoints here).
+A step = one forward of the whole block stack over the chunk; N ranks shard the query tokens (strong
+scaling) and all-gather each block's new K/V over NCCL.
+
+Printed JSON (rank 0): value = query tokens / step time (max over ranks), e2e = the same through host
+buffers (pinned H2D of x, D2H of the result), roofline of the dominant kernel (self-attention), the CPU
+baseline (the oracle port timed on a bounded sample on the host cores), clocks sampled during the
+timed region.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (model, frames, grid_h, grid_w, lead chunks, start_frame, layers override)
+    "c1": dict(model="1.3B", grid=(3, 30, 52), n_lead=2, start_frame=6, layers=1),
+    "c2": dict(model="14B", grid=(3, 30, 52), n_lead=6, start_frame=18, layers=1),
+    "c3": dict(model="1.3B", grid=(3, 30, 52), n_lead=6, start_frame=18, layers=30),
+    "c4": dict(model="14B", grid=(3, 45, 80), n_lead=6, start_frame=18, layers=40),
+}
+TEXT_LEN = 512
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def flops_per_block(lq, lkv, dim, ffn, text=TEXT_LEN):
+    bf16 = 8 * lq * dim * dim + 4 * lq * lkv * dim + 4 * lq * dim * dim + 4 * lq * text * dim
+    mx = 4 * lq * dim * ffn
+    return bf16, mx
+
+
+class Clocks:
+    """nvidia-smi sampler for the timed region (clocks, power, throttle reasons)."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), parts[4:8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        load = [r[0] for r in rows if r[0] > 0.5 * r[1]] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_oracle_step(cfg_name, rows_sample, threads, blocks=1):
+    """One block of the oracle (CPU restatement of the reference block) at the workload's geometry on a
+    sample of the query rows; returns seconds."""
+    from oracle import block as ob
+    import lbw_b200.model as M
+    torch.set_num_threads(threads)
+    c = CONFIGS[cfg_name]
+    m = M.CONFIGS[c["model"]]
+    C, H, F = m["dim"], m["num_heads"], m["ffn_dim"]
+    f, gh, gw = c["grid"]
+    chunk = f * gh * gw
+    g = torch.Generator().manual_seed(0)
+    bf = torch.bfloat16
+    r = lambda *s, std=0.02: (torch.randn(*s, generator=g) * std)  # noqa: E731
+    p = {}
+    for blk in ("self_attn", "cross_attn"):
+        for nm in ("q", "k", "v", "o"):
+            p[f"{blk}.{nm}.weight"] = r(C, C).to(bf)
+            p[f"{blk}.{nm}.bias"] = r(C).to(bf)
+        p[f"{blk}.norm_q.weight"] = r(C).to(bf)
+        p[f"{blk}.norm_k.weight"] = r(C).to(bf)
+    p["norm3.weight"], p["norm3.bias"] = r(C), r(C)
+    p["ffn.0.weight"], p["ffn.0.bias"] = r(F, C).to(bf), r(F).to(bf)
+    p["ffn.2.weight"], p["ffn.2.bias"] = r(C, F).to(bf), r(C).to(bf)
+    p["modulation"] = r(1, 6, C, std=0.1)
+    x = r(rows_sample, C, std=1.0)
+    e0 = r(6, C, std=0.1)
+    k_lead = [r(chunk, H, 128, std=1.0).to(bf) for _ in range(c["n_lead"])]
+    v_lead = [r(chunk, H, 128, std=1.0).to(bf) for _ in range(c["n_lead"])]
+    ctx_k, ctx_v = r(TEXT_LEN, H, 128, std=1.0).to(bf), r(TEXT_LEN, H, 128, std=1.0).to(bf)
+    cos, sin = ob.rope_grid(ob.rope_freqs(), c["grid"], c["start_frame"])
+    film = (r(rows_sample, C, std=0.1).to(bf), r(rows_sample, C, std=0.1).to(bf))
+    # the chunk's own K/V are computed from the sample rows; the rest of the destination chunk is cached data
+    k_lead = k_lead + [r(chunk - rows_sample, H, 128, std=1.0).to(bf)]
+    v_lead = v_lead + [r(chunk - rows_sample, H, 128, std=1.0).to(bf)]
+    t0 = time.perf_counter()
+    for _ in range(blocks):
+        ob.block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos[:rows_sample], sin[:rows_sample], film=film,
+                         mx=True)
+    return time.perf_counter() - t0
+
+
+def cpu_info():
+    model = ""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except Exception:
+        pass
+    return os.cpu_count() or 1, model
+
+
+def run_reference(args):
+    """--impl reference: the reference path's CPU implementation (the oracle port, oracle/block.py) on the
+    host cores, rank 0 only, each step one block over a bounded sample of the chunk's query rows."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import __graft_entry__
+    __graft_entry__.load_package()
+    c = CONFIGS[args.config]
+    f, gh, gw = c["grid"]
+    layers = c["layers"]
+    rows = args.cpu_rows
+    threads, model = cpu_info()
+    times = []
+    for i in range(args.warmup + args.steps):
+        t = cpu_oracle_step(args.config, rows, threads)
+        if i >= args.warmup:
+            times.append(t)
+    t_step = statistics.median(times) * layers          # one block timed, x blocks (identical cost)
+    value = rows / t_step
+    sample = (f"{rows} of {f * gh * gw} query rows, 1 of {layers} blocks (x{layers} extrapolated), "
+              f"full {(c['n_lead'] + 1) * f * gh * gw}-key window; CPU: {model}")
+    out = {"metric": "chunk-forward tokens/s", "value": value, "unit": "tokens/s", "impl": "reference",
+           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3,
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32/bf16 (CPU torch)",
+           "data": "synthetic", "config": {"workload": args.config, "blocks": layers},
+           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="lbw", choices=["lbw", "reference"])
+    ap.add_argument("--cpu-rows", type=int, default=int(os.environ.get("LBW_CPU_ROWS", "1350")))
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch.distributed as dist
+    import __graft_entry__
+    __graft_entry__.build()
+    import lbw_b200._lib as L
+    import lbw_b200.block as B
+    import lbw_b200.model as M
+    import lbw_b200.rope as R
+    import lbw_b200.sp as sp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        sp.set_group(None)
+
+    c = CONFIGS[args.config]
+    m = M.CONFIGS[c["model"]]
+    C, H, F = m["dim"], m["num_heads"], m["ffn_dim"]
+    layers = c["layers"]
+    f, gh, gw = c["grid"]
+    chunk = f * gh * gw
+    if chunk % world:
+        raise SystemExit(f"{chunk} query tokens do not split over {world} ranks")
+    L_loc = chunk // world
+    n_chunks = c["n_lead"] + 1
+    lkv = n_chunks * chunk
+
+    stack = M.BlockStack.synthetic(layers, C, F, H, dev, seed=0, ffn_mx=True)
+    g = torch.Generator(device=dev).manual_seed(1 + rank)
+    bf = torch.bfloat16
+    ks = [[torch.randn(1, chunk, H, 128, generator=g, device=dev, dtype=bf) for _ in range(n_chunks)]
+          for _ in range(layers)]
+    vs = [[torch.randn(1, chunk, H, 128, generator=g, device=dev, dtype=bf) for _ in range(n_chunks)]
+          for _ in range(layers)]
+    ctx = torch.randn(TEXT_LEN, C, generator=g, device=dev, dtype=bf)
+    caches = [{"k": torch.empty(TEXT_LEN, H, 128, dtype=bf, device=dev),
+               "v": torch.empty(TEXT_LEN, H, 128, dtype=bf, device=dev)} for _ in range(layers)]
+    films = [((torch.randn(L_loc, C, generator=g, device=dev) * 0.1).to(bf),
+              (torch.randn(L_loc, C, generator=g, device=dev) * 0.1).to(bf)) for _ in range(layers)]
+    e0 = torch.randn(6, C, generator=g, device=dev) * 0.1
+    x0 = torch.randn(L_loc, C, generator=g, device=dev).to(bf).float()
+    xf = x0.clone()
+    freqs = R.rope_freqs()
+    # cross K/V of the text context: filled once per generation (not part of a denoising step)
+    xf.copy_(x0)
+    stack.forward_chunk(xf, e0, (ks, vs), ctx, caches, c["grid"], c["start_frame"], freqs, films=films,
+                        fill_cross=True)
+    torch.cuda.synchronize()
+    L.check_device_status()
+
+    def step(ev=None):
+        stack.forward_chunk(xf, e0, (ks, vs), ctx, caches, c["grid"], c["start_frame"], freqs, films=films,
+                            attn_events=ev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        xf.copy_(x0)
+        step()
+    barrier()
+    L.check_device_status()
+
+    attn_ev = []
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            step(attn_ev)
+        end.record()
+        barrier()
+    ms = start.elapsed_time(end) / args.steps
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in attn_ev)
+    L.check_device_status()
+    t = torch.tensor([ms, attn_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, attn_ms = float(t[0]), float(t[1])
+
+    # end to end through host buffers: pinned x in, result out, every step
+    e2e = None
+    if not args.no_e2e:
+        xh = x0.cpu().pin_memory()
+        yh = torch.empty_like(xh).pin_memory()
+        for _ in range(2):
+            xf.copy_(xh, non_blocking=True)
+            step()
+            yh.copy_(xf, non_blocking=True)
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            xf.copy_(xh, non_blocking=True)
+            step()
+            yh.copy_(xf, non_blocking=True)
+        e2.record()
+        barrier()
+        ms_e2e = s2.elapsed_time(e2) / args.steps
+        t = torch.tensor([ms_e2e], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t[0])
+        nbytes = xh.numel() * xh.element_size() * world
+        e2e = {"value": chunk / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
+               "d2h_bytes_per_step": nbytes, "ms_per_step": ms_e2e}
+    assert torch.isfinite(yh if e2e else xf).all(), "non-finite block output"
+
+    pk, src = peaks()
+    fb, fm = flops_per_block(chunk, lkv, C, F)
+    flops = (fb + fm) * layers
+    attn_flops = 4 * L_loc * lkv * C
+    attn_tf = attn_flops / (attn_ms / 1e3) / 1e12
+    peak_tc = pk.get("bf16_tflops_sustained") or pk["bf16_tflops"]
+    result = {
+        "metric": "chunk-forward tokens/s", "value": chunk / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (attention, projections) + MXFP8 values (FFN)",
+        "data": "synthetic (seeded N(0,1) latents / KV, N(0,0.02) weights, random init)",
+        "config": {"workload": args.config, "model": c["model"], "blocks": layers, "query_tokens": chunk,
+                   "kv_tokens": lkv, "text_tokens": TEXT_LEN, "parallelism": f"sp{world}",
+                   "l2": "inputs larger than L2 (KV cache and weights >> 126 MB)"},
+        "latency_ms": ms,
+        "tc_frac_of_peak": flops / (ms / 1e3) / (peak_tc * 1e12),
+        "roofline": {"bound": "tensor", "kernel": "chunk_attn_kernel", "achieved": attn_tf, "peak": peak_tc,
+                     "unit": "TFLOP/s", "frac": attn_tf / peak_tc, "traffic": None,
+                     "peak_source": f"{src} bf16_tflops_sustained", "flops_per_launch": attn_flops,
+                     "ms_per_launch": attn_ms},
+        "gpu_launches": args.steps * layers * B.KERNELS_PER_BLOCK,
+        "e2e": e2e,
+    }
+    if rank == 0:
+        result["clocks"] = clk.summary()
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads, model = cpu_info()
+        rows = args.cpu_rows
+        cpu_oracle_step(args.config, 128, threads)     # warm-up (thread pools, allocator)
+        t_cpu = cpu_oracle_step(args.config, rows, threads)
+        cpu_value = rows / (t_cpu * layers)
+        result["cpu_baseline"] = {"value": cpu_value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                  "sample": f"oracle block (oracle/block.py) on {rows} of {chunk} query rows, "
+                                            f"1 block x{layers} extrapolated, full {lkv}-key window; {model}"}
+    if rank == 0:
+        print(json.dumps(result))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

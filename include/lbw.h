@@ -1,0 +1,124 @@
+/*
+ * lbw.h -- C ABI of the B200 (sm_100a) causal-fast DiT block forward.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed as void*,
+ * enqueues its kernels on that stream and returns an int status (LBW_OK = 0). On failure the
+ * message is available from lbw_last_error(). Nothing here allocates per call except the
+ * one 64-byte device status word per device created on first use; all scratch buffers are the
+ * caller's. Tensors are row-major and contiguous unless a row stride ("ld") is given; bf16 means
+ * IEEE bfloat16 stored as uint16.
+ *
+ * Reference interfaces (yahavb/lingbot-world-v2) each entry point replaces are cited beside it.
+ */
+#ifndef LBW_H_
+#define LBW_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LBW_VERSION 1
+
+enum lbw_status {
+  LBW_OK = 0,
+  LBW_ERR_INVALID = 1,     /* null pointer, inconsistent arguments          */
+  LBW_ERR_SHAPE = 2,       /* shape outside what the kernels tile            */
+  LBW_ERR_ALIGN = 3,       /* pointer or row stride not 16-byte aligned      */
+  LBW_ERR_CUDA = 4,        /* CUDA runtime/driver error                      */
+  LBW_ERR_TIMEOUT = 5,     /* a kernel's bounded wait ran out                */
+  LBW_ERR_UNSUPPORTED = 6  /* configuration this build does not implement   */
+};
+
+/* ---- library plumbing --------------------------------------------------------------- */
+int lbw_version(void);
+/* Copies this thread's last error message into buf (always NUL-terminated). */
+int lbw_last_error(char* buf, size_t n);
+const char* lbw_status_string(int code);
+/* Synchronises `stream`, reads and clears the device status word of the current device.
+ * Returns LBW_ERR_TIMEOUT (device_code = 0x100 | site) if a kernel wait ran out. */
+int lbw_check_device_status(void* stream, int* device_code);
+
+/* ---- chunk attention ----------------------------------------------------------------
+ * out[q, h*128:(h+1)*128] = softmax(scale * Q_h K_hᵀ + bias) V_h over the concatenation of
+ * n_chunks KV chunks (chunk i has chunk_rows[i] keys), exact (online-softmax) in fp32.
+ * q/out: [q_rows, heads*128] bf16 with row strides ldq/ldo; each chunk: [rows, heads*128] bf16
+ * with row stride ldkv (the [1, L, n, d] cache layout). key_bias: optional fp32 per key of the
+ * concatenation, in natural-log units (the cross_dedup log-multiplicity), or NULL.
+ * Replaces: wan/modules/attention.py:1048-1058 exact_attention_chunks (SDPA over torch.cat of
+ * the chunks, :1134-1143), attention.py:248-265 const_max_ag_attention (attention part; the
+ * all-gather is done by the caller over NCCL), attention.py:532-554 cross_attention_dedup and
+ * the cross-attention call attention(q, k, v, is_cross_attn=True) in model_fast.py:2830. */
+int lbw_chunk_attention(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                        const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                        const float* key_bias, float softmax_scale, void* out, long long ldo, void* stream);
+
+/* ---- tensor-core linear layers (bf16 x bf16 -> fp32 accumulate) ------------------------
+ * All weights are nn.Linear layout [n_out, k_in] bf16; K must be a multiple of 64, N of 32. */
+
+/* out[m, n] = bf16(a[m,:] · w[n,:] + bias[n]). Replaces torch nn.Linear in bf16
+ * (e.g. model_fast.py:2870-2872 ffn[0], cross k/v projections :2789-2790). */
+int lbw_gemm_bf16(const void* a, long long lda, const void* w, long long ldw, const void* bias, void* out,
+                  long long ldo, int m, int n, int k, void* stream);
+
+/* Fused q|k|v projection of h [m, c] with w_qkv = [Wq; Wk; Wv] [3c, c], b_qkv [3c]:
+ * q_raw, k_raw [m, c] bf16 and their row sums of squares ss_q, ss_k [m] fp32 (zeroed here),
+ * v written to v_out rows v_row_off.. with row stride ldv (the KV-cache destination chunk).
+ * Replaces: qkv_fn's projections, model_fast.py:1821-1828 (q/k/v Linears), and the V half of
+ * the cache write :2398-2409 / qk_post.qk_ss (kernels/qk_post.py:404-413). */
+int lbw_qkv_proj(const void* h, const void* w_qkv, const void* b_qkv, int m, int c, void* q_raw, void* k_raw,
+                 float* ss_q, float* ss_k, void* v_out, long long ldv, int v_row_off, void* stream);
+
+/* out = bf16(a w^T + bias) [m, n] plus its row sums of squares ss [m] (zeroed here).
+ * Replaces: WanCrossAttention q projection before norm_q, model_fast.py:2774-2777. */
+int lbw_linear_rowss(const void* a, const void* w, const void* bias, int m, int n, int k, void* out, float* ss,
+                     void* stream);
+
+/* x[m, n] (fp32, in place) += bf16(a w^T + bias) * gate[n]; then, if film_scale is given,
+ * x = bf16(1 + film_scale) * x + film_shift (film tensors [m, n] bf16). gate may be NULL (= 1).
+ * Replaces: _out_proj + the gated residual and camera FiLM, model_fast.py:2709-2750, :3063-3089;
+ * the cross-attention residual :3098-3100; the FFN residual x + y * e5, :3110-3111. */
+int lbw_linear_residual(const void* a, const void* w, const void* bias, int m, int n, int k, float* x,
+                        const float* gate, const void* film_scale, const void* film_shift, void* stream);
+
+/* out[m, n] = bf16(GELU_tanh(bf16(a w^T) + bias)); with mx_qdq != 0 each 32-column block is then
+ * MXFP8 quantise-dequantised: the FFN-up matmul with the kernels/ffn_epi.py:15-37 bias+GELU
+ * epilogue and the activation quantisation of the down projection (kernels/ffn_mx.py:159-182),
+ * computed on the bf16 tensor pipe. Replaces ffn[0] + ffn[1] (model_fast.py:2870-2872). */
+int lbw_linear_gelu(const void* a, const void* w, const void* bias, int m, int n, int k, void* out, int mx_qdq,
+                    void* stream);
+
+/* ---- row kernels ----------------------------------------------------------------------- */
+
+/* h[m, c] = LN(x)[m, :] * (1 + scale) + shift (fp32 math, eps, no affine) -> bf16, or with
+ * affine weight/bias instead (scale/shift NULL). If mx_qdq != 0 every 32-column block of the
+ * output is MXFP8 quantise-dequantised. Replaces: WanLayerNorm + adaLN modulation
+ * (model_fast.py:3045, :3101; model.py:145-156), norm3 (:2865-2867), glue.ln_mod
+ * (kernels/glue.py:69-166). */
+int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scale, const float* shift,
+                      const float* weight, const float* bias, int mx_qdq, void* out, void* stream);
+
+/* RMSNorm (+ 3-D RoPE) of projected rows: y = bf16(bf16(x * rsqrt(ss/c + eps)) * gamma), then,
+ * if rope_cos != NULL, the interleaved-pair rotation with per-token angles of (frame, h, w).
+ * x [m, c] bf16, ss [m] fp32, gamma [c] bf16; out rows out_row_off.. with row stride ldo.
+ * rope tables: cos/sin [rope_frames*pf + grid_h*ph + grid_w*pw] fp32 laid out as
+ * frame rows (pf = 22 pairs), then height rows (ph = 21), then width rows (pw = 21) for
+ * head_dim 128; token t (global index tok0 + row) -> (t / (grid_h*grid_w), (t / grid_w) % grid_h, t % grid_w).
+ * Replaces: WanRMSNorm (model.py:126-143), causal_rope_apply_rotation (model_fast.py:933-979),
+ * qk_post.qk_norm_rope (kernels/qk_post.py:37-413). */
+int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, int c, float eps,
+                     const float* rope_cos, const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0,
+                     void* out, long long ldo, int out_row_off, void* stream);
+
+/* ---- MXFP8 -------------------------------------------------------------------------------- */
+/* Quantise bf16 x [rows, k] (k % 128 == 0) to E4M3 data [rows, k] and E8M0 scales in the tiled
+ * layout (rows padded to 128, 512-byte atoms of 128 rows x 4 scales); optionally also the
+ * dequantised bf16 values. Replaces: ffn_mx.prequantize_weight (kernels/ffn_mx.py:44-47) and
+ * the in-kernel activation quantisation of ffn_mx.mm. */
+int lbw_mx_quantize(const void* x, int rows, int k, void* data, void* scales, void* dequant, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LBW_H_ */

@@ -1,0 +1,285 @@
+"""Drop-in CausalWanAttentionBlock for B200.
+
+Same constructor, parameter names (state_dict keys) and forward signature as the reference's
+wan/modules/model_fast.py:2837-3116 CausalWanAttentionBlock, for the path the causal-fast pipeline
+runs: the chunked KV cache (kv_chunks=(k_chunks, v_chunks), destination LAST, layout
+[1, chunk_tokens, n, 128]), hoisted camera FiLM (dit_cond_dict={"cam_film": (scale, shift)}), the
+cached text cross-attention (crossattn_cache={"k", "v", "is_init"}), optional cross_dedup, and the
+MXFP8 FFN (ffn_mx=True, LINGBOT_FFN_MX) or the bf16 FFN.
+
+One forward = 13 kernels of liblbw.so on the current stream:
+  layernorm_mod(norm1 + adaLN) -> qkv_proj (v straight into the destination chunk) ->
+  rmsnorm_rope(q) -> rmsnorm_rope(k into the destination chunk) -> [sequence-parallel K/V all-gather]
+  -> chunk_attention -> linear_residual(o-proj, gate e2, FiLM) -> layernorm(norm3 affine) ->
+  linear_rowss(cross q) -> rmsnorm(cross q) -> chunk_attention(cross, optional dedup bias) ->
+  linear_residual(cross o) -> layernorm_mod(norm2 + adaLN, MX QDQ) -> linear_gelu(ffn.0 + GELU, MX QDQ)
+  -> linear_residual(ffn.2, gate e5)
+The fp32 residual is updated in place by the GEMM epilogues.
+"""
+import math
+
+import torch
+import torch.nn as nn
+
+from . import kernels, rope, sp
+from .attention import cross_dedup_bias
+
+BF16 = torch.bfloat16
+HEAD_DIM = 128
+
+
+class _RMSNormParam(nn.Module):
+    def __init__(self, dim):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+
+
+class _AttnParams(nn.Module):
+    """q/k/v/o Linears and the q/k RMSNorm weights (WanSelfAttention / WanCrossAttention layout)."""
+
+    def __init__(self, dim, num_heads, qk_norm=True, eps=1e-6):
+        super().__init__()
+        self.dim, self.num_heads, self.head_dim, self.eps = dim, num_heads, dim // num_heads, eps
+        self.qk_norm = qk_norm
+        self.q, self.k, self.v, self.o = (nn.Linear(dim, dim) for _ in range(4))
+        self.norm_q = _RMSNormParam(dim) if qk_norm else nn.Identity()
+        self.norm_k = _RMSNormParam(dim) if qk_norm else nn.Identity()
+
+
+class Workspace:
+    """Scratch of one block forward over `rows` local query tokens; shared by all blocks of a stack."""
+
+    def __init__(self, rows, dim, ffn_dim, device):
+        self.rows, self.dim, self.ffn_dim = rows, dim, ffn_dim
+        mk = lambda *s, dt=BF16: torch.empty(*s, dtype=dt, device=device)  # noqa: E731
+        self.h = mk(rows, dim)
+        self.q_raw = mk(rows, dim)
+        self.k_raw = mk(rows, dim)
+        self.ss = mk(2, rows, dt=torch.float32)
+        self.q = mk(rows, dim)
+        self.attn = mk(rows, dim)
+        self.u = mk(rows, ffn_dim)
+
+    def fits(self, rows, dim, ffn_dim, device):
+        return (self.rows, self.dim, self.ffn_dim) == (rows, dim, ffn_dim) and self.h.device == device
+
+
+class CausalWanAttentionBlock(nn.Module):
+    def __init__(self, dim, ffn_dim, num_heads, local_attn_size=-1, sink_size=0, qk_norm=True,
+                 cross_attn_norm=False, eps=1e-6, ffn_mx=True, cross_dedup=0):
+        super().__init__()
+        if dim % num_heads or dim // num_heads != HEAD_DIM:
+            raise ValueError("the B200 kernels are built for head_dim 128")
+        if not qk_norm:
+            raise ValueError("the B200 path fuses the q/k RMSNorm; qk_norm=False is not supported")
+        self.dim, self.ffn_dim, self.num_heads = dim, ffn_dim, num_heads
+        self.local_attn_size, self.qk_norm, self.cross_attn_norm, self.eps = local_attn_size, qk_norm, cross_attn_norm, eps
+        self.ffn_mx = bool(ffn_mx)
+        self.cross_dedup = int(cross_dedup)
+        self.norm1 = nn.Identity()
+        self.self_attn = _AttnParams(dim, num_heads, qk_norm, eps)
+        self.norm3 = nn.LayerNorm(dim, eps, elementwise_affine=True) if cross_attn_norm else nn.Identity()
+        self.cross_attn = _AttnParams(dim, num_heads, qk_norm, eps)
+        self.norm2 = nn.Identity()
+        self.ffn = nn.Sequential(nn.Linear(dim, ffn_dim), nn.GELU(approximate="tanh"), nn.Linear(ffn_dim, dim))
+        self.modulation = nn.Parameter(torch.randn(1, 6, dim) / dim ** 0.5)
+        self.cam_injector_layer1 = nn.Linear(dim, dim)
+        self.cam_injector_layer2 = nn.Linear(dim, dim)
+        self.cam_scale_layer = nn.Linear(dim, dim)
+        self.cam_shift_layer = nn.Linear(dim, dim)
+        self._packed = None
+        self._ws = None
+
+    # ------------------------------------------------------------------ weights
+    @torch.no_grad()
+    def prepare(self, free_sources=False):
+        """Pack/convert the weights the kernels read (once; call again after changing weights)."""
+        if getattr(self, "_sources_freed", False):
+            raise ValueError("prepare(free_sources=True) already released the source weights")
+        sa, ca = self.self_attn, self.cross_attn
+        dev = sa.q.weight.device
+        if dev.type != "cuda":
+            raise ValueError("move the block to a CUDA device before the forward")
+        b = lambda t: t.detach().to(BF16).contiguous()  # noqa: E731
+        pk = {}
+        pk["wqkv"] = torch.cat([b(sa.q.weight), b(sa.k.weight), b(sa.v.weight)]).contiguous()
+        pk["bqkv"] = torch.cat([b(sa.q.bias), b(sa.k.bias), b(sa.v.bias)]).contiguous()
+        pk["gq"], pk["gk"] = b(sa.norm_q.weight), b(sa.norm_k.weight)
+        pk["wo"], pk["bo"] = b(sa.o.weight), b(sa.o.bias)
+        pk["wcq"], pk["bcq"] = b(ca.q.weight), b(ca.q.bias)
+        pk["gcq"], pk["gck"] = b(ca.norm_q.weight), b(ca.norm_k.weight)
+        pk["wck"], pk["bck"] = b(ca.k.weight), b(ca.k.bias)
+        pk["wcv"], pk["bcv"] = b(ca.v.weight), b(ca.v.bias)
+        pk["wco"], pk["bco"] = b(ca.o.weight), b(ca.o.bias)
+        if self.cross_attn_norm:
+            pk["n3w"] = self.norm3.weight.detach().float().contiguous()
+            pk["n3b"] = self.norm3.bias.detach().float().contiguous()
+        pk["mod"] = self.modulation.detach().float().reshape(6, self.dim).contiguous()
+        w1, w2 = b(self.ffn[0].weight), b(self.ffn[2].weight)
+        if self.ffn_mx:
+            # MXFP8 weights: E4M3 codes + E8M0 scales; the bf16-pipe GEMM reads their exact dequantisation
+            pk["w1_mx"] = kernels.mx_quantize(w1, dequant=True)
+            pk["w2_mx"] = kernels.mx_quantize(w2, dequant=True)
+            pk["w1"], pk["w2"] = pk["w1_mx"][2], pk["w2_mx"][2]
+        else:
+            pk["w1"], pk["w2"] = w1, w2
+        pk["b1"], pk["b2"] = b(self.ffn[0].bias), b(self.ffn[2].bias)
+        self._packed = pk
+        if free_sources:
+            # Only the packed copies serve the forward from here on (the reference frees its bf16 FFN
+            # weights the same way after MX quantisation, model_fast.py:1574-1581).
+            for lin in (sa.q, sa.k, sa.v, sa.o, ca.q, ca.k, ca.v, ca.o, self.ffn[0], self.ffn[2],
+                        self.cam_injector_layer1, self.cam_injector_layer2, self.cam_scale_layer,
+                        self.cam_shift_layer):
+                lin.weight = nn.Parameter(torch.empty(0, dtype=lin.weight.dtype, device=dev), requires_grad=False)
+            self._sources_freed = True
+        return pk
+
+    def workspace(self, rows, device):
+        if self._ws is None or not self._ws.fits(rows, self.dim, self.ffn_dim, device):
+            self._ws = Workspace(rows, self.dim, self.ffn_dim, device)
+        return self._ws
+
+    # ------------------------------------------------------------------ cross cache
+    @torch.no_grad()
+    def fill_cross_cache(self, context, crossattn_cache):
+        """First call of a generation: K = RMSNorm(Wk ctx + bk), V = Wv ctx + bv into the cache
+        (reference model_fast.py:2784-2798); with cross_dedup > 0 also the log-multiplicity bias."""
+        pk = self._packed
+        C = self.dim
+        ctx = context.reshape(-1, C).to(BF16).contiguous()
+        T = ctx.shape[0]
+        kc = crossattn_cache["k"].view(T, C)
+        vc = crossattn_cache["v"].view(T, C)
+        k_raw = torch.empty(T, C, dtype=BF16, device=ctx.device)
+        ss = torch.empty(T, dtype=torch.float32, device=ctx.device)
+        kernels.linear_rowss(ctx, pk["wck"], pk["bck"], k_raw, ss)
+        kernels.rmsnorm_rope(k_raw, ss, pk["gck"], self.eps, kc)
+        kernels.gemm_bf16(ctx, pk["wcv"], pk["bcv"], out=vc)
+        if self.cross_dedup:
+            crossattn_cache["mult"] = cross_dedup_bias(kc.view(T, self.num_heads, HEAD_DIM),
+                                                       vc.view(T, self.num_heads, HEAD_DIM), self.cross_dedup)
+        if "is_init" in crossattn_cache:
+            crossattn_cache["is_init"].fill_(1)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, x, e, seq_lens=None, grid_sizes=None, freqs=None, context=None, context_lens=None,
+                dit_cond_dict=None, kv_cache=None, crossattn_cache=None, current_start=0,
+                max_attention_size=1_000_000, frame_seqlen=None, cross_attn_first_call=None, seq_lens_int=None,
+                sp_start_row=0, sp_rows=None, rope_grids=None, rope_local_grid=None, kv_write_start=None,
+                kv_write_end=None, kv_roll_dst=0, kv_roll_src=0, kv_roll_len=0, kv_current_end=None,
+                kv_chunks=None, grid_ints=None, fused=None, kv_write=True, kv_only=False):
+        """x [1, L, C] fp32 (this rank's token shard under sequence parallelism), e [1, 1, 6, C] fp32
+        -> new x (fp32). Writes the chunk's roped K and V into kv_chunks[0][-1] / kv_chunks[1][-1]."""
+        if kv_chunks is None:
+            raise ValueError("the B200 block serves the chunked KV cache: pass kv_chunks=(k_chunks, v_chunks)")
+        if fused is not None or kv_roll_len:
+            raise ValueError("fused commit/roll variants of the Trainium path are not part of the B200 block")
+        if not kv_write:
+            raise ValueError("kv_write=False (LINGBOT_STEP_NOWRITE) is not supported by the B200 block")
+        if crossattn_cache is None or context is None:
+            raise ValueError("pass the text context and its crossattn_cache dict")
+        out = x.detach().float().reshape(-1, self.dim).clone()
+        grid = self._grid(grid_ints, grid_sizes, rope_local_grid)
+        if frame_seqlen is None:
+            frame_seqlen = grid[1] * grid[2]
+        start_frame = int(current_start) // int(frame_seqlen)
+        if freqs is None:
+            freqs = rope.rope_freqs()
+        first = cross_attn_first_call
+        if first is None:
+            first = int(crossattn_cache["is_init"].reshape(-1)[0].item()) == 0
+        film = None
+        if dit_cond_dict is not None:
+            if "cam_film" not in dit_cond_dict:
+                raise ValueError("dit_cond_dict must carry the hoisted 'cam_film' (scale, shift)")
+            film = dit_cond_dict["cam_film"]
+        self.forward_inplace(out, e, kv_chunks[0], kv_chunks[1], context, crossattn_cache, grid, start_frame,
+                             freqs, film=film, fill_cross=bool(first), kv_only=kv_only)
+        return out.view(x.shape) if x.dtype == torch.float32 else out.view(x.shape).to(x.dtype)
+
+    @staticmethod
+    def _grid(grid_ints, grid_sizes, local_grid):
+        if grid_ints is not None:
+            g = grid_ints[0]
+        elif local_grid is not None and not torch.is_tensor(local_grid):
+            g = local_grid[0]
+        elif grid_sizes is not None:
+            g = grid_sizes[0].tolist() if torch.is_tensor(grid_sizes) else grid_sizes[0]
+        else:
+            raise ValueError("need the chunk's (frames, h, w) grid")
+        return tuple(int(v) for v in g)
+
+    def forward_inplace(self, xf, e, k_chunks, v_chunks, context, crossattn_cache, grid, start_frame, freqs,
+                        film=None, fill_cross=False, kv_only=False, ws=None, attn_events=None):
+        """The block on the fp32 residual xf [L_local, C] (updated in place). attn_events: optional list
+        that receives a (start, end) pair of CUDA events around the self-attention kernel."""
+        if self._packed is None:
+            self.prepare()
+        pk = self._packed
+        C, H, eps = self.dim, self.num_heads, self.eps
+        dev = xf.device
+        L = xf.shape[0]
+        ws = ws if ws is not None else self.workspace(L, dev)
+        if fill_cross:
+            self.fill_cross_cache(context, crossattn_cache)
+        em = (pk["mod"] + e.reshape(6, C).float()).contiguous()
+        k_dst, v_dst = k_chunks[-1], v_chunks[-1]
+        chunk_rows = k_dst.numel() // C
+        p = sp.world() if sp.active() else 1
+        if chunk_rows != L * p:
+            raise ValueError(f"destination chunk holds {chunk_rows} tokens, expected {L} x {p} ranks")
+        row0 = (sp.rank() * L) if p > 1 else 0
+        f, gh, gw = grid
+        if f * gh * gw != chunk_rows:
+            raise ValueError(f"grid {grid} does not match the chunk's {chunk_rows} tokens")
+        cos, sin = rope.rope_tables(freqs, grid, start_frame, dev)
+        rp = (cos, sin, f)
+        ss_q, ss_k = ws.ss[0], ws.ss[1]
+
+        # self-attention
+        kernels.layernorm_mod(xf, eps, ws.h, scale=em[1], shift=em[0])
+        kernels.qkv_proj(ws.h, pk["wqkv"], pk["bqkv"], ws.q_raw, ws.k_raw, ss_q, ss_k, v_dst, v_row_off=row0)
+        kernels.rmsnorm_rope(ws.q_raw, ss_q, pk["gq"], eps, ws.q, rope=rp, grid=grid, tok0=row0)
+        kernels.rmsnorm_rope(ws.k_raw, ss_k, pk["gk"], eps, k_dst, rope=rp, grid=grid, tok0=row0, out_row_off=row0)
+        if p > 1:
+            sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
+            sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
+        if kv_only:
+            return xf
+        if attn_events is not None:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        kernels.chunk_attention(ws.q, list(k_chunks), list(v_chunks), out=ws.attn)
+        if attn_events is not None:
+            ev1.record()
+            attn_events.append((ev0, ev1))
+        fs, ft = (film[0].reshape(-1, C), film[1].reshape(-1, C)) if film is not None else (None, None)
+        if fs is not None:
+            fs, ft = fs.to(BF16).contiguous(), ft.to(BF16).contiguous()
+        kernels.linear_residual(ws.attn, pk["wo"], pk["bo"], xf, gate=em[2], film_scale=fs, film_shift=ft)
+
+        # cross-attention
+        if self.cross_attn_norm:
+            kernels.layernorm_mod(xf, eps, ws.h, weight=pk["n3w"], bias=pk["n3b"])
+        else:
+            raise ValueError("cross_attn_norm=False is not supported by the B200 block")
+        kernels.linear_rowss(ws.h, pk["wcq"], pk["bcq"], ws.q_raw, ss_q)
+        kernels.rmsnorm_rope(ws.q_raw, ss_q, pk["gcq"], eps, ws.q)
+        T = crossattn_cache["k"].numel() // C
+        kc, vc = crossattn_cache["k"].view(T, C), crossattn_cache["v"].view(T, C)
+        bias = None
+        if self.cross_dedup:
+            n = self.cross_dedup
+            kc, vc, bias = kc[:n], vc[:n], crossattn_cache["mult"]
+        kernels.chunk_attention(ws.q, [kc], [vc], key_bias=bias, out=ws.attn)
+        kernels.linear_residual(ws.attn, pk["wco"], pk["bco"], xf)
+
+        # FFN
+        kernels.layernorm_mod(xf, eps, ws.h, scale=em[4], shift=em[3], mx_qdq=self.ffn_mx)
+        kernels.linear_gelu(ws.h, pk["w1"], pk["b1"], ws.u, mx_qdq=self.ffn_mx)
+        kernels.linear_residual(ws.u, pk["w2"], pk["b2"], xf, gate=em[5])
+        return xf
+
+
+KERNELS_PER_BLOCK = 13

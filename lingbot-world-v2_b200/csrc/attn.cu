@@ -1,0 +1,348 @@
+// Chunk attention on tcgen05: softmax(scale * Q Kᵀ + bias) V over a list of KV-cache chunks.
+//
+// This is the exact (online-softmax) attention of the causal-fast block: the query chunk attends
+// every key of the rolling window, which arrives as separate per-chunk cache tensors ordered
+// (leading..., destination) -- wan/modules/chunked_kv_cache.py:47-76 and
+// wan/modules/attention.py:1048-1058 (exact_attention_chunks -> SDPA over torch.cat of the
+// chunks). There is no token mask: causality is what the cache holds (model_fast.py:2551-2568).
+// With a per-key additive bias the same kernel is the deduplicated text cross-attention
+// (attention.py:516-554).
+//
+// CTA = 2 query tiles x 128 rows of one head; head_dim 128; KV streamed 128 keys per tile.
+//   warps 0-3 / 4-7  softmax of query tile 0 / 1 (thread = query row = TMEM lane)
+//   warp 8           TMA producer: Q once, then K/V tiles through a 2-deep ring
+//   warp 9           UMMA issuer, TMEM owner (512 columns: S0 | S1 | O0 | O1, 128 each)
+// S_i = Q_i Kᵀ lands in TMEM; the softmax warps read it (tcgen05.ld), write bf16 P_i back over
+// the first 64 columns of S_i (tcgen05.st) and the MMA warp accumulates O_i += P_i V from TMEM
+// (A operand) and shared memory (V, MN-major). The running max is only raised when a row's max
+// grows by more than 2^8 (so P <= 256); O_i is then rescaled in TMEM by its own row's thread.
+// MMAs of one CTA execute in issue order, and every tcgen05.commit covers all earlier MMAs:
+// when softmax i sees S_i(j+1) complete, PV_i(j) has completed too, so O_i is stable and P_i(j)
+// has been consumed.
+#include <math.h>
+
+#include "host_common.cuh"
+#include "lbw_common.cuh"
+
+namespace lbw {
+
+namespace attn {
+constexpr int BM = 128, BN = 128, D = 128, QT = 2, STAGES = 2, MAX_CHUNKS = 8;
+constexpr int HALF = 128 * 64 * 2;  // 128 rows x 64 bf16 (one 128-byte swizzled box)
+constexpr int TILE = 2 * HALF;      // 128 rows x 128 bf16
+constexpr int SMEM_BYTES = (QT + 2 * STAGES) * TILE + 1024;
+constexpr int THREADS = 320;
+}  // namespace attn
+
+struct KVMaps {
+  CUtensorMap k[attn::MAX_CHUNKS];
+  CUtensorMap v[attn::MAX_CHUNKS];
+  int rows[attn::MAX_CHUNKS];
+  int n;
+};
+
+template <bool HAS_BIAS>
+__global__ void __launch_bounds__(attn::THREADS, 1)
+    chunk_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KVMaps kv, int q_rows,
+                      float scale_log2, const float* __restrict__ key_bias, __nv_bfloat16* __restrict__ out,
+                      long long ldo, int* status) {
+  using namespace attn;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + QT * TILE;
+  uint8_t* sV = sK + STAGES * TILE;
+  __shared__ __align__(8) uint64_t q_full, k_full[STAGES], k_empty[STAGES], v_full[STAGES], v_empty[STAGES],
+      s_full[QT], p_ready[QT], o_done, done_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int q0 = blockIdx.x * (QT * BM);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < QT; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_ready[i], 128);
+    }
+    mbar_init(&o_done, 1);
+    mbar_init(&done_bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) tmem_alloc(&tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const Abort ab{status, &abort_flag};
+  const int n_chunks = kv.n;
+
+  if (warp == 8) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      mbar_expect_tx(&q_full, QT * TILE);
+      for (int i = 0; i < QT; ++i)
+        for (int h = 0; h < 2; ++h)
+          tma_load_2d(sQ + i * TILE + h * HALF, &tmQ, &q_full, head * D + h * 64, q0 + i * BM);
+      int j = 0;
+      bool ok = true;
+      for (int c = 0; c < n_chunks && ok; ++c) {
+        const int rows = kv.rows[c];
+        for (int t0 = 0; t0 < rows; t0 += BN, ++j) {
+          const int s = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          if (!mbar_wait(&k_empty[s], ph ^ 1, ab, 0x21)) { ok = false; break; }
+          mbar_expect_tx(&k_full[s], TILE);
+          for (int h = 0; h < 2; ++h) tma_load_2d(sK + s * TILE + h * HALF, &kv.k[c], &k_full[s], head * D + h * 64, t0);
+          if (!mbar_wait(&v_empty[s], ph ^ 1, ab, 0x22)) { ok = false; ++j; break; }
+          mbar_expect_tx(&v_full[s], TILE);
+          for (int h = 0; h < 2; ++h) tma_load_2d(sV + s * TILE + h * HALF, &kv.v[c], &v_full[s], head * D + h * 64, t0);
+        }
+      }
+      // Let the last loads of each ring slot land before the CTA can exit.
+      mbar_wait_drain(&q_full, 0);
+      for (int i = (j > STAGES ? j - STAGES : 0); i < j; ++i) {
+        mbar_wait_drain(&k_full[i & 1], (i >> 1) & 1);
+        mbar_wait_drain(&v_full[i & 1], (i >> 1) & 1);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc_s = idesc_bf16(BM, BN, 0, 0);  // S = Q Kᵀ: both K-major (head_dim contiguous)
+      const uint32_t idesc_o = idesc_bf16(BM, D, 0, 1);   // O += P V: P from TMEM, V MN-major
+      int n_tiles = 0;
+      for (int c = 0; c < n_chunks; ++c) n_tiles += (kv.rows[c] + BN - 1) / BN;
+
+      auto issue_s = [&](int i, int stage) {
+        const uint32_t qa = smem_u32(sQ + i * TILE), kb = smem_u32(sK + stage * TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          mma_f16_ss(tmem + i * 128, sdesc_kmajor_sw128(qa + off), sdesc_kmajor_sw128(kb + off), idesc_s, kk > 0);
+        }
+      };
+      auto issue_pv = [&](int i, int stage, bool first) {
+        const uint32_t vb = smem_u32(sV + stage * TILE);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_f16_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8, sdesc_mnmajor_sw128(vb + kk * 2048, HALF), idesc_o,
+                     !(first && kk == 0));
+      };
+
+      bool ok = mbar_wait(&q_full, 0, ab, 0x31) && mbar_wait(&k_full[0], 0, ab, 0x32);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        tc_commit(&s_full[0]);
+        issue_s(1, 0);
+        tc_commit(&s_full[1]);
+        tc_commit(&k_empty[0]);
+        for (int j = 0; j < n_tiles && ok; ++j) {
+          const int s = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          const bool more = j + 1 < n_tiles;
+          const int s1 = (j + 1) & 1;
+          const uint32_t ph1 = ((j + 1) >> 1) & 1;
+          if (!mbar_wait(&v_full[s], ph, ab, 0x33) || !mbar_wait(&p_ready[0], j & 1, ab, 0x34)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(0, s, j == 0);
+          if (more) {
+            if (!mbar_wait(&k_full[s1], ph1, ab, 0x35)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(0, s1);
+            tc_commit(&s_full[0]);
+          }
+          if (!mbar_wait(&p_ready[1], j & 1, ab, 0x36)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(1, s, j == 0);
+          tc_commit(&v_empty[s]);
+          if (more) {
+            issue_s(1, s1);
+            tc_commit(&s_full[1]);
+            tc_commit(&k_empty[s1]);
+          }
+        }
+        if (ok) tc_commit(&o_done);
+      }
+      tc_commit(&done_bar);
+      mbar_wait_drain(&done_bar, 0);
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue ----------------
+    const int wg = warp >> 2;
+    const int quarter = warp & 3;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_off + wg * 128;
+    const uint32_t tO = tmem + lane_off + 256 + wg * 128;
+    const float LOG2E = 1.4426950408889634f;
+    float m = -INFINITY, l = 0.f;
+    int j = 0;
+    bool ok = true;
+    long long key_base = 0;
+    for (int c = 0; c < n_chunks && ok; ++c) {
+      const int rows = kv.rows[c];
+      for (int t0 = 0; t0 < rows; t0 += BN, ++j) {
+        const int valid = rows - t0 < BN ? rows - t0 : BN;
+        if (!mbar_wait(&s_full[wg], j & 1, ab, 0x40 + wg)) { ok = false; break; }
+        tc_fence_after();
+        const float* kb = HAS_BIAS ? key_bias + key_base + t0 : nullptr;
+        // pass 1: row max of this tile
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tS + cc * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int col = cc * 32 + e;
+            float sv = __uint_as_float(r[e]) * scale_log2;
+            if (HAS_BIAS) sv += kb[col < valid ? col : 0] * LOG2E;
+            if (col >= valid) sv = -INFINITY;
+            mx = fmaxf(mx, sv);
+          }
+        }
+        const float m_new = fmaxf(m, mx);
+        if (j == 0) {
+          m = m_new;
+        } else {
+          const bool need = m_new > m + 8.f;
+          if (__any_sync(0xffffffffu, need)) {
+            const float alpha = need ? fast_exp2(m - m_new) : 1.f;
+            if (need) {
+              l *= alpha;
+              m = m_new;
+            }
+#pragma unroll 1
+            for (int cc = 0; cc < 4; ++cc) {
+              uint32_t r[32];
+              tmem_ld32(tO + cc * 32, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+              tmem_st32(tO + cc * 32, r);
+            }
+            tmem_st_wait();
+          }
+        }
+        // pass 2: P = exp2(s - m) -> bf16 into the first 64 columns of S
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tS + cc * 32, r);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const int col = cc * 32 + e;
+            float s0 = __uint_as_float(r[e]) * scale_log2, s1 = __uint_as_float(r[e + 1]) * scale_log2;
+            if (HAS_BIAS) {
+              s0 += kb[col < valid ? col : 0] * LOG2E;
+              s1 += kb[col + 1 < valid ? col + 1 : 0] * LOG2E;
+            }
+            const float p0 = col < valid ? fast_exp2(s0 - m) : 0.f;
+            const float p1 = col + 1 < valid ? fast_exp2(s1 - m) : 0.f;
+            l += p0 + p1;
+            pk[e >> 1] = pack_bf16(p0, p1);
+          }
+          tmem_st16(tS + cc * 16, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_ready[wg]);
+      }
+      key_base += rows;
+    }
+    if (ok && mbar_wait(&o_done, 0, ab, 0x48)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      const int row = q0 + wg * BM + quarter * 32 + lane;
+      __nv_bfloat16* orow = out + (long long)row * ldo + (long long)head * D;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tO + cc * 32, r);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) pk[e >> 1] = pack_bf16(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv);
+        if (row < q_rows) {
+          uint4* d4 = reinterpret_cast<uint4*>(orow + cc * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) d4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace lbw
+
+using namespace lbw;
+
+extern "C" int lbw_chunk_attention(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                                   const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                                   const float* key_bias, float softmax_scale, void* out, long long ldo, void* stream) {
+  using namespace attn;
+  if (!q || !out || !k_chunks || !v_chunks || !chunk_rows) return set_error(LBW_ERR_INVALID, "chunk_attention: null pointer");
+  if (q_rows <= 0 || heads <= 0) return set_error(LBW_ERR_SHAPE, "chunk_attention: empty query");
+  if (n_chunks < 1 || n_chunks > MAX_CHUNKS)
+    return set_error(LBW_ERR_SHAPE, "chunk_attention: %d chunks (1..%d supported)", n_chunks, MAX_CHUNKS);
+  if (ldq % 8 || ldkv % 8 || ldo % 8 || !aligned(out, 16))
+    return set_error(LBW_ERR_ALIGN, "chunk_attention: row strides must be multiples of 8 elements");
+  if (ldq < (long long)heads * D || ldkv < (long long)heads * D || ldo < (long long)heads * D)
+    return set_error(LBW_ERR_SHAPE, "chunk_attention: row stride smaller than heads*128");
+  if (key_bias && !aligned(key_bias, 4)) return set_error(LBW_ERR_ALIGN, "chunk_attention: key_bias alignment");
+  int err = 0;
+  int* st = device_status(&err);
+  if (!st) return err;
+  CUtensorMap tmQ;
+  KVMaps kv;
+  memset(&kv, 0, sizeof(kv));
+  const uint64_t cols = (uint64_t)heads * D;
+  if ((err = make_tmap_2d(&tmQ, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q_rows, cols, ldq, 64, BM))) return err;
+  for (int c = 0; c < n_chunks; ++c) {
+    if (chunk_rows[c] <= 0) return set_error(LBW_ERR_SHAPE, "chunk_attention: chunk %d is empty", c);
+    if (!k_chunks[c] || !v_chunks[c]) return set_error(LBW_ERR_INVALID, "chunk_attention: null chunk %d", c);
+    if ((err = make_tmap_2d(&kv.k[c], k_chunks[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, chunk_rows[c], cols, ldkv, 64, BN)))
+      return err;
+    if ((err = make_tmap_2d(&kv.v[c], v_chunks[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, chunk_rows[c], cols, ldkv, 64, BN)))
+      return err;
+    kv.rows[c] = chunk_rows[c];
+  }
+  kv.n = n_chunks;
+  static bool attr[2] = {false, false};
+  const int hb = key_bias ? 1 : 0;
+  if (!attr[hb]) {
+    err = cuda_check(cudaFuncSetAttribute(hb ? chunk_attn_kernel<true> : chunk_attn_kernel<false>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+                     "attention smem attribute");
+    if (err) return err;
+    attr[hb] = true;
+  }
+  dim3 grid((q_rows + QT * BM - 1) / (QT * BM), heads);
+  const float scale_log2 = softmax_scale * 1.4426950408889634f;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (hb)
+    chunk_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, key_bias,
+                                                              reinterpret_cast<__nv_bfloat16*>(out), ldo, st);
+  else
+    chunk_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, nullptr,
+                                                               reinterpret_cast<__nv_bfloat16*>(out), ldo, st);
+  return cuda_check(cudaGetLastError(), "attention launch");
+}

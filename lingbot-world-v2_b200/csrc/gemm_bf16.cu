@@ -1,0 +1,427 @@
+// Persistent tcgen05 GEMM, bf16 x bf16 -> fp32 (TMEM) -> fused epilogue.
+//
+//   out[m, n] = epilogue( sum_k A[m, k] * W[n, k] )      A: [M, K] activations, W: [N, K] = nn.Linear weight
+//
+// Tiles: 128 x 256 output per tile (one UMMA M=128, N=256 per K step of 16), K staged 64 at a time
+// (one 128-byte swizzled row per M/N row) through a 4-deep TMA ring. Warp roles:
+//   warp 0   TMA producer (one elected lane)
+//   warp 1   UMMA issuer (one elected lane) and TMEM owner (2 x 256 fp32 accumulator columns)
+//   warps 2-5 epilogue: tcgen05.ld of the accumulator (thread = output row), fused math, global stores.
+// The two accumulators let the epilogue of tile i run while the MMAs of tile i+1 proceed.
+//
+// Epilogues used by the block forward (CausalWanAttentionBlock, wan/modules/model_fast.py:2912-3116):
+//   EpiStore     bias + bf16 store into up to three column regions (the fused q|k|v projection writes
+//                q and k to scratch and v straight into the KV-cache destination chunk), optionally
+//                accumulating each row's sum of squares of the rounded outputs for the RMSNorm that
+//                follows (WanRMSNorm, wan/modules/model.py:126-143).
+//   EpiResidual  x += bf16(acc + b) * gate, then optional FiLM x = (1 + s) * x + t (model_fast.py:3063-3089,
+//                :3110-3111) on the fp32 residual stream.
+//   EpiGelu      GELU_tanh(bf16(acc) + b), optionally followed by an MXFP8 quantise-dequantise of each
+//                32-column block (the FFN-up epilogue, kernels/ffn_epi.py:15-37, and the activation
+//                quantisation of kernels/ffn_mx.py:159-182) for the bf16-pipe MX FFN variant.
+#include "host_common.cuh"
+#include "lbw_common.cuh"
+#include "mx_common.cuh"
+
+namespace lbw {
+
+namespace gemm {
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;   // 16 KB
+constexpr int B_BYTES = BN * BK * 2;   // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+constexpr int THREADS = 192;
+}  // namespace gemm
+
+// ------------------------------------------------------------------------------------------
+// epilogues: chunk() gets 32 consecutive fp32 accumulators of one row and returns a partial
+// row statistic; tile_done() receives the sum over the tile's chunks.
+// ------------------------------------------------------------------------------------------
+struct EpiStore {
+  __nv_bfloat16* out[3];
+  long long ld[3];
+  int row_off[3];
+  float* ss[3];          // per-region row sum-of-squares accumulators (nullable)
+  int region_cols;       // columns per region
+  int ss_per_chunk;      // regions not aligned to the 256-column tile: accumulate per 32-column chunk
+  const __nv_bfloat16* bias;  // [N] (nullable)
+
+  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
+    int r = col / region_cols;
+    int cl = col - r * region_cols;
+    __nv_bfloat16* dst = out[r] + (long long)(row + row_off[r]) * ld[r] + cl;
+    float ssum = 0.f;
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 8) {
+      float b[8];
+      if (bias) {
+        uint4 bb = *reinterpret_cast<const uint4*>(bias + col + e);
+        const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) b[q] = __bfloat162float(bp[q]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) b[q] = 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; q += 2) {
+        float y0 = bf16_round(v[e + q] + b[q]);
+        float y1 = bf16_round(v[e + q + 1] + b[q + 1]);
+        ssum += y0 * y0 + y1 * y1;
+        pk[(e + q) / 2] = pack_bf16(y0, y1);
+      }
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    if (ss_per_chunk) {
+      if (ss[r]) atomicAdd(ss[r] + row, ssum);
+      return 0.f;
+    }
+    return ssum;
+  }
+  LBW_DEV void tile_done(int row, int col0, float ssum) const {
+    int r = col0 / region_cols;
+    if (!ss_per_chunk && ss[r]) atomicAdd(ss[r] + row, ssum);
+  }
+};
+
+struct EpiResidual {
+  float* x;                          // [M, ldx] fp32 residual, updated in place
+  long long ldx;
+  const __nv_bfloat16* bias;         // [N] nullable
+  const float* gate;                 // [N] nullable (gate = 1)
+  const __nv_bfloat16* film_scale;   // [M, N] nullable
+  const __nv_bfloat16* film_shift;   // [M, N] (with film_scale)
+  long long ldf;
+
+  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
+    float* xr = x + (long long)row * ldx + col;
+#pragma unroll
+    for (int e = 0; e < 32; e += 8) {
+      float y[8], g[8], xs[8];
+      if (bias) {
+        uint4 bb = *reinterpret_cast<const uint4*>(bias + col + e);
+        const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q] + __bfloat162float(bp[q]));
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q]);
+      }
+      if (gate) {
+        float4 g0 = *reinterpret_cast<const float4*>(gate + col + e);
+        float4 g1 = *reinterpret_cast<const float4*>(gate + col + e + 4);
+        g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) g[q] = 1.f;
+      }
+      float4 x0 = *reinterpret_cast<const float4*>(xr + e);
+      float4 x1 = *reinterpret_cast<const float4*>(xr + e + 4);
+      xs[0] = x0.x; xs[1] = x0.y; xs[2] = x0.z; xs[3] = x0.w; xs[4] = x1.x; xs[5] = x1.y; xs[6] = x1.z; xs[7] = x1.w;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) xs[q] = __fadd_rn(xs[q], __fmul_rn(y[q], g[q]));
+      if (film_scale) {
+        long long fo = (long long)row * ldf + col + e;
+        uint4 s4 = *reinterpret_cast<const uint4*>(film_scale + fo);
+        uint4 t4 = *reinterpret_cast<const uint4*>(film_shift + fo);
+        const __nv_bfloat16* sp = reinterpret_cast<const __nv_bfloat16*>(&s4);
+        const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(&t4);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float s1 = bf16_round(1.f + __bfloat162float(sp[q]));  // (1.0 + bf16 tensor) stays bf16
+          xs[q] = __fadd_rn(__fmul_rn(s1, xs[q]), __bfloat162float(tp[q]));
+        }
+      }
+      *reinterpret_cast<float4*>(xr + e) = make_float4(xs[0], xs[1], xs[2], xs[3]);
+      *reinterpret_cast<float4*>(xr + e + 4) = make_float4(xs[4], xs[5], xs[6], xs[7]);
+    }
+    return 0.f;
+  }
+  LBW_DEV void tile_done(int, int, float) const {}
+};
+
+struct EpiGelu {
+  __nv_bfloat16* out;   // [M, ldo] GELU(u + b), or its MXFP8 quantise-dequantise
+  long long ldo;
+  const __nv_bfloat16* bias;
+  int qdq;
+
+  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
+    float g[32];
+#pragma unroll
+    for (int e = 0; e < 32; e += 8) {
+      uint4 bb = *reinterpret_cast<const uint4*>(bias + col + e);
+      const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float u = bf16_round(bf16_round(v[e + q]) + __bfloat162float(bp[q]));
+        g[e + q] = bf16_round(gelu_tanh(u));
+      }
+    }
+    uint32_t pk[16];
+    if (qdq) {
+      mx_qdq32(g, pk);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) pk[e >> 1] = pack_bf16(g[e], g[e + 1]);
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(out + (long long)row * ldo + col);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    return 0.f;
+  }
+  LBW_DEV void tile_done(int, int, float) const {}
+};
+
+// ------------------------------------------------------------------------------------------
+// kernel
+// ------------------------------------------------------------------------------------------
+template <class Epi>
+__global__ void __launch_bounds__(gemm::THREADS, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                     int K, Epi epi, int* status) {
+  using namespace gemm;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], done_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    mbar_init(&done_bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(&tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const Abort ab{status, &abort_flag};
+
+  const int nM = (M + BM - 1) / BM, nN = (N + BN - 1) / BN, nK = K / BK;
+  const int tiles = nM * nN;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      long long issued = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int m_blk = t / nN, n_blk = t % nN;
+        bool ok = true;
+        for (int kb = 0; kb < nK; ++kb) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, ab, 1)) { ok = false; break; }
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &full_bar[s], kb * BK, m_blk * BM);
+          tma_load_2d(sa + A_BYTES, &tmB, &full_bar[s], kb * BK, n_blk * BN);
+          ++issued;
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+      }
+      // Drain: every load issued into the ring must have landed before the CTA exits.
+      for (long long i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
+        mbar_wait_drain(&full_bar[i % STAGES], (uint32_t)((i / STAGES) & 1));
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(BM, BN, 0, 0);
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        if (!mbar_wait(&tempty_bar[acc], aph ^ 1, ab, 2)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < nK; ++kb) {
+          if (!mbar_wait(&full_bar[s], ph, ab, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t b0 = a0 + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_f16_ss(d, sdesc_kmajor_sw128(a0 + kk * 32), sdesc_kmajor_sw128(b0 + kk * 32), idesc,
+                       (kb | kk) != 0);
+          tc_commit(&empty_bar[s]);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1;
+      }
+      // All MMAs issued by this thread complete before TMEM is released.
+      tc_commit(&done_bar);
+      mbar_wait_drain(&done_bar, 0);
+    }
+  } else {
+    const int quarter = warp & 3;  // warps 2,3,4,5 -> TMEM lane quarters 2,3,0,1
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const int m_blk = t / nN, n_blk = t % nN;
+      if (!mbar_wait(&tfull_bar[acc], aph, ab, 4)) break;
+      tc_fence_after();
+      const int row = m_blk * BM + quarter * 32 + lane;
+      const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      float stat = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col = n_blk * BN + c * 32;
+        if (col >= N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld32(tb + c * 32, r);
+        tmem_ld_wait();
+        if (row < M) stat += epi.chunk(row, col, reinterpret_cast<const float(&)[32]>(r));
+      }
+      if (row < M) epi.tile_done(row, n_blk * BN, stat);
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+template <class Epi>
+static int launch_gemm(const void* A, long long lda, const void* W, long long ldw, int M, int N, int K, const Epi& epi,
+                       cudaStream_t stream) {
+  using namespace gemm;
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(LBW_ERR_SHAPE, "gemm: empty problem %d x %d x %d", M, N, K);
+  if (K % BK) return set_error(LBW_ERR_SHAPE, "gemm: K=%d must be a multiple of %d", K, BK);
+  if (N % 32) return set_error(LBW_ERR_SHAPE, "gemm: N=%d must be a multiple of 32", N);
+  if (!A || !W) return set_error(LBW_ERR_INVALID, "gemm: null operand");
+  int err = 0;
+  int* st = device_status(&err);
+  if (!st) return err;
+  CUtensorMap tmA, tmB;
+  if ((err = make_tmap_2d(&tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, BK, BM))) return err;
+  if ((err = make_tmap_2d(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldw, BK, BN))) return err;
+  static bool attr_set = false;  // one flag per instantiation
+  if (!attr_set) {
+    err = cuda_check(cudaFuncSetAttribute(gemm_bf16_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+                     "gemm smem attribute");
+    if (err) return err;
+    attr_set = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_bf16_kernel<Epi><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, M, N, K, epi, st);
+  return cuda_check(cudaGetLastError(), "gemm launch");
+}
+
+static bool ok16(const void* p) { return p == nullptr || aligned(p, 16); }
+
+}  // namespace lbw
+
+using namespace lbw;
+
+extern "C" {
+
+int lbw_gemm_bf16(const void* a, long long lda, const void* w, long long ldw, const void* bias, void* out,
+                  long long ldo, int m, int n, int k, void* stream) {
+  if (!out) return set_error(LBW_ERR_INVALID, "lbw_gemm_bf16: null output");
+  if (!ok16(bias) || !ok16(out) || ldo % 8) return set_error(LBW_ERR_ALIGN, "lbw_gemm_bf16: output/bias alignment");
+  EpiStore e{};
+  e.out[0] = e.out[1] = e.out[2] = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ld[0] = e.ld[1] = e.ld[2] = ldo;
+  e.region_cols = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  return launch_gemm(a, lda, w, ldw, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_qkv_proj(const void* h, const void* w_qkv, const void* b_qkv, int m, int c, void* q_raw, void* k_raw,
+                 float* ss_q, float* ss_k, void* v_out, long long ldv, int v_row_off, void* stream) {
+  if (!q_raw || !k_raw || !v_out || !ss_q || !ss_k) return set_error(LBW_ERR_INVALID, "lbw_qkv_proj: null pointer");
+  if (c % 128) return set_error(LBW_ERR_SHAPE, "lbw_qkv_proj: dim %d must be a multiple of 128", c);
+  if (!ok16(q_raw) || !ok16(k_raw) || !ok16(v_out) || !ok16(b_qkv) || ldv % 8)
+    return set_error(LBW_ERR_ALIGN, "lbw_qkv_proj: alignment");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int err = cuda_check(cudaMemsetAsync(ss_q, 0, sizeof(float) * m, s), "ss clear");
+  if (!err) err = cuda_check(cudaMemsetAsync(ss_k, 0, sizeof(float) * m, s), "ss clear");
+  if (err) return err;
+  EpiStore e{};
+  e.out[0] = reinterpret_cast<__nv_bfloat16*>(q_raw);
+  e.out[1] = reinterpret_cast<__nv_bfloat16*>(k_raw);
+  e.out[2] = reinterpret_cast<__nv_bfloat16*>(v_out);
+  e.ld[0] = c; e.ld[1] = c; e.ld[2] = ldv;
+  e.row_off[2] = v_row_off;
+  e.ss[0] = ss_q; e.ss[1] = ss_k; e.ss[2] = nullptr;
+  e.region_cols = c;
+  e.ss_per_chunk = (c % gemm::BN) != 0;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(b_qkv);
+  return launch_gemm(h, c, w_qkv, c, m, 3 * c, c, e, s);
+}
+
+int lbw_linear_rowss(const void* a, const void* w, const void* bias, int m, int n, int k, void* out, float* ss,
+                     void* stream) {
+  if (!out || !ss) return set_error(LBW_ERR_INVALID, "lbw_linear_rowss: null pointer");
+  if (!ok16(out) || !ok16(bias)) return set_error(LBW_ERR_ALIGN, "lbw_linear_rowss: alignment");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int err = cuda_check(cudaMemsetAsync(ss, 0, sizeof(float) * m, s), "ss clear");
+  if (err) return err;
+  EpiStore e{};
+  e.out[0] = e.out[1] = e.out[2] = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ld[0] = e.ld[1] = e.ld[2] = n;
+  e.ss[0] = ss;
+  e.region_cols = n;
+  e.ss_per_chunk = (n % gemm::BN) != 0;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  return launch_gemm(a, k, w, k, m, n, k, e, s);
+}
+
+int lbw_linear_residual(const void* a, const void* w, const void* bias, int m, int n, int k, float* x,
+                        const float* gate, const void* film_scale, const void* film_shift, void* stream) {
+  if (!x) return set_error(LBW_ERR_INVALID, "lbw_linear_residual: null residual");
+  if ((film_scale == nullptr) != (film_shift == nullptr))
+    return set_error(LBW_ERR_INVALID, "lbw_linear_residual: FiLM needs both scale and shift");
+  if (!ok16(x) || !ok16(gate) || !ok16(bias) || !ok16(film_scale) || !ok16(film_shift))
+    return set_error(LBW_ERR_ALIGN, "lbw_linear_residual: alignment");
+  EpiResidual e{};
+  e.x = x; e.ldx = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.gate = gate;
+  e.film_scale = reinterpret_cast<const __nv_bfloat16*>(film_scale);
+  e.film_shift = reinterpret_cast<const __nv_bfloat16*>(film_shift);
+  e.ldf = n;
+  return launch_gemm(a, k, w, k, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_linear_gelu(const void* a, const void* w, const void* bias, int m, int n, int k, void* out, int mx_qdq,
+                    void* stream) {
+  if (!out || !bias) return set_error(LBW_ERR_INVALID, "lbw_linear_gelu: null pointer");
+  if (!ok16(out) || !ok16(bias)) return set_error(LBW_ERR_ALIGN, "lbw_linear_gelu: alignment");
+  EpiGelu e{};
+  e.out = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ldo = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.qdq = mx_qdq;
+  return launch_gemm(a, k, w, k, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,36 @@
+// Host-side helpers shared by the C-ABI entry points: status/error reporting, the per-device
+// status word, TMA tensor-map encoding and launch configuration.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/lbw.h"
+
+namespace lbw {
+
+// Records `code` and a formatted message as this thread's last error; returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+// Device status word of the current device (zeroed on first use). Kernels that wait on
+// mbarriers record timeouts there; lbw_check_device_status() reads and clears it.
+int* device_status(int* err);
+
+// cudaError_t -> LBW_ERR_CUDA with the CUDA error string.
+inline int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return LBW_OK;
+  return set_error(LBW_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Encodes a 2-D row-major tensor map: `rows` x `cols` elements of `elem_bytes` each, row pitch
+// `row_stride_elems`, box `box_cols` x `box_rows`, 128-byte swizzle (box_cols * elem_bytes
+// must be 128). Out-of-bounds rows of a box are zero-filled by the TMA unit.
+int make_tmap_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
+                 uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows);
+
+int num_sms();
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+}  // namespace lbw

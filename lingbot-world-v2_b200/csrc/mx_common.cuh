@@ -1,0 +1,72 @@
+// MXFP8 (OCP Microscaling Formats v1.0) block arithmetic shared by the quantiser, the
+// bf16-pipe FFN epilogue and the block-scaled GEMM epilogue.
+//
+// One block = 32 consecutive values along K. Shared scale X = 2^s with
+//   s = clamp(floor(log2(amax)) - 8, -127, 127)      (8 = exponent of E4M3's largest normal, 448)
+// stored as the E8M0 byte s + 127; elements = RNE(v / X) to E4M3 with saturation to +-448.
+// An all-zero block gets s = -127.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+namespace lbw {
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  float inner = k0 * (x + k1 * x * x * x);
+  return 0.5f * x * (1.f + tanhf(inner));
+}
+
+// Shared exponent of a block from its absolute maximum (exact, from the fp32 bit pattern).
+__device__ __forceinline__ int mx_shared_exp(float amax) {
+  if (!(amax > 0.f)) return -127;
+  int e = (int)((__float_as_uint(amax) >> 23) & 0xFF);
+  int fl = (e == 0) ? -127 : e - 127;  // subnormal amax: floor(log2) <= -127
+  int s = fl - 8;
+  return s < -127 ? -127 : (s > 127 ? 127 : s);
+}
+
+__device__ __forceinline__ uint8_t mx_to_e4m3(float q) {
+  return (uint8_t)__nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ float mx_from_e4m3(uint8_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// Quantise 32 values: elements into q[32], returns the E8M0 scale byte.
+__device__ __forceinline__ uint8_t mx_quant32(const float (&v)[32], uint8_t (&q)[32]) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  int s = mx_shared_exp(amax);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) q[i] = mx_to_e4m3(ldexpf(v[i], -s));
+  return (uint8_t)(s + 127);
+}
+
+// Quantise-dequantise 32 values and pack the (exactly representable) results as bf16 pairs.
+__device__ __forceinline__ void mx_qdq32(const float (&v)[32], uint32_t (&pk)[16]) {
+  uint8_t q[32];
+  int s = (int)mx_quant32(v, q) - 127;
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    float a = ldexpf(mx_from_e4m3(q[i]), s), b = ldexpf(mx_from_e4m3(q[i + 1]), s);
+    __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+    pk[i / 2] = *reinterpret_cast<uint32_t*>(&p);
+  }
+}
+
+// Byte offset of scale (row r, scale column j) in the tiled scale-factor layout used by the
+// block-scaled GEMM: 512-byte atoms of 128 rows x 4 scale columns, atoms ordered row-block
+// major; inside an atom row r = r0 + 32 r1 sits at 16 r0 + 4 r1 + (j % 4).
+__host__ __device__ __forceinline__ long long mx_sf_offset(long long r, long long j, long long k_cols) {
+  long long atoms_per_rowblock = k_cols / 128;  // K/32 scales / 4 per atom
+  long long atom = (r >> 7) * atoms_per_rowblock + (j >> 2);
+  int rr = (int)(r & 127);
+  return atom * 512 + 16 * (rr & 31) + 4 * (rr >> 5) + (j & 3);
+}
+
+}  // namespace lbw

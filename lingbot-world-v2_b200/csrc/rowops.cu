@@ -1,0 +1,232 @@
+// Row kernels of the block forward (HBM-bound; one CTA per row, 16-byte vector accesses):
+//   layernorm_mod   LN(x) * (1 + scale) + shift, or LN(x) * w + b  -> bf16 (optionally MXFP8 QDQ)
+//                   WanLayerNorm + adaLN modulation, wan/modules/model_fast.py:3045, :3101, :2865-2867;
+//                   wan/modules/model.py:145-156; kernels/glue.py:69-166
+//   rmsnorm_rope    bf16(bf16(x * rsqrt(mean(x^2) + eps)) * gamma), then the 3-D RoPE rotation
+//                   wan/modules/model.py:126-143; model_fast.py:878-979; kernels/qk_post.py:37-413
+//   mx_quantize     bf16 -> E4M3 + E8M0 scales (tiled layout), kernels/ffn_mx.py:44-47
+#include "host_common.cuh"
+#include "lbw_common.cuh"
+#include "mx_common.cuh"
+
+namespace lbw {
+
+constexpr int ROW_THREADS = 128;
+constexpr int LN_MAXIT = 6;  // 6 x 128 threads x 8 values = rows up to 6144 wide
+
+__device__ __forceinline__ float block_sum128(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  return red[0] + red[1] + red[2] + red[3];
+}
+
+__global__ void __launch_bounds__(ROW_THREADS) layernorm_mod_kernel(const float* __restrict__ x, int C, float eps,
+                                                                    const float* __restrict__ scale,
+                                                                    const float* __restrict__ shift,
+                                                                    const float* __restrict__ weight,
+                                                                    const float* __restrict__ bias, int mx,
+                                                                    __nv_bfloat16* __restrict__ out) {
+  __shared__ float red[4];
+  const long long row = blockIdx.x;
+  const float* xr = x + row * C;
+  const int G = C >> 3;
+  float v[LN_MAXIT][8];
+  float s = 0.f;
+#pragma unroll
+  for (int it = 0; it < LN_MAXIT; ++it) {
+    const int g = it * ROW_THREADS + threadIdx.x;
+    if (g < G) {
+      float4 a = *reinterpret_cast<const float4*>(xr + g * 8);
+      float4 b = *reinterpret_cast<const float4*>(xr + g * 8 + 4);
+      v[it][0] = a.x; v[it][1] = a.y; v[it][2] = a.z; v[it][3] = a.w;
+      v[it][4] = b.x; v[it][5] = b.y; v[it][6] = b.z; v[it][7] = b.w;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += v[it][e];
+    }
+  }
+  const float mean = block_sum128(s, red) / (float)C;
+  float q = 0.f;
+#pragma unroll
+  for (int it = 0; it < LN_MAXIT; ++it) {
+    const int g = it * ROW_THREADS + threadIdx.x;
+    if (g < G) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = v[it][e] - mean;
+        q += d * d;
+      }
+    }
+  }
+  const float var = block_sum128(q, red) / (float)C;
+  const float rstd = 1.f / sqrtf(var + eps);
+#pragma unroll
+  for (int it = 0; it < LN_MAXIT; ++it) {
+    const int g = it * ROW_THREADS + threadIdx.x;
+    if (it * ROW_THREADS >= G) break;  // block-uniform
+    float y[8];
+    if (g < G) {
+      const int c0 = g * 8;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float n = (v[it][e] - mean) * rstd;
+        if (scale) n = n * (1.f + scale[c0 + e]) + shift[c0 + e];
+        else if (weight) n = n * weight[c0 + e] + bias[c0 + e];
+        y[e] = bf16_round(n);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = 0.f;
+    }
+    if (mx) {
+      // 32-value MX block = 4 consecutive threads x 8 values
+      float amax = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(y[e]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const int se = mx_shared_exp(amax);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = ldexpf(mx_from_e4m3(mx_to_e4m3(ldexpf(y[e], -se))), se);
+    }
+    if (g < G) {
+      uint4 o = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+      *reinterpret_cast<uint4*>(out + row * C + g * 8) = o;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(ROW_THREADS) rmsnorm_rope_kernel(
+    const __nv_bfloat16* __restrict__ x, const float* __restrict__ ss, const __nv_bfloat16* __restrict__ gamma, int C,
+    float eps, const float* __restrict__ rcos, const float* __restrict__ rsin, int n_frames, int gh, int gw, int tok0,
+    __nv_bfloat16* __restrict__ out, long long ldo, int out_row_off) {
+  const long long row = blockIdx.x;
+  const float r = 1.f / sqrtf(ss[row] / (float)C + eps);
+  const int tok = tok0 + (int)row;
+  const int f = tok / (gh * gw), hh = (tok / gw) % gh, ww = tok % gw;
+  const int base_h = n_frames * 22, base_w = base_h + gh * 21;
+  const __nv_bfloat16* xr = x + row * C;
+  __nv_bfloat16* orow = out + (row + out_row_off) * ldo;
+  for (int g = threadIdx.x; g < (C >> 3); g += ROW_THREADS) {
+    uint4 xv = *reinterpret_cast<const uint4*>(xr + g * 8);
+    uint4 gv = *reinterpret_cast<const uint4*>(gamma + g * 8);
+    const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(&xv);
+    const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(&gv);
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = bf16_round(bf16_round(__bfloat162float(xp[e]) * r) * __bfloat162float(gp[e]));
+    if (rcos) {
+      const int p0 = ((g * 8) & 127) >> 1;  // first pair index inside the head
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int p = p0 + k;
+        const int idx = p < 22 ? f * 22 + p : (p < 43 ? base_h + hh * 21 + (p - 22) : base_w + ww * 21 + (p - 43));
+        const float c = rcos[idx], s = rsin[idx];
+        const float re = y[2 * k], im = y[2 * k + 1];
+        y[2 * k] = __fsub_rn(__fmul_rn(re, c), __fmul_rn(im, s));
+        y[2 * k + 1] = __fadd_rn(__fmul_rn(re, s), __fmul_rn(im, c));
+      }
+    }
+    uint4 o = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+    *reinterpret_cast<uint4*>(orow + g * 8) = o;
+  }
+}
+
+// One thread per 32-value block; rows up to the next multiple of 128 get zero scales.
+__global__ void mx_quantize_kernel(const __nv_bfloat16* __restrict__ x, int rows, int K, int rows_pad,
+                                   uint8_t* __restrict__ data, uint8_t* __restrict__ scales,
+                                   __nv_bfloat16* __restrict__ deq) {
+  const int nb = K >> 5;
+  const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= (long long)rows_pad * nb) return;
+  const int r = (int)(id / nb), j = (int)(id % nb);
+  if (r >= rows) {
+    scales[mx_sf_offset(r, j, K)] = 0;
+    return;
+  }
+  const __nv_bfloat16* xp = x + (long long)r * K + j * 32;
+  float v[32];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u = *reinterpret_cast<const uint4*>(xp + q * 8);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[q * 8 + e] = __bfloat162float(b[e]);
+  }
+  uint8_t qb[32];
+  const uint8_t sb = mx_quant32(v, qb);
+  scales[mx_sf_offset(r, j, K)] = sb;
+  uint4* dp = reinterpret_cast<uint4*>(data + (long long)r * K + j * 32);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(qb);
+  dp[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  dp[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  if (deq) {
+    const int se = (int)sb - 127;
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 2)
+      pk[e >> 1] = pack_bf16(ldexpf(mx_from_e4m3(qb[e]), se), ldexpf(mx_from_e4m3(qb[e + 1]), se));
+    uint4* d4 = reinterpret_cast<uint4*>(deq + (long long)r * K + j * 32);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+  }
+}
+
+}  // namespace lbw
+
+using namespace lbw;
+
+extern "C" {
+
+int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scale, const float* shift,
+                      const float* weight, const float* bias, int mx_qdq, void* out, void* stream) {
+  if (!x || !out) return set_error(LBW_ERR_INVALID, "layernorm_mod: null pointer");
+  if ((scale == nullptr) != (shift == nullptr) || (weight == nullptr) != (bias == nullptr) || (scale && weight))
+    return set_error(LBW_ERR_INVALID, "layernorm_mod: give either scale+shift or weight+bias");
+  if (m <= 0 || c <= 0 || c % 32 || c > LN_MAXIT * ROW_THREADS * 8)
+    return set_error(LBW_ERR_SHAPE, "layernorm_mod: width %d must be a multiple of 32 and <= %d", c,
+                     LN_MAXIT * ROW_THREADS * 8);
+  if (!aligned(x, 16) || !aligned(out, 16)) return set_error(LBW_ERR_ALIGN, "layernorm_mod: alignment");
+  layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, c, eps, scale, shift, weight, bias, mx_qdq, reinterpret_cast<__nv_bfloat16*>(out));
+  return cuda_check(cudaGetLastError(), "layernorm_mod launch");
+}
+
+int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, int c, float eps,
+                     const float* rope_cos, const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0,
+                     void* out, long long ldo, int out_row_off, void* stream) {
+  if (!x || !ss || !gamma || !out) return set_error(LBW_ERR_INVALID, "rmsnorm_rope: null pointer");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return set_error(LBW_ERR_INVALID, "rmsnorm_rope: cos/sin pair");
+  if (m <= 0 || c <= 0 || c % 128) return set_error(LBW_ERR_SHAPE, "rmsnorm_rope: width %d must be a multiple of 128", c);
+  if (rope_cos && (grid_h <= 0 || grid_w <= 0 || rope_frames <= 0 || tok0 < 0 ||
+                   (tok0 + m - 1) / (grid_h * grid_w) >= rope_frames))
+    return set_error(LBW_ERR_SHAPE, "rmsnorm_rope: tokens %d..%d outside a %d-frame %dx%d grid", tok0, tok0 + m - 1,
+                     rope_frames, grid_h, grid_w);
+  if (!aligned(x, 16) || !aligned(gamma, 16) || !aligned(out, 16) || ldo % 8)
+    return set_error(LBW_ERR_ALIGN, "rmsnorm_rope: alignment");
+  const int n_frames = rope_cos ? rope_frames : 0;
+  rmsnorm_rope_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ss, reinterpret_cast<const __nv_bfloat16*>(gamma), c, eps, rope_cos,
+      rope_sin, n_frames, grid_h > 0 ? grid_h : 1, grid_w > 0 ? grid_w : 1, tok0,
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, out_row_off);
+  return cuda_check(cudaGetLastError(), "rmsnorm_rope launch");
+}
+
+int lbw_mx_quantize(const void* x, int rows, int k, void* data, void* scales, void* dequant, void* stream) {
+  if (!x || !data || !scales) return set_error(LBW_ERR_INVALID, "mx_quantize: null pointer");
+  if (rows <= 0 || k <= 0 || k % 128) return set_error(LBW_ERR_SHAPE, "mx_quantize: K=%d must be a multiple of 128", k);
+  if (!aligned(x, 16) || !aligned(data, 16) || (dequant && !aligned(dequant, 16)))
+    return set_error(LBW_ERR_ALIGN, "mx_quantize: alignment");
+  const int rows_pad = (rows + 127) / 128 * 128;
+  const long long n = (long long)rows_pad * (k / 32);
+  const int threads = 256;
+  mx_quantize_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), rows, k, rows_pad, reinterpret_cast<uint8_t*>(data),
+      reinterpret_cast<uint8_t*>(scales), reinterpret_cast<__nv_bfloat16*>(dequant));
+  return cuda_check(cudaGetLastError(), "mx_quantize launch");
+}
+
+}  // extern "C"

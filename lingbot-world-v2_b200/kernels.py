@@ -1,0 +1,167 @@
+"""Torch-tensor wrappers over the C ABI (one function per lbw_* entry point).
+
+Every wrapper validates dtypes/devices, passes raw pointers and the current CUDA stream, and turns a
+non-zero status into ValueError / LbwError. Outputs may be passed in (written in place) or are
+allocated here.
+"""
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from ._lib import check, load, ptr, require_cuda, stream_of
+
+BF16 = torch.bfloat16
+HEAD_DIM = 128
+
+
+def _c(t, dtype=None):
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"expected {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError("expected a contiguous tensor")
+    return t
+
+
+def _rows(t):
+    """2-D [rows, cols] view of a [.., rows, heads, d] / [rows, cols] tensor (must be contiguous)."""
+    _c(t)
+    return t.reshape(-1, t.shape[-2] * t.shape[-1]) if t.dim() >= 3 else t
+
+
+def chunk_attention(q, k_chunks, v_chunks, key_bias=None, out=None, softmax_scale=None):
+    """q [Lq, H, 128] (or [1, Lq, H, 128] / [Lq, H*128]) bf16; chunks [L_i, H, 128]-like bf16 ->
+    out [Lq, H*128] bf16 = softmax(q kᵀ * scale + bias) v over the concatenated chunks."""
+    require_cuda(q, *k_chunks, *v_chunks, key_bias, out)
+    q2 = _rows(_c(q, BF16))
+    lq, cols = q2.shape
+    if cols % HEAD_DIM:
+        raise ValueError("head_dim must be 128")
+    heads = cols // HEAD_DIM
+    n = len(k_chunks)
+    if n != len(v_chunks) or n == 0:
+        raise ValueError("need the same, non-zero number of K and V chunks")
+    ks = [_rows(_c(k, BF16)) for k in k_chunks]
+    vs = [_rows(_c(v, BF16)) for v in v_chunks]
+    for k, v in zip(ks, vs):
+        if k.shape != v.shape or k.shape[1] != cols:
+            raise ValueError(f"chunk shape {tuple(k.shape)} / {tuple(v.shape)} does not match q width {cols}")
+    if out is None:
+        out = torch.empty(lq, cols, dtype=BF16, device=q.device)
+    o2 = _rows(_c(out, BF16))
+    kp = (ctypes.c_void_p * n)(*[k.data_ptr() for k in ks])
+    vp = (ctypes.c_void_p * n)(*[v.data_ptr() for v in vs])
+    rows = (ctypes.c_int * n)(*[k.shape[0] for k in ks])
+    if key_bias is not None:
+        key_bias = _c(key_bias, torch.float32)
+        if key_bias.numel() != sum(k.shape[0] for k in ks):
+            raise ValueError("key_bias needs one value per key")
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(HEAD_DIM)
+    check(load().lbw_chunk_attention(ptr(q2), q2.stride(0), lq, heads, kp, vp, rows, n, cols, ptr(key_bias),
+                                     ctypes.c_float(scale), ptr(o2), o2.stride(0), stream_of(q.device)),
+          "chunk_attention")
+    return out
+
+
+def gemm_bf16(a, w, bias=None, out=None):
+    require_cuda(a, w, bias, out)
+    _c(a, BF16), _c(w, BF16)
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError("gemm_bf16: K mismatch")
+    if out is None:
+        out = torch.empty(m, n, dtype=BF16, device=a.device)
+    check(load().lbw_gemm_bf16(ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(bias), ptr(out), out.stride(0), m, n,
+                               k, stream_of(a.device)), "gemm_bf16")
+    return out
+
+
+def qkv_proj(h, w_qkv, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, v_row_off=0):
+    require_cuda(h, w_qkv, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out)
+    m, c = h.shape
+    v2 = _rows(v_out)
+    if w_qkv.shape != (3 * c, c) or q_raw.shape != (m, c) or k_raw.shape != (m, c) or ss_q.numel() < m:
+        raise ValueError("qkv_proj: shape mismatch")
+    if v2.shape[1] != c or v_row_off < 0 or v_row_off + m > v2.shape[0]:
+        raise ValueError(f"qkv_proj: rows {v_row_off}..{v_row_off + m} outside the V destination ({v2.shape[0]} rows)")
+    check(load().lbw_qkv_proj(ptr(h), ptr(w_qkv), ptr(b_qkv), m, c, ptr(q_raw), ptr(k_raw), ptr(ss_q), ptr(ss_k),
+                              ptr(v2), v2.stride(0), v_row_off, stream_of(h.device)), "qkv_proj")
+
+
+def linear_rowss(a, w, bias, out, ss):
+    require_cuda(a, w, bias, out, ss)
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k or out.shape != (m, n) or ss.numel() < m:
+        raise ValueError("linear_rowss: shape mismatch")
+    check(load().lbw_linear_rowss(ptr(a), ptr(w), ptr(bias), m, n, k, ptr(out), ptr(ss), stream_of(a.device)),
+          "linear_rowss")
+    return out
+
+
+def linear_residual(a, w, bias, x, gate=None, film_scale=None, film_shift=None):
+    require_cuda(a, w, bias, x, gate, film_scale, film_shift)
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k or x.shape != (m, n) or x.dtype != torch.float32:
+        raise ValueError("linear_residual: x must be fp32 [m, n]")
+    for t in (film_scale, film_shift):
+        if t is not None and (t.shape != (m, n) or t.dtype != BF16 or not t.is_contiguous()):
+            raise ValueError("linear_residual: FiLM tensors must be contiguous bf16 [m, n]")
+    check(load().lbw_linear_residual(ptr(a), ptr(w), ptr(bias), m, n, k, ptr(x), ptr(gate), ptr(film_scale),
+                                     ptr(film_shift), stream_of(a.device)), "linear_residual")
+    return x
+
+
+def linear_gelu(a, w, bias, out, mx_qdq):
+    require_cuda(a, w, bias, out)
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k or out.shape != (m, n):
+        raise ValueError("linear_gelu: shape mismatch")
+    check(load().lbw_linear_gelu(ptr(a), ptr(w), ptr(bias), m, n, k, ptr(out), int(mx_qdq), stream_of(a.device)),
+          "linear_gelu")
+    return out
+
+
+def layernorm_mod(x, eps, out, scale=None, shift=None, weight=None, bias=None, mx_qdq=False):
+    require_cuda(x, out)
+    _c(x, torch.float32)
+    m, c = x.shape
+    check(load().lbw_layernorm_mod(ptr(x), m, c, ctypes.c_float(eps), ptr(scale), ptr(shift), ptr(weight), ptr(bias),
+                                   int(mx_qdq), ptr(out), stream_of(x.device)), "layernorm_mod")
+    return out
+
+
+def rmsnorm_rope(x, ss, gamma, eps, out, rope=None, grid=None, tok0=0, out_row_off=0):
+    """rope = (cos, sin, n_frames) from rope.rope_tables; grid = (f, h, w)."""
+    require_cuda(x, ss, gamma, out)
+    m, c = x.shape
+    o2 = _rows(out)
+    if o2.shape[1] != c or out_row_off < 0 or out_row_off + m > o2.shape[0] or ss.numel() < m:
+        raise ValueError(f"rmsnorm_rope: rows {out_row_off}..{out_row_off + m} outside the output ({o2.shape[0]} rows)")
+    if rope is not None:
+        cos, sin, nf = rope
+        gh, gw = int(grid[1]), int(grid[2])
+    else:
+        cos = sin = None
+        nf = gh = gw = 0
+    check(load().lbw_rmsnorm_rope(ptr(x), ptr(ss), ptr(gamma), m, c, ctypes.c_float(eps), ptr(cos), ptr(sin), nf, gh,
+                                  gw, tok0, ptr(o2), o2.stride(0), out_row_off, stream_of(x.device)), "rmsnorm_rope")
+    return out
+
+
+def mx_quantize(x, dequant=False):
+    """x [rows, K] bf16 -> (data uint8 [rows, K] E4M3 codes, scales uint8 tiled, dequant bf16 or None)."""
+    require_cuda(x)
+    _c(x, BF16)
+    rows, k = x.shape
+    rows_pad = (rows + 127) // 128 * 128
+    data = torch.empty(rows, k, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(rows_pad * (k // 32), dtype=torch.uint8, device=x.device)
+    deq = torch.empty_like(x) if dequant else None
+    check(load().lbw_mx_quantize(ptr(x), rows, k, ptr(data), ptr(scales), ptr(deq), stream_of(x.device)),
+          "mx_quantize")
+    return data, scales, deq

@@ -1,0 +1,85 @@
+"""Seeded synthetic inputs for one block (TEST INFRASTRUCTURE ONLY, see oracle/__init__.py).
+
+Distributions follow the benchmark definition: Linear weights and biases ~N(0, 0.02); RMSNorm
+gammas and the norm3 affine ~N(0, 0.02) ("flat" scores) or 1 + N(0, 0.02) ("peaked", which
+exercises the online softmax max); adaLN modulation and e0 ~N(0, 0.1); x ~N(0, 1) rounded to bf16
+and kept fp32; KV-cache entries and the text context ~N(0, 1) bf16; hoisted camera FiLM
+scale/shift ~N(0, 0.1) bf16. Everything is drawn from numpy's PCG64 so the same seed gives the
+same tensors on any machine.
+"""
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+HEAD_DIM = 128
+
+
+@dataclass
+class BlockCase:
+    dim: int = 256
+    ffn: int = 512
+    grid: tuple = (3, 4, 6)        # (frames, h, w) of the query chunk
+    n_lead: int = 2                # leading cache chunks (each one chunk of grid tokens)
+    lead_rows: tuple = ()          # override per-chunk lengths of the leading chunks
+    text_len: int = 32
+    start_frame: int = 6
+    peaked: bool = False
+    film: bool = True
+    dedup_rows: int = 0            # >0: context rows >= this are identical (cross_dedup input)
+    seed: int = 0
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def heads(self):
+        return self.dim // HEAD_DIM
+
+    @property
+    def lq(self):
+        f, h, w = self.grid
+        return f * h * w
+
+
+def _n(rng, shape, std, mean=0.0):
+    return torch.from_numpy((rng.standard_normal(shape) * std + mean).astype(np.float32))
+
+
+def make_params(case: BlockCase, rng):
+    C, Fd = case.dim, case.ffn
+    bf = torch.bfloat16
+    p = {}
+    for blk in ("self_attn", "cross_attn"):
+        for nm in ("q", "k", "v", "o"):
+            p[f"{blk}.{nm}.weight"] = _n(rng, (C, C), 0.02).to(bf)
+            p[f"{blk}.{nm}.bias"] = _n(rng, (C,), 0.02).to(bf)
+        g_mean = 1.0 if case.peaked else 0.0
+        p[f"{blk}.norm_q.weight"] = _n(rng, (C,), 0.02, g_mean).to(bf)
+        p[f"{blk}.norm_k.weight"] = _n(rng, (C,), 0.02, g_mean).to(bf)
+    n3_mean = 1.0 if case.peaked else 0.0
+    p["norm3.weight"] = _n(rng, (C,), 0.02, n3_mean).to(bf).float()
+    p["norm3.bias"] = _n(rng, (C,), 0.02).to(bf).float()
+    p["ffn.0.weight"] = _n(rng, (Fd, C), 0.02).to(bf)
+    p["ffn.0.bias"] = _n(rng, (Fd,), 0.02).to(bf)
+    p["ffn.2.weight"] = _n(rng, (C, Fd), 0.02).to(bf)
+    p["ffn.2.bias"] = _n(rng, (C,), 0.02).to(bf)
+    p["modulation"] = _n(rng, (1, 6, C), 0.1)
+    return p
+
+
+def make_case(case: BlockCase):
+    """Returns (params, inputs) as CPU tensors."""
+    rng = np.random.Generator(np.random.PCG64(case.seed))
+    p = make_params(case, rng)
+    C, H, Lq = case.dim, case.heads, case.lq
+    e0 = _n(rng, (6, C), 0.1)
+    x = _n(rng, (Lq, C), 1.0).to(torch.bfloat16).float()
+    rows = list(case.lead_rows) if case.lead_rows else [Lq] * case.n_lead
+    k_lead = [_n(rng, (r, H, HEAD_DIM), 1.0).to(torch.bfloat16) for r in rows]
+    v_lead = [_n(rng, (r, H, HEAD_DIM), 1.0).to(torch.bfloat16) for r in rows]
+    ctx = _n(rng, (case.text_len, C), 1.0).to(torch.bfloat16)
+    if case.dedup_rows:
+        ctx[case.dedup_rows:] = ctx[case.dedup_rows]
+    film = None
+    if case.film:
+        film = (_n(rng, (Lq, C), 0.1).to(torch.bfloat16), _n(rng, (Lq, C), 0.1).to(torch.bfloat16))
+    return p, dict(x=x, e0=e0, k_lead=k_lead, v_lead=v_lead, context=ctx, film=film)

@@ -1,0 +1,174 @@
+"""Generate golden fixtures from the REFERENCE implementation's own PyTorch code.
+
+Run in the build container, where the reference checkout exists (default /root/reference, or
+$LBW_REFERENCE):   python tests/golden/make_golden.py
+
+It imports yahavb/lingbot-world-v2's wan/modules/model_fast.py on CPU through small import shims
+(the Neuron-only packages diffusers/easydict/torch_neuronx are absent here), builds one
+CausalWanAttentionBlock (model_fast.py:2837-3116) with the seeded parameters of oracle.inputs,
+runs its chunked-KV forward (kv_chunks path, exact attention -> SDPA) and saves the block output,
+the destination-chunk K/V it writes and the outputs of self_attn / cross_attn / ffn. It also saves
+the reference's cross_dedup_bias + cross_attention_dedup (wan/modules/attention.py:516-554) on a
+duplicated-context case and the reference's RoPE grids. Inputs are NOT stored: they are
+regenerated from the seed by oracle.inputs.make_case; a checksum guards against drift.
+
+Nothing at test or bench time reads the reference; only the .pt files produced here are used.
+"""
+import contextlib
+import os
+import sys
+import types
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("LBW_REFERENCE", "/root/reference")
+sys.path.insert(0, ROOT)
+
+from oracle.inputs import BlockCase, make_case  # noqa: E402
+
+CASES = {
+    "block_flat": BlockCase(dim=256, ffn=512, grid=(3, 4, 6), n_lead=2, text_len=32, start_frame=6, seed=1),
+    "block_peaked": BlockCase(dim=256, ffn=384, grid=(3, 5, 7), lead_rows=(50, 105), text_len=40, start_frame=9,
+                              peaked=True, seed=2),
+    "block_nofilm": BlockCase(dim=384, ffn=512, grid=(2, 4, 8), n_lead=1, text_len=24, start_frame=2, film=False,
+                              seed=3),
+}
+DEDUP = BlockCase(dim=256, ffn=256, grid=(1, 8, 8), n_lead=0, text_len=64, dedup_rows=20, peaked=True, seed=4)
+
+
+def install_shims():
+    """Minimal stand-ins for the Neuron-only imports of the reference modules."""
+    d = types.ModuleType("diffusers")
+    cu = types.ModuleType("diffusers.configuration_utils")
+    mu = types.ModuleType("diffusers.models.modeling_utils")
+    dm = types.ModuleType("diffusers.models")
+
+    class ConfigMixin:
+        pass
+
+    def register_to_config(f):
+        return f
+
+    cu.ConfigMixin, cu.register_to_config = ConfigMixin, register_to_config
+    mu.ModelMixin = torch.nn.Module
+    d.configuration_utils, d.models, dm.modeling_utils = cu, dm, mu
+    sys.modules.update({"diffusers": d, "diffusers.configuration_utils": cu, "diffusers.models": dm,
+                        "diffusers.models.modeling_utils": mu})
+    ed = types.ModuleType("easydict")
+
+    class EasyDict(dict):
+        __getattr__ = dict.get
+
+    ed.EasyDict = EasyDict
+    sys.modules["easydict"] = ed
+    # packages without their __init__ (wan/__init__.py pulls the whole pipeline)
+    for name, sub in (("wan", ""), ("wan.modules", "modules"), ("wan.distributed", "distributed")):
+        m = types.ModuleType(name)
+        m.__path__ = [os.path.join(REF, "wan", sub) if sub else os.path.join(REF, "wan")]
+        sys.modules[name] = m
+    sys.path.insert(0, REF)
+    # model_fast decorates with torch.compile(backend="neuron") at import
+    from torch._dynamo import register_backend
+
+    @register_backend(name="neuron")
+    def _neuron_backend(gm, example_inputs):
+        return gm.forward
+
+    # autocast('neuron', ...) -> the CPU autocast (fp32 requests are a no-op there)
+    orig = torch.amp.autocast
+
+    class _Autocast(orig):
+        def __init__(self, device_type, *a, **k):
+            super().__init__("cpu" if device_type == "neuron" else device_type, *a, **k)
+
+    torch.amp.autocast = _Autocast
+
+
+def checksum(p, inp):
+    s = 0.0
+    for t in list(p.values()) + [inp["x"], inp["e0"], inp["context"]] + inp["k_lead"] + inp["v_lead"]:
+        s += float(t.float().abs().sum())
+    return s
+
+
+def run_block(mf, case):
+    p, inp = make_case(case)
+    C, H, (f, h, w) = case.dim, case.heads, case.grid
+    Lq = case.lq
+    blk = mf.CausalWanAttentionBlock(C, case.ffn, H, local_attn_size=-1, sink_size=0, qk_norm=True,
+                                     cross_attn_norm=True, eps=1e-6)
+    blk = blk.to(torch.bfloat16)
+    blk.modulation.data = blk.modulation.data.float()
+    blk.norm3.weight.data = blk.norm3.weight.data.float()
+    blk.norm3.bias.data = blk.norm3.bias.data.float()
+    sd = blk.state_dict()
+    for k_, v_ in p.items():
+        assert k_ in sd, k_
+        sd[k_] = v_.to(sd[k_].dtype)
+    blk.load_state_dict(sd)
+    blk.eval()
+    caps = {}
+    for nm in ("self_attn", "cross_attn", "ffn"):
+        getattr(blk, nm).register_forward_hook(lambda m, a, o, nm=nm: caps.__setitem__(nm, o.detach().clone()))
+    d = 128
+    freqs = torch.cat([mf.rope_params(1024, d - 4 * (d // 6)), mf.rope_params(1024, 2 * (d // 6)),
+                       mf.rope_params(1024, 2 * (d // 6))], dim=1)
+    grid_sizes = torch.tensor([[f, h, w]])
+    cos_g, sin_g = mf._causal_rope_grids_build(freqs, grid_sizes, "cpu", case.start_frame)
+    k_chunks = [k.unsqueeze(0).clone() for k in inp["k_lead"]] + [torch.zeros(1, Lq, H, d, dtype=torch.bfloat16)]
+    v_chunks = [v.unsqueeze(0).clone() for v in inp["v_lead"]] + [torch.zeros(1, Lq, H, d, dtype=torch.bfloat16)]
+    ccache = {"k": torch.zeros(1, case.text_len, H, d, dtype=torch.bfloat16),
+              "v": torch.zeros(1, case.text_len, H, d, dtype=torch.bfloat16), "is_init": torch.zeros(1)}
+    cond = {"cam_film": (inp["film"][0].unsqueeze(0), inp["film"][1].unsqueeze(0))} if inp["film"] else None
+    with torch.no_grad():
+        out = blk(inp["x"].unsqueeze(0), inp["e0"].view(1, 1, 6, C), seq_lens=torch.tensor([Lq]),
+                  grid_sizes=grid_sizes, freqs=freqs, context=inp["context"].unsqueeze(0), context_lens=None,
+                  dit_cond_dict=cond, crossattn_cache=ccache, current_start=case.start_frame * h * w,
+                  frame_seqlen=h * w, cross_attn_first_call=True, rope_grids=(cos_g, sin_g),
+                  rope_local_grid=[(f, h, w)], kv_chunks=(k_chunks, v_chunks), grid_ints=[(f, h, w)])
+    return dict(case=case.__dict__, checksum=checksum(p, inp), x=out[0].float(), k_dest=k_chunks[-1][0].clone(),
+                v_dest=v_chunks[-1][0].clone(), self_attn=caps["self_attn"][0], cross_attn=caps["cross_attn"][0],
+                ffn=caps["ffn"][0], ctx_k=ccache["k"][0].clone(), ctx_v=ccache["v"][0].clone(),
+                rope_cos=cos_g[0].reshape(Lq, -1).clone(), rope_sin=sin_g[0].reshape(Lq, -1).clone())
+
+
+def run_dedup(attn_mod, mf):
+    """Reference cross_dedup on a context whose rows >= dedup_rows are identical."""
+    case = DEDUP
+    p, inp = make_case(case)
+    C, H, d = case.dim, case.heads, 128
+    from oracle.block import cross_kv
+    ck, cv = cross_kv(p, inp["context"])            # [T, H, d] each (restated projection)
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(1, case.lq, H, d, generator=g).to(torch.bfloat16)
+    kc = 32
+    bias = attn_mod.cross_dedup_bias(ck, cv, kc)
+    out = attn_mod.cross_attention_dedup(q, ck.permute(1, 2, 0).contiguous(), cv.permute(1, 0, 2).contiguous(),
+                                         bias, kc)
+    full = attn_mod.attention(q, ck.unsqueeze(0), cv.unsqueeze(0))
+    return dict(case=case.__dict__, q=q[0], ctx_k=ck, ctx_v=cv, kc=kc, bias=bias, out=out[0], full=full[0])
+
+
+def main():
+    install_shims()
+    with contextlib.redirect_stdout(sys.stderr):
+        import wan.modules.model_fast as mf
+        import wan.modules.attention as attn_mod
+        import wan.modules.chunked_kv_cache as ckv
+    torch.manual_seed(0)
+    for name, case in CASES.items():
+        res = run_block(mf, case)
+        torch.save(res, os.path.join(HERE, f"{name}.pt"))
+        print(name, "x", tuple(res["x"].shape), "saved")
+    res = run_dedup(attn_mod, mf)
+    torch.save(res, os.path.join(HERE, "cross_dedup.pt"))
+    print("cross_dedup saved")
+    table = {(i, n): ckv.chunk_routing(i, n) for n in (1, 2, 3, 4, 7) for i in range(0, 12)}
+    torch.save(table, os.path.join(HERE, "chunk_routing.pt"))
+    print("chunk_routing saved")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+"""Block parity on a B200: the drop-in CausalWanAttentionBlock (lbw_b200.block) against the reference
+block's own outputs (golden fixtures) and the CPU oracle, through the C ABI kernels."""
+import pytest
+import torch
+
+from conftest import load_golden, max_abs, rel_l2
+from oracle import block as ob
+from oracle.inputs import BlockCase, make_case
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def _build(case, p, dev, ffn_mx, dedup=0):
+    import lbw_b200.block as B
+    blk = B.CausalWanAttentionBlock(case.dim, case.ffn, case.heads, qk_norm=True, cross_attn_norm=True,
+                                    ffn_mx=ffn_mx, cross_dedup=dedup)
+    sd = blk.state_dict()
+    for k, v in p.items():
+        sd[k] = v.to(sd[k].dtype)
+    blk.load_state_dict(sd)
+    return blk.to(dev)
+
+
+def _run(blk, case, inp, dev, poison=False):
+    C, H, Lq = case.dim, case.heads, case.lq
+    ks = [k.unsqueeze(0).to(dev) for k in inp["k_lead"]] + [torch.zeros(1, Lq, H, 128, dtype=BF, device=dev)]
+    vs = [v.unsqueeze(0).to(dev) for v in inp["v_lead"]] + [torch.zeros(1, Lq, H, 128, dtype=BF, device=dev)]
+    if poison:
+        ks[-1].fill_(float("nan"))
+        vs[-1].fill_(float("nan"))
+    cc = {"k": torch.zeros(1, case.text_len, H, 128, dtype=BF, device=dev),
+          "v": torch.zeros(1, case.text_len, H, 128, dtype=BF, device=dev), "is_init": torch.zeros(1, device=dev)}
+    cond = None
+    if inp["film"] is not None:
+        cond = {"cam_film": (inp["film"][0].unsqueeze(0).to(dev), inp["film"][1].unsqueeze(0).to(dev))}
+    f, h, w = case.grid
+    out = blk(inp["x"].unsqueeze(0).to(dev), inp["e0"].view(1, 1, 6, C).to(dev), grid_ints=[case.grid],
+              context=inp["context"].unsqueeze(0).to(dev), crossattn_cache=cc,
+              current_start=case.start_frame * h * w, frame_seqlen=h * w, kv_chunks=(ks, vs), dit_cond_dict=cond)
+    torch.cuda.synchronize()
+    import lbw_b200._lib as L
+    L.check_device_status()
+    return out[0].float().cpu(), ks[-1][0].cpu(), vs[-1][0].cpu(), cc
+
+
+@pytest.mark.parametrize("name", ["block_flat", "block_peaked", "block_nofilm"])
+def test_block_vs_reference_golden(cuda_dev, name):
+    g = load_golden(name)
+    case = BlockCase(**g["case"])
+    p, inp = make_case(case)
+    blk = _build(case, p, cuda_dev, ffn_mx=False)
+    x, k, v, cc = _run(blk, case, inp, cuda_dev)
+    assert rel_l2(x, g["x"]) <= 1e-2 and max_abs(x, g["x"]) <= 5e-2
+    assert rel_l2(x - inp["x"], g["x"] - inp["x"]) <= 2e-2
+    assert rel_l2(k, g["k_dest"]) <= 1e-2 and rel_l2(v, g["v_dest"]) <= 1e-2
+    assert rel_l2(cc["k"][0].cpu(), g["ctx_k"]) <= 1e-2 and rel_l2(cc["v"][0].cpu(), g["ctx_v"]) <= 1e-2
+
+
+@pytest.mark.parametrize("peaked", [False, True])
+def test_block_mx_vs_oracle(cuda_dev, peaked):
+    case = BlockCase(dim=512, ffn=1024, grid=(3, 6, 10), n_lead=3, text_len=64, start_frame=9, peaked=peaked, seed=21)
+    p, inp = make_case(case)
+    blk = _build(case, p, cuda_dev, ffn_mx=True)
+    x, k, v, _ = _run(blk, case, inp, cuda_dev)
+    cos, sin = ob.rope_grid(ob.rope_freqs(), case.grid, case.start_frame)
+    ck, cv = ob.cross_kv(p, inp["context"])
+    r = ob.block_forward(p, inp["x"], inp["e0"], inp["k_lead"], inp["v_lead"], ck, cv, cos, sin, film=inp["film"],
+                         mx=True, return_all=True)
+    assert rel_l2(x, r["x"]) <= 1e-2 and max_abs(x, r["x"]) <= 5e-2
+    assert rel_l2(x - inp["x"], r["x"] - inp["x"]) <= 2e-2
+    assert rel_l2(k.view(-1, case.heads, 128), r["k"]) <= 1e-2
+
+
+def test_block_cross_dedup_vs_oracle(cuda_dev):
+    case = BlockCase(dim=256, ffn=512, grid=(2, 4, 8), n_lead=1, text_len=64, dedup_rows=20, seed=23)
+    p, inp = make_case(case)
+    blk = _build(case, p, cuda_dev, ffn_mx=False, dedup=32)
+    x, _, _, _ = _run(blk, case, inp, cuda_dev)
+    cos, sin = ob.rope_grid(ob.rope_freqs(), case.grid, case.start_frame)
+    ck, cv = ob.cross_kv(p, inp["context"])
+    ref = ob.block_forward(p, inp["x"], inp["e0"], inp["k_lead"], inp["v_lead"], ck, cv, cos, sin,
+                           film=inp["film"], dedup_kc=32)
+    full = ob.block_forward(p, inp["x"], inp["e0"], inp["k_lead"], inp["v_lead"], ck, cv, cos, sin, film=inp["film"])
+    assert rel_l2(x, ref) <= 1e-2 and rel_l2(x - inp["x"], ref - inp["x"]) <= 2e-2
+    assert rel_l2(x - inp["x"], full - inp["x"]) <= 3e-2
+
+
+def test_destination_slot_poisoned_with_nan(cuda_dev):
+    """The destination chunk is written before it is read (reference block_bench ZERO_DEST idea)."""
+    case = BlockCase(dim=256, ffn=512, grid=(3, 4, 6), n_lead=2, text_len=32, seed=25)
+    p, inp = make_case(case)
+    blk = _build(case, p, cuda_dev, ffn_mx=True)
+    a = _run(blk, case, inp, cuda_dev)
+    b = _run(blk, case, inp, cuda_dev, poison=True)
+    assert torch.isfinite(b[0]).all()
+    assert rel_l2(a[0], b[0]) < 1e-6 and torch.equal(a[1], b[1])
+
+
+def test_attention_deterministic(cuda_dev):
+    import lbw_b200.kernels as K
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(1000, 4, 128, generator=g).to(BF).to(cuda_dev)
+    ks = [torch.randn(700, 4, 128, generator=g).to(BF).to(cuda_dev) for _ in range(3)]
+    vs = [torch.randn(700, 4, 128, generator=g).to(BF).to(cuda_dev) for _ in range(3)]
+    a = K.chunk_attention(q, ks, vs)
+    b = K.chunk_attention(q, ks, vs)
+    assert torch.equal(a, b)
+
+
+def test_block_stack_two_blocks(cuda_dev):
+    import lbw_b200.model as M
+    case = BlockCase(dim=256, ffn=512, grid=(3, 4, 6), n_lead=1, text_len=32, seed=27)
+    p, inp = make_case(case)
+    p2, _ = make_case(BlockCase(dim=256, ffn=512, grid=(3, 4, 6), n_lead=1, text_len=32, seed=28))
+    d = cuda_dev
+    st = M.BlockStack(2, case.dim, case.ffn, case.heads, ffn_mx=True)
+    for blk, pp in zip(st.blocks, (p, p2)):
+        sd = blk.state_dict()
+        for k, v in pp.items():
+            sd[k] = v.to(sd[k].dtype)
+        blk.load_state_dict(sd)
+    st = st.to(d)
+    Lq, H, C = case.lq, case.heads, case.dim
+    kl = [[inp["k_lead"][0].unsqueeze(0).to(d), torch.zeros(1, Lq, H, 128, dtype=BF, device=d)] for _ in range(2)]
+    vl = [[inp["v_lead"][0].unsqueeze(0).to(d), torch.zeros(1, Lq, H, 128, dtype=BF, device=d)] for _ in range(2)]
+    caches = [{"k": torch.zeros(case.text_len, H, 128, dtype=BF, device=d),
+               "v": torch.zeros(case.text_len, H, 128, dtype=BF, device=d)} for _ in range(2)]
+    import lbw_b200.rope as R
+    xf = inp["x"].to(d).clone()
+    film = [(inp["film"][0].to(d), inp["film"][1].to(d))] * 2
+    st.forward_chunk(xf, inp["e0"].to(d), (kl, vl), inp["context"].to(d), caches, case.grid, case.start_frame,
+                     R.rope_freqs(), films=film, fill_cross=True)
+    torch.cuda.synchronize()
+    cos, sin = ob.rope_grid(ob.rope_freqs(), case.grid, case.start_frame)
+    x = inp["x"]
+    for pp in (p, p2):
+        ck, cv = ob.cross_kv(pp, inp["context"])
+        x = ob.block_forward(pp, x, inp["e0"], inp["k_lead"], inp["v_lead"], ck, cv, cos, sin, film=inp["film"], mx=True)
+    assert rel_l2(xf, x) <= 1e-2 and rel_l2(xf.cpu() - inp["x"], x - inp["x"]) <= 2e-2

@@ -1,0 +1,204 @@
+"""Kernel parity on a B200: every liblbw.so kernel against the CPU oracle (or an fp32 torch reference for
+the plain GEMM) on seeded inputs, through the C ABI."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import max_abs, rel_l2
+from oracle import block as ob
+from oracle import mx as omx
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def _g(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (200, 512, 320), (1000, 768, 1536), (4680, 1536, 1536),
+                                   (77, 96, 128)])
+def test_gemm_bf16(cuda_dev, m, n, k):
+    import lbw_b200.kernels as K
+    g = _g(m + n + k)
+    a = torch.randn(m, k, generator=g).to(BF)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(BF)
+    b = (torch.randn(n, generator=g) * 0.1).to(BF)
+    out = K.gemm_bf16(a.to(cuda_dev), w.to(cuda_dev), b.to(cuda_dev))
+    ref = a.float() @ w.float().t() + b.float()
+    assert rel_l2(out, ref) < 4e-3
+    assert max_abs(out, ref) < 2e-2 * float(ref.abs().max())
+
+
+def test_qkv_proj_regions_and_row_ss(cuda_dev):
+    import lbw_b200.kernels as K
+    g = _g(3)
+    m, c = 300, 512
+    h = torch.randn(m, c, generator=g).to(BF)
+    w = (torch.randn(3 * c, c, generator=g) * 0.02).to(BF)
+    b = (torch.randn(3 * c, generator=g) * 0.02).to(BF)
+    d = cuda_dev
+    q, k = torch.empty(m, c, dtype=BF, device=d), torch.empty(m, c, dtype=BF, device=d)
+    ss = torch.empty(2, m, device=d)
+    v_dst = torch.full((m + 64, c), float("nan"), dtype=BF, device=d)
+    K.qkv_proj(h.to(d), w.to(d), b.to(d), q, k, ss[0], ss[1], v_dst, v_row_off=64)
+    ref = ob.linear(h, w, b)
+    assert rel_l2(q, ref[:, :c]) < 4e-3 and rel_l2(k, ref[:, c:2 * c]) < 4e-3
+    assert rel_l2(v_dst[64:], ref[:, 2 * c:]) < 4e-3
+    assert torch.isnan(v_dst[:64].float()).all()
+    assert rel_l2(ss[0], q.float().pow(2).sum(1)) < 1e-5
+    assert rel_l2(ss[1], k.float().pow(2).sum(1)) < 1e-5
+
+
+def test_linear_residual_gate_and_film(cuda_dev):
+    import lbw_b200.kernels as K
+    g = _g(4)
+    m, n, k = 260, 512, 256
+    a = torch.randn(m, k, generator=g).to(BF)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(BF)
+    b = (torch.randn(n, generator=g) * 0.05).to(BF)
+    x = torch.randn(m, n, generator=g)
+    gate = torch.randn(n, generator=g) * 0.1
+    fs, ft = (torch.randn(m, n, generator=g) * 0.1).to(BF), (torch.randn(m, n, generator=g) * 0.1).to(BF)
+    d = cuda_dev
+    xd = x.to(d)
+    K.linear_residual(a.to(d), w.to(d), b.to(d), xd, gate=gate.to(d), film_scale=fs.to(d), film_shift=ft.to(d))
+    y = ob.linear(a, w, b)
+    ref = (1.0 + fs) * (x + y.float() * gate) + ft
+    assert rel_l2(xd, ref) < 1e-4 and rel_l2(xd - x.to(d), ref - x) < 5e-3
+    xd2 = x.to(d)
+    K.linear_residual(a.to(d), w.to(d), None, xd2)
+    assert rel_l2(xd2 - x.to(d), ob.linear(a, w, None).float()) < 5e-3
+
+
+@pytest.mark.parametrize("qdq", [False, True])
+def test_linear_gelu(cuda_dev, qdq):
+    import lbw_b200.kernels as K
+    g = _g(5)
+    m, n, k = 333, 768, 512
+    a = torch.randn(m, k, generator=g).to(BF)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(BF)
+    b = (torch.randn(n, generator=g) * 0.05).to(BF)
+    out = torch.empty(m, n, dtype=BF, device=cuda_dev)
+    K.linear_gelu(a.to(cuda_dev), w.to(cuda_dev), b.to(cuda_dev), out, qdq)
+    u = ((a.float() @ w.float().t()).to(BF) + b).to(BF)
+    ref = F.gelu(u.float(), approximate="tanh").to(BF)
+    if qdq:
+        ref = omx.qdq(ref)
+    assert rel_l2(out, ref) < 1e-2
+
+
+def _attn_case(lq, rows, heads, seed, qscale=1.0):
+    g = _g(seed)
+    q = (torch.randn(lq, heads, 128, generator=g) * qscale).to(BF)
+    ks = [torch.randn(r, heads, 128, generator=g).to(BF) for r in rows]
+    vs = [torch.randn(r, heads, 128, generator=g).to(BF) for r in rows]
+    return q, ks, vs
+
+
+@pytest.mark.parametrize("lq,rows,heads,qscale", [
+    (256, [256], 1, 1.0),
+    (300, [200, 77, 128], 2, 1.0),          # ragged query tile and ragged KV tiles
+    (129, [1000], 3, 3.0),                  # peaked: logits up to ~50 -> running-max rescales
+    (512, [72, 72, 72, 72, 72, 72, 72], 2, 2.0),   # 7 chunks (the 21-frame window)
+    (40, [4680, 4680, 4680], 1, 0.5),
+])
+def test_chunk_attention(cuda_dev, lq, rows, heads, qscale):
+    import lbw_b200.kernels as K
+    q, ks, vs = _attn_case(lq, rows, heads, lq + sum(rows), qscale)
+    d = cuda_dev
+    out = K.chunk_attention(q.to(d), [k.to(d) for k in ks], [v.to(d) for v in vs])
+    ref = ob.attention(q, torch.cat(ks), torch.cat(vs))
+    assert rel_l2(out.view(lq, heads, 128), ref) < 1e-2
+    assert max_abs(out.view(lq, heads, 128), ref) < 5e-2
+
+
+def test_chunk_attention_hot_head_rescale(cuda_dev):
+    """Row maxima that grow by far more than 2^8 across KV tiles (hot heads, row max in the hundreds)."""
+    import lbw_b200.kernels as K
+    g = _g(7)
+    lq, heads = 128, 1
+    q = torch.randn(lq, heads, 128, generator=g).to(BF)
+    k = torch.randn(1024, heads, 128, generator=g)
+    k[512:] *= 6.0                          # later tiles have much larger scores
+    k = k.to(BF)
+    v = torch.randn(1024, heads, 128, generator=g).to(BF)
+    out = K.chunk_attention(q.to(cuda_dev), [k.to(cuda_dev)], [v.to(cuda_dev)])
+    ref = ob.attention(q, k, v)
+    assert rel_l2(out.view(lq, heads, 128), ref) < 1e-2
+
+
+def test_chunk_attention_key_bias(cuda_dev):
+    import lbw_b200.kernels as K
+    q, ks, vs = _attn_case(200, [96], 2, 9)
+    bias = torch.zeros(96)
+    bias[40:] = math.log(7.0)
+    out = K.chunk_attention(q.to(cuda_dev), [ks[0].to(cuda_dev)], [vs[0].to(cuda_dev)], key_bias=bias.to(cuda_dev))
+    ref = ob.attention(q, ks[0], vs[0], key_bias=bias)
+    assert rel_l2(out.view(200, 2, 128), ref) < 1e-2
+
+
+def test_cross_dedup_against_reference_golden(cuda_dev):
+    from conftest import load_golden
+    import lbw_b200.attention as A
+    g = load_golden("cross_dedup")
+    d = cuda_dev
+    bias = A.cross_dedup_bias(g["ctx_k"].to(d), g["ctx_v"].to(d), g["kc"])
+    assert torch.allclose(bias.cpu(), g["bias"])
+    out = A.cross_attention_dedup(g["q"].unsqueeze(0).to(d), g["ctx_k"].to(d), g["ctx_v"].to(d), bias, g["kc"])
+    assert rel_l2(out[0], g["out"]) < 1e-2 and rel_l2(out[0], g["full"]) < 1e-2
+
+
+@pytest.mark.parametrize("mode", ["mod", "affine", "mod_mx"])
+def test_layernorm_mod(cuda_dev, mode):
+    import lbw_b200.kernels as K
+    g = _g(11)
+    m, c = 257, 1536
+    x = torch.randn(m, c, generator=g) * 2 + 0.5
+    s, t = torch.randn(c, generator=g) * 0.1, torch.randn(c, generator=g) * 0.1
+    out = torch.empty(m, c, dtype=BF, device=cuda_dev)
+    ln = ob.layer_norm(x, 1e-6)
+    if mode == "affine":
+        K.layernorm_mod(x.to(cuda_dev), 1e-6, out, weight=s.to(cuda_dev), bias=t.to(cuda_dev))
+        ref = ob.layer_norm(x, 1e-6, s, t).to(BF)
+    else:
+        K.layernorm_mod(x.to(cuda_dev), 1e-6, out, scale=s.to(cuda_dev), shift=t.to(cuda_dev), mx_qdq=mode == "mod_mx")
+        ref = (ln * (1 + s) + t).to(BF)
+        if mode == "mod_mx":
+            ref = omx.qdq(ref)
+    assert rel_l2(out, ref) < 2e-3
+
+
+@pytest.mark.parametrize("grid,start,tok0,m", [((3, 4, 6), 6, 0, 72), ((3, 30, 52), 18, 1170, 1170)])
+def test_rmsnorm_rope(cuda_dev, grid, start, tok0, m):
+    import lbw_b200.kernels as K
+    import lbw_b200.rope as R
+    g = _g(13)
+    c = 512
+    x = torch.randn(m, c, generator=g).to(BF)
+    gamma = (1 + 0.02 * torch.randn(c, generator=g)).to(BF)
+    ss = x.float().pow(2).sum(1)
+    d = cuda_dev
+    cos, sin = R.rope_tables(R.rope_freqs(), grid, start, d)
+    out = torch.empty(m + 8, c, dtype=BF, device=d)
+    K.rmsnorm_rope(x.to(d), ss.to(d), gamma.to(d), 1e-6, out, rope=(cos, sin, grid[0]), grid=grid, tok0=tok0,
+                   out_row_off=8)
+    gc, gs = ob.rope_grid(ob.rope_freqs(), grid, start)
+    ref = ob.rope_apply(ob.rms_norm(x, gamma, 1e-6).view(m, c // 128, 128), gc[tok0:tok0 + m], gs[tok0:tok0 + m])
+    assert rel_l2(out[8:].view(m, -1, 128), ref) < 2e-3
+
+
+def test_mx_quantize_bit_exact(cuda_dev):
+    import lbw_b200.kernels as K
+    g = _g(17)
+    rows, k = 300, 512
+    x = (torch.randn(rows, k, generator=g) * torch.logspace(-3, 3, rows).view(-1, 1)).to(BF)
+    x[5] = 0
+    x[7, :32] = 1000.0
+    data, scales, deq = K.mx_quantize(x.to(cuda_dev), dequant=True)
+    q, s = omx.quantize(x)
+    assert torch.equal(data.cpu(), q.view(torch.uint8))
+    assert torch.equal(scales.cpu(), omx.scales_tiled(s, k))
+    assert torch.equal(deq.cpu().float(), omx.dequantize(q, s))

@@ -1,0 +1,44 @@
+"""Pins the CPU oracle (oracle/) to fixtures produced by the reference's own code
+(tests/golden/make_golden.py running wan/modules/model_fast.py CausalWanAttentionBlock on CPU)."""
+import pytest
+import torch
+
+from conftest import load_golden, max_abs, rel_l2
+from oracle import block as ob
+from oracle.inputs import BlockCase, make_case
+from tests.golden.make_golden import checksum
+
+
+@pytest.mark.parametrize("name", ["block_flat", "block_peaked", "block_nofilm"])
+def test_block_matches_reference(name):
+    g = load_golden(name)
+    case = BlockCase(**g["case"])
+    p, inp = make_case(case)
+    assert abs(checksum(p, inp) - g["checksum"]) <= 1e-4 * g["checksum"], "input generator drifted"
+    cos, sin = ob.rope_grid(ob.rope_freqs(), case.grid, case.start_frame)
+    assert torch.equal(cos, g["rope_cos"]) and torch.equal(sin, g["rope_sin"])
+    ck, cv = ob.cross_kv(p, inp["context"])
+    assert rel_l2(ck, g["ctx_k"]) < 1e-3 and rel_l2(cv, g["ctx_v"]) < 1e-3
+    r = ob.block_forward(p, inp["x"], inp["e0"], inp["k_lead"], inp["v_lead"], ck, cv, cos, sin, film=inp["film"],
+                         return_all=True)
+    assert rel_l2(r["x"], g["x"]) < 1e-3
+    assert rel_l2(r["x"] - inp["x"], g["x"] - inp["x"]) < 1e-2
+    assert max_abs(r["x"], g["x"]) < 5e-3
+    assert rel_l2(r["k"], g["k_dest"]) < 1e-3 and rel_l2(r["v"], g["v_dest"]) < 1e-3
+
+
+def test_cross_dedup_matches_reference():
+    g = load_golden("cross_dedup")
+    bias = ob.cross_dedup_bias(g["ctx_k"], g["ctx_v"], g["kc"])
+    assert torch.allclose(bias, g["bias"])
+    out = ob.attention(g["q"], g["ctx_k"][:g["kc"]], g["ctx_v"][:g["kc"]], key_bias=bias)
+    assert rel_l2(out, g["out"]) < 5e-3
+    # dedup with the log-multiplicity bias equals attention over the full duplicated context
+    assert rel_l2(out, g["full"]) < 1e-2
+
+
+def test_chunk_routing_table():
+    import lbw_b200.chunked_kv_cache as ckv
+    table = load_golden("chunk_routing")
+    for (i, n), want in table.items():
+        assert ckv.chunk_routing(i, n) == want, (i, n)
