@@ -7,7 +7,7 @@ runs: the chunked KV cache (kv_chunks=(k_chunks, v_chunks), destination LAST, la
 cached text cross-attention (crossattn_cache={"k", "v", "is_init"}), optional cross_dedup, and the
 MXFP8 FFN (ffn_mx=True, LINGBOT_FFN_MX) or the bf16 FFN.
 
-One forward = 13 kernels of liblbw.so on the current stream:
+One forward = 14 kernels of liblbw.so on the current stream:
   layernorm_mod(norm1 + adaLN) -> qkv_proj (v straight into the destination chunk) ->
   rmsnorm_rope(q) -> rmsnorm_rope(k into the destination chunk) -> [sequence-parallel K/V all-gather]
   -> chunk_attention -> linear_residual(o-proj, gate e2, FiLM) -> layernorm(norm3 affine) ->
@@ -282,4 +282,4 @@ class CausalWanAttentionBlock(nn.Module):
         return xf
 
 
-KERNELS_PER_BLOCK = 13
+KERNELS_PER_BLOCK = 14

@@ -16,6 +16,9 @@
 // the first 64 columns of S_i (tcgen05.st) and the MMA warp accumulates O_i += P_i V from TMEM
 // (A operand) and shared memory (V, MN-major). The running max is only raised when a row's max
 // grows by more than 2^8 (so P <= 256); O_i is then rescaled in TMEM by its own row's thread.
+// Softmax is one tcgen05.ld pass per tile (the row's 128 scores stay in registers), packed fp32x2
+// arithmetic, and a quarter of the exponentials on the FMA pipe (exp2_poly2) so that the SFU, whose
+// rate is exactly one exp per 512 MMA flops, does not bound the loop.
 // MMAs of one CTA execute in issue order, and every tcgen05.commit covers all earlier MMAs:
 // when softmax i sees S_i(j+1) complete, PV_i(j) has completed too, so O_i is stable and P_i(j)
 // has been consumed.
@@ -197,66 +200,108 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         if (!mbar_wait(&s_full[wg], j & 1, ab, 0x40 + wg)) { ok = false; break; }
         tc_fence_after();
         const float* kb = HAS_BIAS ? key_bias + key_base + t0 : nullptr;
-        // pass 1: row max of this tile
-        float mx = -INFINITY;
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t r[32];
-          tmem_ld32(tS + cc * 32, r);
-          tmem_ld_wait();
+        // One pass over S: all 128 scores of this row into registers (4 loads, one wait).
+        uint32_t r[128];
+        tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+        tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+        tmem_ld_wait();
+        float* sv = reinterpret_cast<float*>(r);
+        float a = scale_log2;  // p = exp2(a * s - m); with a key bias the scores are pre-scaled (a = 1)
+        if (HAS_BIAS) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int col = cc * 32 + e;
-            float sv = __uint_as_float(r[e]) * scale_log2;
-            if (HAS_BIAS) sv += kb[col < valid ? col : 0] * LOG2E;
-            if (col >= valid) sv = -INFINITY;
-            mx = fmaxf(mx, sv);
-          }
+          for (int e = 0; e < BN; ++e) sv[e] = sv[e] * scale_log2 + kb[e < valid ? e : 0] * LOG2E;
+          a = 1.f;
         }
+        if (valid < BN) {  // ragged last tile of a chunk (warp-uniform)
+#pragma unroll
+          for (int e = 0; e < BN; ++e)
+            if (e >= valid) sv[e] = -INFINITY;
+        }
+        // row max: 8 independent chains of 3-input max
+        float t8[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t8[q] = sv[q];
+#pragma unroll
+        for (int e = 8; e < 120; e += 16)
+#pragma unroll
+          for (int q = 0; q < 8; ++q) t8[q] = fmax3(t8[q], sv[e + q], sv[e + 8 + q]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t8[q] = fmaxf(t8[q], sv[120 + q]);
+        const float mx = fmaxf(fmax3(t8[0], t8[1], t8[2]), fmax3(fmax3(t8[3], t8[4], t8[5]), t8[6], t8[7])) * a;
         const float m_new = fmaxf(m, mx);
+        // The running max only moves when a row's max grew by more than 2^8; O is then rescaled by
+        // alpha before PV(j) accumulates onto it (below, after P is written and the scores are dead,
+        // but before p_ready releases PV(j)).
+        float alpha = 1.f;
+        bool rescale = false;
         if (j == 0) {
           m = m_new;
         } else {
           const bool need = m_new > m + 8.f;
-          if (__any_sync(0xffffffffu, need)) {
-            const float alpha = need ? fast_exp2(m - m_new) : 1.f;
-            if (need) {
-              l *= alpha;
-              m = m_new;
-            }
-#pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
-              uint32_t r[32];
-              tmem_ld32(tO + cc * 32, r);
-              tmem_ld_wait();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-              tmem_st32(tO + cc * 32, r);
-            }
-            tmem_st_wait();
+          rescale = __any_sync(0xffffffffu, need);
+          if (need) {
+            alpha = fast_exp2(m - m_new);
+            l *= alpha;
+            m = m_new;
           }
         }
-        // pass 2: P = exp2(s - m) -> bf16 into the first 64 columns of S
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t r[32];
-          tmem_ld32(tS + cc * 32, r);
-          tmem_ld_wait();
-          uint32_t pk[16];
+        // P = exp2(a*s - m): 3 of every 4 pairs on the SFU (ex2.approx), 1 on the FMA pipe (exp2_poly2),
+        // which keeps the SFU from being the limit (one exp per 512 MMA flops is exactly its rate).
+        // Scaling, subtraction and the row sum use packed fp32x2 instructions.
+        const uint64_t a2 = f2_pack(a, a), b2 = f2_pack(-m, -m);
+        uint64_t lsum[4] = {0ull, 0ull, 0ull, 0ull};
+        if (valid == BN) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const int col = cc * 32 + e;
-            float s0 = __uint_as_float(r[e]) * scale_log2, s1 = __uint_as_float(r[e + 1]) * scale_log2;
-            if (HAS_BIAS) {
-              s0 += kb[col < valid ? col : 0] * LOG2E;
-              s1 += kb[col + 1 < valid ? col + 1 : 0] * LOG2E;
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const int col = cc * 32 + e;
+              float x0, x1, p0, p1;
+              f2_unpack(f2_fma(f2_pack(sv[col], sv[col + 1]), a2, b2), x0, x1);
+              if ((e & 6) == 6) {
+                exp2_poly2(x0, x1, p0, p1);
+              } else {
+                p0 = fast_exp2(x0);
+                p1 = fast_exp2(x1);
+              }
+              lsum[(e >> 1) & 3] = f2_add(lsum[(e >> 1) & 3], f2_pack(p0, p1));
+              pk[e >> 1] = pack_bf16(p0, p1);
             }
-            const float p0 = col < valid ? fast_exp2(s0 - m) : 0.f;
-            const float p1 = col + 1 < valid ? fast_exp2(s1 - m) : 0.f;
-            l += p0 + p1;
-            pk[e >> 1] = pack_bf16(p0, p1);
+            tmem_st16(tS + cc * 16, pk);
           }
-          tmem_st16(tS + cc * 16, pk);
+        } else {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const int col = cc * 32 + e;
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(sv[col], sv[col + 1]), a2, b2), x0, x1);
+              const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);  // masked scores are -inf -> 0
+              lsum[(e >> 1) & 3] = f2_add(lsum[(e >> 1) & 3], f2_pack(p0, p1));
+              pk[e >> 1] = pack_bf16(p0, p1);
+            }
+            tmem_st16(tS + cc * 16, pk);
+          }
+        }
+        float l0, l1, l2, l3;
+        f2_unpack(f2_add(lsum[0], lsum[1]), l0, l1);
+        f2_unpack(f2_add(lsum[2], lsum[3]), l2, l3);
+        l += (l0 + l1) + (l2 + l3);
+        if (rescale) {  // warp-uniform
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t o[32];
+            tmem_ld32(tO + cc * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + cc * 32, o);
+          }
         }
         tmem_st_wait();
         tc_fence_before();

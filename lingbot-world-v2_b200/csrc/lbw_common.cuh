@@ -260,5 +260,46 @@ LBW_DEV float fast_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed fp32x2 arithmetic (one instruction for the two lanes of a register pair) and 3-input max.
+LBW_DEV uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+LBW_DEV void f2_unpack(uint64_t v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+LBW_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+LBW_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+LBW_DEV float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// Two 2^x on the FMA/ALU pipes (x finite; results below 2^-126 are flushed up to 2^-126).
+// Cody-Waite style range reduction x = n + f with n = round(x) (adding 1.5 * 2^23 leaves n in the
+// low mantissa bits) and f in [-0.5, 0.5]; 2^f by a cubic whose coefficients were fitted for this
+// library by relative-error least squares on [-0.5, 0.5] (max relative error 1.8e-4, below the 2^-9
+// rounding of a bf16 result); the result's exponent field is then raised by n.
+LBW_DEV void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t x = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t t = f2_add(x, f2_pack(12582912.f, 12582912.f));
+  const uint64_t n = f2_add(t, f2_pack(-12582912.f, -12582912.f));  // round(x), exact
+  const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), x);             // x - round(x), exact
+  uint64_t p = f2_fma(f2_pack(0.054602623f, 0.054602623f), f, f2_pack(0.24192412f, 0.24192412f));
+  p = f2_fma(p, f, f2_pack(0.69331646f, 0.69331646f));
+  p = f2_fma(p, f, f2_pack(1.f, 1.f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  y0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(t0) - 0x4B400000) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(t1) - 0x4B400000) << 23));
+}
 
 }  // namespace lbw
