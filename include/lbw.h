@@ -89,6 +89,20 @@ int lbw_linear_residual(const void* a, const void* w, const void* bias, int m, i
 int lbw_linear_gelu(const void* a, const void* w, const void* bias, int m, int n, int k, void* out, int mx_qdq,
                     void* stream);
 
+/* Allocation-free linear + RMSNorm: out[m, n] = bf16(bf16(y * rsqrt(mean_n(y^2) + eps)) * gamma) with
+ * y = bf16(a w^T + bias) -- the result of lbw_linear_rowss followed by lbw_rmsnorm_rope without RoPE, but
+ * the per-row sums of squares are kept in a fixed 256 KB array inside the library (m <= 65536 rows;
+ * larger m returns LBW_ERR_SHAPE) instead of a caller buffer, and no device memory is ever allocated
+ * (not even the status word: a bounded-wait timeout in this call is not reported). It exists for
+ * callers that cannot allocate: runtimes that reserve all device memory for their own pool up front
+ * and plugins hosted by another framework with no allocator to offer. Every GPU that loads the library
+ * holds the array until the process exits. The first call on a device looks up the array's device
+ * address (make that first call before any stream capture). All calls share the one array, so calls
+ * that overlap on the GPU (other streams, other threads) race; serialise them. No counterpart in the
+ * reference: it is an addition of this library. */
+int lbw_linear_rmsnorm_noalloc(const void* a, const void* w, const void* bias, const void* gamma, int m, int n, int k,
+                               float eps, void* out, void* stream);
+
 /* ---- row kernels ----------------------------------------------------------------------- */
 
 /* h[m, c] = LN(x)[m, :] * (1 + scale) + shift (fp32 math, eps, no affine) -> bf16, or with

@@ -33,6 +33,7 @@ SIGNATURES = {
     "lbw_layernorm_mod": ([_vp, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _vp, _vp], _i),
     "lbw_rmsnorm_rope": ([_vp, _vp, _vp, _i, _i, _f, _vp, _vp, _i, _i, _i, _i, _vp, _ll, _i, _vp], _i),
     "lbw_mx_quantize": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
+    "lbw_linear_rmsnorm_noalloc": ([_vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp], _i),
 }
 
 _lib = None

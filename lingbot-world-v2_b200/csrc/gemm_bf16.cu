@@ -19,6 +19,8 @@
 //   EpiGelu      GELU_tanh(bf16(acc) + b), optionally followed by an MXFP8 quantise-dequantise of each
 //                32-column block (the FFN-up epilogue, kernels/ffn_epi.py:15-37, and the activation
 //                quantisation of kernels/ffn_mx.py:159-182) for the bf16-pipe MX FFN variant.
+#include <mutex>
+
 #include "host_common.cuh"
 #include "lbw_common.cuh"
 #include "mx_common.cuh"
@@ -425,3 +427,106 @@ int lbw_linear_gelu(const void* a, const void* w, const void* bias, int m, int n
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free variant of the linear + RMSNorm pair (lbw_linear_rowss followed by
+// lbw_rmsnorm_rope without RoPE). Some hosts cannot hand this library a scratch buffer or let it
+// call cudaMalloc: runtimes that reserve the whole device memory for their own pool up front (a
+// serving engine sizing its KV cache to fill HBM) and plugins loaded by another framework that
+// exposes no allocator to them. For those callers the row sums of squares live in the fixed array
+// below, which every GPU that loads the library keeps until the process exits.
+// ------------------------------------------------------------------------------------------
+namespace lbw {
+
+constexpr int NOALLOC_MAX_ROWS = 65536;  // 256 KB of fp32 row sums per device
+static __device__ __align__(256) float g_noalloc_rowss[NOALLOC_MAX_ROWS];
+
+// y[row, :] = bf16(bf16(y * rsqrt(ss[row] / C + eps)) * gamma), in place (the same rounding points as
+// rmsnorm_rope_kernel without the rotation). Each thread reads and rewrites its own 8 values.
+__global__ void __launch_bounds__(128) rms_gamma_inplace_kernel(__nv_bfloat16* y, const float* ss,
+                                                                const __nv_bfloat16* __restrict__ gamma, int C,
+                                                                float eps, long long ldy) {
+  const long long row = blockIdx.x;
+  const float r = 1.f / sqrtf(ss[row] / (float)C + eps);
+  __nv_bfloat16* yr = y + row * ldy;
+  for (int g = threadIdx.x; g < (C >> 3); g += 128) {
+    uint4 xv = *reinterpret_cast<const uint4*>(yr + g * 8);
+    uint4 gv = *reinterpret_cast<const uint4*>(gamma + g * 8);
+    const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(&xv);
+    const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(&gv);
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = bf16_round(bf16_round(__bfloat162float(xp[e]) * r) * __bfloat162float(gp[e]));
+    *reinterpret_cast<uint4*>(yr + g * 8) =
+        make_uint4(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]), pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
+  }
+}
+
+// Device address of g_noalloc_rowss for the current device, looked up once per device.
+static float* noalloc_rowss_ptr(int* err) {
+  static std::mutex mu;
+  static float* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = set_error(LBW_ERR_CUDA, "lbw_linear_rmsnorm_noalloc: cudaGetDevice failed");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_rowss);
+    if (e != cudaSuccess || p == nullptr) {
+      *err = set_error(LBW_ERR_CUDA, "lbw_linear_rmsnorm_noalloc: cudaGetSymbolAddress failed: %s",
+                       cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  *err = LBW_OK;
+  return ptrs[dev];
+}
+
+}  // namespace lbw
+
+extern "C" int lbw_linear_rmsnorm_noalloc(const void* a, const void* w, const void* bias, const void* gamma, int m,
+                                          int n, int k, float eps, void* out, void* stream) {
+  using namespace lbw;
+  using namespace lbw::gemm;
+  if (!a || !w || !gamma || !out) return set_error(LBW_ERR_INVALID, "lbw_linear_rmsnorm_noalloc: null pointer");
+  if (m <= 0 || m > NOALLOC_MAX_ROWS)
+    return set_error(LBW_ERR_SHAPE, "lbw_linear_rmsnorm_noalloc: %d rows; the built-in scratch holds at most %d rows",
+                     m, NOALLOC_MAX_ROWS);
+  if (n <= 0 || n % 32 || k <= 0 || k % BK)
+    return set_error(LBW_ERR_SHAPE, "lbw_linear_rmsnorm_noalloc: N=%d must be a multiple of 32 and K=%d of %d", n, k, BK);
+  if (!ok16(out) || !ok16(bias) || !ok16(gamma))
+    return set_error(LBW_ERR_ALIGN, "lbw_linear_rmsnorm_noalloc: alignment");
+  int err = 0;
+  float* ss = noalloc_rowss_ptr(&err);
+  if (!ss) return err;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's sums: clear this call's rows first.
+  if ((err = cuda_check(cudaMemsetAsync(ss, 0, sizeof(float) * (size_t)m, s), "noalloc scratch clear"))) return err;
+  CUtensorMap tmA, tmB;
+  if ((err = make_tmap_2d(&tmA, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, k, k, BK, BM))) return err;
+  if ((err = make_tmap_2d(&tmB, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, k, k, BK, BN))) return err;
+  EpiStore e{};
+  e.out[0] = e.out[1] = e.out[2] = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ld[0] = e.ld[1] = e.ld[2] = n;
+  e.ss[0] = ss;
+  e.region_cols = n;
+  e.ss_per_chunk = (n % BN) != 0;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  if ((err = cuda_check(cudaFuncSetAttribute(gemm_bf16_kernel<EpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SMEM_BYTES),
+                        "gemm smem attribute")))
+    return err;
+  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  // No status word: a bounded-wait timeout still ends the kernel, but is not recorded for this call.
+  gemm_bf16_kernel<EpiStore><<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmB, m, n, k, e, nullptr);
+  if ((err = cuda_check(cudaGetLastError(), "noalloc gemm launch"))) return err;
+  rms_gamma_inplace_kernel<<<m, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), ss,
+                                             reinterpret_cast<const __nv_bfloat16*>(gamma), n, eps, n);
+  return cuda_check(cudaGetLastError(), "noalloc rms launch");
+}
