@@ -330,13 +330,13 @@ def main():
     result = {
         "metric": "chunk-forward tokens/s", "value": chunk / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (attention, projections) + MXFP8 values (FFN)",
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (attention, projections) + mxfp8 e4m3/e8m0 (FFN)",
         "data": "synthetic (seeded N(0,1) latents / KV, N(0,0.02) weights, random init)",
         "config": {"workload": args.config, "model": c["model"], "blocks": layers, "query_tokens": chunk,
                    "kv_tokens": lkv, "text_tokens": TEXT_LEN, "parallelism": f"sp{world}",
                    "l2": "inputs larger than L2 (KV cache and weights >> 126 MB)"},
         "latency_ms": ms,
-        "tc_frac_of_peak": flops / (ms / 1e3) / (peak_tc * 1e12),
+        "tc_frac_of_peak": flops / (ms / 1e3) / (peak_tc * 1e12 * world),
         "roofline": {"bound": "tensor", "kernel": "chunk_attn_kernel", "achieved": attn_tf, "peak": peak_tc,
                      "unit": "TFLOP/s", "frac": attn_tf / peak_tc, "traffic": None,
                      "peak_source": f"{src} bf16_tflops_sustained", "flops_per_launch": attn_flops,

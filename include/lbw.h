@@ -113,6 +113,12 @@ int lbw_linear_rmsnorm_noalloc(const void* a, const void* w, const void* bias, c
 int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scale, const float* shift,
                       const float* weight, const float* bias, int mx_qdq, void* out, void* stream);
 
+/* As lbw_layernorm_mod with scale/shift, but the output is MXFP8: E4M3 codes data[m, c] and E8M0 scales in
+ * the tiled layout of lbw_mx_quantize (rows padded to 128; c % 128 == 0). This is the FFN input
+ * h = (LN(x)(1 + e4) + e3).to(bf16) (model_fast.py:3101) quantised for the MXFP8 FFN (kernels/ffn_mx.py:159-182). */
+int lbw_layernorm_mod_mx(const float* x, int m, int c, float eps, const float* scale, const float* shift, void* data,
+                         void* scales, void* stream);
+
 /* RMSNorm (+ 3-D RoPE) of projected rows: y = bf16(bf16(x * rsqrt(ss/c + eps)) * gamma), then,
  * if rope_cos != NULL, the interleaved-pair rotation with per-token angles of (frame, h, w).
  * x [m, c] bf16, ss [m] fp32, gamma [c] bf16; out rows out_row_off.. with row stride ldo.
@@ -131,6 +137,21 @@ int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, i
  * dequantised bf16 values. Replaces: ffn_mx.prequantize_weight (kernels/ffn_mx.py:44-47) and
  * the in-kernel activation quantisation of ffn_mx.mm. */
 int lbw_mx_quantize(const void* x, int rows, int k, void* data, void* scales, void* dequant, void* stream);
+
+/* Block-scaled tcgen05 GEMMs (kind::mxf8f6f4, E4M3 x E4M3, E8M0 scale per 32 along K, fp32 accumulate).
+ * a: codes [m, k] + tiled scales (rows padded to 128); w: codes [n, k] + tiled scales; k % 128 == 0,
+ * n % 128 == 0. Replaces ffn_mx.mm (kernels/ffn_mx.py:159-182, nkilib matmul_mxfp8). */
+/* out[m, n] = bf16(a w^T + bias) (bias may be NULL). */
+int lbw_mx_linear(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias, int m,
+                  int n, int k, void* out, void* stream);
+/* FFN up: GELU_tanh(bf16(a w^T) + bias) quantised to MXFP8 codes out[m, n] + tiled scales out_scales
+ * (the down projection's A operand). Replaces ffn_mx.mm + ffn_epi.bias_gelu_pad (kernels/ffn_epi.py:15-37). */
+int lbw_mx_linear_gelu(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                       int m, int n, int k, void* out, void* out_scales, void* stream);
+/* FFN down + gated residual: x[m, n] (fp32, in place) += bf16(a w^T + bias) * gate[n] (gate may be NULL).
+ * Replaces ffn_mx.mm + bias and x + y * e5 (model_fast.py:1584-1611, :3110-3111). */
+int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, const void* w_scales,
+                           const void* bias, int m, int n, int k, float* x, const float* gate, void* stream);
 
 #ifdef __cplusplus
 }

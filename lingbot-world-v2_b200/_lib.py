@@ -34,6 +34,10 @@ SIGNATURES = {
     "lbw_rmsnorm_rope": ([_vp, _vp, _vp, _i, _i, _f, _vp, _vp, _i, _i, _i, _i, _vp, _ll, _i, _vp], _i),
     "lbw_mx_quantize": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
     "lbw_linear_rmsnorm_noalloc": ([_vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp], _i),
+    "lbw_layernorm_mod_mx": ([_vp, _i, _i, _f, _vp, _vp, _vp, _vp, _vp], _i),
+    "lbw_mx_linear": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp], _i),
+    "lbw_mx_linear_gelu": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
+    "lbw_mx_linear_residual": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
 }
 
 _lib = None

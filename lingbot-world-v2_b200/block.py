@@ -59,6 +59,9 @@ class Workspace:
         self.q = mk(rows, dim)
         self.attn = mk(rows, dim)
         self.u = mk(rows, ffn_dim)
+        # MXFP8 operands of the FFN: codes + tiled E8M0 scales (rows padded to 128)
+        self.hq, self.hs = kernels.mx_buffers(rows, dim, device)
+        self.uq, self.us = kernels.mx_buffers(rows, ffn_dim, device)
 
     def fits(self, rows, dim, ffn_dim, device):
         return (self.rows, self.dim, self.ffn_dim) == (rows, dim, ffn_dim) and self.h.device == device
@@ -66,7 +69,7 @@ class Workspace:
 
 class CausalWanAttentionBlock(nn.Module):
     def __init__(self, dim, ffn_dim, num_heads, local_attn_size=-1, sink_size=0, qk_norm=True,
-                 cross_attn_norm=False, eps=1e-6, ffn_mx=True, cross_dedup=0):
+                 cross_attn_norm=False, eps=1e-6, ffn_mx=True, cross_dedup=0, mx_pipe="mxf8"):
         super().__init__()
         if dim % num_heads or dim // num_heads != HEAD_DIM:
             raise ValueError("the B200 kernels are built for head_dim 128")
@@ -75,6 +78,9 @@ class CausalWanAttentionBlock(nn.Module):
         self.dim, self.ffn_dim, self.num_heads = dim, ffn_dim, num_heads
         self.local_attn_size, self.qk_norm, self.cross_attn_norm, self.eps = local_attn_size, qk_norm, cross_attn_norm, eps
         self.ffn_mx = bool(ffn_mx)
+        if mx_pipe not in ("mxf8", "bf16"):
+            raise ValueError("mx_pipe is 'mxf8' (tcgen05 block-scaled MMA) or 'bf16' (MX values on the bf16 pipe)")
+        self.mx_pipe = mx_pipe
         self.cross_dedup = int(cross_dedup)
         self.norm1 = nn.Identity()
         self.self_attn = _AttnParams(dim, num_heads, qk_norm, eps)
@@ -116,11 +122,14 @@ class CausalWanAttentionBlock(nn.Module):
             pk["n3b"] = self.norm3.bias.detach().float().contiguous()
         pk["mod"] = self.modulation.detach().float().reshape(6, self.dim).contiguous()
         w1, w2 = b(self.ffn[0].weight), b(self.ffn[2].weight)
-        if self.ffn_mx:
-            # MXFP8 weights: E4M3 codes + E8M0 scales; the bf16-pipe GEMM reads their exact dequantisation
-            pk["w1_mx"] = kernels.mx_quantize(w1, dequant=True)
-            pk["w2_mx"] = kernels.mx_quantize(w2, dequant=True)
-            pk["w1"], pk["w2"] = pk["w1_mx"][2], pk["w2_mx"][2]
+        if self.ffn_mx and self.mx_pipe == "mxf8":
+            # MXFP8 weights: E4M3 codes + E8M0 scales read by the block-scaled tcgen05 GEMM
+            pk["w1_mx"] = kernels.mx_quantize(w1)[:2]
+            pk["w2_mx"] = kernels.mx_quantize(w2)[:2]
+        elif self.ffn_mx:
+            # bf16-pipe variant: the GEMM reads the exact bf16 dequantisation of the MXFP8 weights
+            pk["w1"] = kernels.mx_quantize(w1, dequant=True)[2]
+            pk["w2"] = kernels.mx_quantize(w2, dequant=True)[2]
         else:
             pk["w1"], pk["w2"] = w1, w2
         pk["b1"], pk["b2"] = b(self.ffn[0].bias), b(self.ffn[2].bias)
@@ -276,9 +285,14 @@ class CausalWanAttentionBlock(nn.Module):
         kernels.linear_residual(ws.attn, pk["wco"], pk["bco"], xf)
 
         # FFN
-        kernels.layernorm_mod(xf, eps, ws.h, scale=em[4], shift=em[3], mx_qdq=self.ffn_mx)
-        kernels.linear_gelu(ws.h, pk["w1"], pk["b1"], ws.u, mx_qdq=self.ffn_mx)
-        kernels.linear_residual(ws.u, pk["w2"], pk["b2"], xf, gate=em[5])
+        if self.ffn_mx and self.mx_pipe == "mxf8":
+            kernels.layernorm_mod_mx(xf, eps, em[4], em[3], ws.hq, ws.hs)
+            kernels.mx_linear_gelu(ws.hq, ws.hs, *pk["w1_mx"], pk["b1"], ws.uq, ws.us)
+            kernels.mx_linear_residual(ws.uq, ws.us, *pk["w2_mx"], pk["b2"], xf, gate=em[5])
+        else:
+            kernels.layernorm_mod(xf, eps, ws.h, scale=em[4], shift=em[3], mx_qdq=self.ffn_mx)
+            kernels.linear_gelu(ws.h, pk["w1"], pk["b1"], ws.u, mx_qdq=self.ffn_mx)
+            kernels.linear_residual(ws.u, pk["w2"], pk["b2"], xf, gate=em[5])
         return xf
 
 

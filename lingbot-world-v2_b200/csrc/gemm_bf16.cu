@@ -24,6 +24,7 @@
 #include "host_common.cuh"
 #include "lbw_common.cuh"
 #include "mx_common.cuh"
+#include "epilogues.cuh"
 
 namespace lbw {
 
@@ -35,149 +36,6 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
 constexpr int THREADS = 192;
 }  // namespace gemm
-
-// ------------------------------------------------------------------------------------------
-// epilogues: chunk() gets 32 consecutive fp32 accumulators of one row and returns a partial
-// row statistic; tile_done() receives the sum over the tile's chunks.
-// ------------------------------------------------------------------------------------------
-struct EpiStore {
-  __nv_bfloat16* out[3];
-  long long ld[3];
-  int row_off[3];
-  float* ss[3];          // per-region row sum-of-squares accumulators (nullable)
-  int region_cols;       // columns per region
-  int ss_per_chunk;      // regions not aligned to the 256-column tile: accumulate per 32-column chunk
-  const __nv_bfloat16* bias;  // [N] (nullable)
-
-  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
-    int r = col / region_cols;
-    int cl = col - r * region_cols;
-    __nv_bfloat16* dst = out[r] + (long long)(row + row_off[r]) * ld[r] + cl;
-    float ssum = 0.f;
-    uint32_t pk[16];
-#pragma unroll
-    for (int e = 0; e < 32; e += 8) {
-      float b[8];
-      if (bias) {
-        uint4 bb = *reinterpret_cast<const uint4*>(bias + col + e);
-        const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) b[q] = __bfloat162float(bp[q]);
-      } else {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) b[q] = 0.f;
-      }
-#pragma unroll
-      for (int q = 0; q < 8; q += 2) {
-        float y0 = bf16_round(v[e + q] + b[q]);
-        float y1 = bf16_round(v[e + q + 1] + b[q + 1]);
-        ssum += y0 * y0 + y1 * y1;
-        pk[(e + q) / 2] = pack_bf16(y0, y1);
-      }
-    }
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) d4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-    if (ss_per_chunk) {
-      if (ss[r]) atomicAdd(ss[r] + row, ssum);
-      return 0.f;
-    }
-    return ssum;
-  }
-  LBW_DEV void tile_done(int row, int col0, float ssum) const {
-    int r = col0 / region_cols;
-    if (!ss_per_chunk && ss[r]) atomicAdd(ss[r] + row, ssum);
-  }
-};
-
-struct EpiResidual {
-  float* x;                          // [M, ldx] fp32 residual, updated in place
-  long long ldx;
-  const __nv_bfloat16* bias;         // [N] nullable
-  const float* gate;                 // [N] nullable (gate = 1)
-  const __nv_bfloat16* film_scale;   // [M, N] nullable
-  const __nv_bfloat16* film_shift;   // [M, N] (with film_scale)
-  long long ldf;
-
-  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
-    float* xr = x + (long long)row * ldx + col;
-#pragma unroll
-    for (int e = 0; e < 32; e += 8) {
-      float y[8], g[8], xs[8];
-      if (bias) {
-        uint4 bb = *reinterpret_cast<const uint4*>(bias + col + e);
-        const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q] + __bfloat162float(bp[q]));
-      } else {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q]);
-      }
-      if (gate) {
-        float4 g0 = *reinterpret_cast<const float4*>(gate + col + e);
-        float4 g1 = *reinterpret_cast<const float4*>(gate + col + e + 4);
-        g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
-      } else {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) g[q] = 1.f;
-      }
-      float4 x0 = *reinterpret_cast<const float4*>(xr + e);
-      float4 x1 = *reinterpret_cast<const float4*>(xr + e + 4);
-      xs[0] = x0.x; xs[1] = x0.y; xs[2] = x0.z; xs[3] = x0.w; xs[4] = x1.x; xs[5] = x1.y; xs[6] = x1.z; xs[7] = x1.w;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) xs[q] = __fadd_rn(xs[q], __fmul_rn(y[q], g[q]));
-      if (film_scale) {
-        long long fo = (long long)row * ldf + col + e;
-        uint4 s4 = *reinterpret_cast<const uint4*>(film_scale + fo);
-        uint4 t4 = *reinterpret_cast<const uint4*>(film_shift + fo);
-        const __nv_bfloat16* sp = reinterpret_cast<const __nv_bfloat16*>(&s4);
-        const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(&t4);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float s1 = bf16_round(1.f + __bfloat162float(sp[q]));  // (1.0 + bf16 tensor) stays bf16
-          xs[q] = __fadd_rn(__fmul_rn(s1, xs[q]), __bfloat162float(tp[q]));
-        }
-      }
-      *reinterpret_cast<float4*>(xr + e) = make_float4(xs[0], xs[1], xs[2], xs[3]);
-      *reinterpret_cast<float4*>(xr + e + 4) = make_float4(xs[4], xs[5], xs[6], xs[7]);
-    }
-    return 0.f;
-  }
-  LBW_DEV void tile_done(int, int, float) const {}
-};
-
-struct EpiGelu {
-  __nv_bfloat16* out;   // [M, ldo] GELU(u + b), or its MXFP8 quantise-dequantise
-  long long ldo;
-  const __nv_bfloat16* bias;
-  int qdq;
-
-  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
-    float g[32];
-#pragma unroll
-    for (int e = 0; e < 32; e += 8) {
-      uint4 bb = *reinterpret_cast<const uint4*>(bias + col + e);
-      const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float u = bf16_round(bf16_round(v[e + q]) + __bfloat162float(bp[q]));
-        g[e + q] = bf16_round(gelu_tanh(u));
-      }
-    }
-    uint32_t pk[16];
-    if (qdq) {
-      mx_qdq32(g, pk);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 32; e += 2) pk[e >> 1] = pack_bf16(g[e], g[e + 1]);
-    }
-    uint4* d4 = reinterpret_cast<uint4*>(out + (long long)row * ldo + col);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) d4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-    return 0.f;
-  }
-  LBW_DEV void tile_done(int, int, float) const {}
-};
 
 // ------------------------------------------------------------------------------------------
 // kernel

@@ -1,0 +1,245 @@
+// Persistent tcgen05 block-scaled GEMM: MXFP8 (E4M3 elements, one E8M0 scale per 32 along K) x MXFP8
+// -> fp32 (TMEM) -> fused epilogue. This is the FFN of the causal-fast block with LINGBOT_FFN_MX=1:
+// ffn_mx.mm (kernels/ffn_mx.py:159-182), the bias + GELU(tanh) epilogue of ffn_epi.bias_gelu_pad
+// (kernels/ffn_epi.py:15-37) and the gated residual x + y * e5 (wan/modules/model_fast.py:3110-3111).
+//
+//   A [M, K] codes + scales (activations),  W [N, K] codes + scales (nn.Linear layout), K % 128 == 0.
+//   Scales use the tiled layout of lbw_mx_quantize: 512-byte atoms of 128 rows x 4 scales (row-block
+//   major), which is exactly the 32-row x 16-byte core-matrix staging tcgen05.cp 32x128b.warpx4 expects.
+//
+// Tiles 128 x 256, K staged 128 codes (one 128-byte swizzled row) per stage through a 4-deep TMA ring;
+// each stage also carries the tile's scales (1 atom for A, 2 for W) as plain bulk copies. The MMA thread
+// copies the stage's scales into TMEM (columns 256..267) and issues 4 tcgen05.mma kind::mxf8f6f4
+// (K = 32 each; the instruction's scale-id selects the byte of the 32-bit scale column). TMEM holds one
+// 256-column accumulator (the other 256 columns would leave no room for the scales), so the 8 epilogue
+// warps first pull the whole tile into registers (thread = row, 128 columns each), release the
+// accumulator, and only then run the epilogue math while the next tile's MMAs proceed.
+//   warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-9 epilogue.
+#include "epilogues.cuh"
+#include "host_common.cuh"
+#include "lbw_common.cuh"
+#include "mx_common.cuh"
+
+namespace lbw {
+
+namespace mxg {
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int A_BYTES = BM * BK;   // 16 KB
+constexpr int B_BYTES = BN * BK;   // 32 KB
+constexpr int SFA_BYTES = 512, SFB_BYTES = 1024, SF_BYTES = SFA_BYTES + SFB_BYTES;
+constexpr int TX_BYTES = A_BYTES + B_BYTES + SF_BYTES;
+constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES + SF_BYTES) + 1024;
+constexpr int THREADS = 320;
+constexpr uint32_t SFA_COL = 256, SFB_COL = 260;
+}  // namespace mxg
+
+template <class Epi>
+__global__ void __launch_bounds__(mxg::THREADS, 1)
+    gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int M, int N, int K, Epi epi,
+                   int* status) {
+  using namespace mxg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sSF = sB + STAGES * B_BYTES;
+  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar, tempty_bar, done_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&tfull_bar, 1);
+    mbar_init(&tempty_bar, 256);
+    mbar_init(&done_bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(&tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const Abort ab{status, &abort_flag};
+
+  const int nM = (M + BM - 1) / BM, nN = (N + BN - 1) / BN, nK = K / BK;
+  const int n_sf_blocks = (N + 127) / 128;  // 128-row scale blocks of W that exist
+  const int tiles = nM * nN;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      long long issued = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int m_blk = t / nN, n_blk = t % nN;
+        const int b0 = 2 * n_blk, b1 = (2 * n_blk + 1 < n_sf_blocks) ? 2 * n_blk + 1 : 2 * n_blk;
+        bool ok = true;
+        for (int kb = 0; kb < nK; ++kb) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, ab, 0x51)) { ok = false; break; }
+          uint8_t* sf = sSF + s * SF_BYTES;
+          mbar_expect_tx(&full_bar[s], TX_BYTES);
+          tma_load_2d(sA + s * A_BYTES, &tmA, &full_bar[s], kb * BK, m_blk * BM);
+          tma_load_2d(sB + s * B_BYTES, &tmB, &full_bar[s], kb * BK, n_blk * BN);
+          bulk_load(sf, sfa + ((long long)m_blk * nK + kb) * 512, 512, &full_bar[s]);
+          bulk_load(sf + 512, sfb + ((long long)b0 * nK + kb) * 512, 512, &full_bar[s]);
+          bulk_load(sf + 1024, sfb + ((long long)b1 * nK + kb) * 512, 512, &full_bar[s]);
+          ++issued;
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+      }
+      for (long long i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
+        mbar_wait_drain(&full_bar[i % STAGES], (uint32_t)((i / STAGES) & 1));
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, aph = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        if (!mbar_wait(&tempty_bar, aph ^ 1, ab, 0x52)) break;
+        tc_fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < nK; ++kb) {
+          if (!mbar_wait(&full_bar[s], ph, ab, 0x53)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+          const uint32_t sf = smem_u32(sSF + s * SF_BYTES);
+          tmem_cp_32x128b_x4(tmem + SFA_COL, sdesc_sf(sf));
+          tmem_cp_32x128b_x4(tmem + SFB_COL, sdesc_sf(sf + 512));
+          tmem_cp_32x128b_x4(tmem + SFB_COL + 4, sdesc_sf(sf + 1024));
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk)
+            mma_mxf8_ss(tmem, sdesc_kmajor_sw128(a0 + kk * 32), sdesc_kmajor_sw128(b0 + kk * 32),
+                        idesc_mxf8(BM, BN, kk), (kb | kk) != 0, tmem + SFA_COL, tmem + SFB_COL);
+          tc_commit(&empty_bar[s]);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar);
+        aph ^= 1;
+      }
+      tc_commit(&done_bar);
+      mbar_wait_drain(&done_bar, 0);
+    }
+  } else {
+    const int quarter = warp & 3;            // warps 2..9 -> lane quarters 2,3,0,1,2,3,0,1
+    const int half = (warp - 2) >> 2;        // columns [0,128) or [128,256) of the tile
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const int m_blk = t / nN, n_blk = t % nN;
+      if (!mbar_wait(&tfull_bar, aph, ab, 0x54)) break;
+      tc_fence_after();
+      const int row = m_blk * BM + quarter * 32 + lane;
+      const int col0 = n_blk * BN + half * 128;
+      const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + half * 128;
+      uint32_t r[128];
+      tmem_ld32(tb + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld32(tb + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+      tmem_ld32(tb + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&tempty_bar);  // the accumulator may be overwritten from here on
+      aph ^= 1;
+      float stat = 0.f;
+      if (row < M) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int col = col0 + c * 32;
+          if (col < N) stat += epi.chunk(row, col, *reinterpret_cast<const float(*)[32]>(&r[c * 32]));
+        }
+        epi.tile_done(row, col0, stat);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+template <class Epi>
+static int launch_gemm_mx(const void* a, const void* a_scales, const void* w, const void* w_scales, int M, int N, int K,
+                          const Epi& epi, cudaStream_t stream) {
+  using namespace mxg;
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(LBW_ERR_SHAPE, "mx gemm: empty problem %d x %d x %d", M, N, K);
+  if (K % BK) return set_error(LBW_ERR_SHAPE, "mx gemm: K=%d must be a multiple of %d", K, BK);
+  if (N % 128) return set_error(LBW_ERR_SHAPE, "mx gemm: N=%d must be a multiple of 128", N);
+  if (!a || !w || !a_scales || !w_scales) return set_error(LBW_ERR_INVALID, "mx gemm: null operand");
+  if (!aligned(a_scales, 16) || !aligned(w_scales, 16)) return set_error(LBW_ERR_ALIGN, "mx gemm: scales alignment");
+  int err = 0;
+  int* st = device_status(&err);
+  if (!st) return err;
+  CUtensorMap tmA, tmB;
+  if ((err = make_tmap_2d(&tmA, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, BK, BM))) return err;
+  if ((err = make_tmap_2d(&tmB, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, BK, BN))) return err;
+  static bool attr_set = false;
+  if (!attr_set) {
+    err = cuda_check(cudaFuncSetAttribute(gemm_mx_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+                     "mx gemm smem attribute");
+    if (err) return err;
+    attr_set = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_mx_kernel<Epi><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, reinterpret_cast<const uint8_t*>(a_scales),
+                                                             reinterpret_cast<const uint8_t*>(w_scales), M, N, K, epi, st);
+  return cuda_check(cudaGetLastError(), "mx gemm launch");
+}
+
+static bool ok16mx(const void* p) { return p == nullptr || aligned(p, 16); }
+
+}  // namespace lbw
+
+using namespace lbw;
+
+extern "C" {
+
+int lbw_mx_linear(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias, int m,
+                  int n, int k, void* out, void* stream) {
+  if (!out) return set_error(LBW_ERR_INVALID, "lbw_mx_linear: null output");
+  if (!ok16mx(out) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear: alignment");
+  EpiStore e{};
+  e.out[0] = e.out[1] = e.out[2] = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ld[0] = e.ld[1] = e.ld[2] = n;
+  e.region_cols = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_mx_linear_gelu(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                       int m, int n, int k, void* out, void* out_scales, void* stream) {
+  if (!out || !out_scales || !bias) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_gelu: null pointer");
+  if (!ok16mx(out) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_gelu: alignment");
+  EpiGeluMX e{};
+  e.data = reinterpret_cast<uint8_t*>(out);
+  e.scales = reinterpret_cast<uint8_t*>(out_scales);
+  e.ld = n;
+  e.sf_cols = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, const void* w_scales,
+                           const void* bias, int m, int n, int k, float* x, const float* gate, void* stream) {
+  if (!x) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual: null residual");
+  if (!ok16mx(x) || !ok16mx(gate) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_residual: alignment");
+  EpiResidual e{};
+  e.x = x;
+  e.ldx = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.gate = gate;
+  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -29,7 +29,9 @@ __global__ void __launch_bounds__(ROW_THREADS) layernorm_mod_kernel(const float*
                                                                     const float* __restrict__ shift,
                                                                     const float* __restrict__ weight,
                                                                     const float* __restrict__ bias, int mx,
-                                                                    __nv_bfloat16* __restrict__ out) {
+                                                                    __nv_bfloat16* __restrict__ out,
+                                                                    uint8_t* __restrict__ mx_data,
+                                                                    uint8_t* __restrict__ mx_scales) {
   __shared__ float red[4];
   const long long row = blockIdx.x;
   const float* xr = x + row * C;
@@ -81,7 +83,7 @@ __global__ void __launch_bounds__(ROW_THREADS) layernorm_mod_kernel(const float*
 #pragma unroll
       for (int e = 0; e < 8; ++e) y[e] = 0.f;
     }
-    if (mx) {
+    if (mx || mx_data) {
       // 32-value MX block = 4 consecutive threads x 8 values
       float amax = 0.f;
 #pragma unroll
@@ -89,6 +91,16 @@ __global__ void __launch_bounds__(ROW_THREADS) layernorm_mod_kernel(const float*
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       const int se = mx_shared_exp(amax);
+      if (mx_data) {  // E4M3 codes + E8M0 scale (tiled layout): the next MXFP8 GEMM's A operand
+        uint8_t qb[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qb[e] = mx_to_e4m3(ldexpf(y[e], -se));
+        if (g < G) {
+          *reinterpret_cast<uint2*>(mx_data + row * C + g * 8) = *reinterpret_cast<const uint2*>(qb);
+          if ((g & 3) == 0) mx_scales[mx_sf_offset(row, g >> 2, C)] = (uint8_t)(se + 127);
+        }
+        continue;
+      }
 #pragma unroll
       for (int e = 0; e < 8; ++e) y[e] = ldexpf(mx_from_e4m3(mx_to_e4m3(ldexpf(y[e], -se))), se);
     }
@@ -191,8 +203,21 @@ int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scal
                      LN_MAXIT * ROW_THREADS * 8);
   if (!aligned(x, 16) || !aligned(out, 16)) return set_error(LBW_ERR_ALIGN, "layernorm_mod: alignment");
   layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, c, eps, scale, shift, weight, bias, mx_qdq, reinterpret_cast<__nv_bfloat16*>(out));
+      x, c, eps, scale, shift, weight, bias, mx_qdq, reinterpret_cast<__nv_bfloat16*>(out), nullptr, nullptr);
   return cuda_check(cudaGetLastError(), "layernorm_mod launch");
+}
+
+int lbw_layernorm_mod_mx(const float* x, int m, int c, float eps, const float* scale, const float* shift, void* data,
+                         void* scales, void* stream) {
+  if (!x || !data || !scales || !scale || !shift) return set_error(LBW_ERR_INVALID, "layernorm_mod_mx: null pointer");
+  if (m <= 0 || c <= 0 || c % 128 || c > LN_MAXIT * ROW_THREADS * 8)
+    return set_error(LBW_ERR_SHAPE, "layernorm_mod_mx: width %d must be a multiple of 128 and <= %d", c,
+                     LN_MAXIT * ROW_THREADS * 8);
+  if (!aligned(x, 16) || !aligned(data, 16)) return set_error(LBW_ERR_ALIGN, "layernorm_mod_mx: alignment");
+  layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, c, eps, scale, shift, nullptr, nullptr, 1, nullptr, reinterpret_cast<uint8_t*>(data),
+      reinterpret_cast<uint8_t*>(scales));
+  return cuda_check(cudaGetLastError(), "layernorm_mod_mx launch");
 }
 
 int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, int c, float eps,

@@ -165,3 +165,59 @@ def mx_quantize(x, dequant=False):
     check(load().lbw_mx_quantize(ptr(x), rows, k, ptr(data), ptr(scales), ptr(deq), stream_of(x.device)),
           "mx_quantize")
     return data, scales, deq
+
+
+def mx_buffers(rows, k, device):
+    """Zeroed MXFP8 operand buffers: codes [rows, k] uint8 and tiled scales (rows padded to 128)."""
+    rows_pad = (rows + 127) // 128 * 128
+    return (torch.zeros(rows, k, dtype=torch.uint8, device=device),
+            torch.zeros(rows_pad * (k // 32), dtype=torch.uint8, device=device))
+
+
+def layernorm_mod_mx(x, eps, scale, shift, data, scales):
+    require_cuda(x, scale, shift, data, scales)
+    _c(x, torch.float32)
+    m, c = x.shape
+    if data.shape != (m, c) or scales.numel() < (m + 127) // 128 * 128 * (c // 32):
+        raise ValueError("layernorm_mod_mx: output buffers do not match x")
+    check(load().lbw_layernorm_mod_mx(ptr(x), m, c, ctypes.c_float(eps), ptr(scale), ptr(shift), ptr(data),
+                                      ptr(scales), stream_of(x.device)), "layernorm_mod_mx")
+    return data, scales
+
+
+def _mx_check(a, a_s, w, w_s):
+    require_cuda(a, a_s, w, w_s)
+    m, k = a.shape
+    n = w.shape[0]
+    if a.dtype != torch.uint8 or w.dtype != torch.uint8 or w.shape[1] != k:
+        raise ValueError("mx gemm: codes must be uint8 [m, k] and [n, k]")
+    if a_s.numel() < (m + 127) // 128 * 128 * (k // 32) or w_s.numel() < (n + 127) // 128 * 128 * (k // 32):
+        raise ValueError("mx gemm: scale buffers too small")
+    return m, n, k
+
+
+def mx_linear(a, a_s, w, w_s, bias=None, out=None):
+    m, n, k = _mx_check(a, a_s, w, w_s)
+    if out is None:
+        out = torch.empty(m, n, dtype=BF16, device=a.device)
+    check(load().lbw_mx_linear(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(out), stream_of(a.device)),
+          "mx_linear")
+    return out
+
+
+def mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales):
+    m, n, k = _mx_check(a, a_s, w, w_s)
+    if out.shape != (m, n) or out.dtype != torch.uint8:
+        raise ValueError("mx_linear_gelu: out must be uint8 [m, n]")
+    check(load().lbw_mx_linear_gelu(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(out), ptr(out_scales),
+                                    stream_of(a.device)), "mx_linear_gelu")
+    return out, out_scales
+
+
+def mx_linear_residual(a, a_s, w, w_s, bias, x, gate=None):
+    m, n, k = _mx_check(a, a_s, w, w_s)
+    if x.shape != (m, n) or x.dtype != torch.float32:
+        raise ValueError("mx_linear_residual: x must be fp32 [m, n]")
+    check(load().lbw_mx_linear_residual(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(x), ptr(gate),
+                                        stream_of(a.device)), "mx_linear_residual")
+    return x

@@ -11,10 +11,10 @@ pytestmark = pytest.mark.gpu
 BF = torch.bfloat16
 
 
-def _build(case, p, dev, ffn_mx, dedup=0):
+def _build(case, p, dev, ffn_mx, dedup=0, mx_pipe="mxf8"):
     import lbw_b200.block as B
     blk = B.CausalWanAttentionBlock(case.dim, case.ffn, case.heads, qk_norm=True, cross_attn_norm=True,
-                                    ffn_mx=ffn_mx, cross_dedup=dedup)
+                                    ffn_mx=ffn_mx, cross_dedup=dedup, mx_pipe=mx_pipe)
     sd = blk.state_dict()
     for k, v in p.items():
         sd[k] = v.to(sd[k].dtype)
@@ -57,11 +57,11 @@ def test_block_vs_reference_golden(cuda_dev, name):
     assert rel_l2(cc["k"][0].cpu(), g["ctx_k"]) <= 1e-2 and rel_l2(cc["v"][0].cpu(), g["ctx_v"]) <= 1e-2
 
 
-@pytest.mark.parametrize("peaked", [False, True])
-def test_block_mx_vs_oracle(cuda_dev, peaked):
+@pytest.mark.parametrize("peaked,pipe", [(False, "mxf8"), (True, "mxf8"), (False, "bf16")])
+def test_block_mx_vs_oracle(cuda_dev, peaked, pipe):
     case = BlockCase(dim=512, ffn=1024, grid=(3, 6, 10), n_lead=3, text_len=64, start_frame=9, peaked=peaked, seed=21)
     p, inp = make_case(case)
-    blk = _build(case, p, cuda_dev, ffn_mx=True)
+    blk = _build(case, p, cuda_dev, ffn_mx=True, mx_pipe=pipe)
     x, k, v, _ = _run(blk, case, inp, cuda_dev)
     cos, sin = ob.rope_grid(ob.rope_freqs(), case.grid, case.start_frame)
     ck, cv = ob.cross_kv(p, inp["context"])
