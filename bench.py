@@ -277,6 +277,7 @@ def main():
     L.check_device_status()
 
     attn_ev = []
+    calls0 = L.CALLS[0]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         barrier()
@@ -285,6 +286,7 @@ def main():
             step(attn_ev)
         end.record()
         barrier()
+    launches = L.CALLS[0] - calls0
     ms = start.elapsed_time(end) / args.steps
     attn_ms = statistics.mean(a.elapsed_time(b) for a, b in attn_ev)
     L.check_device_status()
@@ -341,7 +343,7 @@ def main():
                      "unit": "TFLOP/s", "frac": attn_tf / peak_tc, "traffic": None,
                      "peak_source": f"{src} bf16_tflops_sustained", "flops_per_launch": attn_flops,
                      "ms_per_launch": attn_ms},
-        "gpu_launches": args.steps * layers * B.KERNELS_PER_BLOCK,
+        "gpu_launches": launches,
         "e2e": e2e,
     }
     if rank == 0:

@@ -54,6 +54,21 @@ int lbw_chunk_attention(const void* q, long long ldq, int q_rows, int heads, con
                         const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
                         const float* key_bias, float softmax_scale, void* out, long long ldo, void* stream);
 
+/* Split-KV form of lbw_chunk_attention: the window's 128-key tiles are divided into n_splits contiguous
+ * ranges (1 <= n_splits <= number of tiles), one CTA per (query block, head, range). Each range writes its
+ * unnormalised fp32 output to part_o[slot][q_rows][heads][128] and (running max m in log2 units, row sum l)
+ * to part_ml[slot][q_rows][heads][2], slot = slot0 + range. Used to fill the GPU when a rank has few query
+ * rows and to attend the cached chunks while the new chunk's K/V are still being all-gathered (the
+ * reference's merged per-chunk partials, wan/modules/attention.py:963-1045, cte_partial / cte_merge). */
+int lbw_chunk_attention_partial(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                                const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                                const float* key_bias, float softmax_scale, int n_splits, float* part_o,
+                                float* part_ml, int slot0, void* stream);
+/* out[q, h*128:] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s over slots 0..n_slots-1 (M = max m_s), bf16.
+ * Replaces attention.py:963-990 cte_merge. */
+int lbw_attention_merge(const float* part_o, const float* part_ml, int n_slots, int q_rows, int heads, void* out,
+                        long long ldo, void* stream);
+
 /* ---- tensor-core linear layers (bf16 x bf16 -> fp32 accumulate) ------------------------
  * All weights are nn.Linear layout [n_out, k_in] bf16; K must be a multiple of 64, N of 32. */
 

@@ -34,6 +34,8 @@ SIGNATURES = {
     "lbw_rmsnorm_rope": ([_vp, _vp, _vp, _i, _i, _f, _vp, _vp, _i, _i, _i, _i, _vp, _ll, _i, _vp], _i),
     "lbw_mx_quantize": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
     "lbw_linear_rmsnorm_noalloc": ([_vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp], _i),
+    "lbw_chunk_attention_partial": ([_vp, _ll, _i, _i, _vp, _vp, _vp, _i, _ll, _vp, _f, _i, _vp, _vp, _i, _vp], _i),
+    "lbw_attention_merge": ([_vp, _vp, _i, _i, _i, _vp, _ll, _vp], _i),
     "lbw_layernorm_mod_mx": ([_vp, _i, _i, _f, _vp, _vp, _vp, _vp, _vp], _i),
     "lbw_mx_linear": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp], _i),
     "lbw_mx_linear_gelu": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
@@ -74,8 +76,15 @@ def last_error():
     return buf.value.decode(errors="replace")
 
 
+# Entry points called successfully (each enqueues one kernel of liblbw.so, except
+# lbw_linear_rmsnorm_noalloc, which enqueues two); bench.py reads this for its launch count.
+CALLS = [0]
+
+
 def check(rc, what):
     if rc == LBW_OK:
+        if what != "device status":
+            CALLS[0] += 1
         return
     msg = f"{what}: {last_error()} (status {rc})"
     if rc in (LBW_ERR_INVALID, LBW_ERR_SHAPE, LBW_ERR_ALIGN, LBW_ERR_UNSUPPORTED):

@@ -63,6 +63,12 @@ class Workspace:
         self.hq, self.hs = kernels.mx_buffers(rows, dim, device)
         self.uq, self.us = kernels.mx_buffers(rows, ffn_dim, device)
 
+    def attn_parts(self, slots, heads):
+        """Split-KV workspace (fp32 partial outputs + (m, l)), grown on demand."""
+        if getattr(self, "_parts", None) is None or self._parts[0].shape[0] < slots:
+            self._parts = kernels.attention_workspace(slots, self.rows, heads, self.h.device)
+        return self._parts
+
     def fits(self, rows, dim, ffn_dim, device):
         return (self.rows, self.dim, self.ffn_dim) == (rows, dim, ffn_dim) and self.h.device == device
 
@@ -171,6 +177,52 @@ class CausalWanAttentionBlock(nn.Module):
         if "is_init" in crossattn_cache:
             crossattn_cache["is_init"].fill_(1)
 
+    # ------------------------------------------------------------------ self-attention scheduling
+    _comm_streams = {}
+
+    def _self_attention(self, ws, k_chunks, v_chunks, L, chunk_rows, p):
+        """Attention of the local queries over (leading..., destination).
+
+        With sequence parallelism (p > 1) the destination chunk still has to be all-gathered: the gather runs
+        on a side stream while the leading chunks are attended, and the destination chunk's partial is merged
+        afterwards (the reference attends cached chunks early the same way, model_fast.py:2033-2110). When the
+        rank has few query rows the KV window is also split across CTAs so that the GPU is filled."""
+        C, H = self.dim, self.num_heads
+        rows = [k.numel() // C for k in k_chunks]
+        n_tiles = kernels.n_kv_tiles(rows)
+        k_dst, v_dst = k_chunks[-1], v_chunks[-1]
+        overlap = p > 1 and len(k_chunks) > 1
+        if not overlap:
+            if p > 1:
+                sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
+                sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
+            splits = kernels.pick_kv_splits(L, H, n_tiles)
+            if splits == 1:
+                kernels.chunk_attention(ws.q, k_chunks, v_chunks, out=ws.attn)
+            else:
+                po, pml = ws.attn_parts(splits, H)
+                kernels.chunk_attention_partial(ws.q, k_chunks, v_chunks, splits, po, pml, 0)
+                kernels.attention_merge(po, pml, splits, ws.attn)
+            return
+        dev = ws.q.device
+        comm = self._comm_streams.get(dev)
+        if comm is None:
+            comm = self._comm_streams[dev] = torch.cuda.Stream(device=dev)
+        main = torch.cuda.current_stream(dev)
+        ready = torch.cuda.Event()
+        ready.record(main)                       # this rank's K/V rows are written
+        with torch.cuda.stream(comm):
+            comm.wait_event(ready)
+            sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
+            sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
+        lead_tiles = kernels.n_kv_tiles(rows[:-1])
+        splits = kernels.pick_kv_splits(L, H, lead_tiles)
+        po, pml = ws.attn_parts(splits + 1, H)
+        kernels.chunk_attention_partial(ws.q, k_chunks[:-1], v_chunks[:-1], splits, po, pml, 0)
+        main.wait_stream(comm)
+        kernels.chunk_attention_partial(ws.q, [k_dst], [v_dst], 1, po, pml, splits)
+        kernels.attention_merge(po, pml, splits + 1, ws.attn)
+
     # ------------------------------------------------------------------ forward
     def forward(self, x, e, seq_lens=None, grid_sizes=None, freqs=None, context=None, context_lens=None,
                 dit_cond_dict=None, kv_cache=None, crossattn_cache=None, current_start=0,
@@ -251,15 +303,15 @@ class CausalWanAttentionBlock(nn.Module):
         kernels.qkv_proj(ws.h, pk["wqkv"], pk["bqkv"], ws.q_raw, ws.k_raw, ss_q, ss_k, v_dst, v_row_off=row0)
         kernels.rmsnorm_rope(ws.q_raw, ss_q, pk["gq"], eps, ws.q, rope=rp, grid=grid, tok0=row0)
         kernels.rmsnorm_rope(ws.k_raw, ss_k, pk["gk"], eps, k_dst, rope=rp, grid=grid, tok0=row0, out_row_off=row0)
-        if p > 1:
-            sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
-            sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
         if kv_only:
+            if p > 1:
+                sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
+                sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
             return xf
         if attn_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
-        kernels.chunk_attention(ws.q, list(k_chunks), list(v_chunks), out=ws.attn)
+        self._self_attention(ws, list(k_chunks), list(v_chunks), L, chunk_rows, p)
         if attn_events is not None:
             ev1.record()
             attn_events.append((ev0, ev1))

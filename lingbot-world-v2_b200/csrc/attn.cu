@@ -42,13 +42,39 @@ struct KVMaps {
   CUtensorMap v[attn::MAX_CHUNKS];
   int rows[attn::MAX_CHUNKS];
   int n;
+  int n_tiles;  // 128-key tiles over all chunks (each chunk's last tile may be ragged)
 };
+
+// Combines split-KV partials: out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, M = max_s m_s.
+// One warp per (row, head); each lane owns 4 of the 128 head dims.
+__global__ void attn_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int n_slots,
+                                  int q_rows, int heads, __nv_bfloat16* __restrict__ out, long long ldo) {
+  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (long long)q_rows * heads) return;
+  const long long row = wid / heads;
+  const int head = (int)(wid % heads);
+  float M = -INFINITY;
+  for (int s = 0; s < n_slots; ++s) M = fmaxf(M, part_ml[((s * (long long)q_rows + row) * heads + head) * 2]);
+  float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < n_slots; ++s) {
+    const long long base = (s * (long long)q_rows + row) * heads + head;
+    const float2 ml = *reinterpret_cast<const float2*>(part_ml + base * 2);
+    const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+    L += w * ml.y;
+    const float4 o = *reinterpret_cast<const float4*>(part_o + base * attn::D + lane * 4);
+    acc[0] += w * o.x; acc[1] += w * o.y; acc[2] += w * o.z; acc[3] += w * o.w;
+  }
+  const float inv = 1.f / L;
+  uint2 pk = make_uint2(pack_bf16(acc[0] * inv, acc[1] * inv), pack_bf16(acc[2] * inv, acc[3] * inv));
+  *reinterpret_cast<uint2*>(out + row * ldo + (long long)head * attn::D + lane * 4) = pk;
+}
 
 template <bool HAS_BIAS>
 __global__ void __launch_bounds__(attn::THREADS, 1)
     chunk_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KVMaps kv, int q_rows,
                       float scale_log2, const float* __restrict__ key_bias, __nv_bfloat16* __restrict__ out,
-                      long long ldo, int* status) {
+                      long long ldo, float* __restrict__ part_o, float* __restrict__ part_ml, int slot0, int* status) {
   using namespace attn;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -63,6 +89,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
   const int q0 = blockIdx.x * (QT * BM);
+  // KV split: this CTA attends the window's 128-key tiles [g_begin, g_end) (all of them when gridDim.z == 1).
+  const int g_begin = (int)((long long)blockIdx.z * kv.n_tiles / gridDim.z);
+  const int g_end = (int)((long long)(blockIdx.z + 1) * kv.n_tiles / gridDim.z);
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
@@ -97,11 +126,12 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       for (int i = 0; i < QT; ++i)
         for (int h = 0; h < 2; ++h)
           tma_load_2d(sQ + i * TILE + h * HALF, &tmQ, &q_full, head * D + h * 64, q0 + i * BM);
-      int j = 0;
+      int j = 0, g = 0;
       bool ok = true;
-      for (int c = 0; c < n_chunks && ok; ++c) {
+      for (int c = 0; c < n_chunks && ok && g < g_end; ++c) {
         const int rows = kv.rows[c];
-        for (int t0 = 0; t0 < rows; t0 += BN, ++j) {
+        for (int t0 = 0; t0 < rows && g < g_end; t0 += BN, ++g) {
+          if (g < g_begin) continue;
           const int s = j & 1;
           const uint32_t ph = (j >> 1) & 1;
           if (!mbar_wait(&k_empty[s], ph ^ 1, ab, 0x21)) { ok = false; break; }
@@ -110,6 +140,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           if (!mbar_wait(&v_empty[s], ph ^ 1, ab, 0x22)) { ok = false; ++j; break; }
           mbar_expect_tx(&v_full[s], TILE);
           for (int h = 0; h < 2; ++h) tma_load_2d(sV + s * TILE + h * HALF, &kv.v[c], &v_full[s], head * D + h * 64, t0);
+          ++j;
         }
       }
       // Let the last loads of each ring slot land before the CTA can exit.
@@ -124,8 +155,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     if (lane == 0) {
       const uint32_t idesc_s = idesc_bf16(BM, BN, 0, 0);  // S = Q Kᵀ: both K-major (head_dim contiguous)
       const uint32_t idesc_o = idesc_bf16(BM, D, 0, 1);   // O += P V: P from TMEM, V MN-major
-      int n_tiles = 0;
-      for (int c = 0; c < n_chunks; ++c) n_tiles += (kv.rows[c] + BN - 1) / BN;
+      const int n_tiles = g_end - g_begin;
 
       auto issue_s = [&](int i, int stage) {
         const uint32_t qa = smem_u32(sQ + i * TILE), kb = smem_u32(sK + stage * TILE);
@@ -193,9 +223,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     int j = 0;
     bool ok = true;
     long long key_base = 0;
-    for (int c = 0; c < n_chunks && ok; ++c) {
+    int g = 0;
+    for (int c = 0; c < n_chunks && ok && g < g_end; ++c) {
       const int rows = kv.rows[c];
-      for (int t0 = 0; t0 < rows; t0 += BN, ++j) {
+      for (int t0 = 0; t0 < rows && g < g_end; t0 += BN, ++g) {
+        if (g < g_begin) continue;
         const int valid = rows - t0 < BN ? rows - t0 : BN;
         if (!mbar_wait(&s_full[wg], j & 1, ab, 0x40 + wg)) { ok = false; break; }
         tc_fence_after();
@@ -306,13 +338,35 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&p_ready[wg]);
+        ++j;
       }
       key_base += rows;
     }
-    if (ok && mbar_wait(&o_done, 0, ab, 0x48)) {
+    const int row = q0 + wg * BM + quarter * 32 + lane;
+    if (part_o && ok && mbar_wait(&o_done, 0, ab, 0x49)) {
+      // split-KV partial: unnormalised O (fp32) and this row's (m, l), merged by attn_merge_kernel
+      tc_fence_after();
+      const int heads = gridDim.y;
+      const long long slot = slot0 + blockIdx.z;
+      float* orow = part_o + ((slot * q_rows + row) * heads + head) * (long long)D;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tO + cc * 32, r);
+        tmem_ld_wait();
+        if (row < q_rows) {
+          float4* d4 = reinterpret_cast<float4*>(orow + cc * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            d4[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                                __uint_as_float(r[4 * q + 3]));
+        }
+      }
+      if (row < q_rows)
+        *reinterpret_cast<float2*>(part_ml + ((slot * q_rows + row) * heads + head) * 2) = make_float2(m, l);
+    } else if (!part_o && ok && mbar_wait(&o_done, 0, ab, 0x48)) {
       tc_fence_after();
       const float inv = 1.f / l;
-      const int row = q0 + wg * BM + quarter * 32 + lane;
       __nv_bfloat16* orow = out + (long long)row * ldo + (long long)head * D;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
@@ -340,19 +394,23 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 
 using namespace lbw;
 
-extern "C" int lbw_chunk_attention(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
-                                   const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
-                                   const float* key_bias, float softmax_scale, void* out, long long ldo, void* stream) {
+static int launch_attention(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                            const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                            const float* key_bias, float softmax_scale, void* out, long long ldo, int n_splits,
+                            float* part_o, float* part_ml, int slot0, cudaStream_t s) {
   using namespace attn;
-  if (!q || !out || !k_chunks || !v_chunks || !chunk_rows) return set_error(LBW_ERR_INVALID, "chunk_attention: null pointer");
+  if (!q || !k_chunks || !v_chunks || !chunk_rows) return set_error(LBW_ERR_INVALID, "chunk_attention: null pointer");
+  if (!out && !part_o) return set_error(LBW_ERR_INVALID, "chunk_attention: null output");
   if (q_rows <= 0 || heads <= 0) return set_error(LBW_ERR_SHAPE, "chunk_attention: empty query");
   if (n_chunks < 1 || n_chunks > MAX_CHUNKS)
     return set_error(LBW_ERR_SHAPE, "chunk_attention: %d chunks (1..%d supported)", n_chunks, MAX_CHUNKS);
-  if (ldq % 8 || ldkv % 8 || ldo % 8 || !aligned(out, 16))
+  if (ldq % 8 || ldkv % 8 || (out && (ldo % 8 || !aligned(out, 16))))
     return set_error(LBW_ERR_ALIGN, "chunk_attention: row strides must be multiples of 8 elements");
-  if (ldq < (long long)heads * D || ldkv < (long long)heads * D || ldo < (long long)heads * D)
+  if (ldq < (long long)heads * D || ldkv < (long long)heads * D || (out && ldo < (long long)heads * D))
     return set_error(LBW_ERR_SHAPE, "chunk_attention: row stride smaller than heads*128");
   if (key_bias && !aligned(key_bias, 4)) return set_error(LBW_ERR_ALIGN, "chunk_attention: key_bias alignment");
+  if (part_o && (!part_ml || !aligned(part_o, 16) || !aligned(part_ml, 8) || slot0 < 0))
+    return set_error(LBW_ERR_INVALID, "chunk_attention: partial buffers missing or misaligned");
   int err = 0;
   int* st = device_status(&err);
   if (!st) return err;
@@ -361,6 +419,7 @@ extern "C" int lbw_chunk_attention(const void* q, long long ldq, int q_rows, int
   memset(&kv, 0, sizeof(kv));
   const uint64_t cols = (uint64_t)heads * D;
   if ((err = make_tmap_2d(&tmQ, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q_rows, cols, ldq, 64, BM))) return err;
+  int n_tiles = 0;
   for (int c = 0; c < n_chunks; ++c) {
     if (chunk_rows[c] <= 0) return set_error(LBW_ERR_SHAPE, "chunk_attention: chunk %d is empty", c);
     if (!k_chunks[c] || !v_chunks[c]) return set_error(LBW_ERR_INVALID, "chunk_attention: null chunk %d", c);
@@ -369,8 +428,12 @@ extern "C" int lbw_chunk_attention(const void* q, long long ldq, int q_rows, int
     if ((err = make_tmap_2d(&kv.v[c], v_chunks[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, chunk_rows[c], cols, ldkv, 64, BN)))
       return err;
     kv.rows[c] = chunk_rows[c];
+    n_tiles += (chunk_rows[c] + BN - 1) / BN;
   }
   kv.n = n_chunks;
+  kv.n_tiles = n_tiles;
+  if (n_splits < 1 || n_splits > n_tiles)
+    return set_error(LBW_ERR_SHAPE, "chunk_attention: %d KV splits for %d key tiles", n_splits, n_tiles);
   static bool attr[2] = {false, false};
   const int hb = key_bias ? 1 : 0;
   if (!attr[hb]) {
@@ -380,14 +443,49 @@ extern "C" int lbw_chunk_attention(const void* q, long long ldq, int q_rows, int
     if (err) return err;
     attr[hb] = true;
   }
-  dim3 grid((q_rows + QT * BM - 1) / (QT * BM), heads);
+  dim3 grid((q_rows + QT * BM - 1) / (QT * BM), heads, n_splits);
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
   if (hb)
-    chunk_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, key_bias,
-                                                              reinterpret_cast<__nv_bfloat16*>(out), ldo, st);
+    chunk_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, key_bias, o, ldo, part_o,
+                                                              part_ml, slot0, st);
   else
-    chunk_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, nullptr,
-                                                               reinterpret_cast<__nv_bfloat16*>(out), ldo, st);
+    chunk_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, nullptr, o, ldo, part_o,
+                                                               part_ml, slot0, st);
   return cuda_check(cudaGetLastError(), "attention launch");
 }
+
+extern "C" {
+
+int lbw_chunk_attention(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                        const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                        const float* key_bias, float softmax_scale, void* out, long long ldo, void* stream) {
+  if (!out) return set_error(LBW_ERR_INVALID, "chunk_attention: null output");
+  return launch_attention(q, ldq, q_rows, heads, k_chunks, v_chunks, chunk_rows, n_chunks, ldkv, key_bias,
+                          softmax_scale, out, ldo, 1, nullptr, nullptr, 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_chunk_attention_partial(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                                const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                                const float* key_bias, float softmax_scale, int n_splits, float* part_o,
+                                float* part_ml, int slot0, void* stream) {
+  if (!part_o || !part_ml) return set_error(LBW_ERR_INVALID, "chunk_attention_partial: null workspace");
+  return launch_attention(q, ldq, q_rows, heads, k_chunks, v_chunks, chunk_rows, n_chunks, ldkv, key_bias,
+                          softmax_scale, nullptr, 0, n_splits, part_o, part_ml, slot0,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_attention_merge(const float* part_o, const float* part_ml, int n_slots, int q_rows, int heads, void* out,
+                        long long ldo, void* stream) {
+  using namespace attn;
+  if (!part_o || !part_ml || !out) return set_error(LBW_ERR_INVALID, "attention_merge: null pointer");
+  if (n_slots < 1 || q_rows <= 0 || heads <= 0) return set_error(LBW_ERR_SHAPE, "attention_merge: empty");
+  if (ldo % 8 || ldo < (long long)heads * D || !aligned(out, 16) || !aligned(part_o, 16) || !aligned(part_ml, 8))
+    return set_error(LBW_ERR_ALIGN, "attention_merge: alignment");
+  const long long threads = (long long)q_rows * heads * 32;
+  attn_merge_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      part_o, part_ml, n_slots, q_rows, heads, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  return cuda_check(cudaGetLastError(), "attention_merge launch");
+}
+
+}  // extern "C"

@@ -132,7 +132,7 @@ struct EpiGelu {
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         float u = bf16_round(bf16_round(v[e + q]) + __bfloat162float(bp[q]));
-        g[e + q] = bf16_round(gelu_tanh(u));
+        g[e + q] = bf16_round(gelu_tanh_fast(u));
       }
     }
     uint32_t pk[16];
@@ -166,7 +166,7 @@ struct EpiGeluMX {
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         float u = bf16_round(bf16_round(v[e + q]) + __bfloat162float(bp[q]));
-        g[e + q] = bf16_round(gelu_tanh(u));
+        g[e + q] = bf16_round(gelu_tanh_fast(u));
       }
     }
     uint8_t qb[32];

@@ -64,6 +64,64 @@ def chunk_attention(q, k_chunks, v_chunks, key_bias=None, out=None, softmax_scal
     return out
 
 
+def n_kv_tiles(chunk_rows):
+    return sum((r + 127) // 128 for r in chunk_rows)
+
+
+def attention_workspace(n_slots, q_rows, heads, device):
+    """fp32 partial outputs [n_slots, q_rows, heads, 128] and (m, l) [n_slots, q_rows, heads, 2]."""
+    return (torch.empty(n_slots, q_rows, heads, HEAD_DIM, dtype=torch.float32, device=device),
+            torch.empty(n_slots, q_rows, heads, 2, dtype=torch.float32, device=device))
+
+
+def chunk_attention_partial(q, k_chunks, v_chunks, n_splits, part_o, part_ml, slot0=0, key_bias=None,
+                            softmax_scale=None):
+    """Split-KV attention into workspace slots slot0 .. slot0 + n_splits - 1 (see lbw.h)."""
+    require_cuda(q, *k_chunks, *v_chunks, key_bias, part_o, part_ml)
+    q2 = _rows(_c(q, BF16))
+    lq, cols = q2.shape
+    heads = cols // HEAD_DIM
+    n = len(k_chunks)
+    ks = [_rows(_c(k, BF16)) for k in k_chunks]
+    vs = [_rows(_c(v, BF16)) for v in v_chunks]
+    if part_o.shape[1:] != (lq, heads, HEAD_DIM) or part_ml.shape[1:] != (lq, heads, 2):
+        raise ValueError("attention workspace does not match q")
+    if slot0 < 0 or slot0 + n_splits > part_o.shape[0]:
+        raise ValueError(f"slots {slot0}..{slot0 + n_splits - 1} outside a {part_o.shape[0]}-slot workspace")
+    kp = (ctypes.c_void_p * n)(*[k.data_ptr() for k in ks])
+    vp = (ctypes.c_void_p * n)(*[v.data_ptr() for v in vs])
+    rows = (ctypes.c_int * n)(*[k.shape[0] for k in ks])
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(HEAD_DIM)
+    check(load().lbw_chunk_attention_partial(ptr(q2), q2.stride(0), lq, heads, kp, vp, rows, n, cols, ptr(key_bias),
+                                             ctypes.c_float(scale), int(n_splits), ptr(part_o), ptr(part_ml),
+                                             int(slot0), stream_of(q.device)), "chunk_attention_partial")
+
+
+def attention_merge(part_o, part_ml, n_slots, out):
+    require_cuda(part_o, part_ml, out)
+    _, lq, heads, _ = part_o.shape
+    o2 = _rows(_c(out, BF16))
+    check(load().lbw_attention_merge(ptr(part_o), ptr(part_ml), int(n_slots), lq, heads, ptr(o2), o2.stride(0),
+                                     stream_of(out.device)), "attention_merge")
+    return out
+
+
+def pick_kv_splits(q_rows, heads, n_tiles, sms=148, max_splits=4):
+    """Fewest KV splits whose CTA count fills the last wave to >= 90% (else the best fill)."""
+    blocks = (q_rows + 255) // 256 * heads
+    best, best_eff = 1, 0.0
+    for s in range(1, max_splits + 1):
+        if s > n_tiles:
+            break
+        waves = blocks * s / sms
+        eff = waves / math.ceil(waves)
+        if eff >= 0.9:
+            return s
+        if eff > best_eff + 1e-9:
+            best, best_eff = s, eff
+    return best
+
+
 def gemm_bf16(a, w, bias=None, out=None):
     require_cuda(a, w, bias, out)
     _c(a, BF16), _c(w, BF16)

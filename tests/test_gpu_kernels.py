@@ -202,3 +202,31 @@ def test_mx_quantize_bit_exact(cuda_dev):
     assert torch.equal(data.cpu(), q.view(torch.uint8))
     assert torch.equal(scales.cpu(), omx.scales_tiled(s, k))
     assert torch.equal(deq.cpu().float(), omx.dequantize(q, s))
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7])
+def test_chunk_attention_split_kv_and_merge(cuda_dev, splits):
+    import lbw_b200.kernels as K
+    q, ks, vs = _attn_case(300, [200, 77, 500], 2, 19, qscale=2.0)
+    d = cuda_dev
+    kd, vd = [k.to(d) for k in ks], [v.to(d) for v in vs]
+    po, pml = K.attention_workspace(splits + 1, 300, 2, d)
+    K.chunk_attention_partial(q.to(d), kd, vd, splits, po, pml, slot0=1)
+    out = torch.empty(300, 256, dtype=BF, device=d)
+    K.attention_merge(po[1:], pml[1:], splits, out)
+    ref = ob.attention(q, torch.cat(ks), torch.cat(vs))
+    assert rel_l2(out.view(300, 2, 128), ref) < 1e-2
+    # a cached-chunks call and a destination-chunk call merged = one call over the whole window
+    K.chunk_attention_partial(q.to(d), kd[:-1], vd[:-1], 1, po, pml, slot0=0)
+    K.chunk_attention_partial(q.to(d), kd[-1:], vd[-1:], 1, po, pml, slot0=1)
+    out2 = torch.empty_like(out)
+    K.attention_merge(po, pml, 2, out2)
+    assert rel_l2(out2.view(300, 2, 128), ref) < 1e-2
+
+
+def test_split_count_is_validated(cuda_dev):
+    import lbw_b200.kernels as K
+    q, ks, vs = _attn_case(128, [100], 1, 23)
+    po, pml = K.attention_workspace(2, 128, 1, cuda_dev)
+    with pytest.raises(ValueError, match="KV splits"):
+        K.chunk_attention_partial(q.to(cuda_dev), [ks[0].to(cuda_dev)], [vs[0].to(cuda_dev)], 2, po, pml)
