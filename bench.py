@@ -170,13 +170,15 @@ def run_reference(args):
     c = CONFIGS[args.config]
     f, gh, gw = c["grid"]
     layers = c["layers"]
-    rows = args.cpu_rows
     threads, model = cpu_info()
-    times = []
-    for i in range(args.warmup + args.steps):
-        t = cpu_oracle_step(args.config, rows, threads)
-        if i >= args.warmup:
-            times.append(t)
+    # Warm-up on a small sample (thread pools, allocator), which also calibrates the per-row cost so that
+    # the timed steps together stay near LBW_CPU_BUDGET_S seconds (default 150) whatever --steps is.
+    probe_rows = 128
+    t_probe = min(cpu_oracle_step(args.config, probe_rows, threads) for _ in range(max(1, min(args.warmup, 2))))
+    budget = float(os.environ.get("LBW_CPU_BUDGET_S", "150"))
+    rows = int(budget / max(args.steps, 1) / max(t_probe / probe_rows, 1e-9))
+    rows = max(probe_rows, min(args.cpu_rows, rows // 8 * 8))
+    times = [cpu_oracle_step(args.config, rows, threads) for _ in range(args.steps)]
     t_step = statistics.median(times) * layers          # one block timed, x blocks (identical cost)
     value = rows / t_step
     sample = (f"{rows} of {f * gh * gw} query rows, 1 of {layers} blocks (x{layers} extrapolated), "

@@ -13,7 +13,8 @@
 //   warp 8           TMA producer: Q once, then K/V tiles through a 2-deep ring
 //   warp 9           UMMA issuer, TMEM owner (512 columns: S0 | S1 | O0 | O1, 128 each)
 // S_i = Q_i Kᵀ lands in TMEM; the softmax warps read it (tcgen05.ld), write bf16 P_i back over
-// the first 64 columns of S_i (tcgen05.st) and the MMA warp accumulates O_i += P_i V from TMEM
+// the first 64 columns of S_i (tcgen05.st, signalled per half tile so that P V on keys 0..63 starts
+// while the exponentials of keys 64..127 are computed) and the MMA warp accumulates O_i += P_i V from TMEM
 // (A operand) and shared memory (V, MN-major). The running max is only raised when a row's max
 // grows by more than 2^8 (so P <= 256); O_i is then rescaled in TMEM by its own row's thread.
 // Softmax is one tcgen05.ld pass per tile (the row's 128 scores stay in registers), packed fp32x2
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint8_t* sK = smem + QT * TILE;
   uint8_t* sV = sK + STAGES * TILE;
   __shared__ __align__(8) uint64_t q_full, k_full[STAGES], k_empty[STAGES], v_full[STAGES], v_empty[STAGES],
-      s_full[QT], p_ready[QT], o_done, done_bar;
+      s_full[QT], p_ready[QT][2], o_done, done_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -103,7 +104,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     }
     for (int i = 0; i < QT; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_ready[i], 128);
+      mbar_init(&p_ready[i][0], 128);  // P of keys 0..63 written
+      mbar_init(&p_ready[i][1], 128);  // P of keys 64..127 written
     }
     mbar_init(&o_done, 1);
     mbar_init(&done_bar, 1);
@@ -165,10 +167,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           mma_f16_ss(tmem + i * 128, sdesc_kmajor_sw128(qa + off), sdesc_kmajor_sw128(kb + off), idesc_s, kk > 0);
         }
       };
-      auto issue_pv = [&](int i, int stage, bool first) {
+      // O_i += P_i V over one half of the tile's keys (half 0: keys 0..63, half 1: keys 64..127)
+      auto issue_pv = [&](int i, int stage, bool first, int half) {
         const uint32_t vb = smem_u32(sV + stage * TILE);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
+        for (int kk = half * 4; kk < half * 4 + 4; ++kk)
           mma_f16_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8, sdesc_mnmajor_sw128(vb + kk * 2048, HALF), idesc_o,
                      !(first && kk == 0));
       };
@@ -187,18 +190,24 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           const bool more = j + 1 < n_tiles;
           const int s1 = (j + 1) & 1;
           const uint32_t ph1 = ((j + 1) >> 1) & 1;
-          if (!mbar_wait(&v_full[s], ph, ab, 0x33) || !mbar_wait(&p_ready[0], j & 1, ab, 0x34)) { ok = false; break; }
+          if (!mbar_wait(&v_full[s], ph, ab, 0x33) || !mbar_wait(&p_ready[0][0], j & 1, ab, 0x34)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(0, s, j == 0);
+          issue_pv(0, s, j == 0, 0);
+          if (!mbar_wait(&p_ready[0][1], j & 1, ab, 0x37)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(0, s, j == 0, 1);
           if (more) {
             if (!mbar_wait(&k_full[s1], ph1, ab, 0x35)) { ok = false; break; }
             tc_fence_after();
             issue_s(0, s1);
             tc_commit(&s_full[0]);
           }
-          if (!mbar_wait(&p_ready[1], j & 1, ab, 0x36)) { ok = false; break; }
+          if (!mbar_wait(&p_ready[1][0], j & 1, ab, 0x36)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(1, s, j == 0);
+          issue_pv(1, s, j == 0, 0);
+          if (!mbar_wait(&p_ready[1][1], j & 1, ab, 0x38)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(1, s, j == 0, 1);
           tc_commit(&v_empty[s]);
           if (more) {
             issue_s(1, s1);
@@ -287,6 +296,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         if (valid == BN) {
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
+            if (cc == 2 && !rescale) {  // keys 0..63 are in TMEM: let P V start on them (warp-uniform branch)
+              tmem_st_wait();
+              tc_fence_before();
+              mbar_arrive(&p_ready[wg][0]);
+            }
             uint32_t pk[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
@@ -337,7 +351,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&p_ready[wg]);
+        if (rescale || valid != BN) mbar_arrive(&p_ready[wg][0]);  // (O rescaled first, or ragged tile)
+        mbar_arrive(&p_ready[wg][1]);
         ++j;
       }
       key_base += rows;
