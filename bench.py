@@ -193,6 +193,74 @@ def run_reference(args):
     return 0
 
 
+def run_sweep(args):
+    """BASELINE configs[4] (c5): kernel sweep on one GPU. Chunk attention with 40 heads x 128 over
+    Lq in {1560, 4680, 10800} x Lkv in {4096, 16384, 32768, 75600, 131072}; MXFP8 FFN GEMMs (E4M3, E8M0 per
+    32) M in {4680, 10800, 43200} for up (K 5120 -> N 13824) and down (13824 -> 5120). One JSON line per
+    point: TFLOP/s from CUDA events around each launch (median of 5, an L2 flush before each launch) and the
+    fraction of the measured bf16 peak (burst: each kernel is timed alone)."""
+    import __graft_entry__
+    __graft_entry__.build()
+    import lbw_b200.kernels as K
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pk, src = peaks()
+    peak = pk["bf16_tflops"]
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    bf = torch.bfloat16
+
+    def timed(fn, reps=5):
+        ts = []
+        for _ in range(reps + 1):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts[1:])
+
+    H, C = 40, 5120
+    for lq in (1560, 4680, 10800):
+        q = torch.randn(lq, C, generator=g, device=dev, dtype=bf)
+        out = torch.empty(lq, C, dtype=bf, device=dev)
+        for lkv in (4096, 16384, 32768, 75600, 131072):
+            n_chunks = max(1, -(-lkv // 18900))
+            rows = [lkv // n_chunks + (1 if i < lkv % n_chunks else 0) for i in range(n_chunks)]
+            ks = [torch.randn(r, C, generator=g, device=dev, dtype=bf) for r in rows]
+            vs = [torch.randn(r, C, generator=g, device=dev, dtype=bf) for r in rows]
+            splits = K.pick_kv_splits(lq, H, K.n_kv_tiles(rows))
+            parts = K.attention_workspace(splits, lq, H, dev) if splits > 1 else None
+
+            def run():
+                if parts is None:
+                    K.chunk_attention(q, ks, vs, out=out)
+                else:
+                    K.chunk_attention_partial(q, ks, vs, splits, *parts)
+                    K.attention_merge(*parts, splits, out)
+            ms = timed(run)
+            tf = 4.0 * lq * lkv * C / (ms / 1e3) / 1e12
+            print(json.dumps({"sweep": "chunk_attention", "q_rows": lq, "kv_rows": lkv, "heads": H, "kv_splits": splits,
+                              "ms": ms, "tflops": tf, "frac_of_peak": tf / peak, "peak": f"{src} bf16_tflops {peak}"}))
+            del ks, vs, parts
+    for m in (4680, 10800, 43200):
+        for kk, nn in ((5120, 13824), (13824, 5120)):
+            a = torch.randn(m, kk, generator=g, device=dev, dtype=bf)
+            w = (torch.randn(nn, kk, generator=g, device=dev) * 0.02).to(bf)
+            ad, as_, _ = K.mx_quantize(a)
+            wd, ws, _ = K.mx_quantize(w)
+            o = torch.empty(m, nn, dtype=bf, device=dev)
+            ms = timed(lambda: K.mx_linear(ad, as_, wd, ws, None, o))
+            tf = 2.0 * m * kk * nn / (ms / 1e3) / 1e12
+            print(json.dumps({"sweep": "mxfp8_gemm", "m": m, "k": kk, "n": nn, "ms": ms, "tflops": tf,
+                              "frac_of_bf16_peak": tf / peak, "frac_of_2x_bf16_peak": tf / (2 * peak),
+                              "peak": f"{src} bf16_tflops {peak}"}))
+            del a, w, ad, as_, wd, ws, o
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -203,7 +271,10 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=int(os.environ.get("LBW_CPU_ROWS", "1350")))
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="kernel sweep (BASELINE configs[4]) instead of the step")
     args = ap.parse_args()
+    if args.sweep:
+        return run_sweep(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -211,16 +211,18 @@ class CausalWanAttentionBlock(nn.Module):
         main = torch.cuda.current_stream(dev)
         ready = torch.cuda.Event()
         ready.record(main)                       # this rank's K/V rows are written
-        with torch.cuda.stream(comm):
-            comm.wait_event(ready)
-            sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
-            sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
         lead_tiles = kernels.n_kv_tiles(rows[:-1])
         splits = kernels.pick_kv_splits(L, H, lead_tiles)
         po, pml = ws.attn_parts(splits + 1, H)
+        with torch.cuda.stream(comm):
+            # gather, then the destination chunk's partial right behind it on the same stream: it runs
+            # alongside the leading chunks' launch instead of queueing after it
+            comm.wait_event(ready)
+            sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
+            sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
+            kernels.chunk_attention_partial(ws.q, [k_dst], [v_dst], 1, po, pml, splits)
         kernels.chunk_attention_partial(ws.q, k_chunks[:-1], v_chunks[:-1], splits, po, pml, 0)
         main.wait_stream(comm)
-        kernels.chunk_attention_partial(ws.q, [k_dst], [v_dst], 1, po, pml, splits)
         kernels.attention_merge(po, pml, splits + 1, ws.attn)
 
     # ------------------------------------------------------------------ forward

@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
   const int q0 = blockIdx.x * (QT * BM);
+  const bool two = q0 + BM < q_rows;  // false when the block's second query tile lies past the last row
   // KV split: this CTA attends the window's 128-key tiles [g_begin, g_end) (all of them when gridDim.z == 1).
   const int g_begin = (int)((long long)blockIdx.z * kv.n_tiles / gridDim.z);
   const int g_end = (int)((long long)(blockIdx.z + 1) * kv.n_tiles / gridDim.z);
@@ -181,8 +182,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tc_fence_after();
         issue_s(0, 0);
         tc_commit(&s_full[0]);
-        issue_s(1, 0);
-        tc_commit(&s_full[1]);
+        if (two) {
+          issue_s(1, 0);
+          tc_commit(&s_full[1]);
+        }
         tc_commit(&k_empty[0]);
         for (int j = 0; j < n_tiles && ok; ++j) {
           const int s = j & 1;
@@ -202,16 +205,20 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             issue_s(0, s1);
             tc_commit(&s_full[0]);
           }
-          if (!mbar_wait(&p_ready[1][0], j & 1, ab, 0x36)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(1, s, j == 0, 0);
-          if (!mbar_wait(&p_ready[1][1], j & 1, ab, 0x38)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(1, s, j == 0, 1);
+          if (two) {
+            if (!mbar_wait(&p_ready[1][0], j & 1, ab, 0x36)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(1, s, j == 0, 0);
+            if (!mbar_wait(&p_ready[1][1], j & 1, ab, 0x38)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(1, s, j == 0, 1);
+          }
           tc_commit(&v_empty[s]);
           if (more) {
-            issue_s(1, s1);
-            tc_commit(&s_full[1]);
+            if (two) {
+              issue_s(1, s1);
+              tc_commit(&s_full[1]);
+            }
             tc_commit(&k_empty[s1]);
           }
         }
@@ -224,6 +231,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     // ---------------- softmax / correction / epilogue ----------------
     const int wg = warp >> 2;
     const int quarter = warp & 3;
+    const bool active = wg == 0 || two;  // an all-padding second tile has no softmax to do
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_off + wg * 128;
     const uint32_t tO = tmem + lane_off + 256 + wg * 128;
@@ -233,7 +241,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     bool ok = true;
     long long key_base = 0;
     int g = 0;
-    for (int c = 0; c < n_chunks && ok && g < g_end; ++c) {
+    for (int c = 0; c < n_chunks && ok && active && g < g_end; ++c) {
       const int rows = kv.rows[c];
       for (int t0 = 0; t0 < rows && g < g_end; t0 += BN, ++g) {
         if (g < g_begin) continue;
@@ -358,7 +366,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       key_base += rows;
     }
     const int row = q0 + wg * BM + quarter * 32 + lane;
-    if (part_o && ok && mbar_wait(&o_done, 0, ab, 0x49)) {
+    if (!active) {
+      // nothing to write: every row of this tile is past q_rows
+    } else if (part_o && ok && mbar_wait(&o_done, 0, ab, 0x49)) {
       // split-KV partial: unnormalised O (fp32) and this row's (m, l), merged by attn_merge_kernel
       tc_fence_after();
       const int heads = gridDim.y;

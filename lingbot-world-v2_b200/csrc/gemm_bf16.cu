@@ -19,6 +19,8 @@
 //   EpiGelu      GELU_tanh(bf16(acc) + b), optionally followed by an MXFP8 quantise-dequantise of each
 //                32-column block (the FFN-up epilogue, kernels/ffn_epi.py:15-37, and the activation
 //                quantisation of kernels/ffn_mx.py:159-182) for the bf16-pipe MX FFN variant.
+#include <math.h>
+
 #include <mutex>
 
 #include "host_common.cuh"
@@ -35,16 +37,31 @@ constexpr int B_BYTES = BN * BK * 2;   // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
 constexpr int THREADS = 192;
+// Tile width TBN (256, or 128 when 256-wide tiles would leave the last wave mostly idle): ring depth and
+// shared memory per tile width.
+template <int TBN> struct Cfg {
+  static constexpr int B_BYTES = TBN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = TBN == 256 ? 4 : 6;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * TBN;
+};
 }  // namespace gemm
 
 // ------------------------------------------------------------------------------------------
 // kernel
 // ------------------------------------------------------------------------------------------
-template <class Epi>
+template <class Epi, int TBN = 256>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                      int K, Epi epi, int* status) {
-  using namespace gemm;
+  using gemm::BM;
+  using gemm::BK;
+  using gemm::A_BYTES;
+  constexpr int BN = TBN;
+  constexpr int STAGES = gemm::Cfg<TBN>::STAGES;
+  constexpr int STAGE_BYTES = gemm::Cfg<TBN>::STAGE_BYTES;
+  constexpr uint32_t TMEM_COLS = gemm::Cfg<TBN>::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], done_bar;
@@ -69,7 +86,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc(&tmem_slot, 512);
+  if (warp == 1) tmem_alloc(&tmem_slot, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -165,7 +182,38 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+inline void fit_epi(EpiStore& e, int tbn) { e.ss_per_chunk = (e.region_cols % tbn) != 0; }
+template <class Epi>
+inline void fit_epi(Epi&, int) {}
+
+static double wave_fill(long long tiles) {
+  const double w = (double)tiles / num_sms();
+  return w / ceil(w);
+}
+
+template <class Epi, int TBN>
+static int launch_gemm_t(const CUtensorMap& tmA, const void* W, long long ldw, int M, int N, int K, Epi epi,
+                         cudaStream_t stream, int* st) {
+  using C = gemm::Cfg<TBN>;
+  CUtensorMap tmB;
+  int err = make_tmap_2d(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldw, gemm::BK, TBN);
+  if (err) return err;
+  fit_epi(epi, TBN);
+  static bool attr_set = false;  // one flag per instantiation
+  if (!attr_set) {
+    err = cuda_check(cudaFuncSetAttribute(gemm_bf16_kernel<Epi, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          C::SMEM_BYTES),
+                     "gemm smem attribute");
+    if (err) return err;
+    attr_set = true;
+  }
+  const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + TBN - 1) / TBN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_bf16_kernel<Epi, TBN><<<grid, gemm::THREADS, C::SMEM_BYTES, stream>>>(tmA, tmB, M, N, K, epi, st);
+  return cuda_check(cudaGetLastError(), "gemm launch");
 }
 
 template <class Epi>
@@ -179,20 +227,13 @@ static int launch_gemm(const void* A, long long lda, const void* W, long long ld
   int err = 0;
   int* st = device_status(&err);
   if (!st) return err;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA;
   if ((err = make_tmap_2d(&tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, BK, BM))) return err;
-  if ((err = make_tmap_2d(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldw, BK, BN))) return err;
-  static bool attr_set = false;  // one flag per instantiation
-  if (!attr_set) {
-    err = cuda_check(cudaFuncSetAttribute(gemm_bf16_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
-                     "gemm smem attribute");
-    if (err) return err;
-    attr_set = true;
-  }
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_bf16_kernel<Epi><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, M, N, K, epi, st);
-  return cuda_check(cudaGetLastError(), "gemm launch");
+  // 128-wide tiles when 256-wide ones would leave the last wave mostly idle (few rows per rank)
+  const long long mt = (M + BM - 1) / BM;
+  const double f256 = wave_fill(mt * ((N + 255) / 256)), f128 = wave_fill(mt * ((N + 127) / 128));
+  if (f256 < 0.85 && f128 > f256 + 0.08) return launch_gemm_t<Epi, 128>(tmA, W, ldw, M, N, K, epi, stream, st);
+  return launch_gemm_t<Epi, 256>(tmA, W, ldw, M, N, K, epi, stream, st);
 }
 
 static bool ok16(const void* p) { return p == nullptr || aligned(p, 16); }

@@ -15,6 +15,8 @@
 // warps first pull the whole tile into registers (thread = row, 128 columns each), release the
 // accumulator, and only then run the epilogue math while the next tile's MMAs proceed.
 //   warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-9 epilogue.
+#include <math.h>
+
 #include "epilogues.cuh"
 #include "host_common.cuh"
 #include "lbw_common.cuh"
@@ -23,22 +25,35 @@
 namespace lbw {
 
 namespace mxg {
-constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int BM = 128, BK = 128;
 constexpr int A_BYTES = BM * BK;   // 16 KB
-constexpr int B_BYTES = BN * BK;   // 32 KB
-constexpr int SFA_BYTES = 512, SFB_BYTES = 1024, SF_BYTES = SFA_BYTES + SFB_BYTES;
-constexpr int TX_BYTES = A_BYTES + B_BYTES + SF_BYTES;
-constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES + SF_BYTES) + 1024;
+constexpr int SFA_BYTES = 512;
 constexpr int THREADS = 320;
-constexpr uint32_t SFA_COL = 256, SFB_COL = 260;
+// Tile width TBN = 256 (default) or 128 (when 256-wide tiles would leave the last wave mostly idle).
+template <int TBN> struct Cfg {
+  static constexpr int B_BYTES = TBN * BK;
+  static constexpr int SFB_BYTES = TBN / 128 * 512;
+  static constexpr int SF_BYTES = SFA_BYTES + SFB_BYTES;
+  static constexpr int TX_BYTES = A_BYTES + B_BYTES + SF_BYTES;
+  static constexpr int STAGES = TBN == 256 ? 4 : 6;
+  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES + SF_BYTES) + 1024;
+  static constexpr uint32_t SFA_COL = TBN, SFB_COL = TBN + 4;  // scale columns right after the accumulator
+};
 }  // namespace mxg
 
-template <class Epi>
+template <class Epi, int TBN = 256>
 __global__ void __launch_bounds__(mxg::THREADS, 1)
     gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int M, int N, int K, Epi epi,
                    int* status) {
-  using namespace mxg;
+  using mxg::BM;
+  using mxg::BK;
+  using mxg::A_BYTES;
+  using Cf = mxg::Cfg<TBN>;
+  constexpr int BN = TBN, STAGES = Cf::STAGES, B_BYTES = Cf::B_BYTES, SF_BYTES = Cf::SF_BYTES;
+  constexpr int TX_BYTES = Cf::TX_BYTES;
+  constexpr uint32_t SFA_COL = Cf::SFA_COL, SFB_COL = Cf::SFB_COL;
+  constexpr int HALF_COLS = BN / 2;  // columns per epilogue warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -91,8 +106,12 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
           tma_load_2d(sA + s * A_BYTES, &tmA, &full_bar[s], kb * BK, m_blk * BM);
           tma_load_2d(sB + s * B_BYTES, &tmB, &full_bar[s], kb * BK, n_blk * BN);
           bulk_load(sf, sfa + ((long long)m_blk * nK + kb) * 512, 512, &full_bar[s]);
-          bulk_load(sf + 512, sfb + ((long long)b0 * nK + kb) * 512, 512, &full_bar[s]);
-          bulk_load(sf + 1024, sfb + ((long long)b1 * nK + kb) * 512, 512, &full_bar[s]);
+          if (BN == 256) {
+            bulk_load(sf + 512, sfb + ((long long)b0 * nK + kb) * 512, 512, &full_bar[s]);
+            bulk_load(sf + 1024, sfb + ((long long)b1 * nK + kb) * 512, 512, &full_bar[s]);
+          } else {
+            bulk_load(sf + 512, sfb + ((long long)n_blk * nK + kb) * 512, 512, &full_bar[s]);
+          }
           ++issued;
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
@@ -116,7 +135,7 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
           const uint32_t sf = smem_u32(sSF + s * SF_BYTES);
           tmem_cp_32x128b_x4(tmem + SFA_COL, sdesc_sf(sf));
           tmem_cp_32x128b_x4(tmem + SFB_COL, sdesc_sf(sf + 512));
-          tmem_cp_32x128b_x4(tmem + SFB_COL + 4, sdesc_sf(sf + 1024));
+          if (BN == 256) tmem_cp_32x128b_x4(tmem + SFB_COL + 4, sdesc_sf(sf + 1024));
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk)
             mma_mxf8_ss(tmem, sdesc_kmajor_sw128(a0 + kk * 32), sdesc_kmajor_sw128(b0 + kk * 32),
@@ -133,20 +152,18 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
     }
   } else {
     const int quarter = warp & 3;            // warps 2..9 -> lane quarters 2,3,0,1,2,3,0,1
-    const int half = (warp - 2) >> 2;        // columns [0,128) or [128,256) of the tile
+    const int half = (warp - 2) >> 2;        // first or second half of the tile's columns
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       const int m_blk = t / nN, n_blk = t % nN;
       if (!mbar_wait(&tfull_bar, aph, ab, 0x54)) break;
       tc_fence_after();
       const int row = m_blk * BM + quarter * 32 + lane;
-      const int col0 = n_blk * BN + half * 128;
-      const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + half * 128;
-      uint32_t r[128];
-      tmem_ld32(tb + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      tmem_ld32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_ld32(tb + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-      tmem_ld32(tb + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      const int col0 = n_blk * BN + half * HALF_COLS;
+      const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + half * HALF_COLS;
+      uint32_t r[HALF_COLS];
+#pragma unroll
+      for (int c = 0; c < HALF_COLS / 32; ++c) tmem_ld32(tb + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&tempty_bar);  // the accumulator may be overwritten from here on
@@ -154,7 +171,7 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
       float stat = 0.f;
       if (row < M) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < HALF_COLS / 32; ++c) {
           const int col = col0 + c * 32;
           if (col < N) stat += epi.chunk(row, col, *reinterpret_cast<const float(*)[32]>(&r[c * 32]));
         }
@@ -166,6 +183,34 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+template <class Epi, int TBN>
+static int launch_gemm_mx_t(const CUtensorMap& tmA, const void* a_scales, const void* w, const void* w_scales, int M,
+                            int N, int K, const Epi& epi, cudaStream_t stream, int* st) {
+  using C = mxg::Cfg<TBN>;
+  CUtensorMap tmB;
+  int err = make_tmap_2d(&tmB, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, mxg::BK, TBN);
+  if (err) return err;
+  static bool attr_set = false;
+  if (!attr_set) {
+    err = cuda_check(cudaFuncSetAttribute(gemm_mx_kernel<Epi, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          C::SMEM_BYTES),
+                     "mx gemm smem attribute");
+    if (err) return err;
+    attr_set = true;
+  }
+  const int tiles = ((M + mxg::BM - 1) / mxg::BM) * ((N + TBN - 1) / TBN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_mx_kernel<Epi, TBN><<<grid, mxg::THREADS, C::SMEM_BYTES, stream>>>(
+      tmA, tmB, reinterpret_cast<const uint8_t*>(a_scales), reinterpret_cast<const uint8_t*>(w_scales), M, N, K, epi,
+      st);
+  return cuda_check(cudaGetLastError(), "mx gemm launch");
+}
+
+static double mx_wave_fill(long long tiles) {
+  const double w = (double)tiles / num_sms();
+  return w / ceil(w);
 }
 
 template <class Epi>
@@ -180,21 +225,13 @@ static int launch_gemm_mx(const void* a, const void* a_scales, const void* w, co
   int err = 0;
   int* st = device_status(&err);
   if (!st) return err;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA;
   if ((err = make_tmap_2d(&tmA, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, BK, BM))) return err;
-  if ((err = make_tmap_2d(&tmB, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, BK, BN))) return err;
-  static bool attr_set = false;
-  if (!attr_set) {
-    err = cuda_check(cudaFuncSetAttribute(gemm_mx_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
-                     "mx gemm smem attribute");
-    if (err) return err;
-    attr_set = true;
-  }
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_mx_kernel<Epi><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, reinterpret_cast<const uint8_t*>(a_scales),
-                                                             reinterpret_cast<const uint8_t*>(w_scales), M, N, K, epi, st);
-  return cuda_check(cudaGetLastError(), "mx gemm launch");
+  const long long mt = (M + BM - 1) / BM;
+  const double f256 = mx_wave_fill(mt * ((N + 255) / 256)), f128 = mx_wave_fill(mt * ((N + 127) / 128));
+  if (f256 < 0.85 && f128 > f256 + 0.08)
+    return launch_gemm_mx_t<Epi, 128>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st);
+  return launch_gemm_mx_t<Epi, 256>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st);
 }
 
 static bool ok16mx(const void* p) { return p == nullptr || aligned(p, 16); }

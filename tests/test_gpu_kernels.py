@@ -19,7 +19,7 @@ def _g(seed):
 
 
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (200, 512, 320), (1000, 768, 1536), (4680, 1536, 1536),
-                                   (77, 96, 128)])
+                                   (77, 96, 128), (1350, 5120, 512)])   # the last one runs 128-wide tiles
 def test_gemm_bf16(cuda_dev, m, n, k):
     import lbw_b200.kernels as K
     g = _g(m + n + k)
@@ -230,3 +230,26 @@ def test_split_count_is_validated(cuda_dev):
     po, pml = K.attention_workspace(2, 128, 1, cuda_dev)
     with pytest.raises(ValueError, match="KV splits"):
         K.chunk_attention_partial(q.to(cuda_dev), [ks[0].to(cuda_dev)], [vs[0].to(cuda_dev)], 2, po, pml)
+
+
+def test_small_m_residual_and_qkv_use_narrow_tiles(cuda_dev):
+    """M = 1350 rows (one of 8 ranks at 720p): 256-wide tiles would fill 1.5 waves, so 128-wide ones run."""
+    import lbw_b200.kernels as K
+    g = _g(29)
+    m, c = 1350, 1536
+    h = torch.randn(m, c, generator=g).to(BF)
+    w = (torch.randn(3 * c, c, generator=g) * 0.02).to(BF)
+    b = (torch.randn(3 * c, generator=g) * 0.02).to(BF)
+    d = cuda_dev
+    q, k = torch.empty(m, c, dtype=BF, device=d), torch.empty(m, c, dtype=BF, device=d)
+    ss = torch.empty(2, m, device=d)
+    v = torch.empty(m, c, dtype=BF, device=d)
+    K.qkv_proj(h.to(d), w.to(d), b.to(d), q, k, ss[0], ss[1], v)
+    ref = ob.linear(h, w, b)
+    assert rel_l2(q, ref[:, :c]) < 4e-3 and rel_l2(v, ref[:, 2 * c:]) < 4e-3
+    assert rel_l2(ss[1], k.float().pow(2).sum(1)) < 1e-5
+    x = torch.randn(m, 5120, generator=g)
+    wo = (torch.randn(5120, c, generator=g) * 0.02).to(BF)
+    xd = x.to(d)
+    K.linear_residual(h.to(d), wo.to(d), None, xd)
+    assert rel_l2(xd - x.to(d), ob.linear(h, wo, None).float()) < 5e-3

@@ -21,7 +21,8 @@ def _ab(m, n, k, seed):
 
 
 @pytest.mark.parametrize("m,n,k", [(128, 256, 128), (300, 512, 640), (77, 384, 256), (4680, 1536, 1536),
-                                   (1000, 13824 // 4, 5120 // 4)])
+                                   (1000, 13824 // 4, 5120 // 4),
+                                   (1350, 5120, 1024)])   # 1,350 rows (8-way split of 720p): 128-wide tiles
 def test_mx_linear_vs_emulation(cuda_dev, m, n, k):
     import lbw_b200.kernels as K
     a, w, b = _ab(m, n, k, m + n + k)
@@ -94,3 +95,17 @@ def test_ffn_mx_mm_interface(cuda_dev):
     data, scales = FM.prequantize_weight(w.to(cuda_dev))
     out = FM.mm(a.to(cuda_dev), data, scales)
     assert rel_l2(out, omx.mx_linear(a, w)) < 4e-3
+
+
+def test_mx_linear_residual_narrow_tiles(cuda_dev):
+    import lbw_b200.kernels as K
+    m, n, k = 1350, 5120, 512
+    a, w, b = _ab(m, n, k, 17)
+    x = torch.randn(m, n, generator=torch.Generator().manual_seed(18))
+    d = cuda_dev
+    ad, as_, _ = K.mx_quantize(a.to(d))
+    wd, ws, _ = K.mx_quantize(w.to(d))
+    xd = x.to(d)
+    K.mx_linear_residual(ad, as_, wd, ws, b.to(d), xd)
+    y = (omx.qdq(a) @ omx.qdq(w).t() + b.float()).to(BF)
+    assert rel_l2(xd - x.to(d), y.float()) < 5e-3
