@@ -272,6 +272,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="kernel sweep (BASELINE configs[4]) instead of the step")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="after the timed steps, time each phase of the block with CUDA event marks")
     args = ap.parse_args()
     if args.sweep:
         return run_sweep(args)
@@ -334,9 +336,9 @@ def main():
     torch.cuda.synchronize()
     L.check_device_status()
 
-    def step(ev=None):
+    def step(ev=None, phases=None):
         stack.forward_chunk(xf, e0, (ks, vs), ctx, caches, c["grid"], c["start_frame"], freqs, films=films,
-                            attn_events=ev)
+                            attn_events=ev, phases=phases)
 
     def barrier():
         if world > 1:
@@ -367,6 +369,27 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, attn_ms = float(t[0]), float(t[1])
+
+    # per-phase times (outside the timed region): event marks between the block's kernels, summed over the
+    # blocks of a step and averaged over steps; max over ranks
+    breakdown = None
+    if args.breakdown:
+        marks = []
+        barrier()
+        for _ in range(args.steps):
+            step(phases=marks)
+        barrier()
+        acc = {}
+        prev = None
+        for name, ev in marks:
+            if name != "start" and prev is not None:
+                acc[name] = acc.get(name, 0.0) + prev.elapsed_time(ev)
+            prev = ev
+        names = list(acc)
+        t = torch.tensor([acc[n] / args.steps for n in names], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        breakdown = {n: round(float(v), 3) for n, v in zip(names, t)}
 
     # end to end through host buffers: pinned x in, result out, every step
     e2e = None
@@ -419,6 +442,8 @@ def main():
         "gpu_launches": launches,
         "e2e": e2e,
     }
+    if breakdown is not None:
+        result["phases_ms_per_step"] = breakdown
     if rank == 0:
         result["clocks"] = clk.summary()
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -118,6 +118,12 @@ int lbw_linear_gelu(const void* a, const void* w, const void* bias, int m, int n
 int lbw_linear_rmsnorm_noalloc(const void* a, const void* w, const void* bias, const void* gamma, int m, int n, int k,
                                float eps, void* out, void* stream);
 
+/* out[m, n] = bf16(act(bf16(a w^T + bias))) (+ addend[m, n], rounded to bf16); act = SiLU if silu != 0.
+ * The block's camera-FiLM MLP: cam_injector_layer1 + SiLU and cam_injector_layer2 + the camera
+ * embedding (CausalWanAttentionBlock.cam_film, model_fast.py:2882-2891). */
+int lbw_linear_act(const void* a, const void* w, const void* bias, const void* addend, int silu, int m, int n, int k,
+                   void* out, void* stream);
+
 /* ---- row kernels ----------------------------------------------------------------------- */
 
 /* h[m, c] = LN(x)[m, :] * (1 + scale) + shift (fp32 math, eps, no affine) -> bf16, or with

@@ -36,6 +36,7 @@ SIGNATURES = {
     "lbw_linear_rmsnorm_noalloc": ([_vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp], _i),
     "lbw_chunk_attention_partial": ([_vp, _ll, _i, _i, _vp, _vp, _vp, _i, _ll, _vp, _f, _i, _vp, _vp, _i, _vp], _i),
     "lbw_attention_merge": ([_vp, _vp, _i, _i, _i, _vp, _ll, _vp], _i),
+    "lbw_linear_act": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
     "lbw_layernorm_mod_mx": ([_vp, _i, _i, _f, _vp, _vp, _vp, _vp, _vp], _i),
     "lbw_mx_linear": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp], _i),
     "lbw_mx_linear_gelu": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),

@@ -46,6 +46,12 @@ class _AttnParams(nn.Module):
         self.norm_k = _RMSNormParam(dim) if qk_norm else nn.Identity()
 
 
+def _event():
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record()
+    return ev
+
+
 class Workspace:
     """Scratch of one block forward over `rows` local query tokens; shared by all blocks of a stack."""
 
@@ -104,8 +110,9 @@ class CausalWanAttentionBlock(nn.Module):
 
     # ------------------------------------------------------------------ weights
     @torch.no_grad()
-    def prepare(self, free_sources=False):
-        """Pack/convert the weights the kernels read (once; call again after changing weights)."""
+    def prepare(self, free_sources=False, with_cam=True):
+        """Pack/convert the weights the kernels read (once; call again after changing weights). with_cam keeps
+        the camera-FiLM MLP weights for cam_film()."""
         if getattr(self, "_sources_freed", False):
             raise ValueError("prepare(free_sources=True) already released the source weights")
         sa, ca = self.self_attn, self.cross_attn
@@ -139,6 +146,10 @@ class CausalWanAttentionBlock(nn.Module):
         else:
             pk["w1"], pk["w2"] = w1, w2
         pk["b1"], pk["b2"] = b(self.ffn[0].bias), b(self.ffn[2].bias)
+        if with_cam:
+            for key, lin in (("c1", self.cam_injector_layer1), ("c2", self.cam_injector_layer2),
+                             ("cs", self.cam_scale_layer), ("csh", self.cam_shift_layer)):
+                pk["w" + key], pk["b" + key] = b(lin.weight), b(lin.bias)
         self._packed = pk
         if free_sources:
             # Only the packed copies serve the forward from here on (the reference frees its bf16 FFN
@@ -149,6 +160,25 @@ class CausalWanAttentionBlock(nn.Module):
                 lin.weight = nn.Parameter(torch.empty(0, dtype=lin.weight.dtype, device=dev), requires_grad=False)
             self._sources_freed = True
         return pk
+
+    @torch.no_grad()
+    def cam_film(self, c2ws_plucker_emb):
+        """Camera FiLM parameters (cam_scale, cam_shift) of this block for the chunk's camera condition
+        [1, L, C] (reference model_fast.py:2882-2891): silu(l1(c)) -> l2(.) + c -> (scale_layer, shift_layer),
+        every Linear a tcgen05 GEMM. Depends only on the camera condition, so callers hoist it per chunk."""
+        if self._packed is None:
+            self.prepare()
+        pk = self._packed
+        if "wc1" not in pk:
+            raise ValueError("cam_film needs prepare(with_cam=True)")
+        C = self.dim
+        c = c2ws_plucker_emb.reshape(-1, C).to(BF16).contiguous()
+        h1 = kernels.linear_act(c, pk["wc1"], pk["bc1"], silu=True)
+        h2 = kernels.linear_act(h1, pk["wc2"], pk["bc2"], addend=c)
+        scale = kernels.linear_act(h2, pk["wcs"], pk["bcs"])
+        shift = kernels.linear_act(h2, pk["wcsh"], pk["bcsh"])
+        shape = c2ws_plucker_emb.shape[:-1] + (C,)
+        return scale.view(shape), shift.view(shape)
 
     def workspace(self, rows, device):
         if self._ws is None or not self._ws.fits(rows, self.dim, self.ffn_dim, device):
@@ -207,7 +237,9 @@ class CausalWanAttentionBlock(nn.Module):
         dev = ws.q.device
         comm = self._comm_streams.get(dev)
         if comm is None:
-            comm = self._comm_streams[dev] = torch.cuda.Stream(device=dev)
+            # high priority: once the gather is done, the destination chunk's CTAs are dispatched ahead of the
+            # leading-chunk launch's remaining ones instead of trailing it
+            comm = self._comm_streams[dev] = torch.cuda.Stream(device=dev, priority=-1)
         main = torch.cuda.current_stream(dev)
         ready = torch.cuda.Event()
         ready.record(main)                       # this rank's K/V rows are written
@@ -274,9 +306,12 @@ class CausalWanAttentionBlock(nn.Module):
         return tuple(int(v) for v in g)
 
     def forward_inplace(self, xf, e, k_chunks, v_chunks, context, crossattn_cache, grid, start_frame, freqs,
-                        film=None, fill_cross=False, kv_only=False, ws=None, attn_events=None):
+                        film=None, fill_cross=False, kv_only=False, ws=None, attn_events=None, phases=None):
         """The block on the fp32 residual xf [L_local, C] (updated in place). attn_events: optional list
-        that receives a (start, end) pair of CUDA events around the self-attention kernel."""
+        that receives a (start, end) pair of CUDA events around the self-attention kernel. phases: optional
+        list that receives (name, event) marks after each step, for per-phase timing."""
+        mark = (lambda name: phases.append((name, _event()))) if phases is not None else (lambda name: None)
+        mark("start")
         if self._packed is None:
             self.prepare()
         pk = self._packed
@@ -302,9 +337,12 @@ class CausalWanAttentionBlock(nn.Module):
 
         # self-attention
         kernels.layernorm_mod(xf, eps, ws.h, scale=em[1], shift=em[0])
+        mark("ln1")
         kernels.qkv_proj(ws.h, pk["wqkv"], pk["bqkv"], ws.q_raw, ws.k_raw, ss_q, ss_k, v_dst, v_row_off=row0)
+        mark("qkv")
         kernels.rmsnorm_rope(ws.q_raw, ss_q, pk["gq"], eps, ws.q, rope=rp, grid=grid, tok0=row0)
         kernels.rmsnorm_rope(ws.k_raw, ss_k, pk["gk"], eps, k_dst, rope=rp, grid=grid, tok0=row0, out_row_off=row0)
+        mark("qk_norm_rope")
         if kv_only:
             if p > 1:
                 sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
@@ -317,18 +355,22 @@ class CausalWanAttentionBlock(nn.Module):
         if attn_events is not None:
             ev1.record()
             attn_events.append((ev0, ev1))
+        mark("self_attn")
         fs, ft = (film[0].reshape(-1, C), film[1].reshape(-1, C)) if film is not None else (None, None)
         if fs is not None:
             fs, ft = fs.to(BF16).contiguous(), ft.to(BF16).contiguous()
         kernels.linear_residual(ws.attn, pk["wo"], pk["bo"], xf, gate=em[2], film_scale=fs, film_shift=ft)
+        mark("o_proj_film")
 
         # cross-attention
         if self.cross_attn_norm:
             kernels.layernorm_mod(xf, eps, ws.h, weight=pk["n3w"], bias=pk["n3b"])
+            mark("ln3")
         else:
             raise ValueError("cross_attn_norm=False is not supported by the B200 block")
         kernels.linear_rowss(ws.h, pk["wcq"], pk["bcq"], ws.q_raw, ss_q)
         kernels.rmsnorm_rope(ws.q_raw, ss_q, pk["gcq"], eps, ws.q)
+        mark("cross_q")
         T = crossattn_cache["k"].numel() // C
         kc, vc = crossattn_cache["k"].view(T, C), crossattn_cache["v"].view(T, C)
         bias = None
@@ -336,17 +378,22 @@ class CausalWanAttentionBlock(nn.Module):
             n = self.cross_dedup
             kc, vc, bias = kc[:n], vc[:n], crossattn_cache["mult"]
         kernels.chunk_attention(ws.q, [kc], [vc], key_bias=bias, out=ws.attn)
+        mark("cross_attn")
         kernels.linear_residual(ws.attn, pk["wco"], pk["bco"], xf)
+        mark("cross_o")
 
         # FFN
         if self.ffn_mx and self.mx_pipe == "mxf8":
             kernels.layernorm_mod_mx(xf, eps, em[4], em[3], ws.hq, ws.hs)
+            mark("ln2")
             kernels.mx_linear_gelu(ws.hq, ws.hs, *pk["w1_mx"], pk["b1"], ws.uq, ws.us)
+            mark("ffn_up")
             kernels.mx_linear_residual(ws.uq, ws.us, *pk["w2_mx"], pk["b2"], xf, gate=em[5])
         else:
             kernels.layernorm_mod(xf, eps, ws.h, scale=em[4], shift=em[3], mx_qdq=self.ffn_mx)
             kernels.linear_gelu(ws.h, pk["w1"], pk["b1"], ws.u, mx_qdq=self.ffn_mx)
             kernels.linear_residual(ws.u, pk["w2"], pk["b2"], xf, gate=em[5])
+        mark("ffn_down")
         return xf
 
 

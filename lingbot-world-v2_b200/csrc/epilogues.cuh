@@ -150,6 +150,57 @@ struct EpiGelu {
   LBW_DEV void tile_done(int, int, float) const {}
 };
 
+// out = bf16(act(bf16(acc + b))) [+ addend, rounded to bf16], act = identity or SiLU: the camera-FiLM
+// MLP of the block (cam_injector_layer1 + SiLU, cam_injector_layer2 + the camera embedding).
+struct EpiAct {
+  __nv_bfloat16* out;           // [M, ldo]
+  long long ldo;
+  const __nv_bfloat16* bias;    // [N] nullable
+  const __nv_bfloat16* addend;  // [M, ldo] nullable
+  int silu;
+
+  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
+    const long long off = (long long)row * ldo + col;
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 8) {
+      float b[8], a[8];
+      if (bias) {
+        uint4 bb = *reinterpret_cast<const uint4*>(bias + col + e);
+        const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) b[q] = __bfloat162float(bp[q]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) b[q] = 0.f;
+      }
+      if (addend) {
+        uint4 aa = *reinterpret_cast<const uint4*>(addend + off + e);
+        const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&aa);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) a[q] = __bfloat162float(ap[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < 8; q += 2) {
+        float y[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          float t = bf16_round(v[e + q + u] + b[q + u]);
+          if (silu) t = bf16_round(t / (1.f + __expf(-t)));
+          if (addend) t = bf16_round(t + a[q + u]);
+          y[u] = t;
+        }
+        pk[(e + q) / 2] = pack_bf16(y[0], y[1]);
+      }
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(out + off);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    return 0.f;
+  }
+  LBW_DEV void tile_done(int, int, float) const {}
+};
+
 struct EpiGeluMX {
   uint8_t* data;     // [M, ld] E4M3 codes of GELU(u + b)
   uint8_t* scales;   // E8M0 scales in the tiled layout of a [M, sf_cols] matrix (mx_sf_offset)

@@ -325,6 +325,19 @@ int lbw_linear_gelu(const void* a, const void* w, const void* bias, int m, int n
   return launch_gemm(a, k, w, k, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int lbw_linear_act(const void* a, const void* w, const void* bias, const void* addend, int silu, int m, int n, int k,
+                   void* out, void* stream) {
+  if (!out) return set_error(LBW_ERR_INVALID, "lbw_linear_act: null output");
+  if (!ok16(out) || !ok16(bias) || !ok16(addend) || n % 8) return set_error(LBW_ERR_ALIGN, "lbw_linear_act: alignment");
+  EpiAct e{};
+  e.out = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ldo = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.addend = reinterpret_cast<const __nv_bfloat16*>(addend);
+  e.silu = silu;
+  return launch_gemm(a, k, w, k, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------------------------------------

@@ -173,6 +173,23 @@ def linear_residual(a, w, bias, x, gate=None, film_scale=None, film_shift=None):
     return x
 
 
+def linear_act(a, w, bias=None, addend=None, silu=False, out=None):
+    """bf16(act(bf16(a w^T + bias))) (+ addend): the camera-FiLM MLP layers."""
+    require_cuda(a, w, bias, addend, out)
+    _c(a, BF16), _c(w, BF16)
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k or (addend is not None and (addend.shape != (m, n) or addend.dtype != BF16)):
+        raise ValueError("linear_act: shape mismatch")
+    if addend is not None:
+        _c(addend)
+    if out is None:
+        out = torch.empty(m, n, dtype=BF16, device=a.device)
+    check(load().lbw_linear_act(ptr(a), ptr(w), ptr(bias), ptr(addend), int(bool(silu)), m, n, k, ptr(out),
+                                stream_of(a.device)), "linear_act")
+    return out
+
+
 def linear_gelu(a, w, bias, out, mx_qdq):
     require_cuda(a, w, bias, out)
     m, k = a.shape

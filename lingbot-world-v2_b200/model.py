@@ -31,7 +31,7 @@ class BlockStack(nn.Module):
             b.prepare()
 
     def forward_chunk(self, xf, e, kv_chunks_by_block, context, cross_caches, grid, start_frame, freqs, films=None,
-                      fill_cross=False, attn_events=None):
+                      fill_cross=False, attn_events=None, phases=None):
         """xf [L_local, C] fp32 residual (updated in place); kv_chunks_by_block = (ks, vs) with ks[i] the
         ordered K chunk list of block i; films[i] = (scale, shift) or None."""
         L = xf.shape[0]
@@ -41,7 +41,7 @@ class BlockStack(nn.Module):
         for i, blk in enumerate(self.blocks):
             blk.forward_inplace(xf, e, ks[i], vs[i], context, cross_caches[i], grid, start_frame, freqs,
                                 film=None if films is None else films[i], fill_cross=fill_cross, ws=self._ws,
-                                attn_events=attn_events)
+                                attn_events=attn_events, phases=phases)
         return xf
 
     @classmethod
@@ -58,7 +58,7 @@ class BlockStack(nn.Module):
         g = torch.Generator(device=device).manual_seed(seed)
         init_synthetic_(st, g, peaked=peaked)
         for blk in st.blocks:
-            blk.prepare(free_sources=True)
+            blk.prepare(free_sources=True, with_cam=False)   # the benchmark feeds hoisted FiLM tensors
         return st
 
 

@@ -184,3 +184,12 @@ def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, m
     if return_all:
         return dict(x=x3, q=q, k=k, v=v, attn=attn, x1=x1, h3=h3, qc=qc, ca=ca, x2=x2, h2=h2, g=g, y2=y2)
     return x3
+
+
+def cam_film(p, c):
+    """CausalWanAttentionBlock.cam_film (model_fast.py:2882-2891): bf16 Linears, SiLU on the bf16 hidden,
+    the camera embedding added to layer 2's bf16 output. c [L, C] bf16 -> (scale, shift) bf16."""
+    h = F.silu(linear(c, p["cam_injector_layer1.weight"], p["cam_injector_layer1.bias"]).float()).to(torch.bfloat16)
+    h2 = (linear(h, p["cam_injector_layer2.weight"], p["cam_injector_layer2.bias"]) + c).to(torch.bfloat16)
+    return (linear(h2, p["cam_scale_layer.weight"], p["cam_scale_layer.bias"]),
+            linear(h2, p["cam_shift_layer.weight"], p["cam_shift_layer.bias"]))

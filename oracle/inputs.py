@@ -27,6 +27,7 @@ class BlockCase:
     peaked: bool = False
     film: bool = True
     dedup_rows: int = 0            # >0: context rows >= this are identical (cross_dedup input)
+    cam: bool = False              # also draw the camera-FiLM MLP weights and a camera condition (last)
     seed: int = 0
     extra: dict = field(default_factory=dict)
 
@@ -82,4 +83,10 @@ def make_case(case: BlockCase):
     film = None
     if case.film:
         film = (_n(rng, (Lq, C), 0.1).to(torch.bfloat16), _n(rng, (Lq, C), 0.1).to(torch.bfloat16))
-    return p, dict(x=x, e0=e0, k_lead=k_lead, v_lead=v_lead, context=ctx, film=film)
+    inp = dict(x=x, e0=e0, k_lead=k_lead, v_lead=v_lead, context=ctx, film=film)
+    if case.cam:   # drawn after everything else, so the draws above are the same with or without it
+        for nm in ("cam_injector_layer1", "cam_injector_layer2", "cam_scale_layer", "cam_shift_layer"):
+            p[f"{nm}.weight"] = _n(rng, (C, C), 0.02).to(torch.bfloat16)
+            p[f"{nm}.bias"] = _n(rng, (C,), 0.02).to(torch.bfloat16)
+        inp["cam"] = _n(rng, (Lq, C), 1.0).to(torch.bfloat16)
+    return p, inp

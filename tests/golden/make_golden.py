@@ -36,6 +36,7 @@ CASES = {
                               seed=3),
 }
 DEDUP = BlockCase(dim=256, ffn=256, grid=(1, 8, 8), n_lead=0, text_len=64, dedup_rows=20, peaked=True, seed=4)
+CAM = BlockCase(dim=256, ffn=256, grid=(1, 6, 8), n_lead=0, text_len=16, cam=True, seed=6)
 
 
 def install_shims():
@@ -151,6 +152,21 @@ def run_dedup(attn_mod, mf):
     return dict(case=case.__dict__, q=q[0], ctx_k=ck, ctx_v=cv, kc=kc, bias=bias, out=out[0], full=full[0])
 
 
+def run_cam(mf):
+    """Reference CausalWanAttentionBlock.cam_film (model_fast.py:2882-2891) on a seeded camera condition."""
+    case = CAM
+    p, inp = make_case(case)
+    blk = mf.CausalWanAttentionBlock(case.dim, case.ffn, case.heads, qk_norm=True, cross_attn_norm=True, eps=1e-6)
+    blk = blk.to(torch.bfloat16)
+    sd = blk.state_dict()
+    for k_, v_ in p.items():
+        sd[k_] = v_.to(sd[k_].dtype)
+    blk.load_state_dict(sd)
+    with torch.no_grad():
+        scale, shift = blk.cam_film(inp["cam"].unsqueeze(0))
+    return dict(case=case.__dict__, checksum=checksum(p, inp), scale=scale[0].clone(), shift=shift[0].clone())
+
+
 def main():
     install_shims()
     with contextlib.redirect_stdout(sys.stderr):
@@ -165,6 +181,8 @@ def main():
     res = run_dedup(attn_mod, mf)
     torch.save(res, os.path.join(HERE, "cross_dedup.pt"))
     print("cross_dedup saved")
+    torch.save(run_cam(mf), os.path.join(HERE, "cam_film.pt"))
+    print("cam_film saved")
     table = {(i, n): ckv.chunk_routing(i, n) for n in (1, 2, 3, 4, 7) for i in range(0, 12)}
     torch.save(table, os.path.join(HERE, "chunk_routing.pt"))
     print("chunk_routing saved")

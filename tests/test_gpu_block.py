@@ -138,3 +138,13 @@ def test_block_stack_two_blocks(cuda_dev):
         ck, cv = ob.cross_kv(pp, inp["context"])
         x = ob.block_forward(pp, x, inp["e0"], inp["k_lead"], inp["v_lead"], ck, cv, cos, sin, film=inp["film"], mx=True)
     assert rel_l2(xf, x) <= 1e-2 and rel_l2(xf.cpu() - inp["x"], x - inp["x"]) <= 2e-2
+
+
+def test_cam_film_vs_reference_golden(cuda_dev):
+    g = load_golden("cam_film")
+    case = BlockCase(**g["case"])
+    p, inp = make_case(case)
+    blk = _build(case, p, cuda_dev, ffn_mx=True)
+    scale, shift = blk.cam_film(inp["cam"].unsqueeze(0).to(cuda_dev))
+    assert scale.shape == (1, case.lq, case.dim)
+    assert rel_l2(scale[0], g["scale"]) < 1e-2 and rel_l2(shift[0], g["shift"]) < 1e-2

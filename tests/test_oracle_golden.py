@@ -42,3 +42,12 @@ def test_chunk_routing_table():
     table = load_golden("chunk_routing")
     for (i, n), want in table.items():
         assert ckv.chunk_routing(i, n) == want, (i, n)
+
+
+def test_cam_film_matches_reference():
+    g = load_golden("cam_film")
+    case = BlockCase(**g["case"])
+    p, inp = make_case(case)
+    assert abs(checksum(p, inp) - g["checksum"]) <= 1e-4 * g["checksum"]
+    scale, shift = ob.cam_film(p, inp["cam"])
+    assert rel_l2(scale, g["scale"]) < 2e-3 and rel_l2(shift, g["shift"]) < 2e-3
