@@ -30,7 +30,13 @@
 
 namespace lbw {
 
+#ifndef LBW_ATTN_POLY_EIGHTHS
+#define LBW_ATTN_POLY_EIGHTHS 2  // eighths of the exponentials computed on the FMA pipe (exp2_poly2)
+#endif
+
 namespace attn {
+constexpr int POLY = LBW_ATTN_POLY_EIGHTHS;
+static_assert(POLY >= 0 && POLY <= 8, "LBW_ATTN_POLY_EIGHTHS must lie in [0, 8]");
 constexpr int BM = 128, BN = 128, D = 128, QT = 2, STAGES = 2, MAX_CHUNKS = 8;
 constexpr int HALF = 128 * 64 * 2;  // 128 rows x 64 bf16 (one 128-byte swizzled box)
 constexpr int TILE = 2 * HALF;      // 128 rows x 128 bf16
@@ -315,7 +321,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
               const int col = cc * 32 + e;
               float x0, x1, p0, p1;
               f2_unpack(f2_fma(f2_pack(sv[col], sv[col + 1]), a2, b2), x0, x1);
-              if ((e & 6) == 6) {
+              if ((((e >> 1) * POLY) & 7) >= 8 - POLY) {  // spreads POLY of every 8 pairs evenly
                 exp2_poly2(x0, x1, p0, p1);
               } else {
                 p0 = fast_exp2(x0);

@@ -61,7 +61,11 @@ struct EpiStore {
   }
 };
 
-struct EpiResidual {
+// FILM = false: no FiLM operands (the MXFP8 FFN-down GEMM). That GEMM's epilogue holds 128 accumulators per
+// thread, so its chunks are read in four 8-column rounds to stay inside the register budget (wider rounds
+// spilled and measured slower there).
+template <bool FILM>
+struct EpiResidualT {
   float* x;                          // [M, ldx] fp32 residual, updated in place
   long long ldx;
   const __nv_bfloat16* bias;         // [N] nullable
@@ -70,52 +74,71 @@ struct EpiResidual {
   const __nv_bfloat16* film_shift;   // [M, N] (with film_scale)
   long long ldf;
 
-  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
-    float* xr = x + (long long)row * ldx + col;
+  // Columns [off, off + W) of the chunk. Every global read is issued before the first store (the stores may
+  // alias those rows as far as the compiler knows), so a part costs one memory round trip.
+  template <int W>
+  LBW_DEV void part(int row, int col, int off, const float (&v)[32]) const {
+    float* xr = x + (long long)row * ldx + col + off;
+    float4 xv[W / 4];
 #pragma unroll
-    for (int e = 0; e < 32; e += 8) {
-      float y[8], g[8], xs[8];
+    for (int q = 0; q < W / 4; ++q) xv[q] = reinterpret_cast<const float4*>(xr)[q];
+    uint4 sv[W / 8], tv[W / 8];
+    if (FILM && film_scale) {
+      const long long fo = (long long)row * ldf + col + off;
+#pragma unroll
+      for (int q = 0; q < W / 8; ++q) {
+        sv[q] = reinterpret_cast<const uint4*>(film_scale + fo)[q];
+        tv[q] = reinterpret_cast<const uint4*>(film_shift + fo)[q];
+      }
+    }
+    float* xs = reinterpret_cast<float*>(xv);   // updated in place, 8 values at a time
+#pragma unroll
+    for (int e = 0; e < W; e += 8) {
+      float y[8];
       if (bias) {
-        uint4 bb = *reinterpret_cast<const uint4*>(bias + col + e);
+        const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + col + off + e));
         const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q] + __bfloat162float(bp[q]));
+        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[off + e + q] + __bfloat162float(bp[q]));
       } else {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q]);
+        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[off + e + q]);
       }
       if (gate) {
-        float4 g0 = *reinterpret_cast<const float4*>(gate + col + e);
-        float4 g1 = *reinterpret_cast<const float4*>(gate + col + e + 4);
-        g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
-      } else {
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + col + off + e));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + col + off + e + 4));
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
-        for (int q = 0; q < 8; ++q) g[q] = 1.f;
+        for (int q = 0; q < 8; ++q) y[q] = __fmul_rn(y[q], g[q]);
       }
-      float4 x0 = *reinterpret_cast<const float4*>(xr + e);
-      float4 x1 = *reinterpret_cast<const float4*>(xr + e + 4);
-      xs[0] = x0.x; xs[1] = x0.y; xs[2] = x0.z; xs[3] = x0.w; xs[4] = x1.x; xs[5] = x1.y; xs[6] = x1.z; xs[7] = x1.w;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) xs[q] = __fadd_rn(xs[q], __fmul_rn(y[q], g[q]));
-      if (film_scale) {
-        long long fo = (long long)row * ldf + col + e;
-        uint4 s4 = *reinterpret_cast<const uint4*>(film_scale + fo);
-        uint4 t4 = *reinterpret_cast<const uint4*>(film_shift + fo);
-        const __nv_bfloat16* sp = reinterpret_cast<const __nv_bfloat16*>(&s4);
-        const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(&t4);
+      for (int q = 0; q < 8; ++q) xs[e + q] = __fadd_rn(xs[e + q], y[q]);
+      if (FILM && film_scale) {
+        const __nv_bfloat16* sp = reinterpret_cast<const __nv_bfloat16*>(&sv[e / 8]);
+        const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(&tv[e / 8]);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          float s1 = bf16_round(1.f + __bfloat162float(sp[q]));  // (1.0 + bf16 tensor) stays bf16
-          xs[q] = __fadd_rn(__fmul_rn(s1, xs[q]), __bfloat162float(tp[q]));
+          const float s1 = bf16_round(1.f + __bfloat162float(sp[q]));  // (1.0 + bf16 tensor) stays bf16
+          xs[e + q] = __fadd_rn(__fmul_rn(s1, xs[e + q]), __bfloat162float(tp[q]));
         }
       }
-      *reinterpret_cast<float4*>(xr + e) = make_float4(xs[0], xs[1], xs[2], xs[3]);
-      *reinterpret_cast<float4*>(xr + e + 4) = make_float4(xs[4], xs[5], xs[6], xs[7]);
+    }
+#pragma unroll
+    for (int q = 0; q < W / 4; ++q) reinterpret_cast<float4*>(xr)[q] = xv[q];
+  }
+
+  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
+    if constexpr (FILM) {
+      part<32>(row, col, 0, v);
+    } else {
+#pragma unroll
+      for (int off = 0; off < 32; off += 8) part<8>(row, col, off, v);
     }
     return 0.f;
   }
   LBW_DEV void tile_done(int, int, float) const {}
 };
+using EpiResidual = EpiResidualT<true>;
 
 struct EpiGelu {
   __nv_bfloat16* out;   // [M, ldo] GELU(u + b), or its MXFP8 quantise-dequantise

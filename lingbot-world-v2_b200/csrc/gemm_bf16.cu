@@ -6,7 +6,8 @@
 // (one 128-byte swizzled row per M/N row) through a 4-deep TMA ring. Warp roles:
 //   warp 0   TMA producer (one elected lane)
 //   warp 1   UMMA issuer (one elected lane) and TMEM owner (2 x 256 fp32 accumulator columns)
-//   warps 2-5 epilogue: tcgen05.ld of the accumulator (thread = output row), fused math, global stores.
+//   warps 2-9 epilogue: tcgen05.ld of the accumulator (thread = output row), fused math, global stores;
+//            warps w and w+4 share TMEM lane quarter w % 4 and take the left / right half of the tile's columns.
 // The two accumulators let the epilogue of tile i run while the MMAs of tile i+1 proceed.
 //
 // Epilogues used by the block forward (CausalWanAttentionBlock, wan/modules/model_fast.py:2912-3116):
@@ -36,7 +37,8 @@ constexpr int A_BYTES = BM * BK * 2;   // 16 KB
 constexpr int B_BYTES = BN * BK * 2;   // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
+constexpr int EPI_THREADS = THREADS - 64;
 // Tile width TBN (256, or 128 when 256-wide tiles would leave the last wave mostly idle): ring depth and
 // shared memory per tile width.
 template <int TBN> struct Cfg {
@@ -76,7 +78,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], gemm::EPI_THREADS);
     }
     mbar_init(&done_bar, 1);
     abort_flag = 0;
@@ -153,7 +155,9 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       mbar_wait_drain(&done_bar, 0);
     }
   } else {
-    const int quarter = warp & 3;  // warps 2,3,4,5 -> TMEM lane quarters 2,3,0,1
+    const int quarter = warp & 3;          // warps 2..9 -> TMEM lane quarters 2,3,0,1,2,3,0,1
+    constexpr int NCH = BN / 32 / 2;       // 32-column chunks per warp
+    const int c0 = ((warp - 2) >> 2) * NCH;
     int acc = 0;
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -164,7 +168,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       float stat = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = c0; c < c0 + NCH; ++c) {
         const int col = n_blk * BN + c * 32;
         if (col >= N) break;  // warp-uniform
         uint32_t r[32];

@@ -271,7 +271,7 @@ int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, c
                            const void* bias, int m, int n, int k, float* x, const float* gate, void* stream) {
   if (!x) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual: null residual");
   if (!ok16mx(x) || !ok16mx(gate) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_residual: alignment");
-  EpiResidual e{};
+  EpiResidualT<false> e{};
   e.x = x;
   e.ldx = n;
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);

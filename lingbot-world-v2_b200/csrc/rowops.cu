@@ -12,7 +12,8 @@
 namespace lbw {
 
 constexpr int ROW_THREADS = 128;
-constexpr int LN_MAXIT = 6;  // 6 x 128 threads x 8 values = rows up to 6144 wide
+constexpr int LN_MAXV = 12;  // 12 x 128 threads x 4 values = rows up to 6144 wide
+constexpr int RR_MAXIT = 6;  // 6 x 128 threads x 8 bf16 values = rows up to 6144 wide
 
 __device__ __forceinline__ float block_sum128(float v, float* red) {
 #pragma unroll
@@ -24,6 +25,9 @@ __device__ __forceinline__ float block_sum128(float v, float* red) {
   return red[0] + red[1] + red[2] + red[3];
 }
 
+// One CTA per row; thread t owns the float4 groups t, t + 128, ... so every warp access (x, the
+// modulation vectors, the output) is one contiguous 512-byte (or 256/128-byte) span. The row stays
+// in registers between the mean, the variance and the output pass.
 __global__ void __launch_bounds__(ROW_THREADS) layernorm_mod_kernel(const float* __restrict__ x, int C, float eps,
                                                                     const float* __restrict__ scale,
                                                                     const float* __restrict__ shift,
@@ -34,79 +38,74 @@ __global__ void __launch_bounds__(ROW_THREADS) layernorm_mod_kernel(const float*
                                                                     uint8_t* __restrict__ mx_scales) {
   __shared__ float red[4];
   const long long row = blockIdx.x;
-  const float* xr = x + row * C;
-  const int G = C >> 3;
-  float v[LN_MAXIT][8];
+  const float4* xr = reinterpret_cast<const float4*>(x + row * C);
+  const int G = C >> 2;
+  float4 v[LN_MAXV];
   float s = 0.f;
 #pragma unroll
-  for (int it = 0; it < LN_MAXIT; ++it) {
+  for (int it = 0; it < LN_MAXV; ++it) {
     const int g = it * ROW_THREADS + threadIdx.x;
     if (g < G) {
-      float4 a = *reinterpret_cast<const float4*>(xr + g * 8);
-      float4 b = *reinterpret_cast<const float4*>(xr + g * 8 + 4);
-      v[it][0] = a.x; v[it][1] = a.y; v[it][2] = a.z; v[it][3] = a.w;
-      v[it][4] = b.x; v[it][5] = b.y; v[it][6] = b.z; v[it][7] = b.w;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) s += v[it][e];
+      v[it] = __ldcs(xr + g);
+      s += (v[it].x + v[it].y) + (v[it].z + v[it].w);
     }
   }
   const float mean = block_sum128(s, red) / (float)C;
   float q = 0.f;
 #pragma unroll
-  for (int it = 0; it < LN_MAXIT; ++it) {
+  for (int it = 0; it < LN_MAXV; ++it) {
     const int g = it * ROW_THREADS + threadIdx.x;
     if (g < G) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float d = v[it][e] - mean;
-        q += d * d;
-      }
+      const float a = v[it].x - mean, b = v[it].y - mean, c = v[it].z - mean, d = v[it].w - mean;
+      q += (a * a + b * b) + (c * c + d * d);
     }
   }
   const float var = block_sum128(q, red) / (float)C;
   const float rstd = 1.f / sqrtf(var + eps);
+  const float4* mul4 = reinterpret_cast<const float4*>(scale ? scale : weight);
+  const float4* add4 = reinterpret_cast<const float4*>(scale ? shift : bias);
+  const float one = scale ? 1.f : 0.f;  // (1 + scale) for the adaLN modulation, w for the affine
 #pragma unroll
-  for (int it = 0; it < LN_MAXIT; ++it) {
+  for (int it = 0; it < LN_MAXV; ++it) {
     const int g = it * ROW_THREADS + threadIdx.x;
     if (it * ROW_THREADS >= G) break;  // block-uniform
-    float y[8];
+    float y[4] = {0.f, 0.f, 0.f, 0.f};
     if (g < G) {
-      const int c0 = g * 8;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float n = (v[it][e] - mean) * rstd;
-        if (scale) n = n * (1.f + scale[c0 + e]) + shift[c0 + e];
-        else if (weight) n = n * weight[c0 + e] + bias[c0 + e];
-        y[e] = bf16_round(n);
+      float n[4] = {(v[it].x - mean) * rstd, (v[it].y - mean) * rstd, (v[it].z - mean) * rstd,
+                    (v[it].w - mean) * rstd};
+      if (mul4) {
+        const float4 m4 = __ldg(mul4 + g), a4 = __ldg(add4 + g);
+        n[0] = n[0] * (one + m4.x) + a4.x;
+        n[1] = n[1] * (one + m4.y) + a4.y;
+        n[2] = n[2] * (one + m4.z) + a4.z;
+        n[3] = n[3] * (one + m4.w) + a4.w;
       }
-    } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = 0.f;
+      for (int e = 0; e < 4; ++e) y[e] = bf16_round(n[e]);
     }
     if (mx || mx_data) {
-      // 32-value MX block = 4 consecutive threads x 8 values
-      float amax = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(y[e]));
+      // 32-value MX block = 8 consecutive threads x 4 values (C % 32 == 0 keeps blocks inside the row)
+      float amax = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
       const int se = mx_shared_exp(amax);
       if (mx_data) {  // E4M3 codes + E8M0 scale (tiled layout): the next MXFP8 GEMM's A operand
-        uint8_t qb[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) qb[e] = mx_to_e4m3(ldexpf(y[e], -se));
+        // y * 2^-se is exact: se lies in [-127, 119] for bf16-range values, so 2^-se is a normal float
+        const float inv = exp2i(-se);
+        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(y[0] * inv, y[1] * inv), __NV_SATFINITE, __NV_E4M3);
+        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(y[2] * inv, y[3] * inv), __NV_SATFINITE, __NV_E4M3);
         if (g < G) {
-          *reinterpret_cast<uint2*>(mx_data + row * C + g * 8) = *reinterpret_cast<const uint2*>(qb);
-          if ((g & 3) == 0) mx_scales[mx_sf_offset(row, g >> 2, C)] = (uint8_t)(se + 127);
+          *reinterpret_cast<uint32_t*>(mx_data + row * C + g * 4) = lo | (hi << 16);
+          if ((g & 7) == 0) mx_scales[mx_sf_offset(row, g >> 3, C)] = (uint8_t)(se + 127);
         }
         continue;
       }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = ldexpf(mx_from_e4m3(mx_to_e4m3(ldexpf(y[e], -se))), se);
+      for (int e = 0; e < 4; ++e) y[e] = ldexpf(mx_from_e4m3(mx_to_e4m3(ldexpf(y[e], -se))), se);
     }
     if (g < G) {
-      uint4 o = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
-      *reinterpret_cast<uint4*>(out + row * C + g * 8) = o;
+      *reinterpret_cast<uint2*>(out + row * C + g * 4) = make_uint2(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]));
     }
   }
 }
@@ -198,10 +197,12 @@ int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scal
   if (!x || !out) return set_error(LBW_ERR_INVALID, "layernorm_mod: null pointer");
   if ((scale == nullptr) != (shift == nullptr) || (weight == nullptr) != (bias == nullptr) || (scale && weight))
     return set_error(LBW_ERR_INVALID, "layernorm_mod: give either scale+shift or weight+bias");
-  if (m <= 0 || c <= 0 || c % 32 || c > LN_MAXIT * ROW_THREADS * 8)
+  if (m <= 0 || c <= 0 || c % 32 || c > LN_MAXV * ROW_THREADS * 4)
     return set_error(LBW_ERR_SHAPE, "layernorm_mod: width %d must be a multiple of 32 and <= %d", c,
-                     LN_MAXIT * ROW_THREADS * 8);
-  if (!aligned(x, 16) || !aligned(out, 16)) return set_error(LBW_ERR_ALIGN, "layernorm_mod: alignment");
+                     LN_MAXV * ROW_THREADS * 4);
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(scale, 16) || !aligned(shift, 16) || !aligned(weight, 16) ||
+      !aligned(bias, 16))
+    return set_error(LBW_ERR_ALIGN, "layernorm_mod: x, out and the modulation vectors need 16-byte alignment");
   layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, c, eps, scale, shift, weight, bias, mx_qdq, reinterpret_cast<__nv_bfloat16*>(out), nullptr, nullptr);
   return cuda_check(cudaGetLastError(), "layernorm_mod launch");
@@ -210,10 +211,11 @@ int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scal
 int lbw_layernorm_mod_mx(const float* x, int m, int c, float eps, const float* scale, const float* shift, void* data,
                          void* scales, void* stream) {
   if (!x || !data || !scales || !scale || !shift) return set_error(LBW_ERR_INVALID, "layernorm_mod_mx: null pointer");
-  if (m <= 0 || c <= 0 || c % 128 || c > LN_MAXIT * ROW_THREADS * 8)
+  if (m <= 0 || c <= 0 || c % 128 || c > LN_MAXV * ROW_THREADS * 4)
     return set_error(LBW_ERR_SHAPE, "layernorm_mod_mx: width %d must be a multiple of 128 and <= %d", c,
-                     LN_MAXIT * ROW_THREADS * 8);
-  if (!aligned(x, 16) || !aligned(data, 16)) return set_error(LBW_ERR_ALIGN, "layernorm_mod_mx: alignment");
+                     LN_MAXV * ROW_THREADS * 4);
+  if (!aligned(x, 16) || !aligned(data, 16) || !aligned(scale, 16) || !aligned(shift, 16))
+    return set_error(LBW_ERR_ALIGN, "layernorm_mod_mx: x, data and the modulation vectors need 16-byte alignment");
   layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, c, eps, scale, shift, nullptr, nullptr, 1, nullptr, reinterpret_cast<uint8_t*>(data),
       reinterpret_cast<uint8_t*>(scales));
@@ -225,7 +227,9 @@ int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, i
                      void* out, long long ldo, int out_row_off, void* stream) {
   if (!x || !ss || !gamma || !out) return set_error(LBW_ERR_INVALID, "rmsnorm_rope: null pointer");
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return set_error(LBW_ERR_INVALID, "rmsnorm_rope: cos/sin pair");
-  if (m <= 0 || c <= 0 || c % 128) return set_error(LBW_ERR_SHAPE, "rmsnorm_rope: width %d must be a multiple of 128", c);
+  if (m <= 0 || c <= 0 || c % 128 || c > RR_MAXIT * ROW_THREADS * 8)
+    return set_error(LBW_ERR_SHAPE, "rmsnorm_rope: width %d must be a multiple of 128 and <= %d", c,
+                     RR_MAXIT * ROW_THREADS * 8);
   if (rope_cos && (grid_h <= 0 || grid_w <= 0 || rope_frames <= 0 || tok0 < 0 ||
                    (tok0 + m - 1) / (grid_h * grid_w) >= rope_frames))
     return set_error(LBW_ERR_SHAPE, "rmsnorm_rope: tokens %d..%d outside a %d-frame %dx%d grid", tok0, tok0 + m - 1,

@@ -151,11 +151,12 @@ def test_cross_dedup_against_reference_golden(cuda_dev):
     assert rel_l2(out[0], g["out"]) < 1e-2 and rel_l2(out[0], g["full"]) < 1e-2
 
 
+@pytest.mark.parametrize("c", [96, 1536, 5120, 6144])
 @pytest.mark.parametrize("mode", ["mod", "affine", "mod_mx"])
-def test_layernorm_mod(cuda_dev, mode):
+def test_layernorm_mod(cuda_dev, mode, c):
     import lbw_b200.kernels as K
     g = _g(11)
-    m, c = 257, 1536
+    m = 257
     x = torch.randn(m, c, generator=g) * 2 + 0.5
     s, t = torch.randn(c, generator=g) * 0.1, torch.randn(c, generator=g) * 0.1
     out = torch.empty(m, c, dtype=BF, device=cuda_dev)
@@ -171,12 +172,12 @@ def test_layernorm_mod(cuda_dev, mode):
     assert rel_l2(out, ref) < 2e-3
 
 
-@pytest.mark.parametrize("grid,start,tok0,m", [((3, 4, 6), 6, 0, 72), ((3, 30, 52), 18, 1170, 1170)])
-def test_rmsnorm_rope(cuda_dev, grid, start, tok0, m):
+@pytest.mark.parametrize("grid,start,tok0,m,c", [((3, 4, 6), 6, 0, 72, 512), ((3, 30, 52), 18, 1170, 1170, 512),
+                                                   ((3, 4, 6), 2, 12, 60, 5120), ((1, 2, 3), 0, 0, 6, 6144)])
+def test_rmsnorm_rope(cuda_dev, grid, start, tok0, m, c):
     import lbw_b200.kernels as K
     import lbw_b200.rope as R
     g = _g(13)
-    c = 512
     x = torch.randn(m, c, generator=g).to(BF)
     gamma = (1 + 0.02 * torch.randn(c, generator=g)).to(BF)
     ss = x.float().pow(2).sum(1)

@@ -74,10 +74,11 @@ def test_mx_linear_residual(cuda_dev):
     assert rel_l2(xd - x.to(d), ref - x) < 5e-3
 
 
-def test_layernorm_mod_mx(cuda_dev):
+@pytest.mark.parametrize("c", [128, 1536, 5120])
+def test_layernorm_mod_mx(cuda_dev, c):
     import lbw_b200.kernels as K
     g = torch.Generator().manual_seed(11)
-    m, c = 257, 1536
+    m = 257
     x = torch.randn(m, c, generator=g) * 2 + 0.5
     s, t = torch.randn(c, generator=g) * 0.1, torch.randn(c, generator=g) * 0.1
     dq, ds = K.mx_buffers(m, c, cuda_dev)
