@@ -166,21 +166,29 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       const uint32_t idesc_o = idesc_bf16(BM, D, 0, 1);   // O += P V: P from TMEM, V MN-major
       const int n_tiles = g_end - g_begin;
 
+      // Descriptors are built once; a byte offset o inside shared memory moves the 14-bit start-address
+      // field by o >> 4 (shared addresses stay below 2^18 bytes, so the field never carries). The issuing
+      // thread is alone on its warp, so every instruction between two MMAs is latency the tensor pipe sees.
+      const uint64_t dQ = sdesc_kmajor_sw128(smem_u32(sQ));
+      const uint64_t dK = sdesc_kmajor_sw128(smem_u32(sK));
+      const uint64_t dV = sdesc_mnmajor_sw128(smem_u32(sV), HALF);
       auto issue_s = [&](int i, int stage) {
-        const uint32_t qa = smem_u32(sQ + i * TILE), kb = smem_u32(sK + stage * TILE);
+        const uint64_t q = dQ + (uint64_t)((i * TILE) >> 4), k = dK + (uint64_t)((stage * TILE) >> 4);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          mma_f16_ss(tmem + i * 128, sdesc_kmajor_sw128(qa + off), sdesc_kmajor_sw128(kb + off), idesc_s, kk > 0);
+          const uint64_t off = (uint64_t)(((kk >> 2) * HALF + (kk & 3) * 32) >> 4);
+          mma_f16_ss(tmem + i * 128, q + off, k + off, idesc_s, kk > 0);
         }
       };
       // O_i += P_i V over one half of the tile's keys (half 0: keys 0..63, half 1: keys 64..127)
       auto issue_pv = [&](int i, int stage, bool first, int half) {
-        const uint32_t vb = smem_u32(sV + stage * TILE);
+        const uint64_t v = dV + (uint64_t)((stage * TILE) >> 4);
 #pragma unroll
-        for (int kk = half * 4; kk < half * 4 + 4; ++kk)
-          mma_f16_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8, sdesc_mnmajor_sw128(vb + kk * 2048, HALF), idesc_o,
+        for (int q = 0; q < 4; ++q) {
+          const int kk = half * 4 + q;
+          mma_f16_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8, v + (uint64_t)((kk * 2048) >> 4), idesc_o,
                      !(first && kk == 0));
+        }
       };
 
       bool ok = mbar_wait(&q_full, 0, ab, 0x31) && mbar_wait(&k_full[0], 0, ab, 0x32);

@@ -124,6 +124,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16(BM, BN, 0, 0);
+      // descriptors built once: a shared-memory byte offset o adds o >> 4 to the start-address field
+      const uint64_t d0 = sdesc_kmajor_sw128(smem_u32(smem));
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;
@@ -136,12 +138,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         for (int kb = 0; kb < nK; ++kb) {
           if (!mbar_wait(&full_bar[s], ph, ab, 3)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t b0 = a0 + A_BYTES;
+          const uint64_t da = d0 + (uint64_t)((s * STAGE_BYTES) >> 4), db = da + (uint64_t)(A_BYTES >> 4);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            mma_f16_ss(d, sdesc_kmajor_sw128(a0 + kk * 32), sdesc_kmajor_sw128(b0 + kk * 32), idesc,
-                       (kb | kk) != 0);
+            mma_f16_ss(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
           tc_commit(&empty_bar[s]);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }

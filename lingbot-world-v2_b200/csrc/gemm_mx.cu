@@ -122,6 +122,9 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // descriptors built once: a shared-memory byte offset o adds o >> 4 to the start-address field
+      const uint64_t dA = sdesc_kmajor_sw128(smem_u32(sA)), dB = sdesc_kmajor_sw128(smem_u32(sB));
+      const uint64_t dS = sdesc_sf(smem_u32(sSF));
       int s = 0;
       uint32_t ph = 0, aph = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -131,15 +134,15 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
         for (int kb = 0; kb < nK; ++kb) {
           if (!mbar_wait(&full_bar[s], ph, ab, 0x53)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
-          const uint32_t sf = smem_u32(sSF + s * SF_BYTES);
-          tmem_cp_32x128b_x4(tmem + SFA_COL, sdesc_sf(sf));
-          tmem_cp_32x128b_x4(tmem + SFB_COL, sdesc_sf(sf + 512));
-          if (BN == 256) tmem_cp_32x128b_x4(tmem + SFB_COL + 4, sdesc_sf(sf + 1024));
+          const uint64_t da = dA + (uint64_t)((s * A_BYTES) >> 4), db = dB + (uint64_t)((s * B_BYTES) >> 4);
+          const uint64_t ds = dS + (uint64_t)((s * SF_BYTES) >> 4);
+          tmem_cp_32x128b_x4(tmem + SFA_COL, ds);
+          tmem_cp_32x128b_x4(tmem + SFB_COL, ds + (uint64_t)(512 >> 4));
+          if (BN == 256) tmem_cp_32x128b_x4(tmem + SFB_COL + 4, ds + (uint64_t)(1024 >> 4));
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk)
-            mma_mxf8_ss(tmem, sdesc_kmajor_sw128(a0 + kk * 32), sdesc_kmajor_sw128(b0 + kk * 32),
-                        idesc_mxf8(BM, BN, kk), (kb | kk) != 0, tmem + SFA_COL, tmem + SFB_COL);
+            mma_mxf8_ss(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc_mxf8(BM, BN, kk), (kb | kk) != 0,
+                        tmem + SFA_COL, tmem + SFB_COL);
           tc_commit(&empty_bar[s]);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
