@@ -30,6 +30,9 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+ATTN_TRAFFIC_C2_BYTES = 804.108288e6 + 183.372544e6   # ncu, chunk_attn_kernel, c2 (see the profiles folder)
+ATTN_KV_BYTES_C2 = 4.0 * 32760 * 5120
+
 CONFIGS = {
     # name: (model, frames, grid_h, grid_w, lead chunks, start_frame, layers override)
     "c1": dict(model="1.3B", grid=(3, 30, 52), n_lead=2, start_frame=6, layers=1),
@@ -204,6 +207,11 @@ def run_sweep(args):
     import lbw_b200.kernels as K
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    # DRAM traffic of one attention launch: an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of
+    # the c2 self-attention, 4,680 queries x 32,760 keys, measured 987.5 MB; K/V (re-read from L2 by the query
+    # blocks of a head) dominate it, so it is scaled by this workload's K/V bytes.
+    kv_bytes = 4.0 * lkv * C
+    attn_traffic = ATTN_TRAFFIC_C2_BYTES * kv_bytes / ATTN_KV_BYTES_C2 / world if world == 1 else None
     pk, src = peaks()
     peak = pk["bf16_tflops"]
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
@@ -436,7 +444,9 @@ def main():
         "latency_ms": ms,
         "tc_frac_of_peak": flops / (ms / 1e3) / (peak_tc * 1e12 * world),
         "roofline": {"bound": "tensor", "kernel": "chunk_attn_kernel", "achieved": attn_tf, "peak": peak_tc,
-                     "unit": "TFLOP/s", "frac": attn_tf / peak_tc, "traffic": None,
+                     "unit": "TFLOP/s", "frac": attn_tf / peak_tc, "traffic": attn_traffic,
+                     "traffic_source": "ncu dram bytes of the c2 launch scaled by K/V bytes" if attn_traffic else None,
+                     "algorithmic_bytes": 2.0 * L_loc * C * 2 + kv_bytes,
                      "peak_source": f"{src} bf16_tflops_sustained", "flops_per_launch": attn_flops,
                      "ms_per_launch": attn_ms},
         "gpu_launches": launches,
