@@ -207,11 +207,6 @@ def run_sweep(args):
     import lbw_b200.kernels as K
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    # DRAM traffic of one attention launch: an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of
-    # the c2 self-attention, 4,680 queries x 32,760 keys, measured 987.5 MB; K/V (re-read from L2 by the query
-    # blocks of a head) dominate it, so it is scaled by this workload's K/V bytes.
-    kv_bytes = 4.0 * lkv * C
-    attn_traffic = ATTN_TRAFFIC_C2_BYTES * kv_bytes / ATTN_KV_BYTES_C2 / world if world == 1 else None
     pk, src = peaks()
     peak = pk["bf16_tflops"]
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
@@ -427,6 +422,11 @@ def main():
                "d2h_bytes_per_step": nbytes, "ms_per_step": ms_e2e}
     assert torch.isfinite(yh if e2e else xf).all(), "non-finite block output"
 
+    # DRAM traffic of one attention launch: an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of
+    # the c2 self-attention, 4,680 queries x 32,760 keys, measured 987.5 MB; K/V (re-read from L2 by the query
+    # blocks of a head) dominate it, so it is scaled by this workload's K/V bytes.
+    kv_bytes = 4.0 * lkv * C
+    attn_traffic = ATTN_TRAFFIC_C2_BYTES * kv_bytes / ATTN_KV_BYTES_C2 / world if world == 1 else None
     pk, src = peaks()
     fb, fm = flops_per_block(chunk, lkv, C, F)
     flops = (fb + fm) * layers

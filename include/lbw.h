@@ -64,6 +64,17 @@ int lbw_chunk_attention_partial(const void* q, long long ldq, int q_rows, int he
                                 const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
                                 const float* key_bias, float softmax_scale, int n_splits, float* part_o,
                                 float* part_ml, int slot0, void* stream);
+/* lbw_chunk_attention (out != NULL, n_splits = 1) or lbw_chunk_attention_partial (part_o/part_ml) where the
+ * chunks gate_chunk..n_chunks-1 may still be arriving: each CTA waits (bounded) until *gate_flag reaches
+ * gate_value (wrap-safe) before its first load from them. gate_flag is written by a stream memory operation
+ * on another stream once copy engines have filled those chunks (lbw_sp_kv_gather writes it), so the gather of
+ * the new chunk's K/V runs under the attention of the cached chunks without a separate launch for the new
+ * chunk (the reference overlaps the same way, wan/modules/model_fast.py:2033-2110). No key bias. */
+int lbw_chunk_attention_gated(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                              const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                              float softmax_scale, void* out, long long ldo, int n_splits, float* part_o,
+                              float* part_ml, int slot0, const unsigned int* gate_flag, unsigned int gate_value,
+                              int gate_chunk, void* stream);
 /* out[q, h*128:] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s over slots 0..n_slots-1 (M = max m_s), bf16.
  * Replaces attention.py:963-990 cte_merge. */
 int lbw_attention_merge(const float* part_o, const float* part_ml, int n_slots, int q_rows, int heads, void* out,
@@ -173,6 +184,32 @@ int lbw_mx_linear_gelu(const void* a, const void* a_scales, const void* w, const
  * Replaces ffn_mx.mm + bias and x + y * e5 (model_fast.py:1584-1611, :3110-3111). */
 int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, const void* w_scales,
                            const void* bias, int m, int n, int k, float* x, const float* gate, void* stream);
+
+/* ---- sequence-parallel K/V exchange (one process per GPU, same node, NVLink) ----------------
+ * Replaces the all-gather of the new chunk's K/V shards into every rank's destination cache chunk
+ * (wan/modules/model_fast.py:2066-2108 _gather_new, wan/distributed/tensor_parallel.py:106-139
+ * all_gather_fn). Each rank owns one peer buffer (lbw_peer_buffer_create: cudaMalloc + CUDA IPC handle,
+ * 64 bytes, exchanged by the caller) and opens the others' (lbw_peer_buffer_open). The exchange uses copy
+ * engines and stream memory operations only: no SM is occupied, so it overlaps the attention of the cached
+ * chunks. Buffer size: 4096 + 2 * local_rows * cols * 2 bytes. */
+int lbw_peer_buffer_create(long long bytes, void** ptr, void* ipc_handle);
+int lbw_peer_buffer_open(const void* ipc_handle, void** ptr);
+/* owned = 1 for the caller's own buffer (freed), 0 for an opened peer buffer (unmapped). */
+int lbw_peer_buffer_close(void* ptr, int owned);
+/* One exchange = lbw_sp_kv_stage then lbw_sp_kv_gather with the same arguments (they may go on different
+ * streams; stage first in stream order). Rank r's rows [r*local_rows, (r+1)*local_rows) of k_dest and v_dest
+ * ([world*local_rows, ld] bf16, row stride ld elements, cols used) are sent to every peer, and the peers'
+ * rows are received. bufs[p] = rank p's buffer as mapped in this process (bufs[rank] = own).
+ * epoch = 1, 2, ...: the number of this exchange on these buffers, the same on every rank.
+ * stage: waits until every peer has finished reading the previous epoch, then copies this rank's rows into
+ * its buffer. gather: announces them, waits (without a timeout) until every peer has staged the same epoch,
+ * pulls the peers' rows with copy engines (helper streams joined back into `stream`), and, when all rows
+ * have landed, sets the 32-bit word at byte 512 of the own buffer to epoch (the gate of
+ * lbw_chunk_attention_gated). */
+int lbw_sp_kv_stage(void* const* bufs, int rank, int world, unsigned int epoch, void* k_dest, void* v_dest,
+                    long long ld, int local_rows, int cols, void* stream);
+int lbw_sp_kv_gather(void* const* bufs, int rank, int world, unsigned int epoch, void* k_dest, void* v_dest,
+                     long long ld, int local_rows, int cols, void* stream);
 
 #ifdef __cplusplus
 }

@@ -41,6 +41,13 @@ SIGNATURES = {
     "lbw_mx_linear": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp], _i),
     "lbw_mx_linear_gelu": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "lbw_mx_linear_residual": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
+    "lbw_chunk_attention_gated": ([_vp, _ll, _i, _i, _vp, _vp, _vp, _i, _ll, _f, _vp, _ll, _i, _vp, _vp, _i, _vp,
+                                   ctypes.c_uint, _i, _vp], _i),
+    "lbw_peer_buffer_create": ([_ll, ctypes.POINTER(_vp), _vp], _i),
+    "lbw_peer_buffer_open": ([_vp, ctypes.POINTER(_vp)], _i),
+    "lbw_peer_buffer_close": ([_vp, _i], _i),
+    "lbw_sp_kv_stage": ([ctypes.POINTER(_vp), _i, _i, ctypes.c_uint, _vp, _vp, _ll, _i, _i, _vp], _i),
+    "lbw_sp_kv_gather": ([ctypes.POINTER(_vp), _i, _i, ctypes.c_uint, _vp, _vp, _ll, _i, _i, _vp], _i),
 }
 
 _lib = None
@@ -82,10 +89,11 @@ def last_error():
 CALLS = [0]
 
 
-def check(rc, what):
+def check(rc, what, launches=1):
+    """Raises on a non-zero status; on success counts `launches` kernels enqueued by the call."""
     if rc == LBW_OK:
         if what != "device status":
-            CALLS[0] += 1
+            CALLS[0] += launches
         return
     msg = f"{what}: {last_error()} (status {rc})"
     if rc in (LBW_ERR_INVALID, LBW_ERR_SHAPE, LBW_ERR_ALIGN, LBW_ERR_UNSUPPORTED):

@@ -213,20 +213,21 @@ class CausalWanAttentionBlock(nn.Module):
     def _self_attention(self, ws, k_chunks, v_chunks, L, chunk_rows, p):
         """Attention of the local queries over (leading..., destination).
 
-        With sequence parallelism (p > 1) the destination chunk still has to be all-gathered: the gather runs
-        on a side stream while the leading chunks are attended, and the destination chunk's partial is merged
-        afterwards (the reference attends cached chunks early the same way, model_fast.py:2033-2110). When the
-        rank has few query rows the KV window is also split across CTAs so that the GPU is filled."""
+        With sequence parallelism (p > 1) the destination chunk still has to be all-gathered. On CUDA the
+        gather runs on copy engines from a side stream while ONE attention launch covers the whole window:
+        its CTAs reach the destination chunk last and wait in-kernel for the copy engines' completion flag
+        (the reference attends cached chunks while the gather is in flight the same way,
+        model_fast.py:2033-2110). When the rank has few query rows the KV window is also split across CTAs so
+        that the GPU is filled."""
         C, H = self.dim, self.num_heads
         rows = [k.numel() // C for k in k_chunks]
         n_tiles = kernels.n_kv_tiles(rows)
         k_dst, v_dst = k_chunks[-1], v_chunks[-1]
-        overlap = p > 1 and len(k_chunks) > 1
-        if not overlap:
+        splits = kernels.pick_kv_splits(L, H, n_tiles)
+        pk = sp.peer_kv(k_dst.view(chunk_rows, C), L) if p > 1 else None
+        if pk is None:
             if p > 1:
-                sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
-                sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
-            splits = kernels.pick_kv_splits(L, H, n_tiles)
+                sp.gather_kv_inplace(k_dst.view(chunk_rows, C), v_dst.view(chunk_rows, C), L)
             if splits == 1:
                 kernels.chunk_attention(ws.q, k_chunks, v_chunks, out=ws.attn)
             else:
@@ -237,25 +238,23 @@ class CausalWanAttentionBlock(nn.Module):
         dev = ws.q.device
         comm = self._comm_streams.get(dev)
         if comm is None:
-            # high priority: once the gather is done, the destination chunk's CTAs are dispatched ahead of the
-            # leading-chunk launch's remaining ones instead of trailing it
-            comm = self._comm_streams[dev] = torch.cuda.Stream(device=dev, priority=-1)
+            comm = self._comm_streams[dev] = torch.cuda.Stream(device=dev)
         main = torch.cuda.current_stream(dev)
+        k2d, v2d = k_dst.view(chunk_rows, C), v_dst.view(chunk_rows, C)
+        pk.stage(k2d, v2d)                       # on this stream, so nothing of the exchange waits for an SM later
         ready = torch.cuda.Event()
-        ready.record(main)                       # this rank's K/V rows are written
-        lead_tiles = kernels.n_kv_tiles(rows[:-1])
-        splits = kernels.pick_kv_splits(L, H, lead_tiles)
-        po, pml = ws.attn_parts(splits + 1, H)
+        ready.record(main)
         with torch.cuda.stream(comm):
-            # gather, then the destination chunk's partial right behind it on the same stream: it runs
-            # alongside the leading chunks' launch instead of queueing after it
             comm.wait_event(ready)
-            sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
-            sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
-            kernels.chunk_attention_partial(ws.q, [k_dst], [v_dst], 1, po, pml, splits)
-        kernels.chunk_attention_partial(ws.q, k_chunks[:-1], v_chunks[:-1], splits, po, pml, 0)
-        main.wait_stream(comm)
-        kernels.attention_merge(po, pml, splits + 1, ws.attn)
+            pk.finish(k2d, v2d)
+        gate = (pk.gathered_flag, pk.epoch, len(k_chunks) - 1)
+        if splits == 1:
+            kernels.chunk_attention_gated(ws.q, k_chunks, v_chunks, *gate, out=ws.attn)
+        else:
+            po, pml = ws.attn_parts(splits, H)
+            kernels.chunk_attention_gated(ws.q, k_chunks, v_chunks, *gate, n_splits=splits, part_o=po, part_ml=pml)
+            kernels.attention_merge(po, pml, splits, ws.attn)
+        main.wait_stream(comm)                   # the destination chunk is complete for the caller
 
     # ------------------------------------------------------------------ forward
     def forward(self, x, e, seq_lens=None, grid_sizes=None, freqs=None, context=None, context_lens=None,
@@ -345,8 +344,7 @@ class CausalWanAttentionBlock(nn.Module):
         mark("qk_norm_rope")
         if kv_only:
             if p > 1:
-                sp.gather_rows_inplace(k_dst.view(chunk_rows, C), L)
-                sp.gather_rows_inplace(v_dst.view(chunk_rows, C), L)
+                sp.gather_kv_inplace(k_dst.view(chunk_rows, C), v_dst.view(chunk_rows, C), L)
             return xf
         if attn_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

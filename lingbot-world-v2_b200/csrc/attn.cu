@@ -77,11 +77,33 @@ __global__ void attn_merge_kernel(const float* __restrict__ part_o, const float*
   *reinterpret_cast<uint2*>(out + row * ldo + (long long)head * attn::D + lane * 4) = pk;
 }
 
+// Bounded wait until *flag has reached value (wrap-safe), for K/V rows that a stream memory operation on
+// another stream announces once its copy engines have written them; then order the TMA loads that follow
+// after the flag.
+__device__ __forceinline__ bool gate_wait(const unsigned int* flag, unsigned int value, const Abort& ab, int site) {
+  const long long t0 = clock64();
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if ((int)(v - value) >= 0) break;
+    if (*ab.flag) return false;
+    if (clock64() - t0 > LBW_WAIT_CYCLES) {
+      *ab.flag = 1;
+      if (ab.status) atomicCAS(ab.status, 0, LBW_DEV_TIMEOUT | site);
+      return false;
+    }
+    __nanosleep(256);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
 template <bool HAS_BIAS>
 __global__ void __launch_bounds__(attn::THREADS, 1)
     chunk_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KVMaps kv, int q_rows,
                       float scale_log2, const float* __restrict__ key_bias, __nv_bfloat16* __restrict__ out,
-                      long long ldo, float* __restrict__ part_o, float* __restrict__ part_ml, int slot0, int* status) {
+                      long long ldo, float* __restrict__ part_o, float* __restrict__ part_ml, int slot0,
+                      const unsigned int* gate_flag, unsigned int gate_value, int gate_chunk, int* status) {
   using namespace attn;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -136,11 +158,15 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         for (int h = 0; h < 2; ++h)
           tma_load_2d(sQ + i * TILE + h * HALF, &tmQ, &q_full, head * D + h * 64, q0 + i * BM);
       int j = 0, g = 0;
-      bool ok = true;
+      bool ok = true, gated = false;
       for (int c = 0; c < n_chunks && ok && g < g_end; ++c) {
         const int rows = kv.rows[c];
         for (int t0 = 0; t0 < rows && g < g_end; t0 += BN, ++g) {
           if (g < g_begin) continue;
+          if (c >= gate_chunk && !gated) {  // chunks from gate_chunk on are still being filled by copy engines
+            if (!gate_wait(gate_flag, gate_value, ab, 0x23)) { ok = false; break; }
+            gated = true;
+          }
           const int s = j & 1;
           const uint32_t ph = (j >> 1) & 1;
           if (!mbar_wait(&k_empty[s], ph ^ 1, ab, 0x21)) { ok = false; break; }
@@ -436,7 +462,8 @@ using namespace lbw;
 static int launch_attention(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
                             const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
                             const float* key_bias, float softmax_scale, void* out, long long ldo, int n_splits,
-                            float* part_o, float* part_ml, int slot0, cudaStream_t s) {
+                            float* part_o, float* part_ml, int slot0, const unsigned int* gate_flag,
+                            unsigned int gate_value, int gate_chunk, cudaStream_t s) {
   using namespace attn;
   if (!q || !k_chunks || !v_chunks || !chunk_rows) return set_error(LBW_ERR_INVALID, "chunk_attention: null pointer");
   if (!out && !part_o) return set_error(LBW_ERR_INVALID, "chunk_attention: null output");
@@ -450,6 +477,10 @@ static int launch_attention(const void* q, long long ldq, int q_rows, int heads,
   if (key_bias && !aligned(key_bias, 4)) return set_error(LBW_ERR_ALIGN, "chunk_attention: key_bias alignment");
   if (part_o && (!part_ml || !aligned(part_o, 16) || !aligned(part_ml, 8) || slot0 < 0))
     return set_error(LBW_ERR_INVALID, "chunk_attention: partial buffers missing or misaligned");
+  if (!part_o && n_splits != 1) return set_error(LBW_ERR_INVALID, "chunk_attention: KV splits need partial buffers");
+  if (gate_chunk < n_chunks && (!gate_flag || !aligned(gate_flag, 4)))
+    return set_error(LBW_ERR_INVALID, "chunk_attention: gated chunks need a 4-byte aligned gate flag");
+  if (gate_chunk < 0) gate_chunk = 0;
   int err = 0;
   int* st = device_status(&err);
   if (!st) return err;
@@ -487,10 +518,10 @@ static int launch_attention(const void* q, long long ldq, int q_rows, int heads,
   __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
   if (hb)
     chunk_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, key_bias, o, ldo, part_o,
-                                                              part_ml, slot0, st);
+                                                              part_ml, slot0, gate_flag, gate_value, gate_chunk, st);
   else
     chunk_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, nullptr, o, ldo, part_o,
-                                                               part_ml, slot0, st);
+                                                               part_ml, slot0, gate_flag, gate_value, gate_chunk, st);
   return cuda_check(cudaGetLastError(), "attention launch");
 }
 
@@ -501,7 +532,8 @@ int lbw_chunk_attention(const void* q, long long ldq, int q_rows, int heads, con
                         const float* key_bias, float softmax_scale, void* out, long long ldo, void* stream) {
   if (!out) return set_error(LBW_ERR_INVALID, "chunk_attention: null output");
   return launch_attention(q, ldq, q_rows, heads, k_chunks, v_chunks, chunk_rows, n_chunks, ldkv, key_bias,
-                          softmax_scale, out, ldo, 1, nullptr, nullptr, 0, reinterpret_cast<cudaStream_t>(stream));
+                          softmax_scale, out, ldo, 1, nullptr, nullptr, 0, nullptr, 0, n_chunks,
+                          reinterpret_cast<cudaStream_t>(stream));
 }
 
 int lbw_chunk_attention_partial(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
@@ -510,7 +542,21 @@ int lbw_chunk_attention_partial(const void* q, long long ldq, int q_rows, int he
                                 float* part_ml, int slot0, void* stream) {
   if (!part_o || !part_ml) return set_error(LBW_ERR_INVALID, "chunk_attention_partial: null workspace");
   return launch_attention(q, ldq, q_rows, heads, k_chunks, v_chunks, chunk_rows, n_chunks, ldkv, key_bias,
-                          softmax_scale, nullptr, 0, n_splits, part_o, part_ml, slot0,
+                          softmax_scale, nullptr, 0, n_splits, part_o, part_ml, slot0, nullptr, 0, n_chunks,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_chunk_attention_gated(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                              const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                              float softmax_scale, void* out, long long ldo, int n_splits, float* part_o,
+                              float* part_ml, int slot0, const unsigned int* gate_flag, unsigned int gate_value,
+                              int gate_chunk, void* stream) {
+  if (gate_chunk < 0 || gate_chunk >= n_chunks)
+    return set_error(LBW_ERR_SHAPE, "chunk_attention_gated: gate chunk %d of %d", gate_chunk, n_chunks);
+  if (!out && !part_o) return set_error(LBW_ERR_INVALID, "chunk_attention_gated: null output");
+  if (out && part_o) return set_error(LBW_ERR_INVALID, "chunk_attention_gated: give out or the partial buffers");
+  return launch_attention(q, ldq, q_rows, heads, k_chunks, v_chunks, chunk_rows, n_chunks, ldkv, nullptr,
+                          softmax_scale, out, ldo, n_splits, part_o, part_ml, slot0, gate_flag, gate_value, gate_chunk,
                           reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -97,6 +97,42 @@ def chunk_attention_partial(q, k_chunks, v_chunks, n_splits, part_o, part_ml, sl
                                              int(slot0), stream_of(q.device)), "chunk_attention_partial")
 
 
+def chunk_attention_gated(q, k_chunks, v_chunks, gate_flag_ptr, gate_value, gate_chunk, out=None, n_splits=1,
+                          part_o=None, part_ml=None, slot0=0, softmax_scale=None):
+    """chunk_attention (out) or chunk_attention_partial (part_o, part_ml) whose chunks gate_chunk.. are waited
+    for in-kernel: loads from them start once the 32-bit word at gate_flag_ptr (a device address) has reached
+    gate_value (see lbw.h)."""
+    require_cuda(q, *k_chunks, *v_chunks, out, part_o, part_ml)
+    q2 = _rows(_c(q, BF16))
+    lq, cols = q2.shape
+    heads = cols // HEAD_DIM
+    n = len(k_chunks)
+    ks = [_rows(_c(k, BF16)) for k in k_chunks]
+    vs = [_rows(_c(v, BF16)) for v in v_chunks]
+    o2 = None
+    if out is not None:
+        o2 = _rows(_c(out, BF16))
+        if o2.shape[0] != lq or o2.shape[1] < cols:
+            raise ValueError("chunk_attention_gated: out does not match q")
+    else:
+        if part_o is None or part_ml is None:
+            raise ValueError("chunk_attention_gated: give out or the partial buffers")
+        if part_o.shape[1:] != (lq, heads, HEAD_DIM) or part_ml.shape[1:] != (lq, heads, 2):
+            raise ValueError("attention workspace does not match q")
+        if slot0 < 0 or slot0 + n_splits > part_o.shape[0]:
+            raise ValueError(f"slots {slot0}..{slot0 + n_splits - 1} outside a {part_o.shape[0]}-slot workspace")
+    kp = (ctypes.c_void_p * n)(*[k.data_ptr() for k in ks])
+    vp = (ctypes.c_void_p * n)(*[v.data_ptr() for v in vs])
+    rows = (ctypes.c_int * n)(*[k.shape[0] for k in ks])
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(HEAD_DIM)
+    check(load().lbw_chunk_attention_gated(ptr(q2), q2.stride(0), lq, heads, kp, vp, rows, n, cols,
+                                           ctypes.c_float(scale), ptr(o2), o2.stride(0) if o2 is not None else 0,
+                                           int(n_splits), ptr(part_o), ptr(part_ml), int(slot0),
+                                           ctypes.c_void_p(gate_flag_ptr), ctypes.c_uint(gate_value), int(gate_chunk),
+                                           stream_of(q.device)), "chunk_attention_gated")
+    return out
+
+
 def attention_merge(part_o, part_ml, n_slots, out):
     require_cuda(part_o, part_ml, out)
     _, lq, heads, _ = part_o.shape

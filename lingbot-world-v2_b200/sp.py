@@ -7,9 +7,13 @@ the all-gather of the new chunk's K and V shards into every rank's destination c
 so the cached chunks are replicated. Attention is not token-causal, so the local queries against the
 full window are exact with no softmax reduction across ranks.
 
-The gather is one in-place ncclAllGather per tensor (torch.distributed over NCCL; gloo in the CPU
-tests) on the destination chunk viewed as [chunk_tokens, C].
+On CUDA the gather is PeerKV.gather: each rank stages its shard in a CUDA-IPC buffer and pulls the others'
+with copy engines, synchronised by stream memory operations (liblbw's lbw_sp_kv_gather), so no SM is taken
+from the attention it overlaps. gather_rows_inplace (one in-place all_gather_into_tensor per tensor) is the
+same exchange through torch.distributed; the CPU (gloo) tests use it.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -84,3 +88,93 @@ def write_and_gather(shard, dest):
     d2[a:a + s2.shape[0]].copy_(s2)
     gather_rows_inplace(d2, s2.shape[0])
     return dest
+
+
+class PeerKV:
+    """The copy-engine K/V exchange of one process group: this rank's IPC buffer plus the peers' buffers
+    mapped into this process. Created collectively (every rank, same shapes); reused by every block."""
+
+    def __init__(self, local_rows, cols, device, group=None):
+        from . import _lib
+        self._lib = _lib
+        lib = _lib.load()
+        self.rows, self.cols, self.device, self.group = local_rows, cols, device, group
+        self.rank, self.world = rank(), world()
+        nbytes = 4096 + 2 * local_rows * cols * 2
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        with torch.cuda.device(device):
+            _lib.check(lib.lbw_peer_buffer_create(nbytes, ctypes.byref(own), handle), "peer_buffer_create", 0)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs = []
+        with torch.cuda.device(device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(own.value)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.check(lib.lbw_peer_buffer_open(ctypes.create_string_buffer(h, 64), ctypes.byref(p)),
+                           f"peer_buffer_open(rank {r})", 0)
+                ptrs.append(p.value)
+        self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.epoch = 0
+
+    @property
+    def gathered_flag(self):
+        """Device address of this rank's 32-bit 'gathered' word: the epoch of the last completed exchange."""
+        return self._ptrs[self.rank] + 512
+
+    def fits(self, local_rows, cols, device):
+        return (local_rows, cols, device) == (self.rows, self.cols, device)
+
+    def _call(self, fn, k2d, v2d, stream):
+        self._lib.check(getattr(self._lib.load(), fn)(
+            self._ptrs, self.rank, self.world, ctypes.c_uint(self.epoch), ctypes.c_void_p(k2d.data_ptr()),
+            ctypes.c_void_p(v2d.data_ptr()), k2d.stride(0), self.rows, self.cols,
+            ctypes.c_void_p(stream.cuda_stream)), fn, 0)
+
+    def stage(self, k2d, v2d):
+        """Start an exchange: this rank's rows of k2d, v2d ([world * local_rows, cols] bf16, row stride
+        k2d.stride(0)) are copied to its buffer, in order on the current stream."""
+        if k2d.shape != v2d.shape or k2d.shape[0] != self.rows * self.world or k2d.shape[1] != self.cols \
+                or k2d.stride(0) != v2d.stride(0):
+            raise ValueError(f"PeerKV: K/V {tuple(k2d.shape)} do not match {self.world} x {self.rows} rows")
+        self.epoch += 1
+        self._call("lbw_sp_kv_stage", k2d, v2d, torch.cuda.current_stream(self.device))
+
+    def finish(self, k2d, v2d):
+        """Complete the exchange begun by stage() on the current stream: the peers' rows land in k2d, v2d."""
+        self._call("lbw_sp_kv_gather", k2d, v2d, torch.cuda.current_stream(self.device))
+
+    def gather(self, k2d, v2d):
+        """stage() + finish() on the current stream."""
+        self.stage(k2d, v2d)
+        self.finish(k2d, v2d)
+
+
+_PEERS = {}
+
+
+def peer_kv(k2d, local_rows):
+    """The copy-engine exchange for destination chunks shaped like k2d (CUDA + NCCL group), else None."""
+    if not (active() and k2d.is_cuda and dist.get_backend(_GROUP) == "nccl"):
+        return None
+    key = (k2d.device, local_rows, k2d.shape[1])
+    pk = _PEERS.get(key)
+    if pk is None:
+        pk = _PEERS[key] = PeerKV(local_rows, k2d.shape[1], k2d.device, _GROUP)
+    return pk
+
+
+def gather_kv_inplace(k2d, v2d, local_rows):
+    """All-gather the destination chunk's K and V rows (see gather_rows_inplace) on the current stream: over
+    copy engines on CUDA with the NCCL backend, else through torch.distributed."""
+    if not active():
+        return
+    pk = peer_kv(k2d, local_rows)
+    if pk is not None:
+        pk.gather(k2d, v2d)
+        return
+    gather_rows_inplace(k2d, local_rows)
+    gather_rows_inplace(v2d, local_rows)

@@ -225,6 +225,28 @@ def test_chunk_attention_split_kv_and_merge(cuda_dev, splits):
     assert rel_l2(out2.view(300, 2, 128), ref) < 1e-2
 
 
+def test_gated_attention_matches_ungated(cuda_dev):
+    """With its gate already open, the gated kernel computes exactly what the ungated one does, in both output
+    modes (direct and split-KV partials + merge); a gate chunk outside the window is rejected."""
+    import lbw_b200.kernels as K
+    d = cuda_dev
+    q, ks, vs = _attn_case(300, [256, 200, 130], 2, 31)
+    q, ks, vs = q.to(d), [k.to(d) for k in ks], [v.to(d) for v in vs]
+    flag = torch.full((4,), 7, dtype=torch.int32, device=d)
+    ref = K.chunk_attention(q, ks, vs)
+    out = torch.empty_like(ref)
+    K.chunk_attention_gated(q, ks, vs, flag.data_ptr(), 7, 2, out=out)
+    assert torch.equal(out, ref)
+    po, pml = K.attention_workspace(3, 300, 2, d)
+    K.chunk_attention_partial(q, ks, vs, 3, po, pml)
+    ref3 = K.attention_merge(po, pml, 3, torch.empty_like(ref))
+    po2, pml2 = K.attention_workspace(3, 300, 2, d)
+    K.chunk_attention_gated(q, ks, vs, flag.data_ptr(), 6, 1, n_splits=3, part_o=po2, part_ml=pml2)
+    assert torch.equal(K.attention_merge(po2, pml2, 3, torch.empty_like(ref)), ref3)
+    with pytest.raises(ValueError, match="gate chunk"):
+        K.chunk_attention_gated(q, ks, vs, flag.data_ptr(), 7, 3, out=out)
+
+
 def test_split_count_is_validated(cuda_dev):
     import lbw_b200.kernels as K
     q, ks, vs = _attn_case(128, [100], 1, 23)
