@@ -41,10 +41,16 @@ constexpr int THREADS = 320;
 constexpr int EPI_THREADS = THREADS - 64;
 // Tile width TBN (256, or 128 when 256-wide tiles would leave the last wave mostly idle): ring depth and
 // shared memory per tile width.
+// A 128-wide tile's MMAs (N = 128) take half as long as a 256-wide tile's, so its stages hold two 64-wide K
+// blocks: the MMA thread then waits once per 8 MMAs instead of once per 4 (each wait leaves the tensor pipe
+// idle for ~100 cycles, because the lone issuing thread has nothing else in flight).
 template <int TBN> struct Cfg {
-  static constexpr int B_BYTES = TBN * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = TBN == 256 ? 4 : 6;
+  static constexpr int KSUB = TBN == 256 ? 1 : 2;          // 64-wide K blocks per stage
+  static constexpr int BKS = BK * KSUB;                      // K per stage
+  static constexpr int A_SUB = BM * BK * 2, B_SUB = TBN * BK * 2;
+  static constexpr int A_STAGE = A_SUB * KSUB, B_STAGE = B_SUB * KSUB;
+  static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+  static constexpr int STAGES = TBN == 256 ? 4 : 3;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 2 * TBN;
 };
@@ -59,11 +65,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
                      int K, Epi epi, int* status) {
   using gemm::BM;
   using gemm::BK;
-  using gemm::A_BYTES;
+  using C = gemm::Cfg<TBN>;
   constexpr int BN = TBN;
-  constexpr int STAGES = gemm::Cfg<TBN>::STAGES;
-  constexpr int STAGE_BYTES = gemm::Cfg<TBN>::STAGE_BYTES;
-  constexpr uint32_t TMEM_COLS = gemm::Cfg<TBN>::TMEM_COLS;
+  constexpr int STAGES = C::STAGES;
+  constexpr int STAGE_BYTES = C::STAGE_BYTES;
+  constexpr uint32_t TMEM_COLS = C::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], done_bar;
@@ -95,7 +101,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   const uint32_t tmem = tmem_slot;
   const Abort ab{status, &abort_flag};
 
-  const int nM = (M + BM - 1) / BM, nN = (N + BN - 1) / BN, nK = K / BK;
+  const int nM = (M + BM - 1) / BM, nN = (N + BN - 1) / BN, nK = K / C::BKS;
   const int tiles = nM * nN;
 
   if (warp == 0) {
@@ -110,8 +116,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           if (!mbar_wait(&empty_bar[s], ph ^ 1, ab, 1)) { ok = false; break; }
           uint8_t* sa = smem + s * STAGE_BYTES;
           mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full_bar[s], kb * BK, m_blk * BM);
-          tma_load_2d(sa + A_BYTES, &tmB, &full_bar[s], kb * BK, n_blk * BN);
+#pragma unroll
+          for (int u = 0; u < C::KSUB; ++u) {
+            tma_load_2d(sa + u * C::A_SUB, &tmA, &full_bar[s], kb * C::BKS + u * BK, m_blk * BM);
+            tma_load_2d(sa + C::A_STAGE + u * C::B_SUB, &tmB, &full_bar[s], kb * C::BKS + u * BK, n_blk * BN);
+          }
           ++issued;
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
@@ -138,10 +147,13 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         for (int kb = 0; kb < nK; ++kb) {
           if (!mbar_wait(&full_bar[s], ph, ab, 3)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t da = d0 + (uint64_t)((s * STAGE_BYTES) >> 4), db = da + (uint64_t)(A_BYTES >> 4);
+          const uint64_t da = d0 + (uint64_t)((s * STAGE_BYTES) >> 4), db = da + (uint64_t)(C::A_STAGE >> 4);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            mma_f16_ss(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+          for (int u = 0; u < C::KSUB; ++u)
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              mma_f16_ss(d, da + (uint64_t)((u * C::A_SUB) >> 4) + (uint64_t)(kk * 2),
+                         db + (uint64_t)((u * C::B_SUB) >> 4) + (uint64_t)(kk * 2), idesc, (kb | u | kk) != 0);
           tc_commit(&empty_bar[s]);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
@@ -236,7 +248,8 @@ static int launch_gemm(const void* A, long long lda, const void* W, long long ld
   // 128-wide tiles when 256-wide ones would leave the last wave mostly idle (few rows per rank)
   const long long mt = (M + BM - 1) / BM;
   const double f256 = wave_fill(mt * ((N + 255) / 256)), f128 = wave_fill(mt * ((N + 127) / 128));
-  if (f256 < 0.85 && f128 > f256 + 0.08) return launch_gemm_t<Epi, 128>(tmA, W, ldw, M, N, K, epi, stream, st);
+  if (K % gemm::Cfg<128>::BKS == 0 && f256 < 0.85 && f128 > f256 + 0.08)
+    return launch_gemm_t<Epi, 128>(tmA, W, ldw, M, N, K, epi, stream, st);
   return launch_gemm_t<Epi, 256>(tmA, W, ldw, M, N, K, epi, stream, st);
 }
 
