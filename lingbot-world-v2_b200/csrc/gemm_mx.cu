@@ -30,14 +30,21 @@ constexpr int A_BYTES = BM * BK;   // 16 KB
 constexpr int SFA_BYTES = 512;
 constexpr int THREADS = 320;
 // Tile width TBN = 256 (default) or 128 (when 256-wide tiles would leave the last wave mostly idle).
+// A 128-wide tile's MMAs take half as long as a 256-wide tile's, so its stages hold two 128-code K blocks (and
+// their scale atoms): the lone MMA-issuing thread then waits once per 8 MMAs instead of once per 4.
 template <int TBN> struct Cfg {
-  static constexpr int B_BYTES = TBN * BK;
-  static constexpr int SFB_BYTES = TBN / 128 * 512;
-  static constexpr int SF_BYTES = SFA_BYTES + SFB_BYTES;
-  static constexpr int TX_BYTES = A_BYTES + B_BYTES + SF_BYTES;
-  static constexpr int STAGES = TBN == 256 ? 4 : 6;
-  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES + SF_BYTES) + 1024;
-  static constexpr uint32_t SFA_COL = TBN, SFB_COL = TBN + 4;  // scale columns right after the accumulator
+  static constexpr int KSUB = TBN == 256 ? 1 : 2;                 // 128-code K blocks per stage
+  static constexpr int B_SUB = TBN * BK;
+  static constexpr int A_STAGE = A_BYTES * KSUB, B_STAGE = B_SUB * KSUB;
+  static constexpr int B_BYTES = B_STAGE;
+  static constexpr int SFA_STAGE = SFA_BYTES * KSUB;
+  static constexpr int SFB_STAGE = TBN / 128 * 512 * KSUB;
+  static constexpr int SF_BYTES = SFA_STAGE + SFB_STAGE;
+  static constexpr int TX_BYTES = A_STAGE + B_STAGE + SF_BYTES;
+  static constexpr int STAGES = TBN == 256 ? 4 : 3;
+  static constexpr int SMEM_BYTES = STAGES * TX_BYTES + 1024;
+  // scale columns right after the accumulator: 4 per K block for A, then 4 per K block and 128-row W block
+  static constexpr uint32_t SFA_COL = TBN, SFB_COL = TBN + 4 * KSUB;
 };
 }  // namespace mxg
 
@@ -56,8 +63,9 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
   constexpr int HALF_COLS = BN / 2;  // columns per epilogue warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int KSUB = Cf::KSUB, A_STAGE = Cf::A_STAGE;
   uint8_t* sA = smem;
-  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sB = sA + STAGES * A_STAGE;
   uint8_t* sSF = sB + STAGES * B_BYTES;
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar, tempty_bar, done_bar;
   __shared__ uint32_t tmem_slot;
@@ -86,7 +94,7 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
   const uint32_t tmem = tmem_slot;
   const Abort ab{status, &abort_flag};
 
-  const int nM = (M + BM - 1) / BM, nN = (N + BN - 1) / BN, nK = K / BK;
+  const int nM = (M + BM - 1) / BM, nN = (N + BN - 1) / BN, nK = K / BK, nS = nK / KSUB;
   const int n_sf_blocks = (N + 127) / 128;  // 128-row scale blocks of W that exist
   const int tiles = nM * nN;
 
@@ -99,18 +107,23 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
         const int m_blk = t / nN, n_blk = t % nN;
         const int b0 = 2 * n_blk, b1 = (2 * n_blk + 1 < n_sf_blocks) ? 2 * n_blk + 1 : 2 * n_blk;
         bool ok = true;
-        for (int kb = 0; kb < nK; ++kb) {
+        for (int ks = 0; ks < nS; ++ks) {
           if (!mbar_wait(&empty_bar[s], ph ^ 1, ab, 0x51)) { ok = false; break; }
           uint8_t* sf = sSF + s * SF_BYTES;
+          const int kb = ks * KSUB;  // first 128-code K block of the stage
           mbar_expect_tx(&full_bar[s], TX_BYTES);
-          tma_load_2d(sA + s * A_BYTES, &tmA, &full_bar[s], kb * BK, m_blk * BM);
-          tma_load_2d(sB + s * B_BYTES, &tmB, &full_bar[s], kb * BK, n_blk * BN);
-          bulk_load(sf, sfa + ((long long)m_blk * nK + kb) * 512, 512, &full_bar[s]);
+#pragma unroll
+          for (int u = 0; u < KSUB; ++u) {
+            tma_load_2d(sA + s * A_STAGE + u * A_BYTES, &tmA, &full_bar[s], (kb + u) * BK, m_blk * BM);
+            tma_load_2d(sB + s * B_BYTES + u * Cf::B_SUB, &tmB, &full_bar[s], (kb + u) * BK, n_blk * BN);
+          }
+          // scale atoms of consecutive K blocks are consecutive 512-byte atoms
+          bulk_load(sf, sfa + ((long long)m_blk * nK + kb) * 512, 512 * KSUB, &full_bar[s]);
           if (BN == 256) {
             bulk_load(sf + 512, sfb + ((long long)b0 * nK + kb) * 512, 512, &full_bar[s]);
             bulk_load(sf + 1024, sfb + ((long long)b1 * nK + kb) * 512, 512, &full_bar[s]);
           } else {
-            bulk_load(sf + 512, sfb + ((long long)n_blk * nK + kb) * 512, 512, &full_bar[s]);
+            bulk_load(sf + Cf::SFA_STAGE, sfb + ((long long)n_blk * nK + kb) * 512, 512 * KSUB, &full_bar[s]);
           }
           ++issued;
           if (++s == STAGES) { s = 0; ph ^= 1; }
@@ -131,18 +144,29 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
         if (!mbar_wait(&tempty_bar, aph ^ 1, ab, 0x52)) break;
         tc_fence_after();
         bool ok = true;
-        for (int kb = 0; kb < nK; ++kb) {
+        for (int ks = 0; ks < nS; ++ks) {
           if (!mbar_wait(&full_bar[s], ph, ab, 0x53)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t da = dA + (uint64_t)((s * A_BYTES) >> 4), db = dB + (uint64_t)((s * B_BYTES) >> 4);
+          const uint64_t da = dA + (uint64_t)((s * A_STAGE) >> 4), db = dB + (uint64_t)((s * B_BYTES) >> 4);
           const uint64_t ds = dS + (uint64_t)((s * SF_BYTES) >> 4);
-          tmem_cp_32x128b_x4(tmem + SFA_COL, ds);
-          tmem_cp_32x128b_x4(tmem + SFB_COL, ds + (uint64_t)(512 >> 4));
-          if (BN == 256) tmem_cp_32x128b_x4(tmem + SFB_COL + 4, ds + (uint64_t)(1024 >> 4));
+          if (BN == 256) {
+            tmem_cp_32x128b_x4(tmem + SFA_COL, ds);
+            tmem_cp_32x128b_x4(tmem + SFB_COL, ds + (uint64_t)(512 >> 4));
+            tmem_cp_32x128b_x4(tmem + SFB_COL + 4, ds + (uint64_t)(1024 >> 4));
+          } else {
 #pragma unroll
-          for (int kk = 0; kk < BK / 32; ++kk)
-            mma_mxf8_ss(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc_mxf8(BM, BN, kk), (kb | kk) != 0,
-                        tmem + SFA_COL, tmem + SFB_COL);
+            for (int u = 0; u < KSUB; ++u) {
+              tmem_cp_32x128b_x4(tmem + SFA_COL + 4 * u, ds + (uint64_t)((u * 512) >> 4));
+              tmem_cp_32x128b_x4(tmem + SFB_COL + 4 * u, ds + (uint64_t)((Cf::SFA_STAGE + u * 512) >> 4));
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < KSUB; ++u)
+#pragma unroll
+            for (int kk = 0; kk < BK / 32; ++kk)
+              mma_mxf8_ss(tmem, da + (uint64_t)((u * A_BYTES) >> 4) + (uint64_t)(kk * 2),
+                          db + (uint64_t)((u * Cf::B_SUB) >> 4) + (uint64_t)(kk * 2), idesc_mxf8(BM, BN, kk),
+                          (ks | u | kk) != 0, tmem + SFA_COL + 4 * u, tmem + SFB_COL + 4 * u);
           tc_commit(&empty_bar[s]);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
@@ -232,7 +256,7 @@ static int launch_gemm_mx(const void* a, const void* a_scales, const void* w, co
   if ((err = make_tmap_2d(&tmA, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, BK, BM))) return err;
   const long long mt = (M + BM - 1) / BM;
   const double f256 = mx_wave_fill(mt * ((N + 255) / 256)), f128 = mx_wave_fill(mt * ((N + 127) / 128));
-  if (f256 < 0.85 && f128 > f256 + 0.08)
+  if ((K / BK) % mxg::Cfg<128>::KSUB == 0 && f256 < 0.85 && f128 > f256 + 0.08)
     return launch_gemm_mx_t<Epi, 128>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st);
   return launch_gemm_mx_t<Epi, 256>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st);
 }

@@ -22,7 +22,9 @@ def _ab(m, n, k, seed):
 
 @pytest.mark.parametrize("m,n,k", [(128, 256, 128), (300, 512, 640), (77, 384, 256), (4680, 1536, 1536),
                                    (1000, 13824 // 4, 5120 // 4),
-                                   (1350, 5120, 1024)])   # 1,350 rows (8-way split of 720p): 128-wide tiles
+                                   (1350, 5120, 1024),    # 1,350 rows (8-way split of 720p): 128-wide tiles,
+                                   (1350, 5120, 1152),    # ... an odd number of K blocks: 256-wide tiles
+                                   (1350, 2560, 2048)])   # ... two K blocks per stage over 8 stages
 def test_mx_linear_vs_emulation(cuda_dev, m, n, k):
     import lbw_b200.kernels as K
     a, w, b = _ab(m, n, k, m + n + k)
