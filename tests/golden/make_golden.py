@@ -9,7 +9,8 @@ CausalWanAttentionBlock (model_fast.py:2837-3116) with the seeded parameters of 
 runs its chunked-KV forward (kv_chunks path, exact attention -> SDPA) and saves the block output,
 the destination-chunk K/V it writes and the outputs of self_attn / cross_attn / ffn. It also saves
 the reference's cross_dedup_bias + cross_attention_dedup (wan/modules/attention.py:516-554) on a
-duplicated-context case and the reference's RoPE grids. Inputs are NOT stored: they are
+duplicated-context case, the reference's RoPE grids, its camera FiLM MLP, and one whole
+WanModelFast.forward (model_fast.py:3283-3935) of a 2-block i2v model with the camera condition. Inputs are NOT stored: they are
 regenerated from the seed by oracle.inputs.make_case; a checksum guards against drift.
 
 Nothing at test or bench time reads the reference; only the .pt files produced here are used.
@@ -26,7 +27,7 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 REF = os.environ.get("LBW_REFERENCE", "/root/reference")
 sys.path.insert(0, ROOT)
 
-from oracle.inputs import BlockCase, make_case  # noqa: E402
+from oracle.inputs import BlockCase, ModelCase, make_case, make_model_case  # noqa: E402
 
 CASES = {
     "block_flat": BlockCase(dim=256, ffn=512, grid=(3, 4, 6), n_lead=2, text_len=32, start_frame=6, seed=1),
@@ -37,6 +38,7 @@ CASES = {
 }
 DEDUP = BlockCase(dim=256, ffn=256, grid=(1, 8, 8), n_lead=0, text_len=64, dedup_rows=20, peaked=True, seed=4)
 CAM = BlockCase(dim=256, ffn=256, grid=(1, 6, 8), n_lead=0, text_len=16, cam=True, seed=6)
+MODEL = ModelCase()
 
 
 def install_shims():
@@ -167,6 +169,53 @@ def run_cam(mf):
     return dict(case=case.__dict__, checksum=checksum(p, inp), scale=scale[0].clone(), shift=shift[0].clone())
 
 
+def run_model(mf, ckv):
+    """Reference WanModelFast.forward (model_fast.py:3283-3935) on the chunked cache, i2v with the camera
+    condition: patch + camera + text + timestep embeddings, the blocks, the head and unpatchify."""
+    case = MODEL
+    sd, inp = make_model_case(case)
+    m = mf.WanModelFast(model_type="i2v", patch_size=(1, 2, 2), text_len=case.text_len, in_dim=case.in_dim,
+                        dim=case.dim, ffn_dim=case.ffn, freq_dim=case.freq_dim, text_dim=case.text_dim,
+                        out_dim=case.out_dim, num_heads=case.heads, num_layers=case.layers, qk_norm=True,
+                        cross_attn_norm=True, eps=1e-6)
+    m = m.to(torch.bfloat16)
+    for name in ("time_embedding", "time_projection", "head"):   # fp32 under the reference's fp32 autocast
+        getattr(m, name).float()
+    for blk in m.blocks:
+        blk.modulation.data = blk.modulation.data.float()
+        blk.norm3.float()
+    msd = m.state_dict()
+    for k_, v_ in sd.items():
+        assert k_ in msd, k_
+        msd[k_] = v_.to(msd[k_].dtype)
+    missing = [k_ for k_ in msd if k_ not in sd and not k_.endswith("freqs")]
+    assert not missing, missing
+    m.load_state_dict(msd)
+    m.eval()
+    L, H = case.lq, case.heads
+    cache = ckv.allocate_self_kv_chunks(case.layers, 1, L, H, 128, case.n_chunks, torch.bfloat16, "cpu")
+    for bc, lead in zip(cache, inp["cache"]):
+        for slot, (k_, v_) in enumerate(lead):
+            bc["k"][slot].copy_(k_.unsqueeze(0))
+            bc["v"][slot].copy_(v_.unsqueeze(0))
+    cc = [{"k": torch.zeros(1, case.text_len, H, 128, dtype=torch.bfloat16),
+           "v": torch.zeros(1, case.text_len, H, 128, dtype=torch.bfloat16), "is_init": torch.zeros(1)}
+          for _ in range(case.layers)]
+    caps = {}
+    m.head.register_forward_hook(lambda mod, a, o: caps.__setitem__("head", o.detach().float().clone()))
+    m.text_embedding.register_forward_hook(lambda mod, a, o: caps.__setitem__("context", o.detach().clone()))
+    f = case.grid[0]
+    with torch.no_grad():
+        out = m([inp["x"]], inp["t"], [inp["context"]], L, y=[inp["y"]],
+                dit_cond_dict={"c2ws_plucker_emb": [inp["cam"]]}, kv_cache=cache, crossattn_cache=cc,
+                current_start=case.chunk_index * L, frame_seqlen=L // f, cross_attn_first_call=True)
+    dest, lead_slots = ckv.chunk_routing(case.chunk_index, case.n_chunks)
+    return dict(case=case.__dict__, out=out[0].float().clone(), head=caps["head"][0], context=caps["context"][0],
+                dest=dest, leading=tuple(lead_slots),
+                k_dest=[bc["k"][dest][0].clone() for bc in cache], v_dest=[bc["v"][dest][0].clone() for bc in cache],
+                ctx_k=[c["k"][0].clone() for c in cc], ctx_v=[c["v"][0].clone() for c in cc])
+
+
 def main():
     install_shims()
     with contextlib.redirect_stdout(sys.stderr):
@@ -183,6 +232,8 @@ def main():
     print("cross_dedup saved")
     torch.save(run_cam(mf), os.path.join(HERE, "cam_film.pt"))
     print("cam_film saved")
+    torch.save(run_model(mf, ckv), os.path.join(HERE, "model_forward.pt"))
+    print("model_forward saved")
     table = {(i, n): ckv.chunk_routing(i, n) for n in (1, 2, 3, 4, 7) for i in range(0, 12)}
     torch.save(table, os.path.join(HERE, "chunk_routing.pt"))
     print("chunk_routing saved")

@@ -1,0 +1,75 @@
+"""The whole causal-fast model forward (CausalWanModel: patch/camera/text/timestep embeddings, the blocks on
+the chunked KV cache, head, unpatchify) against the reference's own WanModelFast.forward on the same seeded
+inputs (tests/golden/model_forward.pt)."""
+import pytest
+import torch
+
+from conftest import load_golden, max_abs, rel_l2
+from oracle.inputs import ModelCase, make_model_case
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def _build(case, dev):
+    import lbw_b200.model as M
+    m = M.CausalWanModel(model_type="i2v", patch_size=(1, 2, 2), text_len=case.text_len, in_dim=case.in_dim,
+                         dim=case.dim, ffn_dim=case.ffn, freq_dim=case.freq_dim, text_dim=case.text_dim,
+                         out_dim=case.out_dim, num_heads=case.heads, num_layers=case.layers, ffn_mx=False)
+    sd, inp = make_model_case(case)
+    msd = m.state_dict()
+    for k, v in sd.items():
+        msd[k] = v.to(msd[k].dtype)
+    m.load_state_dict(msd)
+    return m.to(dev), inp
+
+
+def _cache(case, inp, dev):
+    import lbw_b200.chunked_kv_cache as ckv
+    L, H = case.lq, case.heads
+    cache = ckv.allocate_self_kv_chunks(case.layers, 1, L, H, 128, case.n_chunks, BF, dev)
+    for bc, lead in zip(cache, inp["cache"]):
+        for slot, (k, v) in enumerate(lead):
+            bc["k"][slot].copy_(k.unsqueeze(0))
+            bc["v"][slot].copy_(v.unsqueeze(0))
+    cc = [{"k": torch.zeros(1, case.text_len, H, 128, dtype=BF, device=dev),
+           "v": torch.zeros(1, case.text_len, H, 128, dtype=BF, device=dev), "is_init": torch.zeros(1, device=dev)}
+          for _ in range(case.layers)]
+    return cache, cc
+
+
+def _run(m, case, inp, cache, cc, dev, skip_head=False):
+    L = case.lq
+    return m([inp["x"].to(dev)], inp["t"].to(dev), [inp["context"].to(dev)], L, y=[inp["y"].to(dev)],
+             dit_cond_dict={"c2ws_plucker_emb": [inp["cam"].to(dev)]}, kv_cache=cache, crossattn_cache=cc,
+             current_start=case.chunk_index * L, frame_seqlen=L // case.grid[0], cross_attn_first_call=True,
+             skip_head=skip_head)
+
+
+def test_model_forward_vs_reference_golden(cuda_dev):
+    g = load_golden("model_forward")
+    case = ModelCase(**g["case"])
+    m, inp = _build(case, cuda_dev)
+    cache, cc = _cache(case, inp, cuda_dev)
+    out = _run(m, case, inp, cache, cc, cuda_dev)
+    torch.cuda.synchronize()
+    o = out[0].float().cpu()
+    assert o.shape == g["out"].shape
+    assert rel_l2(o, g["out"]) < 1e-2 and max_abs(o, g["out"]) < 5e-2
+    dest = g["dest"]
+    for i in range(case.layers):
+        assert rel_l2(cache[i]["k"][dest][0].cpu(), g["k_dest"][i]) < 1e-2
+        assert rel_l2(cache[i]["v"][dest][0].cpu(), g["v_dest"][i]) < 1e-2
+        assert rel_l2(cc[i]["k"][0].cpu(), g["ctx_k"][i]) < 1e-2
+
+
+def test_model_kv_commit_forward_writes_the_cache(cuda_dev):
+    """skip_head (the KV-commit forward at t = 0 in the reference) returns None but writes the same K/V."""
+    g = load_golden("model_forward")
+    case = ModelCase(**g["case"])
+    m, inp = _build(case, cuda_dev)
+    cache, cc = _cache(case, inp, cuda_dev)
+    assert _run(m, case, inp, cache, cc, cuda_dev, skip_head=True) is None
+    torch.cuda.synchronize()
+    for i in range(case.layers):
+        assert rel_l2(cache[i]["k"][g["dest"]][0].cpu(), g["k_dest"][i]) < 1e-2

@@ -80,3 +80,18 @@ def test_shard_range():
     assert sp.shard_range(10800, 3, 8) == (4050, 5400)
     with pytest.raises(ValueError):
         sp.shard_range(10, 0, 3)
+
+
+def test_model_state_dict_keys_match_the_reference():
+    """CausalWanModel carries exactly the reference WanModelFast parameter names (checked against the keys the
+    golden generator loaded into the reference model), so a reference checkpoint loads unchanged."""
+    import lbw_b200.model as M
+    from oracle.inputs import ModelCase, make_model_case
+    case = ModelCase()
+    sd, _ = make_model_case(case)
+    m = M.CausalWanModel(model_type="i2v", in_dim=case.in_dim, dim=case.dim, ffn_dim=case.ffn, freq_dim=case.freq_dim,
+                         text_dim=case.text_dim, out_dim=case.out_dim, num_heads=case.heads, num_layers=case.layers,
+                         text_len=case.text_len)
+    assert set(m.state_dict()) == set(sd)
+    for k, v in m.state_dict().items():
+        assert tuple(v.shape) == tuple(sd[k].shape), k

@@ -51,3 +51,20 @@ def test_cam_film_matches_reference():
     assert abs(checksum(p, inp) - g["checksum"]) <= 1e-4 * g["checksum"]
     scale, shift = ob.cam_film(p, inp["cam"])
     assert rel_l2(scale, g["scale"]) < 2e-3 and rel_l2(shift, g["shift"]) < 2e-3
+
+
+def test_model_forward_matches_reference():
+    """The oracle's whole WanModelFast.forward (embeddings, camera FiLM, 2 blocks on the chunked cache, head,
+    unpatchify) against the reference's own forward on the same seeded inputs."""
+    from oracle import model as om
+    from oracle.inputs import ModelCase, make_model_case
+    import lbw_b200.chunked_kv_cache as routing
+    g = load_golden("model_forward")
+    case = ModelCase(**g["case"])
+    sd, inp = make_model_case(case)
+    out, k_dest, v_dest, ctx_k, ctx_v = om.model_forward(sd, inp, case, routing.chunk_routing)
+    assert (g["dest"], g["leading"]) == routing.chunk_routing(case.chunk_index, case.n_chunks)
+    assert rel_l2(out, g["out"]) < 2e-3 and max_abs(out, g["out"]) < 2e-2
+    for i in range(case.layers):
+        assert rel_l2(k_dest[i], g["k_dest"][i]) < 1e-2 and rel_l2(v_dest[i], g["v_dest"][i]) < 1e-2
+        assert rel_l2(ctx_k[i], g["ctx_k"][i]) < 1e-2 and rel_l2(ctx_v[i], g["ctx_v"][i]) < 1e-2
