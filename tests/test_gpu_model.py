@@ -73,3 +73,18 @@ def test_model_kv_commit_forward_writes_the_cache(cuda_dev):
     torch.cuda.synchronize()
     for i in range(case.layers):
         assert rel_l2(cache[i]["k"][g["dest"]][0].cpu(), g["k_dest"][i]) < 1e-2
+
+
+def test_model_from_checkpoint_folder_vs_reference_golden(cuda_dev, tmp_path):
+    """The reference-layout checkpoint folder (config.json + sharded safetensors) through load_model gives the
+    golden forward."""
+    import lbw_b200.checkpoint as ck
+    from test_host import _write_checkpoint
+    g = load_golden("model_forward")
+    case, _ = _write_checkpoint(tmp_path, sharded=True)
+    m, unexpected = ck.load_model(str(tmp_path), device=cuda_dev)
+    assert unexpected == []
+    _, inp = make_model_case(case)
+    cache, cc = _cache(case, inp, cuda_dev)
+    o = _run(m, case, inp, cache, cc, cuda_dev)[0].float().cpu()
+    assert rel_l2(o, g["out"]) < 1e-2 and max_abs(o, g["out"]) < 5e-2

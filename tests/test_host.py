@@ -95,3 +95,63 @@ def test_model_state_dict_keys_match_the_reference():
     assert set(m.state_dict()) == set(sd)
     for k, v in m.state_dict().items():
         assert tuple(v.shape) == tuple(sd[k].shape), k
+
+
+def _write_checkpoint(tmp_path, sharded):
+    import json
+    from safetensors.torch import save_file
+    from oracle.inputs import ModelCase, make_model_case
+    case = ModelCase()
+    sd, _ = make_model_case(case)
+    d = tmp_path / "transformers"
+    d.mkdir()
+    cfg = dict(model_type="i2v", patch_size=[1, 2, 2], text_len=case.text_len, in_dim=case.in_dim, dim=case.dim,
+               ffn_dim=case.ffn, freq_dim=case.freq_dim, text_dim=case.text_dim, out_dim=case.out_dim,
+               num_heads=case.heads, num_layers=case.layers, qk_norm=True, cross_attn_norm=True, eps=1e-6)
+    (d / "config.json").write_text(json.dumps(cfg))
+    tensors = {k: v.contiguous() for k, v in sd.items()}
+    if sharded:
+        keys = sorted(tensors)
+        halves = [keys[: len(keys) // 2], keys[len(keys) // 2:]]
+        wmap = {}
+        for i, ks in enumerate(halves):
+            name = f"diffusion_pytorch_model-0000{i + 1}-of-00002.safetensors"
+            save_file({k: tensors[k] for k in ks}, str(d / name))
+            wmap.update({k: name for k in ks})
+        (d / "diffusion_pytorch_model.safetensors.index.json").write_text(json.dumps({"weight_map": wmap}))
+    else:
+        save_file(tensors, str(d / "model.safetensors"))
+    return case, sd
+
+
+@pytest.mark.parametrize("sharded", [False, True])
+def test_checkpoint_loader_reads_reference_layout(tmp_path, sharded):
+    """A DiT folder laid out like the reference upload (transformers/, config.json, sharded safetensors + index)
+    loads into CausalWanModel with every parameter, in the pipeline's dtypes, values unchanged."""
+    import lbw_b200.checkpoint as ck
+    case, sd = _write_checkpoint(tmp_path, sharded)
+    model, unexpected = ck.load_model(str(tmp_path), device="cpu", pack=False)
+    assert unexpected == []
+    msd = model.state_dict()
+    assert set(msd) == set(sd)
+    for k, v in sd.items():
+        assert torch.equal(msd[k].float(), v.float()), k
+    assert msd["time_embedding.0.weight"].dtype == torch.float32 and msd["blocks.0.modulation"].dtype == torch.float32
+    assert msd["blocks.1.self_attn.q.weight"].dtype == torch.bfloat16
+    assert model.num_layers == case.layers and model.dim == case.dim
+
+
+def test_checkpoint_loader_rejects_missing_and_misshapen(tmp_path):
+    import lbw_b200.checkpoint as ck
+    from safetensors.torch import load_file, save_file
+    _write_checkpoint(tmp_path, sharded=False)
+    path = tmp_path / "transformers" / "model.safetensors"
+    t = load_file(str(path))
+    t.pop("blocks.1.ffn.2.bias")
+    save_file(t, str(path))
+    with pytest.raises(ValueError, match="lacks 1 parameters"):
+        ck.load_model(str(tmp_path), device="cpu", pack=False)
+    t["blocks.1.ffn.2.bias"] = torch.zeros(7)
+    save_file(t, str(path))
+    with pytest.raises(ValueError, match="checkpoint shape"):
+        ck.load_model(str(tmp_path), device="cpu", pack=False)
