@@ -62,7 +62,7 @@ template <int TBN> struct Cfg {
 template <class Epi, int TBN = 256>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                     int K, Epi epi, int* status) {
+                     int K, int group_m, Epi epi, int* status) {
   using gemm::BM;
   using gemm::BK;
   using C = gemm::Cfg<TBN>;
@@ -110,7 +110,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       uint32_t ph = 0;
       long long issued = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-        const int m_blk = t / nN, n_blk = t % nN;
+        int m_blk, n_blk;
+        tile_coords(t, nM, nN, group_m, m_blk, n_blk);
         bool ok = true;
         for (int kb = 0; kb < nK; ++kb) {
           if (!mbar_wait(&empty_bar[s], ph ^ 1, ab, 1)) { ok = false; break; }
@@ -173,7 +174,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     int acc = 0;
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-      const int m_blk = t / nN, n_blk = t % nN;
+      int m_blk, n_blk;
+        tile_coords(t, nM, nN, group_m, m_blk, n_blk);
       if (!mbar_wait(&tfull_bar[acc], aph, ab, 4)) break;
       tc_fence_after();
       const int row = m_blk * BM + quarter * 32 + lane;
@@ -228,7 +230,8 @@ static int launch_gemm_t(const CUtensorMap& tmA, const void* W, long long ldw, i
   }
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + TBN - 1) / TBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_bf16_kernel<Epi, TBN><<<grid, gemm::THREADS, C::SMEM_BYTES, stream>>>(tmA, tmB, M, N, K, epi, st);
+  gemm_bf16_kernel<Epi, TBN><<<grid, gemm::THREADS, C::SMEM_BYTES, stream>>>(tmA, tmB, M, N, K,
+                                                                             group_rows(M, K, 2), epi, st);
   return cuda_check(cudaGetLastError(), "gemm launch");
 }
 
@@ -453,7 +456,7 @@ extern "C" int lbw_linear_rmsnorm_noalloc(const void* a, const void* w, const vo
   const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
   // No status word: a bounded-wait timeout still ends the kernel, but is not recorded for this call.
-  gemm_bf16_kernel<EpiStore><<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmB, m, n, k, e, nullptr);
+  gemm_bf16_kernel<EpiStore><<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmB, m, n, k, group_rows(m, k, 2), e, nullptr);
   if ((err = cuda_check(cudaGetLastError(), "noalloc gemm launch"))) return err;
   rms_gamma_inplace_kernel<<<m, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), ss,
                                              reinterpret_cast<const __nv_bfloat16*>(gamma), n, eps, n);

@@ -51,7 +51,8 @@ template <int TBN> struct Cfg {
 template <class Epi, int TBN = 256>
 __global__ void __launch_bounds__(mxg::THREADS, 1)
     gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int M, int N, int K, Epi epi,
+                   const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int M, int N, int K, int group_m,
+                   Epi epi,
                    int* status) {
   using mxg::BM;
   using mxg::BK;
@@ -104,7 +105,8 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
       uint32_t ph = 0;
       long long issued = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-        const int m_blk = t / nN, n_blk = t % nN;
+        int m_blk, n_blk;
+        tile_coords(t, nM, nN, group_m, m_blk, n_blk);
         const int b0 = 2 * n_blk, b1 = (2 * n_blk + 1 < n_sf_blocks) ? 2 * n_blk + 1 : 2 * n_blk;
         bool ok = true;
         for (int ks = 0; ks < nS; ++ks) {
@@ -182,7 +184,8 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
     const int half = (warp - 2) >> 2;        // first or second half of the tile's columns
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-      const int m_blk = t / nN, n_blk = t % nN;
+      int m_blk, n_blk;
+        tile_coords(t, nM, nN, group_m, m_blk, n_blk);
       if (!mbar_wait(&tfull_bar, aph, ab, 0x54)) break;
       tc_fence_after();
       const int row = m_blk * BM + quarter * 32 + lane;
@@ -230,8 +233,8 @@ static int launch_gemm_mx_t(const CUtensorMap& tmA, const void* a_scales, const 
   const int tiles = ((M + mxg::BM - 1) / mxg::BM) * ((N + TBN - 1) / TBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
   gemm_mx_kernel<Epi, TBN><<<grid, mxg::THREADS, C::SMEM_BYTES, stream>>>(
-      tmA, tmB, reinterpret_cast<const uint8_t*>(a_scales), reinterpret_cast<const uint8_t*>(w_scales), M, N, K, epi,
-      st);
+      tmA, tmB, reinterpret_cast<const uint8_t*>(a_scales), reinterpret_cast<const uint8_t*>(w_scales), M, N, K,
+      group_rows(M, K, 1), epi, st);
   return cuda_check(cudaGetLastError(), "mx gemm launch");
 }
 

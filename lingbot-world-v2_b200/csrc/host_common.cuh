@@ -30,6 +30,16 @@ int make_tmap_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, 
                  uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows);
 
 int num_sms();
+// Row blocks (of 128) per tile group of the persistent GEMMs (see tile_coords): about 40 MB of activation rows
+// (K elements of elem_bytes each) so that a group stays in the 126 MB L2 with the weights streaming past.
+inline int group_rows(int M, int K, int elem_bytes) {
+  const long long per = 128LL * K * elem_bytes;
+  long long g = (40LL << 20) / (per > 0 ? per : 1);
+  const long long nm = (M + 127) / 128;
+  if (g < 1) g = 1;
+  if (g > nm) g = nm;
+  return (int)g;
+}
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 

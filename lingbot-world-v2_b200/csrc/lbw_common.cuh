@@ -88,6 +88,20 @@ LBW_DEV bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
+// Persistent GEMM tile order: tile t of an nM x nN grid of output tiles, walked in groups of gm row blocks
+// with the row block varying fastest inside a group. The tiles in flight then share a few weight column
+// blocks, and the group's activation rows stay in L2 while the weights stream past once per group (a plain
+// row-major walk re-reads every weight block from DRAM on every wave once the weights exceed L2).
+LBW_DEV void tile_coords(int t, int nM, int nN, int gm, int& m, int& n) {
+  const int per = gm * nN;
+  const int grp = t / per;
+  const int m0 = grp * gm;
+  const int rows = nM - m0 < gm ? nM - m0 : gm;
+  const int loc = t - grp * per;
+  m = m0 + loc % rows;
+  n = loc / rows;
+}
+
 // ------------------------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ------------------------------------------------------------------------------------------

@@ -115,6 +115,28 @@ def test_chunk_attention(cuda_dev, lq, rows, heads, qscale):
     assert max_abs(out.view(lq, heads, 128), ref) < 5e-2
 
 
+def test_chunk_attention_row_max_near_900(cuda_dev):
+    """Real-weight hot heads reach row maxima of ~864 (the reference's const-max guard, model_fast.py:254-263):
+    a key aligned with each query and scaled x80 sits in a late tile of a later chunk, so the running max jumps
+    from ~4 to ~900 mid-window; the exact online softmax must still match fp32."""
+    import lbw_b200.kernels as K
+    g = _g(71)
+    lq, heads, n = 160, 2, 700
+    q = torch.randn(lq, heads, 128, generator=g).to(BF)
+    ks = [torch.randn(n, heads, 128, generator=g) for _ in range(2)]
+    for r in range(lq):                      # row r's hot key: 80 x q_r, in chunk 1 at position 300 + r
+        ks[1][300 + r] = q[r].float() * 80.0
+    ks = [k.to(BF) for k in ks]
+    vs = [torch.randn(n, heads, 128, generator=g).to(BF) for _ in range(2)]
+    d = cuda_dev
+    logits = torch.einsum("qhd,khd->qhk", q.float(), torch.cat(ks).float()) / 128 ** 0.5
+    assert float(logits.max()) > 800
+    out = K.chunk_attention(q.to(d), [k.to(d) for k in ks], [v.to(d) for v in vs])
+    ref = ob.attention(q, torch.cat(ks), torch.cat(vs))
+    assert torch.isfinite(out).all()
+    assert rel_l2(out.view(lq, heads, 128), ref) < 1e-2 and max_abs(out.view(lq, heads, 128), ref) < 5e-2
+
+
 def test_chunk_attention_hot_head_rescale(cuda_dev):
     """Row maxima that grow by far more than 2^8 across KV tiles (hot heads, row max in the hundreds)."""
     import lbw_b200.kernels as K
