@@ -226,7 +226,8 @@ def run_sweep(args):
         return statistics.median(ts[1:])
 
     H, C = 40, 5120
-    for lq in (1560, 4680, 10800):
+    only = args.sweep_only
+    for lq in ((1560, 4680, 10800) if only in ("all", "attention") else ()):
         q = torch.randn(lq, C, generator=g, device=dev, dtype=bf)
         out = torch.empty(lq, C, dtype=bf, device=dev)
         for lkv in (4096, 16384, 32768, 75600, 131072):
@@ -248,7 +249,7 @@ def run_sweep(args):
             print(json.dumps({"sweep": "chunk_attention", "q_rows": lq, "kv_rows": lkv, "heads": H, "kv_splits": splits,
                               "ms": ms, "tflops": tf, "frac_of_peak": tf / peak, "peak": f"{src} bf16_tflops {peak}"}))
             del ks, vs, parts
-    for m in (4680, 10800, 43200):
+    for m in ((4680, 10800, 43200) if only in ("all", "mxfp8") else ()):
         for kk, nn in ((5120, 13824), (13824, 5120)):
             a = torch.randn(m, kk, generator=g, device=dev, dtype=bf)
             w = (torch.randn(nn, kk, generator=g, device=dev) * 0.02).to(bf)
@@ -261,6 +262,28 @@ def run_sweep(args):
                               "frac_of_bf16_peak": tf / peak, "frac_of_2x_bf16_peak": tf / (2 * peak),
                               "peak": f"{src} bf16_tflops {peak}"}))
             del a, w, ad, as_, wd, ws, o
+    # the block's bf16 GEMMs (q|k|v with the row sums of squares; o-projection with the gated residual + FiLM) at
+    # the 1- and 8-GPU row counts of c4; 3 untimed launches first (an ncu capture can skip them with -s)
+    for m in ((10800, 1350) if only in ("all", "gemm") else ()):
+        h = torch.randn(m, C, generator=g, device=dev, dtype=bf)
+        wqkv = (torch.randn(3 * C, C, generator=g, device=dev) * 0.02).to(bf)
+        bqkv = (torch.randn(3 * C, generator=g, device=dev) * 0.02).to(bf)
+        wo = (torch.randn(C, C, generator=g, device=dev) * 0.02).to(bf)
+        bo = (torch.randn(C, generator=g, device=dev) * 0.02).to(bf)
+        qr, kr, vv = (torch.empty(m, C, dtype=bf, device=dev) for _ in range(3))
+        ss = torch.zeros(2, m, device=dev)
+        xres = torch.randn(m, C, generator=g, device=dev)
+        gate = torch.randn(C, generator=g, device=dev) * 0.1
+        fs, ft = ((torch.randn(m, C, generator=g, device=dev) * 0.1).to(bf) for _ in range(2))
+        for name, n, fn in (("qkv_rowss", 3 * C, lambda: K.qkv_proj(h, wqkv, bqkv, qr, kr, ss[0], ss[1], vv)),
+                            ("o_proj_residual_film", C,
+                             lambda: K.linear_residual(h, wo, bo, xres, gate=gate, film_scale=fs, film_shift=ft))):
+            for _ in range(3):
+                fn()
+            ms = timed(fn, reps=3)
+            tf = 2.0 * m * C * n / (ms / 1e3) / 1e12
+            print(json.dumps({"sweep": "bf16_gemm", "name": name, "m": m, "k": C, "n": n, "ms": ms, "tflops": tf,
+                              "frac_of_peak": tf / peak, "peak": f"{src} bf16_tflops {peak}"}))
     return 0
 
 
@@ -275,6 +298,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="kernel sweep (BASELINE configs[4]) instead of the step")
+    ap.add_argument("--sweep-only", default="all", choices=["all", "attention", "mxfp8", "gemm"],
+                    help="with --sweep: one family of points (gemm = the block's bf16 GEMMs at 10,800 and 1,350 rows)")
     ap.add_argument("--breakdown", action="store_true",
                     help="after the timed steps, time each phase of the block with CUDA event marks")
     args = ap.parse_args()
