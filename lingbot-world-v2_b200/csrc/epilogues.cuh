@@ -12,6 +12,7 @@
 namespace lbw {
 
 struct EpiStore {
+  static constexpr int WARP_SMEM = 0;  // no warp-cooperative chunk()
   __nv_bfloat16* out[3];
   long long ld[3];
   int row_off[3];
@@ -66,6 +67,10 @@ struct EpiStore {
 // spilled and measured slower there).
 template <bool FILM>
 struct EpiResidualT {
+  // FILM: the bf16 GEMM (o-projection, cross-o) hands each warp's 32 rows x 32 columns to chunk_warp(), which
+  // transposes them through this much shared memory per warp so that the residual and FiLM rows are read and
+  // written with coalesced 128-byte accesses. The MXFP8 GEMM (FILM = false) has no shared memory left for it.
+  static constexpr int WARP_SMEM = FILM ? 32 * 33 * 4 : 0;
   float* x;                          // [M, ldx] fp32 residual, updated in place
   long long ldx;
   const __nv_bfloat16* bias;         // [N] nullable
@@ -127,6 +132,70 @@ struct EpiResidualT {
     for (int q = 0; q < W / 4; ++q) reinterpret_cast<float4*>(xr)[q] = xv[q];
   }
 
+  // Warp-cooperative form (all 32 lanes, lane i = row row0 + i, the same 32 columns): y = bf16(acc + b) * gate
+  // per row into shared memory, then 8 lanes per row read x / FiLM and write x with 16-byte accesses, 4 rows per
+  // pass, all loads of the chunk before its stores. Rows >= M are skipped.
+  LBW_DEV void chunk_warp(int row0, int lane, int col, const float (&v)[32], int M, float* sm) const {
+#pragma unroll
+    for (int e = 0; e < 32; e += 8) {
+      float y[8];
+      if (bias) {
+        const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + col + e));
+        const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q] + __bfloat162float(bp[q]));
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q]);
+      }
+      if (gate) {
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + col + e));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + col + e + 4));
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) y[q] = __fmul_rn(y[q], g[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) sm[lane * 33 + e + q] = y[q];
+    }
+    __syncwarp();
+    const int rr = lane >> 3, c4 = (lane & 7) * 4;
+    float4 xv[8];
+    uint2 sv[8], tv[8];
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int row = row0 + it * 4 + rr;
+      if (row < M) {
+        xv[it] = *reinterpret_cast<const float4*>(x + (long long)row * ldx + col + c4);
+        if (FILM && film_scale) {
+          const long long fo = (long long)row * ldf + col + c4;
+          sv[it] = *reinterpret_cast<const uint2*>(film_scale + fo);
+          tv[it] = *reinterpret_cast<const uint2*>(film_shift + fo);
+        }
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int r = it * 4 + rr, row = row0 + r;
+      if (row < M) {
+        float o[4] = {xv[it].x, xv[it].y, xv[it].z, xv[it].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o[q] = __fadd_rn(o[q], sm[r * 33 + c4 + q]);
+        if (FILM && film_scale) {
+          const __nv_bfloat16* sp = reinterpret_cast<const __nv_bfloat16*>(&sv[it]);
+          const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(&tv[it]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float s1 = bf16_round(1.f + __bfloat162float(sp[q]));  // (1.0 + bf16 tensor) stays bf16
+            o[q] = __fadd_rn(__fmul_rn(s1, o[q]), __bfloat162float(tp[q]));
+          }
+        }
+        *reinterpret_cast<float4*>(x + (long long)row * ldx + col + c4) = make_float4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    __syncwarp();
+  }
+
   LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
     if constexpr (FILM) {
       part<32>(row, col, 0, v);
@@ -141,6 +210,7 @@ struct EpiResidualT {
 using EpiResidual = EpiResidualT<true>;
 
 struct EpiGelu {
+  static constexpr int WARP_SMEM = 0;  // no warp-cooperative chunk()
   __nv_bfloat16* out;   // [M, ldo] GELU(u + b), or its MXFP8 quantise-dequantise
   long long ldo;
   const __nv_bfloat16* bias;
@@ -176,6 +246,7 @@ struct EpiGelu {
 // out = bf16(act(bf16(acc + b))) [+ addend, rounded to bf16], act = identity or SiLU: the camera-FiLM
 // MLP of the block (cam_injector_layer1 + SiLU, cam_injector_layer2 + the camera embedding).
 struct EpiAct {
+  static constexpr int WARP_SMEM = 0;  // no warp-cooperative chunk()
   __nv_bfloat16* out;           // [M, ldo]
   long long ldo;
   const __nv_bfloat16* bias;    // [N] nullable
@@ -225,6 +296,7 @@ struct EpiAct {
 };
 
 struct EpiGeluMX {
+  static constexpr int WARP_SMEM = 0;  // no warp-cooperative chunk()
   uint8_t* data;     // [M, ld] E4M3 codes of GELU(u + b)
   uint8_t* scales;   // E8M0 scales in the tiled layout of a [M, sf_cols] matrix (mx_sf_offset)
   long long ld;

@@ -39,6 +39,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
 constexpr int THREADS = 320;
 constexpr int EPI_THREADS = THREADS - 64;
+constexpr int EPI_WARPS = EPI_THREADS / 32;
 // Tile width TBN (256, or 128 when 256-wide tiles would leave the last wave mostly idle): ring depth and
 // shared memory per tile width.
 // A 128-wide tile's MMAs (N = 128) take half as long as a 256-wide tile's, so its stages hold two 64-wide K
@@ -188,7 +189,12 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         uint32_t r[32];
         tmem_ld32(tb + c * 32, r);
         tmem_ld_wait();
-        if (row < M) stat += epi.chunk(row, col, reinterpret_cast<const float(&)[32]>(r));
+        if constexpr (Epi::WARP_SMEM > 0) {
+          float* sm = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + (warp - 2) * Epi::WARP_SMEM);
+          epi.chunk_warp(m_blk * BM + quarter * 32, lane, col, reinterpret_cast<const float(&)[32]>(r), M, sm);
+        } else if (row < M) {
+          stat += epi.chunk(row, col, reinterpret_cast<const float(&)[32]>(r));
+        }
       }
       if (row < M) epi.tile_done(row, n_blk * BN, stat);
       tc_fence_before();
@@ -223,15 +229,15 @@ static int launch_gemm_t(const CUtensorMap& tmA, const void* W, long long ldw, i
   static bool attr_set = false;  // one flag per instantiation
   if (!attr_set) {
     err = cuda_check(cudaFuncSetAttribute(gemm_bf16_kernel<Epi, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          C::SMEM_BYTES),
+                                          C::SMEM_BYTES + gemm::EPI_WARPS * Epi::WARP_SMEM),
                      "gemm smem attribute");
     if (err) return err;
     attr_set = true;
   }
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + TBN - 1) / TBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_bf16_kernel<Epi, TBN><<<grid, gemm::THREADS, C::SMEM_BYTES, stream>>>(tmA, tmB, M, N, K,
-                                                                             group_rows(M, K, 2), epi, st);
+  gemm_bf16_kernel<Epi, TBN><<<grid, gemm::THREADS, C::SMEM_BYTES + gemm::EPI_WARPS * Epi::WARP_SMEM, stream>>>(
+      tmA, tmB, M, N, K, group_rows(M, K, 2), epi, st);
   return cuda_check(cudaGetLastError(), "gemm launch");
 }
 
