@@ -493,6 +493,7 @@ def main():
     if rank == 0:
         print(json.dumps(result))
     if world > 1:
+        sp.close_peers()
         dist.barrier()
         dist.destroy_process_group()
     return 0

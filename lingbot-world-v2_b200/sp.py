@@ -120,6 +120,20 @@ class PeerKV:
         self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
         self.epoch = 0
 
+    def close(self):
+        """Collective: every rank's pulls have completed (device synchronisation + barrier) before the peers'
+        mappings are closed and this rank's buffer is freed."""
+        if self._ptrs is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        lib = self._lib.load()
+        with torch.cuda.device(self.device):
+            for r, p in enumerate(self._ptrs):
+                self._lib.check(lib.lbw_peer_buffer_close(ctypes.c_void_p(p), int(r == self.rank)),
+                                "peer_buffer_close", 0)
+        self._ptrs = None
+
     @property
     def gathered_flag(self):
         """Device address of this rank's 32-bit 'gathered' word: the epoch of the last completed exchange."""
@@ -157,14 +171,21 @@ _PEERS = {}
 
 
 def peer_kv(k2d, local_rows):
-    """The copy-engine exchange for destination chunks shaped like k2d (CUDA + NCCL group), else None."""
+    """The copy-engine exchange for destination chunks shaped like k2d (CUDA + NCCL group), else None. One per
+    (group, device, shard shape), created collectively on first use."""
     if not (active() and k2d.is_cuda and dist.get_backend(_GROUP) == "nccl"):
         return None
-    key = (k2d.device, local_rows, k2d.shape[1])
+    key = (id(_GROUP), world(), rank(), k2d.device, local_rows, k2d.shape[1])
     pk = _PEERS.get(key)
     if pk is None:
         pk = _PEERS[key] = PeerKV(local_rows, k2d.shape[1], k2d.device, _GROUP)
     return pk
+
+
+def close_peers():
+    """Collective: release every copy-engine exchange of this process (before destroying its process group)."""
+    for key in list(_PEERS):
+        _PEERS.pop(key).close()
 
 
 def gather_kv_inplace(k2d, v2d, local_rows):

@@ -120,6 +120,7 @@ def _gather_worker(rank, world, port, q):
             torch.cuda.synchronize()
             ok = ok and torch.equal(k[:, :cols], want_k) and torch.equal(v[:, :cols], want_v)
             ok = ok and bool((k[:, cols:] == -1).all()) and bool((v[:, cols:] == -1).all())   # padding untouched
+        sp.close_peers()
         q.put((rank, "ok" if ok else "mismatch"))
     except Exception as e:
         q.put((rank, repr(e)))
