@@ -300,6 +300,8 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="kernel sweep (BASELINE configs[4]) instead of the step")
     ap.add_argument("--sweep-only", default="all", choices=["all", "attention", "mxfp8", "gemm"],
                     help="with --sweep: one family of points (gemm = the block's bf16 GEMMs at 10,800 and 1,350 rows)")
+    ap.add_argument("--lin-mx", action="store_true",
+                    help="every block Linear in MXFP8 (the reference's LINGBOT_LIN_MX option; not the headline config)")
     ap.add_argument("--breakdown", action="store_true",
                     help="after the timed steps, time each phase of the block with CUDA event marks")
     args = ap.parse_args()
@@ -341,7 +343,7 @@ def main():
     n_chunks = c["n_lead"] + 1
     lkv = n_chunks * chunk
 
-    stack = M.BlockStack.synthetic(layers, C, F, H, dev, seed=0, ffn_mx=True)
+    stack = M.BlockStack.synthetic(layers, C, F, H, dev, seed=0, ffn_mx=True, lin_mx=args.lin_mx)
     g = torch.Generator(device=dev).manual_seed(1 + rank)
     bf = torch.bfloat16
     ks = [[torch.randn(1, chunk, H, 128, generator=g, device=dev, dtype=bf) for _ in range(n_chunks)]
@@ -461,10 +463,12 @@ def main():
     result = {
         "metric": "chunk-forward tokens/s", "value": chunk / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (attention, projections) + mxfp8 e4m3/e8m0 (FFN)",
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": ("bf16 (attention) + mxfp8 e4m3/e8m0 (every Linear, LINGBOT_LIN_MX)" if args.lin_mx else
+                  "bf16 (attention, projections) + mxfp8 e4m3/e8m0 (FFN)"),
         "data": "synthetic (seeded N(0,1) latents / KV, N(0,0.02) weights, random init)",
         "config": {"workload": args.config, "model": c["model"], "blocks": layers, "query_tokens": chunk,
-                   "kv_tokens": lkv, "text_tokens": TEXT_LEN, "parallelism": f"sp{world}",
+                   "kv_tokens": lkv, "text_tokens": TEXT_LEN, "parallelism": f"sp{world}", "lin_mx": args.lin_mx,
                    "l2": "inputs larger than L2 (KV cache and weights >> 126 MB)"},
         "latency_ms": ms,
         "tc_frac_of_peak": flops / (ms / 1e3) / (peak_tc * 1e12 * world),

@@ -150,6 +150,11 @@ int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scal
  * h = (LN(x)(1 + e4) + e3).to(bf16) (model_fast.py:3101) quantised for the MXFP8 FFN (kernels/ffn_mx.py:159-182). */
 int lbw_layernorm_mod_mx(const float* x, int m, int c, float eps, const float* scale, const float* shift, void* data,
                          void* scales, void* stream);
+/* As lbw_layernorm_mod_mx with the affine weight/bias of norm3 (fp32 [c]) instead of the modulation: the
+ * cross-attention q input LN(x) * w3 + b3 (model_fast.py:2865-2867) quantised for an MXFP8 cross_attn.q
+ * (LINGBOT_LIN_MX, model_fast.py:1266-1269). */
+int lbw_layernorm_affine_mx(const float* x, int m, int c, float eps, const float* weight, const float* bias,
+                            void* data, void* scales, void* stream);
 
 /* RMSNorm (+ 3-D RoPE) of projected rows: y = bf16(bf16(x * rsqrt(ss/c + eps)) * gamma), then,
  * if rope_cos != NULL, the interleaved-pair rotation with per-token angles of (frame, h, w).
@@ -173,7 +178,9 @@ int lbw_mx_quantize(const void* x, int rows, int k, void* data, void* scales, vo
 /* Block-scaled tcgen05 GEMMs (kind::mxf8f6f4, E4M3 x E4M3, E8M0 scale per 32 along K, fp32 accumulate).
  * a: codes [m, k] + tiled scales (rows padded to 128); w: codes [n, k] + tiled scales; k % 128 == 0,
  * n % 128 == 0. Replaces ffn_mx.mm (kernels/ffn_mx.py:159-182, nkilib matmul_mxfp8). */
-/* out[m, n] = bf16(a w^T + bias) (bias may be NULL). */
+/* Every epilogue rounds a w^T to bf16 before adding the bias, as ffn_mx.mm's bf16 result + bias does in the
+ * reference (_mx_matmul, model_fast.py:1403-1410; _ffn_mx :1589-1610). */
+/* out[m, n] = bf16(bf16(a w^T) + bias) (bias may be NULL). */
 int lbw_mx_linear(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias, int m,
                   int n, int k, void* out, void* stream);
 /* FFN up: GELU_tanh(bf16(a w^T) + bias) quantised to MXFP8 codes out[m, n] + tiled scales out_scales
@@ -184,6 +191,28 @@ int lbw_mx_linear_gelu(const void* a, const void* a_scales, const void* w, const
  * Replaces ffn_mx.mm + bias and x + y * e5 (model_fast.py:1584-1611, :3110-3111). */
 int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, const void* w_scales,
                            const void* bias, int m, int n, int k, float* x, const float* gate, void* stream);
+
+/* The block's other Linears in MXFP8 (LINGBOT_LIN_MX=1, model_fast.py:1266-1269; _prequantize_linears_mx
+ * :1442-1494 quantises each weight once, _mx_linear_forward :1413-1416 runs y = _mx_matmul(x) + b). */
+/* q|k|v projection (w_qkv = [Wq; Wk; Wv] codes [3c, c] + scales): q_raw, k_raw [m, c] with row sums of squares
+ * ss_q, ss_k [m] (cleared here) for the following RMSNorm, V rows v_row_off.. of v_out (row stride ldv).
+ * The MXFP8 counterpart of lbw_qkv_proj (self_attn.q/k/v, model_fast.py:1733-1740). */
+int lbw_mx_qkv_proj(const void* h, const void* h_scales, const void* w_qkv, const void* w_qkv_scales,
+                    const void* b_qkv, int m, int c, void* q_raw, void* k_raw, float* ss_q, float* ss_k, void* v_out,
+                    long long ldv, int v_row_off, void* stream);
+/* out[m, n] = bf16(bf16(a w^T) + bias) with row sums of squares ss[m] (cleared here): cross_attn.q and, at the
+ * first call, cross_attn.k on the text context (model_fast.py:2755-2798). */
+int lbw_mx_linear_rowss(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                        int m, int n, int k, void* out, float* ss, void* stream);
+/* self_attn.o + gate + camera FiLM: x += bf16(bf16(a w^T) + bias) * gate, then x = (1 + s) * x + t (film_scale,
+ * film_shift bf16 [m, n], both or neither). The MXFP8 counterpart of lbw_linear_residual (:3056-3089). */
+int lbw_mx_linear_residual_film(const void* a, const void* a_scales, const void* w, const void* w_scales,
+                                const void* bias, int m, int n, int k, float* x, const float* gate,
+                                const void* film_scale, const void* film_shift, void* stream);
+/* Camera FiLM MLP layer: out = bf16(act(bf16(bf16(a w^T) + bias))) [+ addend, rounded to bf16], act = SiLU if silu
+ * else identity. The MXFP8 counterpart of lbw_linear_act (cam_film, model_fast.py:2882-2891, :606-616). */
+int lbw_mx_linear_act(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                      const void* addend, int silu, int m, int n, int k, void* out, void* stream);
 
 /* ---- sequence-parallel K/V exchange (one process per GPU, same node, NVLink) ----------------
  * Replaces the all-gather of the new chunk's K/V shards into every rank's destination cache chunk

@@ -41,6 +41,11 @@ SIGNATURES = {
     "lbw_mx_linear": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp], _i),
     "lbw_mx_linear_gelu": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "lbw_mx_linear_residual": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
+    "lbw_layernorm_affine_mx": ([_vp, _i, _i, _f, _vp, _vp, _vp, _vp, _vp], _i),
+    "lbw_mx_qkv_proj": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _ll, _i, _vp], _i),
+    "lbw_mx_linear_rowss": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
+    "lbw_mx_linear_residual_film": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp], _i),
+    "lbw_mx_linear_act": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
     "lbw_chunk_attention_gated": ([_vp, _ll, _i, _i, _vp, _vp, _vp, _i, _ll, _f, _vp, _ll, _i, _vp, _vp, _i, _vp,
                                    ctypes.c_uint, _i, _vp], _i),
     "lbw_peer_buffer_create": ([_ll, ctypes.POINTER(_vp), _vp], _i),

@@ -5,7 +5,9 @@ wan/modules/model_fast.py:2837-3116 CausalWanAttentionBlock, for the path the ca
 runs: the chunked KV cache (kv_chunks=(k_chunks, v_chunks), destination LAST, layout
 [1, chunk_tokens, n, 128]), hoisted camera FiLM (dit_cond_dict={"cam_film": (scale, shift)}), the
 cached text cross-attention (crossattn_cache={"k", "v", "is_init"}), optional cross_dedup, and the
-MXFP8 FFN (ffn_mx=True, LINGBOT_FFN_MX) or the bf16 FFN.
+MXFP8 FFN (ffn_mx=True, LINGBOT_FFN_MX) or the bf16 FFN. lin_mx=True (LINGBOT_LIN_MX, model_fast.py:1266-1269,
+:1442-1494) puts the other block Linears on the MXFP8 GEMM too, except those named in lin_mx_skip
+(LINGBOT_LIN_MX_SKIP): their inputs are quantised by the producing LayerNorm kernel or by mx_quantize.
 
 One forward = 14 kernels of liblbw.so on the current stream:
   layernorm_mod(norm1 + adaLN) -> qkv_proj (v straight into the destination chunk) ->
@@ -14,6 +16,8 @@ One forward = 14 kernels of liblbw.so on the current stream:
   linear_rowss(cross q) -> rmsnorm(cross q) -> chunk_attention(cross, optional dedup bias) ->
   linear_residual(cross o) -> layernorm_mod(norm2 + adaLN, MX QDQ) -> linear_gelu(ffn.0 + GELU, MX QDQ)
   -> linear_residual(ffn.2, gate e5)
+(with the MXFP8 FFN the last three are layernorm_mod_mx -> mx_linear_gelu -> mx_linear_residual; lin_mx adds
+an mx_quantize of the attention output before each of the two o-projections).
 The fp32 residual is updated in place by the GEMM epilogues.
 """
 import math
@@ -26,6 +30,14 @@ from .attention import cross_dedup_bias
 
 BF16 = torch.bfloat16
 HEAD_DIM = 128
+# model_fast.py:1304-1306 (_MX_LIN_NAMES): the Linears LINGBOT_LIN_MX quantises besides the FFN
+MX_LINEAR_NAMES = ("self_attn.q", "self_attn.k", "self_attn.v", "self_attn.o",
+                   "cross_attn.q", "cross_attn.k", "cross_attn.v", "cross_attn.o",
+                   "cam_injector_layer1", "cam_injector_layer2", "cam_scale_layer", "cam_shift_layer")
+# packed-weight key of each (q|k|v share the fused GEMM)
+_MX_KEYS = {"self_attn.o": "wo", "cross_attn.q": "wcq", "cross_attn.k": "wck", "cross_attn.v": "wcv",
+            "cross_attn.o": "wco", "cam_injector_layer1": "wc1", "cam_injector_layer2": "wc2",
+            "cam_scale_layer": "wcs", "cam_shift_layer": "wcsh"}
 
 
 class _RMSNormParam(nn.Module):
@@ -81,7 +93,8 @@ class Workspace:
 
 class CausalWanAttentionBlock(nn.Module):
     def __init__(self, dim, ffn_dim, num_heads, local_attn_size=-1, sink_size=0, qk_norm=True,
-                 cross_attn_norm=False, eps=1e-6, ffn_mx=True, cross_dedup=0, mx_pipe="mxf8"):
+                 cross_attn_norm=False, eps=1e-6, ffn_mx=True, cross_dedup=0, mx_pipe="mxf8", lin_mx=False,
+                 lin_mx_skip=()):
         super().__init__()
         if dim % num_heads or dim // num_heads != HEAD_DIM:
             raise ValueError("the B200 kernels are built for head_dim 128")
@@ -93,6 +106,19 @@ class CausalWanAttentionBlock(nn.Module):
         if mx_pipe not in ("mxf8", "bf16"):
             raise ValueError("mx_pipe is 'mxf8' (tcgen05 block-scaled MMA) or 'bf16' (MX values on the bf16 pipe)")
         self.mx_pipe = mx_pipe
+        skip = tuple(lin_mx_skip or ())
+        unknown = [n for n in skip if n not in MX_LINEAR_NAMES]
+        if unknown:
+            raise ValueError(f"lin_mx_skip names no block Linear: {unknown} (known: {MX_LINEAR_NAMES})")
+        self.lin_mx = bool(lin_mx)
+        self.mx_linears = frozenset(n for n in MX_LINEAR_NAMES if n not in skip) if self.lin_mx else frozenset()
+        qkv = {"self_attn.q", "self_attn.k", "self_attn.v"} & self.mx_linears
+        if qkv and len(qkv) != 3:
+            raise ValueError("self_attn.q/k/v share one fused GEMM: lin_mx_skip must name all three or none")
+        if self.lin_mx:
+            if mx_pipe != "mxf8":
+                raise ValueError("lin_mx runs on the block-scaled tcgen05 GEMM (mx_pipe='mxf8')")
+            self.ffn_mx = True   # LINGBOT_LIN_MX implies LINGBOT_FFN_MX (model_fast.py:1270)
         self.cross_dedup = int(cross_dedup)
         self.norm1 = nn.Identity()
         self.self_attn = _AttnParams(dim, num_heads, qk_norm, eps)
@@ -120,16 +146,19 @@ class CausalWanAttentionBlock(nn.Module):
         if dev.type != "cuda":
             raise ValueError("move the block to a CUDA device before the forward")
         b = lambda t: t.detach().to(BF16).contiguous()  # noqa: E731
+        mx = self.mx_linears
         pk = {}
-        pk["wqkv"] = torch.cat([b(sa.q.weight), b(sa.k.weight), b(sa.v.weight)]).contiguous()
+        wqkv = torch.cat([b(sa.q.weight), b(sa.k.weight), b(sa.v.weight)]).contiguous()
+        if "self_attn.q" in mx:
+            # quantised per row along K, so the fused [Wq; Wk; Wv] codes equal the three quantised separately
+            pk["wqkv_mx"] = kernels.mx_quantize(wqkv)[:2]
+        else:
+            pk["wqkv"] = wqkv
         pk["bqkv"] = torch.cat([b(sa.q.bias), b(sa.k.bias), b(sa.v.bias)]).contiguous()
         pk["gq"], pk["gk"] = b(sa.norm_q.weight), b(sa.norm_k.weight)
-        pk["wo"], pk["bo"] = b(sa.o.weight), b(sa.o.bias)
-        pk["wcq"], pk["bcq"] = b(ca.q.weight), b(ca.q.bias)
         pk["gcq"], pk["gck"] = b(ca.norm_q.weight), b(ca.norm_k.weight)
-        pk["wck"], pk["bck"] = b(ca.k.weight), b(ca.k.bias)
-        pk["wcv"], pk["bcv"] = b(ca.v.weight), b(ca.v.bias)
-        pk["wco"], pk["bco"] = b(ca.o.weight), b(ca.o.bias)
+        for key, lin in (("o", sa.o), ("cq", ca.q), ("ck", ca.k), ("cv", ca.v), ("co", ca.o)):
+            self._pack_linear(pk, key, lin, b)
         if self.cross_attn_norm:
             pk["n3w"] = self.norm3.weight.detach().float().contiguous()
             pk["n3b"] = self.norm3.bias.detach().float().contiguous()
@@ -149,7 +178,7 @@ class CausalWanAttentionBlock(nn.Module):
         if with_cam:
             for key, lin in (("c1", self.cam_injector_layer1), ("c2", self.cam_injector_layer2),
                              ("cs", self.cam_scale_layer), ("csh", self.cam_shift_layer)):
-                pk["w" + key], pk["b" + key] = b(lin.weight), b(lin.bias)
+                self._pack_linear(pk, key, lin, b)
         self._packed = pk
         if free_sources:
             # Only the packed copies serve the forward from here on (the reference frees its bf16 FFN
@@ -161,6 +190,26 @@ class CausalWanAttentionBlock(nn.Module):
             self._sources_freed = True
         return pk
 
+    def _mx_name(self, key):
+        return next(n for n, k in _MX_KEYS.items() if k == "w" + key)
+
+    def _pack_linear(self, pk, key, lin, b):
+        """pk["w" + key] bf16 weight, or pk["w" + key + "_mx"] its MXFP8 codes + scales (quantised once, as
+        _mx_quantize_linear does at load, model_fast.py:1384-1400); pk["b" + key] the bf16 bias."""
+        if self._mx_name(key) in self.mx_linears:
+            pk["w" + key + "_mx"] = kernels.mx_quantize(b(lin.weight))[:2]
+        else:
+            pk["w" + key] = b(lin.weight)
+        pk["b" + key] = b(lin.bias)
+
+    def _linear_act(self, key, x, **kw):
+        """One camera-FiLM MLP layer on the bf16 GEMM or, under lin_mx, on the MXFP8 GEMM."""
+        pk = self._packed
+        if "w" + key + "_mx" in pk:
+            xq, xs, _ = kernels.mx_quantize(x)
+            return kernels.mx_linear_act(xq, xs, *pk["w" + key + "_mx"], pk["b" + key], **kw)
+        return kernels.linear_act(x, pk["w" + key], pk["b" + key], **kw)
+
     @torch.no_grad()
     def cam_film(self, c2ws_plucker_emb):
         """Camera FiLM parameters (cam_scale, cam_shift) of this block for the chunk's camera condition
@@ -169,14 +218,14 @@ class CausalWanAttentionBlock(nn.Module):
         if self._packed is None:
             self.prepare()
         pk = self._packed
-        if "wc1" not in pk:
+        if "bc1" not in pk:
             raise ValueError("cam_film needs prepare(with_cam=True)")
         C = self.dim
         c = c2ws_plucker_emb.reshape(-1, C).to(BF16).contiguous()
-        h1 = kernels.linear_act(c, pk["wc1"], pk["bc1"], silu=True)
-        h2 = kernels.linear_act(h1, pk["wc2"], pk["bc2"], addend=c)
-        scale = kernels.linear_act(h2, pk["wcs"], pk["bcs"])
-        shift = kernels.linear_act(h2, pk["wcsh"], pk["bcsh"])
+        h1 = self._linear_act("c1", c, silu=True)
+        h2 = self._linear_act("c2", h1, addend=c)
+        scale = self._linear_act("cs", h2)
+        shift = self._linear_act("csh", h2)
         shape = c2ws_plucker_emb.shape[:-1] + (C,)
         return scale.view(shape), shift.view(shape)
 
@@ -198,9 +247,16 @@ class CausalWanAttentionBlock(nn.Module):
         vc = crossattn_cache["v"].view(T, C)
         k_raw = torch.empty(T, C, dtype=BF16, device=ctx.device)
         ss = torch.empty(T, dtype=torch.float32, device=ctx.device)
-        kernels.linear_rowss(ctx, pk["wck"], pk["bck"], k_raw, ss)
+        cq = kernels.mx_quantize(ctx)[:2] if ("wck_mx" in pk or "wcv_mx" in pk) else None
+        if "wck_mx" in pk:
+            kernels.mx_linear_rowss(*cq, *pk["wck_mx"], pk["bck"], k_raw, ss)
+        else:
+            kernels.linear_rowss(ctx, pk["wck"], pk["bck"], k_raw, ss)
         kernels.rmsnorm_rope(k_raw, ss, pk["gck"], self.eps, kc)
-        kernels.gemm_bf16(ctx, pk["wcv"], pk["bcv"], out=vc)
+        if "wcv_mx" in pk:
+            kernels.mx_linear(*cq, *pk["wcv_mx"], pk["bcv"], out=vc)
+        else:
+            kernels.gemm_bf16(ctx, pk["wcv"], pk["bcv"], out=vc)
         if self.cross_dedup:
             crossattn_cache["mult"] = cross_dedup_bias(kc.view(T, self.num_heads, HEAD_DIM),
                                                        vc.view(T, self.num_heads, HEAD_DIM), self.cross_dedup)
@@ -335,9 +391,15 @@ class CausalWanAttentionBlock(nn.Module):
         ss_q, ss_k = ws.ss[0], ws.ss[1]
 
         # self-attention
-        kernels.layernorm_mod(xf, eps, ws.h, scale=em[1], shift=em[0])
-        mark("ln1")
-        kernels.qkv_proj(ws.h, pk["wqkv"], pk["bqkv"], ws.q_raw, ws.k_raw, ss_q, ss_k, v_dst, v_row_off=row0)
+        if "wqkv_mx" in pk:
+            kernels.layernorm_mod_mx(xf, eps, em[1], em[0], ws.hq, ws.hs)
+            mark("ln1")
+            kernels.mx_qkv_proj(ws.hq, ws.hs, *pk["wqkv_mx"], pk["bqkv"], ws.q_raw, ws.k_raw, ss_q, ss_k, v_dst,
+                                v_row_off=row0)
+        else:
+            kernels.layernorm_mod(xf, eps, ws.h, scale=em[1], shift=em[0])
+            mark("ln1")
+            kernels.qkv_proj(ws.h, pk["wqkv"], pk["bqkv"], ws.q_raw, ws.k_raw, ss_q, ss_k, v_dst, v_row_off=row0)
         mark("qkv")
         kernels.rmsnorm_rope(ws.q_raw, ss_q, pk["gq"], eps, ws.q, rope=rp, grid=grid, tok0=row0)
         kernels.rmsnorm_rope(ws.k_raw, ss_k, pk["gk"], eps, k_dst, rope=rp, grid=grid, tok0=row0, out_row_off=row0)
@@ -357,16 +419,25 @@ class CausalWanAttentionBlock(nn.Module):
         fs, ft = (film[0].reshape(-1, C), film[1].reshape(-1, C)) if film is not None else (None, None)
         if fs is not None:
             fs, ft = fs.to(BF16).contiguous(), ft.to(BF16).contiguous()
-        kernels.linear_residual(ws.attn, pk["wo"], pk["bo"], xf, gate=em[2], film_scale=fs, film_shift=ft)
+        if "wo_mx" in pk:
+            kernels.mx_quantize(ws.attn, data=ws.hq, scales=ws.hs)
+            kernels.mx_linear_residual(ws.hq, ws.hs, *pk["wo_mx"], pk["bo"], xf, gate=em[2], film_scale=fs,
+                                       film_shift=ft)
+        else:
+            kernels.linear_residual(ws.attn, pk["wo"], pk["bo"], xf, gate=em[2], film_scale=fs, film_shift=ft)
         mark("o_proj_film")
 
         # cross-attention
-        if self.cross_attn_norm:
+        if not self.cross_attn_norm:
+            raise ValueError("cross_attn_norm=False is not supported by the B200 block")
+        if "wcq_mx" in pk:
+            kernels.layernorm_affine_mx(xf, eps, pk["n3w"], pk["n3b"], ws.hq, ws.hs)
+            mark("ln3")
+            kernels.mx_linear_rowss(ws.hq, ws.hs, *pk["wcq_mx"], pk["bcq"], ws.q_raw, ss_q)
+        else:
             kernels.layernorm_mod(xf, eps, ws.h, weight=pk["n3w"], bias=pk["n3b"])
             mark("ln3")
-        else:
-            raise ValueError("cross_attn_norm=False is not supported by the B200 block")
-        kernels.linear_rowss(ws.h, pk["wcq"], pk["bcq"], ws.q_raw, ss_q)
+            kernels.linear_rowss(ws.h, pk["wcq"], pk["bcq"], ws.q_raw, ss_q)
         kernels.rmsnorm_rope(ws.q_raw, ss_q, pk["gcq"], eps, ws.q)
         mark("cross_q")
         T = crossattn_cache["k"].numel() // C
@@ -377,7 +448,11 @@ class CausalWanAttentionBlock(nn.Module):
             kc, vc, bias = kc[:n], vc[:n], crossattn_cache["mult"]
         kernels.chunk_attention(ws.q, [kc], [vc], key_bias=bias, out=ws.attn)
         mark("cross_attn")
-        kernels.linear_residual(ws.attn, pk["wco"], pk["bco"], xf)
+        if "wco_mx" in pk:
+            kernels.mx_quantize(ws.attn, data=ws.hq, scales=ws.hs)
+            kernels.mx_linear_residual(ws.hq, ws.hs, *pk["wco_mx"], pk["bco"], xf)
+        else:
+            kernels.linear_residual(ws.attn, pk["wco"], pk["bco"], xf)
         mark("cross_o")
 
         # FFN

@@ -90,14 +90,16 @@ def _fp32_names(model):
 
 @torch.no_grad()
 def load_model(checkpoint_dir, subfolder="transformers", config=None, device="cuda", ffn_mx=False, cross_dedup=0,
-               strict=True, pack=True, **overrides):
+               strict=True, pack=True, lin_mx=False, lin_mx_skip=(), **overrides):
     """CausalWanModel with the checkpoint's weights on `device`, packed for the kernels. The model is built on
-    the meta device and materialised once in its final dtypes (no fp32 copy of the bf16 weights). strict:
+    the meta device and materialised once in its final dtypes (no fp32 copy of the bf16 weights). ffn_mx /
+    lin_mx / lin_mx_skip: LINGBOT_FFN_MX / LINGBOT_LIN_MX / LINGBOT_LIN_MX_SKIP (weights quantised at prepare). strict:
     every model parameter must come from the checkpoint (the reference only warns about missing keys);
     unexpected checkpoint keys are reported in the returned list either way. pack=False skips the kernel
     packing (prepare(), CUDA only)."""
     dit_dir = resolve_dit_dir(checkpoint_dir, subfolder)
-    kw = model_kwargs(dit_dir, config, ffn_mx=ffn_mx, cross_dedup=cross_dedup, **overrides)
+    kw = model_kwargs(dit_dir, config, ffn_mx=ffn_mx, cross_dedup=cross_dedup, lin_mx=lin_mx,
+                      lin_mx_skip=tuple(lin_mx_skip), **overrides)
     with torch.device("meta"):
         model = CausalWanModel(**kw)
     fp32 = _fp32_names(model)

@@ -3,8 +3,13 @@
 // and returns a partial row statistic; tile_done() receives the sum over the tile's chunks.
 //   EpiStore     bias + bf16 store into up to three column regions, optional row sums of squares
 //   EpiResidual  x += bf16(acc + b) * gate, then optional FiLM x = (1 + s) * x + t on the fp32 residual
-//   EpiGelu      GELU_tanh(bf16(acc) + b) as bf16, optionally MXFP8 quantise-dequantised
-//   EpiGeluMX    GELU_tanh(bf16(acc) + b) quantised to MXFP8 codes + E8M0 scales (the next GEMM's A operand)
+//   EpiAct       bf16(act(bf16(acc + b))) [+ addend]: the camera-FiLM MLP layers
+//   EpiGelu      GELU_tanh(bf16(acc + b)) as bf16, or GELU_tanh(bf16(bf16(acc) + b)) MXFP8 quantise-dequantised
+//   EpiGeluMX    GELU_tanh(bf16(bf16(acc) + b)) quantised to MXFP8 codes + E8M0 scales (the next GEMM's A operand)
+// round_acc (EpiStore, EpiResidual, EpiAct): the accumulator is rounded to bf16 before the bias is added, the
+// rounding points of an MXFP8 Linear in the reference (kernels/ffn_mx.py mm() returns bf16, then `y + bias` in
+// bf16, wan/modules/model_fast.py:1403-1410, :1602-1610); without it bias and accumulator meet in fp32 once
+// (nn.Linear).
 #pragma once
 #include "lbw_common.cuh"
 #include "mx_common.cuh"
@@ -20,6 +25,7 @@ struct EpiStore {
   int region_cols;       // columns per region
   int ss_per_chunk;      // regions not aligned to the 256-column tile: accumulate per 32-column chunk
   const __nv_bfloat16* bias;  // [N] (nullable)
+  int round_acc;
 
   LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
     int r = col / region_cols;
@@ -41,8 +47,10 @@ struct EpiStore {
       }
 #pragma unroll
       for (int q = 0; q < 8; q += 2) {
-        float y0 = bf16_round(v[e + q] + b[q]);
-        float y1 = bf16_round(v[e + q + 1] + b[q + 1]);
+        const float a0 = round_acc ? bf16_round(v[e + q]) : v[e + q];
+        const float a1 = round_acc ? bf16_round(v[e + q + 1]) : v[e + q + 1];
+        float y0 = bf16_round(a0 + b[q]);
+        float y1 = bf16_round(a1 + b[q + 1]);
         ssum += y0 * y0 + y1 * y1;
         pk[(e + q) / 2] = pack_bf16(y0, y1);
       }
@@ -62,15 +70,15 @@ struct EpiStore {
   }
 };
 
-// FILM = false: no FiLM operands (the MXFP8 FFN-down GEMM). That GEMM's epilogue holds 128 accumulators per
-// thread, so its chunks are read in four 8-column rounds to stay inside the register budget (wider rounds
-// spilled and measured slower there).
-template <bool FILM>
+// FILM = false: no FiLM operands (the MXFP8 FFN-down GEMM, cross-o).
+// WARP: the bf16 GEMM (o-projection, cross-o) hands each warp's 32 rows x 32 columns to chunk_warp(), which
+// transposes them through WARP_SMEM bytes of shared memory per warp so that the residual and FiLM rows are read
+// and written with coalesced 128-byte accesses. The MXFP8 GEMM has no shared memory left for it (WARP = false):
+// its epilogue holds 128 accumulators per thread, so chunk() reads them in four 8-column rounds to stay inside
+// the register budget (wider rounds spilled and measured slower there).
+template <bool FILM, bool WARP = FILM>
 struct EpiResidualT {
-  // FILM: the bf16 GEMM (o-projection, cross-o) hands each warp's 32 rows x 32 columns to chunk_warp(), which
-  // transposes them through this much shared memory per warp so that the residual and FiLM rows are read and
-  // written with coalesced 128-byte accesses. The MXFP8 GEMM (FILM = false) has no shared memory left for it.
-  static constexpr int WARP_SMEM = FILM ? 32 * 33 * 4 : 0;
+  static constexpr int WARP_SMEM = WARP ? 32 * 33 * 4 : 0;
   float* x;                          // [M, ldx] fp32 residual, updated in place
   long long ldx;
   const __nv_bfloat16* bias;         // [N] nullable
@@ -78,6 +86,9 @@ struct EpiResidualT {
   const __nv_bfloat16* film_scale;   // [M, N] nullable
   const __nv_bfloat16* film_shift;   // [M, N] (with film_scale)
   long long ldf;
+  int round_acc;
+
+  LBW_DEV float acc(float v) const { return round_acc ? bf16_round(v) : v; }
 
   // Columns [off, off + W) of the chunk. Every global read is issued before the first store (the stores may
   // alias those rows as far as the compiler knows), so a part costs one memory round trip.
@@ -104,7 +115,7 @@ struct EpiResidualT {
         const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + col + off + e));
         const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[off + e + q] + __bfloat162float(bp[q]));
+        for (int q = 0; q < 8; ++q) y[q] = bf16_round(acc(v[off + e + q]) + __bfloat162float(bp[q]));
       } else {
 #pragma unroll
         for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[off + e + q]);
@@ -143,7 +154,7 @@ struct EpiResidualT {
         const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + col + e));
         const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q] + __bfloat162float(bp[q]));
+        for (int q = 0; q < 8; ++q) y[q] = bf16_round(acc(v[e + q]) + __bfloat162float(bp[q]));
       } else {
 #pragma unroll
         for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q]);
@@ -197,7 +208,7 @@ struct EpiResidualT {
   }
 
   LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
-    if constexpr (FILM) {
+    if constexpr (WARP) {
       part<32>(row, col, 0, v);
     } else {
 #pragma unroll
@@ -224,7 +235,8 @@ struct EpiGelu {
       const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        float u = bf16_round(bf16_round(v[e + q]) + __bfloat162float(bp[q]));
+        // MX (qdq): the matmul's bf16 result, then + bias in bf16; plain Linear: one rounding
+        float u = bf16_round((qdq ? bf16_round(v[e + q]) : v[e + q]) + __bfloat162float(bp[q]));
         g[e + q] = bf16_round(gelu_tanh_fast(u));
       }
     }
@@ -252,6 +264,7 @@ struct EpiAct {
   const __nv_bfloat16* bias;    // [N] nullable
   const __nv_bfloat16* addend;  // [M, ldo] nullable
   int silu;
+  int round_acc;
 
   LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
     const long long off = (long long)row * ldo + col;
@@ -279,7 +292,7 @@ struct EpiAct {
         float y[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          float t = bf16_round(v[e + q + u] + b[q + u]);
+          float t = bf16_round((round_acc ? bf16_round(v[e + q + u]) : v[e + q + u]) + b[q + u]);
           if (silu) t = bf16_round(t / (1.f + __expf(-t)));
           if (addend) t = bf16_round(t + a[q + u]);
           y[u] = t;

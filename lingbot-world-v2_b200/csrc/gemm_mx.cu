@@ -2,6 +2,7 @@
 // -> fp32 (TMEM) -> fused epilogue. This is the FFN of the causal-fast block with LINGBOT_FFN_MX=1:
 // ffn_mx.mm (kernels/ffn_mx.py:159-182), the bias + GELU(tanh) epilogue of ffn_epi.bias_gelu_pad
 // (kernels/ffn_epi.py:15-37) and the gated residual x + y * e5 (wan/modules/model_fast.py:3110-3111).
+// With LINGBOT_LIN_MX=1 the block's other Linears (q|k|v, o, cross q/k/v/o, camera FiLM MLP) run on it too.
 //
 //   A [M, K] codes + scales (activations),  W [N, K] codes + scales (nn.Linear layout), K % 128 == 0.
 //   Scales use the tiled layout of lbw_mx_quantize: 512-byte atoms of 128 rows x 4 scales (row-block
@@ -281,6 +282,7 @@ int lbw_mx_linear(const void* a, const void* a_scales, const void* w, const void
   e.ld[0] = e.ld[1] = e.ld[2] = n;
   e.region_cols = n;
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.round_acc = 1;
   return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -306,6 +308,87 @@ int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, c
   e.ldx = n;
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   e.gate = gate;
+  e.round_acc = 1;
+  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ---- the other block Linears in MXFP8 (LINGBOT_LIN_MX, wan/modules/model_fast.py:1266-1269, :1442-1494): each is
+// y = bf16(mm(x, W)) + b in bf16 (_mx_matmul :1403-1410), so every epilogue below rounds the accumulator first.
+
+int lbw_mx_qkv_proj(const void* h, const void* h_scales, const void* w_qkv, const void* w_qkv_scales,
+                    const void* b_qkv, int m, int c, void* q_raw, void* k_raw, float* ss_q, float* ss_k, void* v_out,
+                    long long ldv, int v_row_off, void* stream) {
+  if (!q_raw || !k_raw || !v_out || !ss_q || !ss_k) return set_error(LBW_ERR_INVALID, "lbw_mx_qkv_proj: null pointer");
+  if (c % mxg::BK) return set_error(LBW_ERR_SHAPE, "lbw_mx_qkv_proj: dim %d must be a multiple of %d", c, mxg::BK);
+  if (!ok16mx(q_raw) || !ok16mx(k_raw) || !ok16mx(v_out) || !ok16mx(b_qkv) || ldv % 8 || v_row_off < 0)
+    return set_error(LBW_ERR_ALIGN, "lbw_mx_qkv_proj: alignment");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int err = cuda_check(cudaMemsetAsync(ss_q, 0, sizeof(float) * m, s), "ss clear");
+  if (!err) err = cuda_check(cudaMemsetAsync(ss_k, 0, sizeof(float) * m, s), "ss clear");
+  if (err) return err;
+  EpiStore e{};
+  e.out[0] = reinterpret_cast<__nv_bfloat16*>(q_raw);
+  e.out[1] = reinterpret_cast<__nv_bfloat16*>(k_raw);
+  e.out[2] = reinterpret_cast<__nv_bfloat16*>(v_out);
+  e.ld[0] = c; e.ld[1] = c; e.ld[2] = ldv;
+  e.row_off[2] = v_row_off;
+  e.ss[0] = ss_q; e.ss[1] = ss_k; e.ss[2] = nullptr;
+  e.region_cols = c;
+  e.ss_per_chunk = (c % 256) != 0;   // a region boundary inside a 256-column tile: sums per 32-column chunk
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(b_qkv);
+  e.round_acc = 1;
+  return launch_gemm_mx(h, h_scales, w_qkv, w_qkv_scales, m, 3 * c, c, e, s);
+}
+
+int lbw_mx_linear_rowss(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                        int m, int n, int k, void* out, float* ss, void* stream) {
+  if (!out || !ss) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_rowss: null pointer");
+  if (!ok16mx(out) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_rowss: alignment");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int err = cuda_check(cudaMemsetAsync(ss, 0, sizeof(float) * m, s), "ss clear");
+  if (err) return err;
+  EpiStore e{};
+  e.out[0] = e.out[1] = e.out[2] = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ld[0] = e.ld[1] = e.ld[2] = n;
+  e.ss[0] = ss;
+  e.region_cols = n;
+  e.ss_per_chunk = (n % 256) != 0;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.round_acc = 1;
+  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, s);
+}
+
+int lbw_mx_linear_residual_film(const void* a, const void* a_scales, const void* w, const void* w_scales,
+                                const void* bias, int m, int n, int k, float* x, const float* gate,
+                                const void* film_scale, const void* film_shift, void* stream) {
+  if (!x) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual_film: null residual");
+  if ((film_scale == nullptr) != (film_shift == nullptr))
+    return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual_film: FiLM needs both scale and shift");
+  if (!ok16mx(x) || !ok16mx(gate) || !ok16mx(bias) || !ok16mx(film_scale) || !ok16mx(film_shift))
+    return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_residual_film: alignment");
+  EpiResidualT<true, false> e{};
+  e.x = x;
+  e.ldx = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.gate = gate;
+  e.film_scale = reinterpret_cast<const __nv_bfloat16*>(film_scale);
+  e.film_shift = reinterpret_cast<const __nv_bfloat16*>(film_shift);
+  e.ldf = n;
+  e.round_acc = 1;
+  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_mx_linear_act(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                      const void* addend, int silu, int m, int n, int k, void* out, void* stream) {
+  if (!out) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_act: null output");
+  if (!ok16mx(out) || !ok16mx(bias) || !ok16mx(addend)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_act: alignment");
+  EpiAct e{};
+  e.out = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ldo = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.addend = reinterpret_cast<const __nv_bfloat16*>(addend);
+  e.silu = silu;
+  e.round_acc = 1;
   return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
 }
 

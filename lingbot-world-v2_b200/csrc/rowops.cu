@@ -192,6 +192,20 @@ using namespace lbw;
 
 extern "C" {
 
+int lbw_layernorm_affine_mx(const float* x, int m, int c, float eps, const float* weight, const float* bias,
+                            void* data, void* scales, void* stream) {
+  if (!x || !data || !scales || !weight || !bias) return set_error(LBW_ERR_INVALID, "layernorm_affine_mx: null pointer");
+  if (m <= 0 || c <= 0 || c % 128 || c > LN_MAXV * ROW_THREADS * 4)
+    return set_error(LBW_ERR_SHAPE, "layernorm_affine_mx: width %d must be a multiple of 128 and <= %d", c,
+                     LN_MAXV * ROW_THREADS * 4);
+  if (!aligned(x, 16) || !aligned(data, 16) || !aligned(weight, 16) || !aligned(bias, 16))
+    return set_error(LBW_ERR_ALIGN, "layernorm_affine_mx: x, data, weight and bias need 16-byte alignment");
+  layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, c, eps, nullptr, nullptr, weight, bias, 1, nullptr, reinterpret_cast<uint8_t*>(data),
+      reinterpret_cast<uint8_t*>(scales));
+  return cuda_check(cudaGetLastError(), "layernorm_affine_mx launch");
+}
+
 int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scale, const float* shift,
                       const float* weight, const float* bias, int mx_qdq, void* out, void* stream) {
   if (!x || !out) return set_error(LBW_ERR_INVALID, "layernorm_mod: null pointer");

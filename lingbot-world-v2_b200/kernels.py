@@ -264,14 +264,21 @@ def rmsnorm_rope(x, ss, gamma, eps, out, rope=None, grid=None, tok0=0, out_row_o
     return out
 
 
-def mx_quantize(x, dequant=False):
-    """x [rows, K] bf16 -> (data uint8 [rows, K] E4M3 codes, scales uint8 tiled, dequant bf16 or None)."""
-    require_cuda(x)
+def mx_quantize(x, dequant=False, data=None, scales=None):
+    """x [rows, K] bf16 -> (data uint8 [rows, K] E4M3 codes, scales uint8 tiled, dequant bf16 or None).
+    data / scales: optional output buffers (mx_buffers(rows, K))."""
+    require_cuda(x, data, scales)
     _c(x, BF16)
     rows, k = x.shape
     rows_pad = (rows + 127) // 128 * 128
-    data = torch.empty(rows, k, dtype=torch.uint8, device=x.device)
-    scales = torch.empty(rows_pad * (k // 32), dtype=torch.uint8, device=x.device)
+    if (data is None) != (scales is None):
+        raise ValueError("mx_quantize: give both data and scales, or neither")
+    if data is None:
+        data = torch.empty(rows, k, dtype=torch.uint8, device=x.device)
+        scales = torch.empty(rows_pad * (k // 32), dtype=torch.uint8, device=x.device)
+    elif (data.shape != (rows, k) or data.dtype != torch.uint8 or not data.is_contiguous()
+          or scales.dtype != torch.uint8 or scales.numel() < rows_pad * (k // 32)):
+        raise ValueError("mx_quantize: output buffers do not match x")
     deq = torch.empty_like(x) if dequant else None
     check(load().lbw_mx_quantize(ptr(x), rows, k, ptr(data), ptr(scales), ptr(deq), stream_of(x.device)),
           "mx_quantize")
@@ -293,6 +300,18 @@ def layernorm_mod_mx(x, eps, scale, shift, data, scales):
         raise ValueError("layernorm_mod_mx: output buffers do not match x")
     check(load().lbw_layernorm_mod_mx(ptr(x), m, c, ctypes.c_float(eps), ptr(scale), ptr(shift), ptr(data),
                                       ptr(scales), stream_of(x.device)), "layernorm_mod_mx")
+    return data, scales
+
+
+def layernorm_affine_mx(x, eps, weight, bias, data, scales):
+    """MXFP8 codes + tiled scales of LN(x) * weight + bias (norm3 before an MXFP8 cross_attn.q)."""
+    require_cuda(x, weight, bias, data, scales)
+    _c(x, torch.float32), _c(weight, torch.float32), _c(bias, torch.float32)
+    m, c = x.shape
+    if data.shape != (m, c) or scales.numel() < (m + 127) // 128 * 128 * (c // 32):
+        raise ValueError("layernorm_affine_mx: output buffers do not match x")
+    check(load().lbw_layernorm_affine_mx(ptr(x), m, c, ctypes.c_float(eps), ptr(weight), ptr(bias), ptr(data),
+                                         ptr(scales), stream_of(x.device)), "layernorm_affine_mx")
     return data, scales
 
 
@@ -325,10 +344,57 @@ def mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales):
     return out, out_scales
 
 
-def mx_linear_residual(a, a_s, w, w_s, bias, x, gate=None):
+def mx_linear_residual(a, a_s, w, w_s, bias, x, gate=None, film_scale=None, film_shift=None):
     m, n, k = _mx_check(a, a_s, w, w_s)
+    require_cuda(x, gate, film_scale, film_shift)
     if x.shape != (m, n) or x.dtype != torch.float32:
         raise ValueError("mx_linear_residual: x must be fp32 [m, n]")
-    check(load().lbw_mx_linear_residual(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(x), ptr(gate),
-                                        stream_of(a.device)), "mx_linear_residual")
+    if film_scale is None and film_shift is None:
+        check(load().lbw_mx_linear_residual(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(x), ptr(gate),
+                                            stream_of(a.device)), "mx_linear_residual")
+        return x
+    for t in (film_scale, film_shift):
+        if t is None or t.shape != (m, n) or t.dtype != BF16 or not t.is_contiguous():
+            raise ValueError("mx_linear_residual: FiLM tensors must both be contiguous bf16 [m, n]")
+    check(load().lbw_mx_linear_residual_film(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(x),
+                                             ptr(gate), ptr(film_scale), ptr(film_shift), stream_of(a.device)),
+          "mx_linear_residual_film")
     return x
+
+
+def mx_qkv_proj(hq, hs, w_qkv, w_qkv_s, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, v_row_off=0):
+    """MXFP8 counterpart of qkv_proj: hq/hs the MXFP8 operand of the normed rows, w_qkv/w_qkv_s of [Wq; Wk; Wv]."""
+    m, n, c = _mx_check(hq, hs, w_qkv, w_qkv_s)
+    require_cuda(b_qkv, q_raw, k_raw, ss_q, ss_k, v_out)
+    v2 = _rows(v_out)
+    if n != 3 * c or q_raw.shape != (m, c) or k_raw.shape != (m, c) or ss_q.numel() < m or ss_k.numel() < m:
+        raise ValueError("mx_qkv_proj: shape mismatch")
+    if v2.shape[1] != c or v_row_off < 0 or v_row_off + m > v2.shape[0]:
+        raise ValueError(f"mx_qkv_proj: rows {v_row_off}..{v_row_off + m} outside the V destination "
+                         f"({v2.shape[0]} rows)")
+    check(load().lbw_mx_qkv_proj(ptr(hq), ptr(hs), ptr(w_qkv), ptr(w_qkv_s), ptr(b_qkv), m, c, ptr(q_raw), ptr(k_raw),
+                                 ptr(ss_q), ptr(ss_k), ptr(v2), v2.stride(0), v_row_off, stream_of(hq.device)),
+          "mx_qkv_proj")
+
+
+def mx_linear_rowss(a, a_s, w, w_s, bias, out, ss):
+    m, n, k = _mx_check(a, a_s, w, w_s)
+    require_cuda(bias, out, ss)
+    if out.shape != (m, n) or out.dtype != BF16 or not out.is_contiguous() or ss.numel() < m:
+        raise ValueError("mx_linear_rowss: shape mismatch")
+    check(load().lbw_mx_linear_rowss(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(out), ptr(ss),
+                                     stream_of(a.device)), "mx_linear_rowss")
+    return out
+
+
+def mx_linear_act(a, a_s, w, w_s, bias=None, addend=None, silu=False, out=None):
+    """MXFP8 counterpart of linear_act (camera-FiLM MLP layers)."""
+    m, n, k = _mx_check(a, a_s, w, w_s)
+    require_cuda(bias, addend, out)
+    if addend is not None and (addend.shape != (m, n) or addend.dtype != BF16 or not addend.is_contiguous()):
+        raise ValueError("mx_linear_act: addend must be contiguous bf16 [m, n]")
+    if out is None:
+        out = torch.empty(m, n, dtype=BF16, device=a.device)
+    check(load().lbw_mx_linear_act(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), ptr(addend), int(bool(silu)), m, n,
+                                   k, ptr(out), stream_of(a.device)), "mx_linear_act")
+    return out

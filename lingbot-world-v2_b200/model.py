@@ -21,12 +21,14 @@ CONFIGS = {
 
 
 class BlockStack(nn.Module):
-    def __init__(self, num_layers, dim, ffn_dim, num_heads, eps=1e-6, ffn_mx=True, cross_dedup=0):
+    def __init__(self, num_layers, dim, ffn_dim, num_heads, eps=1e-6, ffn_mx=True, cross_dedup=0, lin_mx=False,
+                 lin_mx_skip=()):
         super().__init__()
         self.dim, self.ffn_dim, self.num_heads = dim, ffn_dim, num_heads
         self.blocks = nn.ModuleList([
             CausalWanAttentionBlock(dim, ffn_dim, num_heads, qk_norm=True, cross_attn_norm=True, eps=eps,
-                                    ffn_mx=ffn_mx, cross_dedup=cross_dedup) for _ in range(num_layers)])
+                                    ffn_mx=ffn_mx, cross_dedup=cross_dedup, lin_mx=lin_mx, lin_mx_skip=lin_mx_skip)
+            for _ in range(num_layers)])
         self._ws = None
 
     def prepare(self):
@@ -48,11 +50,11 @@ class BlockStack(nn.Module):
         return xf
 
     @classmethod
-    def synthetic(cls, num_layers, dim, ffn_dim, num_heads, device, seed=0, ffn_mx=True, peaked=False):
+    def synthetic(cls, num_layers, dim, ffn_dim, num_heads, device, seed=0, ffn_mx=True, peaked=False, lin_mx=False):
         """Build on the meta device, materialise bf16 weights on `device`, fill with the benchmark
         distributions and pack them for the kernels (source copies freed)."""
         with torch.device("meta"):
-            st = cls(num_layers, dim, ffn_dim, num_heads, ffn_mx=ffn_mx)
+            st = cls(num_layers, dim, ffn_dim, num_heads, ffn_mx=ffn_mx, lin_mx=lin_mx)
         st = st.to(torch.bfloat16).to_empty(device=device)
         for blk in st.blocks:
             blk.modulation.data = blk.modulation.data.float()
@@ -130,7 +132,8 @@ class CausalWanModel(nn.Module):
 
     def __init__(self, model_type="i2v", patch_size=(1, 2, 2), text_len=512, in_dim=16, dim=2048, ffn_dim=8192,
                  freq_dim=256, text_dim=4096, out_dim=16, num_heads=16, num_layers=32, local_attn_size=-1,
-                 sink_size=0, qk_norm=True, cross_attn_norm=True, eps=1e-6, ffn_mx=False, cross_dedup=0):
+                 sink_size=0, qk_norm=True, cross_attn_norm=True, eps=1e-6, ffn_mx=False, cross_dedup=0,
+                 lin_mx=False, lin_mx_skip=()):
         super().__init__()
         if model_type not in ("t2v", "i2v"):
             raise ValueError("model_type is 't2v' or 'i2v'")
@@ -149,7 +152,8 @@ class CausalWanModel(nn.Module):
         self.time_projection = nn.Sequential(nn.SiLU(), nn.Linear(dim, dim * 6))
         self.blocks = nn.ModuleList([
             CausalWanAttentionBlock(dim, ffn_dim, num_heads, local_attn_size, sink_size, qk_norm, cross_attn_norm, eps,
-                                    ffn_mx=ffn_mx, cross_dedup=cross_dedup) for _ in range(num_layers)])
+                                    ffn_mx=ffn_mx, cross_dedup=cross_dedup, lin_mx=lin_mx, lin_mx_skip=lin_mx_skip)
+            for _ in range(num_layers)])
         self.head = CausalHead(dim, out_dim, patch_size, eps)
         self.freqs = None
         self._packed = None

@@ -16,6 +16,8 @@ block takes off-Neuron, keeping the reference's rounding points:
     cross_dedup (attention.py:516-554)
   * h = (LN(x) * (1 + e4) + e3).to(bf16) (:3101); FFN Linear -> GELU(tanh) -> Linear (:2870-2872) or the
     MXFP8 FFN (_ffn_mx :1584-1611) emulated with oracle.mx; x = x + y * e5 (:3110-3111).
+  * LINGBOT_LIN_MX (:1266-1269, :1442-1494): the Linears named in mx_linears (q/k/v/o of both attentions, the
+    camera-FiLM MLP) become _mx_matmul (:1403-1410): bf16(mm(x, W)) + b in bf16, emulated with oracle.mx.
 """
 import math
 
@@ -82,6 +84,18 @@ def linear(x, w, b):
     return y.to(torch.bfloat16)
 
 
+def mx_matmul(x, w, b):
+    """_mx_matmul (model_fast.py:1403-1410): the MXFP8 matmul's bf16 result, then + bias in bf16."""
+    y = mxo.mx_linear(x.to(torch.bfloat16), w)
+    return y if b is None else (y.float() + b.float()).to(torch.bfloat16)
+
+
+def block_linear(p, name, x, mx_linears=()):
+    """Block Linear `name` (e.g. "self_attn.q") on x: nn.Linear, or _mx_matmul when LINGBOT_LIN_MX quantises it."""
+    w, b = p[name + ".weight"], p.get(name + ".bias")
+    return mx_matmul(x, w, b) if name in mx_linears else linear(x, w, b)
+
+
 def rms_norm(x, weight, eps):
     """WanRMSNorm: fp32 normalisation, cast back to x's dtype, times the (bf16) weight."""
     xf = x.float()
@@ -122,21 +136,23 @@ def cross_dedup_bias(k, v, kc):
 # --------------------------------------------------------------------------------------------
 # block
 # --------------------------------------------------------------------------------------------
-def cross_kv(p, context, eps=1e-6):
+def cross_kv(p, context, eps=1e-6, mx_linears=()):
     """Cross-attention K/V of the text context, filled on the first call (model_fast.py:2784-2798)."""
     C = context.shape[-1]
     H = C // HEAD_DIM
     ctx = context.reshape(-1, C).to(torch.bfloat16)
-    k = rms_norm(linear(ctx, p["cross_attn.k.weight"], p["cross_attn.k.bias"]), p["cross_attn.norm_k.weight"], eps)
-    v = linear(ctx, p["cross_attn.v.weight"], p["cross_attn.v.bias"])
+    k = rms_norm(block_linear(p, "cross_attn.k", ctx, mx_linears), p["cross_attn.norm_k.weight"], eps)
+    v = block_linear(p, "cross_attn.v", ctx, mx_linears)
     return k.view(-1, H, HEAD_DIM), v.view(-1, H, HEAD_DIM)
 
 
 def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, mx=False, eps=1e-6,
-                  dedup_kc=None, return_all=False):
+                  dedup_kc=None, return_all=False, mx_linears=()):
     """One block. x [Lq, C] fp32; e0 [6, C] fp32; k_lead/v_lead lists of [L_i, H, d] bf16;
-    ctx_k/ctx_v [T, H, d] bf16; cos/sin [Lq, 64] fp32; film = (scale, shift) [Lq, C] bf16.
+    ctx_k/ctx_v [T, H, d] bf16; cos/sin [Lq, 64] fp32; film = (scale, shift) [Lq, C] bf16; mx: MXFP8 FFN;
+    mx_linears: names of the other Linears in MXFP8 (LINGBOT_LIN_MX).
     Returns x_out (and, with return_all, the intermediates)."""
+    lin = lambda name, t: block_linear(p, name, t, mx_linears)  # noqa: E731
     Lq, C = x.shape
     H = C // HEAD_DIM
     e = (p["modulation"].reshape(6, C).float() + e0.float()).chunk(6, dim=0)
@@ -144,38 +160,36 @@ def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, m
 
     # self-attention
     h = (layer_norm(x, eps) * (1 + e[1]) + e[0]).to(torch.bfloat16)
-    q = rms_norm(linear(h, p["self_attn.q.weight"], p["self_attn.q.bias"]), p["self_attn.norm_q.weight"], eps)
-    k = rms_norm(linear(h, p["self_attn.k.weight"], p["self_attn.k.bias"]), p["self_attn.norm_k.weight"], eps)
-    v = linear(h, p["self_attn.v.weight"], p["self_attn.v.bias"]).view(Lq, H, HEAD_DIM)
+    q = rms_norm(lin("self_attn.q", h), p["self_attn.norm_q.weight"], eps)
+    k = rms_norm(lin("self_attn.k", h), p["self_attn.norm_k.weight"], eps)
+    v = lin("self_attn.v", h).view(Lq, H, HEAD_DIM)
     q = rope_apply(q.view(Lq, H, HEAD_DIM), cos, sin)
     k = rope_apply(k.view(Lq, H, HEAD_DIM), cos, sin)
     ks = torch.cat(list(k_lead) + [k], dim=0)
     vs = torch.cat(list(v_lead) + [v], dim=0)
     attn = attention(q, ks, vs)
-    y = linear(attn.reshape(Lq, C), p["self_attn.o.weight"], p["self_attn.o.bias"])
+    y = lin("self_attn.o", attn.reshape(Lq, C))
     x1 = x + y.float() * e[2]
     if film is not None:
         x1 = (1.0 + film[0]) * x1 + film[1]
 
     # cross-attention
     h3 = layer_norm(x1, eps, p["norm3.weight"].float(), p["norm3.bias"].float()).to(torch.bfloat16)
-    qc = rms_norm(linear(h3, p["cross_attn.q.weight"], p["cross_attn.q.bias"]), p["cross_attn.norm_q.weight"], eps)
+    qc = rms_norm(lin("cross_attn.q", h3), p["cross_attn.norm_q.weight"], eps)
     qc = qc.view(Lq, H, HEAD_DIM)
     if dedup_kc is not None:
         bias = cross_dedup_bias(ctx_k, ctx_v, dedup_kc)
         ca = attention(qc, ctx_k[:dedup_kc], ctx_v[:dedup_kc], key_bias=bias)
     else:
         ca = attention(qc, ctx_k, ctx_v)
-    x2 = x1 + linear(ca.reshape(Lq, C), p["cross_attn.o.weight"], p["cross_attn.o.bias"]).float()
+    x2 = x1 + lin("cross_attn.o", ca.reshape(Lq, C)).float()
 
     # FFN
     h2 = (layer_norm(x2, eps) * (1 + e[4]) + e[3]).to(torch.bfloat16)
-    if mx:
-        u = mxo.mx_linear(h2, p["ffn.0.weight"])
-        u = (u + p["ffn.0.bias"]).to(torch.bfloat16)
+    if mx or mx_linears:
+        u = mx_matmul(h2, p["ffn.0.weight"], p["ffn.0.bias"])
         g = F.gelu(u.float(), approximate="tanh").to(torch.bfloat16)
-        y2 = mxo.mx_linear(g, p["ffn.2.weight"])
-        y2 = y2 + p["ffn.2.bias"]
+        y2 = mx_matmul(g, p["ffn.2.weight"], p["ffn.2.bias"])
     else:
         u = linear(h2, p["ffn.0.weight"], p["ffn.0.bias"])
         g = F.gelu(u.float(), approximate="tanh").to(torch.bfloat16)
@@ -186,10 +200,11 @@ def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, m
     return x3
 
 
-def cam_film(p, c):
-    """CausalWanAttentionBlock.cam_film (model_fast.py:2882-2891): bf16 Linears, SiLU on the bf16 hidden,
-    the camera embedding added to layer 2's bf16 output. c [L, C] bf16 -> (scale, shift) bf16."""
-    h = F.silu(linear(c, p["cam_injector_layer1.weight"], p["cam_injector_layer1.bias"]).float()).to(torch.bfloat16)
-    h2 = (linear(h, p["cam_injector_layer2.weight"], p["cam_injector_layer2.bias"]) + c).to(torch.bfloat16)
-    return (linear(h2, p["cam_scale_layer.weight"], p["cam_scale_layer.bias"]),
-            linear(h2, p["cam_shift_layer.weight"], p["cam_shift_layer.bias"]))
+def cam_film(p, c, mx_linears=()):
+    """CausalWanAttentionBlock.cam_film (model_fast.py:2882-2891): bf16 Linears (or _mx_matmul under
+    LINGBOT_LIN_MX), SiLU on the bf16 hidden, the camera embedding added to layer 2's bf16 output.
+    c [L, C] bf16 -> (scale, shift) bf16."""
+    lin = lambda name, t: block_linear(p, name, t, mx_linears)  # noqa: E731
+    h = F.silu(lin("cam_injector_layer1", c).float()).to(torch.bfloat16)
+    h2 = (lin("cam_injector_layer2", h) + c).to(torch.bfloat16)
+    return lin("cam_scale_layer", h2), lin("cam_shift_layer", h2)

@@ -11,10 +11,11 @@ pytestmark = pytest.mark.gpu
 BF = torch.bfloat16
 
 
-def _build(case, p, dev, ffn_mx, dedup=0, mx_pipe="mxf8"):
+def _build(case, p, dev, ffn_mx, dedup=0, mx_pipe="mxf8", lin_mx=False, lin_mx_skip=()):
     import lbw_b200.block as B
     blk = B.CausalWanAttentionBlock(case.dim, case.ffn, case.heads, qk_norm=True, cross_attn_norm=True,
-                                    ffn_mx=ffn_mx, cross_dedup=dedup, mx_pipe=mx_pipe)
+                                    ffn_mx=ffn_mx, cross_dedup=dedup, mx_pipe=mx_pipe, lin_mx=lin_mx,
+                                    lin_mx_skip=lin_mx_skip)
     sd = blk.state_dict()
     for k, v in p.items():
         sd[k] = v.to(sd[k].dtype)
@@ -70,6 +71,29 @@ def test_block_mx_vs_oracle(cuda_dev, peaked, pipe):
     assert rel_l2(x, r["x"]) <= 1e-2 and max_abs(x, r["x"]) <= 5e-2
     assert rel_l2(x - inp["x"], r["x"] - inp["x"]) <= 2e-2
     assert rel_l2(k.view(-1, case.heads, 128), r["k"]) <= 1e-2
+
+
+@pytest.mark.parametrize("skip", [(), ("self_attn.o", "cross_attn.o", "cross_attn.k")])
+def test_block_lin_mx_vs_oracle(cuda_dev, skip):
+    """LINGBOT_LIN_MX: every block Linear on the MXFP8 GEMM (LINGBOT_LIN_MX_SKIP ones bf16) against the oracle's
+    _mx_matmul emulation, within the MX FFN's tolerance."""
+    import lbw_b200.block as B
+    case = BlockCase(dim=512, ffn=1024, grid=(3, 6, 10), n_lead=3, text_len=64, start_frame=9, seed=29, cam=True)
+    p, inp = make_case(case)
+    blk = _build(case, p, cuda_dev, ffn_mx=True, lin_mx=True, lin_mx_skip=skip)
+    x, k, v, cc = _run(blk, case, inp, cuda_dev)
+    names = [n for n in B.MX_LINEAR_NAMES if n not in skip]
+    cos, sin = ob.rope_grid(ob.rope_freqs(), case.grid, case.start_frame)
+    ck, cv = ob.cross_kv(p, inp["context"], mx_linears=names)
+    r = ob.block_forward(p, inp["x"], inp["e0"], inp["k_lead"], inp["v_lead"], ck, cv, cos, sin, film=inp["film"],
+                         mx=True, return_all=True, mx_linears=names)
+    assert rel_l2(x, r["x"]) <= 1e-2 and max_abs(x, r["x"]) <= 5e-2
+    assert rel_l2(x - inp["x"], r["x"] - inp["x"]) <= 2e-2
+    assert rel_l2(k.view(-1, case.heads, 128), r["k"]) <= 1e-2 and rel_l2(v.view(-1, case.heads, 128), r["v"]) <= 1e-2
+    assert rel_l2(cc["k"][0].cpu(), ck) <= 1e-2 and rel_l2(cc["v"][0].cpu(), cv) <= 1e-2
+    scale, shift = blk.cam_film(inp["cam"].unsqueeze(0).to(cuda_dev))
+    rs, rt = ob.cam_film(p, inp["cam"].to(BF), mx_linears=names)
+    assert rel_l2(scale[0], rs) < 1e-2 and rel_l2(shift[0], rt) < 1e-2
 
 
 def test_block_cross_dedup_vs_oracle(cuda_dev):

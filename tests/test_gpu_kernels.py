@@ -83,7 +83,8 @@ def test_linear_gelu(cuda_dev, qdq):
     b = (torch.randn(n, generator=g) * 0.05).to(BF)
     out = torch.empty(m, n, dtype=BF, device=cuda_dev)
     K.linear_gelu(a.to(cuda_dev), w.to(cuda_dev), b.to(cuda_dev), out, qdq)
-    u = ((a.float() @ w.float().t()).to(BF) + b).to(BF)
+    # plain Linear: one rounding of acc + b; the MX-emulating variant rounds the matmul first (ffn_mx.mm + bias)
+    u = ((a.float() @ w.float().t()).to(BF) + b).to(BF) if qdq else ob.linear(a, w, b)
     ref = F.gelu(u.float(), approximate="tanh").to(BF)
     if qdq:
         ref = omx.qdq(ref)

@@ -1,5 +1,5 @@
-"""MXFP8 block-scaled tcgen05 GEMMs (lbw_mx_linear*, lbw_layernorm_mod_mx) against the OCP-MX emulation
-of the oracle, through the C ABI."""
+"""MXFP8 block-scaled tcgen05 GEMMs (lbw_mx_*, lbw_layernorm_mod_mx, lbw_layernorm_affine_mx) against the
+OCP-MX emulation of the oracle, through the C ABI."""
 import pytest
 import torch
 import torch.nn.functional as F
@@ -32,8 +32,7 @@ def test_mx_linear_vs_emulation(cuda_dev, m, n, k):
     ad, as_, _ = K.mx_quantize(a.to(d))
     wd, ws, _ = K.mx_quantize(w.to(d))
     out = K.mx_linear(ad, as_, wd, ws, b.to(d))
-    ref = (omx.qdq(a) @ omx.qdq(w).t() + b.float()).to(BF)
-    assert rel_l2(out, ref) < 4e-3
+    assert rel_l2(out, ob.mx_matmul(a, w, b)) < 4e-3
 
 
 def test_mx_linear_gelu_emits_mx_codes(cuda_dev):
@@ -112,3 +111,88 @@ def test_mx_linear_residual_narrow_tiles(cuda_dev):
     K.mx_linear_residual(ad, as_, wd, ws, b.to(d), xd)
     y = (omx.qdq(a) @ omx.qdq(w).t() + b.float()).to(BF)
     assert rel_l2(xd - x.to(d), y.float()) < 5e-3
+
+
+# ---- the other block Linears in MXFP8 (LINGBOT_LIN_MX): y = bf16(mm(x, W)) + b in bf16 ----------------------
+
+def _mxq(t, d):
+    import lbw_b200.kernels as K
+    q, s, _ = K.mx_quantize(t.to(d))
+    return q, s
+
+
+def test_mx_qkv_proj_vs_emulation(cuda_dev):
+    import lbw_b200.kernels as K
+    m, c = 300, 512
+    h, w, b = _ab(m, 3 * c, c, 31)
+    d = cuda_dev
+    q_raw = torch.empty(m, c, dtype=BF, device=d)
+    k_raw = torch.empty(m, c, dtype=BF, device=d)
+    ss = torch.full((2, m), 7.0, device=d)           # cleared by the call
+    vbuf = torch.zeros(m + 40, c, dtype=BF, device=d)
+    K.mx_qkv_proj(*_mxq(h, d), *_mxq(w, d), b.to(d), q_raw, k_raw, ss[0], ss[1], vbuf, v_row_off=17)
+    ref = ob.mx_matmul(h, w, b)
+    assert rel_l2(q_raw, ref[:, :c]) < 4e-3 and rel_l2(k_raw, ref[:, c:2 * c]) < 4e-3
+    assert rel_l2(vbuf[17:17 + m], ref[:, 2 * c:]) < 4e-3
+    assert not vbuf[:17].any() and not vbuf[17 + m:].any()
+    for t, s in ((q_raw, ss[0]), (k_raw, ss[1])):
+        assert rel_l2(s, t.float().pow(2).sum(1)) < 1e-5
+
+
+def test_mx_linear_rowss_vs_emulation(cuda_dev):
+    import lbw_b200.kernels as K
+    m, n, k = 333, 768, 512
+    a, w, b = _ab(m, n, k, 33)
+    d = cuda_dev
+    out = torch.empty(m, n, dtype=BF, device=d)
+    ss = torch.full((m,), 3.0, device=d)
+    K.mx_linear_rowss(*_mxq(a, d), *_mxq(w, d), b.to(d), out, ss)
+    assert rel_l2(out, ob.mx_matmul(a, w, b)) < 4e-3
+    assert rel_l2(ss, out.float().pow(2).sum(1)) < 1e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(260, 512, 1024), (1350, 1024, 512)])
+def test_mx_linear_residual_film(cuda_dev, m, n, k):
+    import lbw_b200.kernels as K
+    a, w, b = _ab(m, n, k, 35)
+    g = torch.Generator().manual_seed(36)
+    x = torch.randn(m, n, generator=g)
+    gate = torch.randn(n, generator=g) * 0.1
+    fs = (torch.randn(m, n, generator=g) * 0.1).to(BF)
+    ft = (torch.randn(m, n, generator=g) * 0.1).to(BF)
+    d = cuda_dev
+    xd = x.to(d)
+    K.mx_linear_residual(*_mxq(a, d), *_mxq(w, d), b.to(d), xd, gate=gate.to(d), film_scale=fs.to(d),
+                         film_shift=ft.to(d))
+    x1 = x + ob.mx_matmul(a, w, b).float() * gate
+    ref = (1.0 + fs) * x1 + ft
+    assert rel_l2(xd, ref) < 1e-4 and rel_l2(xd.cpu() - x, ref - x) < 5e-3
+
+
+def test_mx_linear_act(cuda_dev):
+    import lbw_b200.kernels as K
+    m, n, k = 200, 512, 512
+    a, w, b = _ab(m, n, k, 37)
+    c = (torch.randn(m, n, generator=torch.Generator().manual_seed(38))).to(BF)
+    d = cuda_dev
+    aq, w_mx = _mxq(a, d), _mxq(w, d)
+    y = ob.mx_matmul(a, w, b)
+    h = K.mx_linear_act(*aq, *w_mx, b.to(d), silu=True)
+    assert rel_l2(h, F.silu(y.float()).to(BF)) < 5e-3
+    h2 = K.mx_linear_act(*aq, *w_mx, b.to(d), addend=c.to(d))
+    assert rel_l2(h2, (y + c).to(BF)) < 5e-3
+
+
+@pytest.mark.parametrize("c", [512, 5120])
+def test_layernorm_affine_mx(cuda_dev, c):
+    import lbw_b200.kernels as K
+    g = torch.Generator().manual_seed(39)
+    m = 131
+    x = torch.randn(m, c, generator=g) * 2 - 0.3
+    w3, b3 = 1 + torch.randn(c, generator=g) * 0.1, torch.randn(c, generator=g) * 0.1
+    dq, ds = K.mx_buffers(m, c, cuda_dev)
+    K.layernorm_affine_mx(x.to(cuda_dev), 1e-6, w3.to(cuda_dev), b3.to(cuda_dev), dq, ds)
+    h = ob.layer_norm(x, 1e-6, w3, b3).to(BF)
+    q, se = omx.quantize(h)
+    got = omx.dequantize(dq.cpu().view(torch.float8_e4m3fn), _untile(ds.cpu(), m, c))
+    assert rel_l2(got, omx.dequantize(q, se)) < 2e-3

@@ -155,3 +155,39 @@ def test_checkpoint_loader_rejects_missing_and_misshapen(tmp_path):
     save_file(t, str(path))
     with pytest.raises(ValueError, match="checkpoint shape"):
         ck.load_model(str(tmp_path), device="cpu", pack=False)
+
+
+def test_lin_mx_options():
+    """LINGBOT_LIN_MX / LINGBOT_LIN_MX_SKIP host logic: which Linears go to the MXFP8 GEMM."""
+    import lbw_b200.block as B
+    with torch.device("meta"):
+        blk = B.CausalWanAttentionBlock(256, 512, 2, cross_attn_norm=True, ffn_mx=False, lin_mx=True,
+                                        lin_mx_skip=("self_attn.o", "cam_scale_layer"))
+        assert blk.ffn_mx                      # LIN_MX implies the MXFP8 FFN
+        assert blk.mx_linears == frozenset(B.MX_LINEAR_NAMES) - {"self_attn.o", "cam_scale_layer"}
+        assert B.CausalWanAttentionBlock(256, 512, 2).mx_linears == frozenset()
+        with pytest.raises(ValueError, match="names no block Linear"):
+            B.CausalWanAttentionBlock(256, 512, 2, lin_mx=True, lin_mx_skip=("ffn.0",))
+        with pytest.raises(ValueError, match="all three or none"):
+            B.CausalWanAttentionBlock(256, 512, 2, lin_mx=True, lin_mx_skip=("self_attn.k",))
+        with pytest.raises(ValueError, match="mx_pipe"):
+            B.CausalWanAttentionBlock(256, 512, 2, lin_mx=True, mx_pipe="bf16")
+
+
+def test_oracle_lin_mx_changes_only_the_named_linears():
+    """The oracle's LINGBOT_LIN_MX emulation: MXFP8 Linears move the block output by the MX quantisation error
+    (a few percent of the update), and naming no Linear gives the MX-FFN block exactly."""
+    from oracle.inputs import BlockCase, make_case
+    import lbw_b200.block as B
+    case = BlockCase(dim=256, ffn=512, grid=(2, 4, 6), n_lead=1, text_len=32, seed=41)
+    p, inp = make_case(case)
+    cos, sin = ob.rope_grid(ob.rope_freqs(), case.grid, case.start_frame)
+    ck, cv = ob.cross_kv(p, inp["context"])
+    args = (p, inp["x"], inp["e0"], inp["k_lead"], inp["v_lead"], ck, cv, cos, sin)
+    base = ob.block_forward(*args, film=inp["film"], mx=True)
+    assert torch.equal(ob.block_forward(*args, film=inp["film"], mx=True, mx_linears=()), base)
+    ckm, cvm = ob.cross_kv(p, inp["context"], mx_linears=B.MX_LINEAR_NAMES)
+    allmx = ob.block_forward(p, inp["x"], inp["e0"], inp["k_lead"], inp["v_lead"], ckm, cvm, cos, sin,
+                             film=inp["film"], mx_linears=B.MX_LINEAR_NAMES)
+    d = (allmx - base).norm() / (base - inp["x"]).norm()
+    assert 1e-3 < d < 0.1
