@@ -284,6 +284,43 @@ def run_sweep(args):
             tf = 2.0 * m * C * n / (ms / 1e3) / 1e12
             print(json.dumps({"sweep": "bf16_gemm", "name": name, "m": m, "k": C, "n": n, "ms": ms, "tflops": tf,
                               "frac_of_peak": tf / peak, "peak": f"{src} bf16_tflops {peak}"}))
+    # the same Linears in MXFP8 (--lin-mx): activation quantiser, q|k|v, o-projection (+ gate + FiLM), cross-o
+    for m in ((10800, 1350) if only in ("all", "linmx") else ()):
+        h = torch.randn(m, C, generator=g, device=dev, dtype=bf)
+        hq, hs = K.mx_buffers(m, C, dev)
+        wqkv, wqkv_s, _ = K.mx_quantize((torch.randn(3 * C, C, generator=g, device=dev) * 0.02).to(bf))
+        bqkv = (torch.randn(3 * C, generator=g, device=dev) * 0.02).to(bf)
+        wo, wo_s, _ = K.mx_quantize((torch.randn(C, C, generator=g, device=dev) * 0.02).to(bf))
+        bo = (torch.randn(C, generator=g, device=dev) * 0.02).to(bf)
+        qr, kr, vv = (torch.empty(m, C, dtype=bf, device=dev) for _ in range(3))
+        ss = torch.zeros(2, m, device=dev)
+        xres = torch.randn(m, C, generator=g, device=dev)
+        gate = torch.randn(C, generator=g, device=dev) * 0.1
+        fs, ft = ((torch.randn(m, C, generator=g, device=dev) * 0.1).to(bf) for _ in range(2))
+        K.mx_quantize(h, data=hq, scales=hs)
+        F_ = 13824   # the MXFP8 FFN-down GEMM of the headline step (K = 13,824), for comparison
+        uq, us, _ = K.mx_quantize(torch.randn(m, F_, generator=g, device=dev, dtype=bf))
+        w2, w2_s, _ = K.mx_quantize((torch.randn(C, F_, generator=g, device=dev) * 0.02).to(bf))
+        for name, n, fn in (("mx_quantize", 0, lambda: K.mx_quantize(h, data=hq, scales=hs)),
+                            ("mx_qkv_rowss", 3 * C,
+                             lambda: K.mx_qkv_proj(hq, hs, wqkv, wqkv_s, bqkv, qr, kr, ss[0], ss[1], vv)),
+                            ("mx_o_proj_residual_film", C,
+                             lambda: K.mx_linear_residual(hq, hs, wo, wo_s, bo, xres, gate=gate, film_scale=fs,
+                                                          film_shift=ft)),
+                            ("mx_cross_o_residual", C, lambda: K.mx_linear_residual(hq, hs, wo, wo_s, bo, xres)),
+                            ("mx_ffn_down_residual", C,
+                             lambda: K.mx_linear_residual(uq, us, w2, w2_s, bo, xres, gate=gate))):
+            for _ in range(3):
+                fn()
+            ms = timed(fn, reps=3)
+            kk = F_ if name == "mx_ffn_down_residual" else C
+            rec = {"sweep": "lin_mx", "name": name, "m": m, "k": kk, "n": n, "ms": ms}
+            if n:
+                tf = 2.0 * m * kk * n / (ms / 1e3) / 1e12
+                rec.update(tflops=tf, frac_of_2x_bf16_peak=tf / (2 * peak), peak=f"{src} bf16_tflops {peak}")
+            else:
+                rec.update(gbs=(m * C * 2 + m * C + m * C // 32) / (ms / 1e3) / 1e9)
+            print(json.dumps(rec))
     return 0
 
 
@@ -298,7 +335,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="kernel sweep (BASELINE configs[4]) instead of the step")
-    ap.add_argument("--sweep-only", default="all", choices=["all", "attention", "mxfp8", "gemm"],
+    ap.add_argument("--sweep-only", default="all", choices=["all", "attention", "mxfp8", "gemm", "linmx"],
                     help="with --sweep: one family of points (gemm = the block's bf16 GEMMs at 10,800 and 1,350 rows)")
     ap.add_argument("--lin-mx", action="store_true",
                     help="every block Linear in MXFP8 (the reference's LINGBOT_LIN_MX option; not the headline config)")

@@ -71,14 +71,17 @@ struct EpiStore {
 };
 
 // FILM = false: no FiLM operands (the MXFP8 FFN-down GEMM, cross-o).
-// WARP: the bf16 GEMM (o-projection, cross-o) hands each warp's 32 rows x 32 columns to chunk_warp(), which
-// transposes them through WARP_SMEM bytes of shared memory per warp so that the residual and FiLM rows are read
-// and written with coalesced 128-byte accesses. The MXFP8 GEMM has no shared memory left for it (WARP = false):
-// its epilogue holds 128 accumulators per thread, so chunk() reads them in four 8-column rounds to stay inside
-// the register budget (wider rounds spilled and measured slower there).
-template <bool FILM, bool WARP = FILM>
+// WCOLS > 0: the GEMM hands each warp's 32 rows x 32 columns to chunk_warp(), which transposes them through
+// shared memory, WCOLS columns at a time (WARP_SMEM bytes per warp), so that the residual and FiLM rows are
+// read and written with 16-byte accesses by WCOLS / 4 lanes per row, and all loads of a WCOLS-column slice are
+// issued before its stores. The bf16 GEMM stages 32 columns; the MXFP8 GEMM, whose ring leaves ~28 KB of shared
+// memory, stages 16 (measured at 10,800 x 5,120 x 5,120: cross-o 0.70 -> 0.26 ms against one row per thread;
+// 8-column slices made the FiLM variant slower, 0.52 vs 0.48 ms). WCOLS = 0: chunk() on one row per thread in
+// four 8-column rounds.
+template <bool FILM, int WCOLS = (FILM ? 32 : 0)>
 struct EpiResidualT {
-  static constexpr int WARP_SMEM = WARP ? 32 * 33 * 4 : 0;
+  static_assert(WCOLS == 0 || WCOLS == 16 || WCOLS == 32, "WCOLS is 0, 16 or 32");
+  static constexpr int WARP_SMEM = WCOLS ? 32 * (WCOLS + 1) * 4 : 0;
   float* x;                          // [M, ldx] fp32 residual, updated in place
   long long ldx;
   const __nv_bfloat16* bias;         // [N] nullable
@@ -143,72 +146,77 @@ struct EpiResidualT {
     for (int q = 0; q < W / 4; ++q) reinterpret_cast<float4*>(xr)[q] = xv[q];
   }
 
-  // Warp-cooperative form (all 32 lanes, lane i = row row0 + i, the same 32 columns): y = bf16(acc + b) * gate
-  // per row into shared memory, then 8 lanes per row read x / FiLM and write x with 16-byte accesses, 4 rows per
-  // pass, all loads of the chunk before its stores. Rows >= M are skipped.
+  // Warp-cooperative form (all 32 lanes, lane i = row row0 + i, the same 32 columns), one WCOLS-column slice at
+  // a time: y = bf16(acc + b) * gate per row into shared memory, then LPR = WCOLS / 4 lanes per row read x / FiLM
+  // and write x with 16-byte accesses, 32 / LPR rows per pass, all loads of the slice before its stores.
+  // Rows >= M are skipped.
   LBW_DEV void chunk_warp(int row0, int lane, int col, const float (&v)[32], int M, float* sm) const {
+    constexpr int WC = WCOLS > 0 ? WCOLS : 32, SP = WC + 1, LPR = WC / 4, RPP = 32 / LPR, PASSES = 32 / RPP;
 #pragma unroll
-    for (int e = 0; e < 32; e += 8) {
-      float y[8];
-      if (bias) {
-        const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + col + e));
-        const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
+    for (int h = 0; h < 32; h += WC) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) y[q] = bf16_round(acc(v[e + q]) + __bfloat162float(bp[q]));
-      } else {
+      for (int e = 0; e < WC; e += 8) {
+        float y[8];
+        if (bias) {
+          const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + col + h + e));
+          const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[e + q]);
-      }
-      if (gate) {
-        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + col + e));
-        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + col + e + 4));
-        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+          for (int q = 0; q < 8; ++q) y[q] = bf16_round(acc(v[h + e + q]) + __bfloat162float(bp[q]));
+        } else {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) y[q] = __fmul_rn(y[q], g[q]);
-      }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) sm[lane * 33 + e + q] = y[q];
-    }
-    __syncwarp();
-    const int rr = lane >> 3, c4 = (lane & 7) * 4;
-    float4 xv[8];
-    uint2 sv[8], tv[8];
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int row = row0 + it * 4 + rr;
-      if (row < M) {
-        xv[it] = *reinterpret_cast<const float4*>(x + (long long)row * ldx + col + c4);
-        if (FILM && film_scale) {
-          const long long fo = (long long)row * ldf + col + c4;
-          sv[it] = *reinterpret_cast<const uint2*>(film_scale + fo);
-          tv[it] = *reinterpret_cast<const uint2*>(film_shift + fo);
+          for (int q = 0; q < 8; ++q) y[q] = bf16_round(v[h + e + q]);
         }
+        if (gate) {
+          const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + col + h + e));
+          const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + col + h + e + 4));
+          const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+          for (int q = 0; q < 8; ++q) y[q] = __fmul_rn(y[q], g[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sm[lane * SP + e + q] = y[q];
       }
-    }
+      __syncwarp();
+      const int rr = lane / LPR, c4 = (lane % LPR) * 4, cc = col + h + c4;
+      float4 xv[PASSES];
+      uint2 sv[PASSES], tv[PASSES];
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int r = it * 4 + rr, row = row0 + r;
-      if (row < M) {
-        float o[4] = {xv[it].x, xv[it].y, xv[it].z, xv[it].w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) o[q] = __fadd_rn(o[q], sm[r * 33 + c4 + q]);
-        if (FILM && film_scale) {
-          const __nv_bfloat16* sp = reinterpret_cast<const __nv_bfloat16*>(&sv[it]);
-          const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(&tv[it]);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float s1 = bf16_round(1.f + __bfloat162float(sp[q]));  // (1.0 + bf16 tensor) stays bf16
-            o[q] = __fadd_rn(__fmul_rn(s1, o[q]), __bfloat162float(tp[q]));
+      for (int it = 0; it < PASSES; ++it) {
+        const int row = row0 + it * RPP + rr;
+        if (row < M) {
+          xv[it] = *reinterpret_cast<const float4*>(x + (long long)row * ldx + cc);
+          if (FILM && film_scale) {
+            const long long fo = (long long)row * ldf + cc;
+            sv[it] = *reinterpret_cast<const uint2*>(film_scale + fo);
+            tv[it] = *reinterpret_cast<const uint2*>(film_shift + fo);
           }
         }
-        *reinterpret_cast<float4*>(x + (long long)row * ldx + col + c4) = make_float4(o[0], o[1], o[2], o[3]);
       }
+#pragma unroll
+      for (int it = 0; it < PASSES; ++it) {
+        const int r = it * RPP + rr, row = row0 + r;
+        if (row < M) {
+          float o[4] = {xv[it].x, xv[it].y, xv[it].z, xv[it].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) o[q] = __fadd_rn(o[q], sm[r * SP + c4 + q]);
+          if (FILM && film_scale) {
+            const __nv_bfloat16* sp = reinterpret_cast<const __nv_bfloat16*>(&sv[it]);
+            const __nv_bfloat16* tp = reinterpret_cast<const __nv_bfloat16*>(&tv[it]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float s1 = bf16_round(1.f + __bfloat162float(sp[q]));  // (1.0 + bf16 tensor) stays bf16
+              o[q] = __fadd_rn(__fmul_rn(s1, o[q]), __bfloat162float(tp[q]));
+            }
+          }
+          *reinterpret_cast<float4*>(x + (long long)row * ldx + cc) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      __syncwarp();
     }
-    __syncwarp();
   }
 
   LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
-    if constexpr (WARP) {
+    if constexpr (WCOLS == 32) {
       part<32>(row, col, 0, v);
     } else {
 #pragma unroll

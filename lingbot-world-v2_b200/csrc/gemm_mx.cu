@@ -30,6 +30,8 @@ constexpr int BM = 128, BK = 128;
 constexpr int A_BYTES = BM * BK;   // 16 KB
 constexpr int SFA_BYTES = 512;
 constexpr int THREADS = 320;
+constexpr int EPI_WARPS = 8;
+constexpr int SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per CTA on sm_100
 // Tile width TBN = 256 (default) or 128 (when 256-wide tiles would leave the last wave mostly idle).
 // A 128-wide tile's MMAs take half as long as a 256-wide tile's, so its stages hold two 128-code K blocks (and
 // their scale atoms): the lone MMA-issuing thread then waits once per 8 MMAs instead of once per 4.
@@ -200,7 +202,17 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
       mbar_arrive(&tempty_bar);  // the accumulator may be overwritten from here on
       aph ^= 1;
       float stat = 0.f;
-      if (row < M) {
+      if constexpr (Epi::WARP_SMEM > 0) {
+        // warp-cooperative epilogue (all lanes; rows >= M are skipped inside), staged past the operand ring
+        float* sm = reinterpret_cast<float*>(smem + STAGES * TX_BYTES + (warp - 2) * Epi::WARP_SMEM);
+#pragma unroll
+        for (int c = 0; c < HALF_COLS / 32; ++c) {
+          const int col = col0 + c * 32;
+          if (col < N)
+            epi.chunk_warp(m_blk * BM + quarter * 32, lane, col, *reinterpret_cast<const float(*)[32]>(&r[c * 32]),
+                           M, sm);
+        }
+      } else if (row < M) {
 #pragma unroll
         for (int c = 0; c < HALF_COLS / 32; ++c) {
           const int col = col0 + c * 32;
@@ -220,20 +232,22 @@ template <class Epi, int TBN>
 static int launch_gemm_mx_t(const CUtensorMap& tmA, const void* a_scales, const void* w, const void* w_scales, int M,
                             int N, int K, const Epi& epi, cudaStream_t stream, int* st) {
   using C = mxg::Cfg<TBN>;
+  constexpr int smem_bytes = C::SMEM_BYTES + mxg::EPI_WARPS * Epi::WARP_SMEM;
+  static_assert(smem_bytes <= mxg::SMEM_LIMIT, "operand ring + epilogue staging exceed the shared memory of a CTA");
   CUtensorMap tmB;
   int err = make_tmap_2d(&tmB, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, mxg::BK, TBN);
   if (err) return err;
   static bool attr_set = false;
   if (!attr_set) {
     err = cuda_check(cudaFuncSetAttribute(gemm_mx_kernel<Epi, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          C::SMEM_BYTES),
+                                          smem_bytes),
                      "mx gemm smem attribute");
     if (err) return err;
     attr_set = true;
   }
   const int tiles = ((M + mxg::BM - 1) / mxg::BM) * ((N + TBN - 1) / TBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_mx_kernel<Epi, TBN><<<grid, mxg::THREADS, C::SMEM_BYTES, stream>>>(
+  gemm_mx_kernel<Epi, TBN><<<grid, mxg::THREADS, smem_bytes, stream>>>(
       tmA, tmB, reinterpret_cast<const uint8_t*>(a_scales), reinterpret_cast<const uint8_t*>(w_scales), M, N, K,
       group_rows(M, K, 1), epi, st);
   return cuda_check(cudaGetLastError(), "mx gemm launch");
@@ -303,7 +317,7 @@ int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, c
                            const void* bias, int m, int n, int k, float* x, const float* gate, void* stream) {
   if (!x) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual: null residual");
   if (!ok16mx(x) || !ok16mx(gate) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_residual: alignment");
-  EpiResidualT<false> e{};
+  EpiResidualT<false, 16> e{};
   e.x = x;
   e.ldx = n;
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
@@ -366,7 +380,7 @@ int lbw_mx_linear_residual_film(const void* a, const void* a_scales, const void*
     return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual_film: FiLM needs both scale and shift");
   if (!ok16mx(x) || !ok16mx(gate) || !ok16mx(bias) || !ok16mx(film_scale) || !ok16mx(film_shift))
     return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_residual_film: alignment");
-  EpiResidualT<true, false> e{};
+  EpiResidualT<true, 16> e{};
   e.x = x;
   e.ldx = n;
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
