@@ -321,6 +321,63 @@ def run_sweep(args):
             else:
                 rec.update(gbs=(m * C * 2 + m * C + m * C // 32) / (ms / 1e3) / 1e9)
             print(json.dumps(rec))
+    # tile width at the per-rank row counts of 8 / 4 / 1 GPUs: automatic choice vs forced 128 / 256 (LBW_GEMM_TILE_N)
+    for m in ((1350, 2700, 10800) if only == "tiles" else ()):
+        F_ = 13824
+        h = torch.randn(m, C, generator=g, device=dev, dtype=bf)
+        hq, hs, _ = K.mx_quantize(h)
+        wqkv = (torch.randn(3 * C, C, generator=g, device=dev) * 0.02).to(bf)
+        bqkv = (torch.randn(3 * C, generator=g, device=dev) * 0.02).to(bf)
+        wo = (torch.randn(C, C, generator=g, device=dev) * 0.02).to(bf)
+        bo = (torch.randn(C, generator=g, device=dev) * 0.02).to(bf)
+        w1, w1_s, _ = K.mx_quantize((torch.randn(F_, C, generator=g, device=dev) * 0.02).to(bf))
+        b1 = (torch.randn(F_, generator=g, device=dev) * 0.02).to(bf)
+        w2, w2_s, _ = K.mx_quantize((torch.randn(C, F_, generator=g, device=dev) * 0.02).to(bf))
+        uq, us = K.mx_buffers(m, F_, dev)
+        qr, kr, vv = (torch.empty(m, C, dtype=bf, device=dev) for _ in range(3))
+        ss = torch.zeros(2, m, device=dev)
+        xres = torch.randn(m, C, generator=g, device=dev)
+        gate = torch.randn(C, generator=g, device=dev) * 0.1
+        fs, ft = ((torch.randn(m, C, generator=g, device=dev) * 0.1).to(bf) for _ in range(2))
+        ops = (("qkv_rowss", 5120, 3 * C, lambda: K.qkv_proj(h, wqkv, bqkv, qr, kr, ss[0], ss[1], vv)),
+               ("o_proj_residual_film", 5120, C,
+                lambda: K.linear_residual(h, wo, bo, xres, gate=gate, film_scale=fs, film_shift=ft)),
+               ("cross_q_rowss", 5120, C, lambda: K.linear_rowss(h, wo, bo, qr, ss[0])),
+               ("mx_ffn_up_gelu", 5120, F_, lambda: K.mx_linear_gelu(hq, hs, w1, w1_s, b1, uq, us)),
+               ("mx_ffn_down_residual", F_, C, lambda: K.mx_linear_residual(uq, us, w2, w2_s, bo, xres, gate=gate)))
+        for name, kk, n, fn in ops:
+            rec = {"sweep": "tile_width", "name": name, "m": m, "k": kk, "n": n}
+            for tn in ("auto", "128", "256"):
+                if tn == "auto":
+                    os.environ.pop("LBW_GEMM_TILE_N", None)
+                else:
+                    os.environ["LBW_GEMM_TILE_N"] = tn
+                for _ in range(2):
+                    fn()
+                rec[f"ms_{tn}"] = timed(fn, reps=5)
+            os.environ.pop("LBW_GEMM_TILE_N", None)
+            print(json.dumps(rec))
+    # KV splits of the self-attention at the per-rank query rows of 8 / 4 GPUs (c4 window: 7 chunks x 10,800 keys)
+    for lq in ((1350, 2700) if only == "tiles" else ()):
+        q = torch.randn(lq, C, generator=g, device=dev, dtype=bf)
+        out = torch.empty(lq, C, dtype=bf, device=dev)
+        ks = [torch.randn(10800, C, generator=g, device=dev, dtype=bf) for _ in range(7)]
+        vs = [torch.randn(10800, C, generator=g, device=dev, dtype=bf) for _ in range(7)]
+        rec = {"sweep": "kv_splits", "q_rows": lq, "kv_rows": 75600,
+               "auto": K.pick_kv_splits(lq, H, K.n_kv_tiles([10800] * 7))}
+        for sp_ in range(1, 9):
+            parts = K.attention_workspace(sp_, lq, H, dev) if sp_ > 1 else None
+
+            def run():
+                if parts is None:
+                    K.chunk_attention(q, ks, vs, out=out)
+                else:
+                    K.chunk_attention_partial(q, ks, vs, sp_, *parts)
+                    K.attention_merge(*parts, sp_, out)
+            run()
+            rec[f"ms_s{sp_}"] = timed(run, reps=3)
+        print(json.dumps(rec))
+        del ks, vs
     return 0
 
 
@@ -335,7 +392,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="kernel sweep (BASELINE configs[4]) instead of the step")
-    ap.add_argument("--sweep-only", default="all", choices=["all", "attention", "mxfp8", "gemm", "linmx"],
+    ap.add_argument("--sweep-only", default="all", choices=["all", "attention", "mxfp8", "gemm", "linmx", "tiles"],
                     help="with --sweep: one family of points (gemm = the block's bf16 GEMMs at 10,800 and 1,350 rows)")
     ap.add_argument("--lin-mx", action="store_true",
                     help="every block Linear in MXFP8 (the reference's LINGBOT_LIN_MX option; not the headline config)")

@@ -213,11 +213,6 @@ inline void fit_epi(EpiStore& e, int tbn) { e.ss_per_chunk = (e.region_cols % tb
 template <class Epi>
 inline void fit_epi(Epi&, int) {}
 
-static double wave_fill(long long tiles) {
-  const double w = (double)tiles / num_sms();
-  return w / ceil(w);
-}
-
 template <class Epi, int TBN>
 static int launch_gemm_t(const CUtensorMap& tmA, const void* W, long long ldw, int M, int N, int K, Epi epi,
                          cudaStream_t stream, int* st) {
@@ -254,11 +249,12 @@ static int launch_gemm(const void* A, long long lda, const void* W, long long ld
   if (!st) return err;
   CUtensorMap tmA;
   if ((err = make_tmap_2d(&tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, BK, BM))) return err;
-  // 128-wide tiles when 256-wide ones would leave the last wave mostly idle (few rows per rank)
+  // 128-wide tiles when 256-wide ones would leave the last round of tiles mostly idle (few rows per rank)
   const long long mt = (M + BM - 1) / BM;
-  const double f256 = wave_fill(mt * ((N + 255) / 256)), f128 = wave_fill(mt * ((N + 127) / 128));
-  if (K % gemm::Cfg<128>::BKS == 0 && f256 < 0.85 && f128 > f256 + 0.08)
-    return launch_gemm_t<Epi, 128>(tmA, W, ldw, M, N, K, epi, stream, st);
+  const bool can128 = K % gemm::Cfg<128>::BKS == 0;
+  const int force = tile_n_override();
+  const bool use128 = can128 && (force ? force == 128 : prefer_narrow_tiles(mt, N));
+  if (use128) return launch_gemm_t<Epi, 128>(tmA, W, ldw, M, N, K, epi, stream, st);
   return launch_gemm_t<Epi, 256>(tmA, W, ldw, M, N, K, epi, stream, st);
 }
 

@@ -253,11 +253,6 @@ static int launch_gemm_mx_t(const CUtensorMap& tmA, const void* a_scales, const 
   return cuda_check(cudaGetLastError(), "mx gemm launch");
 }
 
-static double mx_wave_fill(long long tiles) {
-  const double w = (double)tiles / num_sms();
-  return w / ceil(w);
-}
-
 template <class Epi>
 static int launch_gemm_mx(const void* a, const void* a_scales, const void* w, const void* w_scales, int M, int N, int K,
                           const Epi& epi, cudaStream_t stream) {
@@ -273,8 +268,9 @@ static int launch_gemm_mx(const void* a, const void* a_scales, const void* w, co
   CUtensorMap tmA;
   if ((err = make_tmap_2d(&tmA, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, BK, BM))) return err;
   const long long mt = (M + BM - 1) / BM;
-  const double f256 = mx_wave_fill(mt * ((N + 255) / 256)), f128 = mx_wave_fill(mt * ((N + 127) / 128));
-  if ((K / BK) % mxg::Cfg<128>::KSUB == 0 && f256 < 0.85 && f128 > f256 + 0.08)
+  const bool can128 = (K / BK) % mxg::Cfg<128>::KSUB == 0;
+  const int force = tile_n_override();
+  if (can128 && (force ? force == 128 : prefer_narrow_tiles(mt, N)))
     return launch_gemm_mx_t<Epi, 128>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st);
   return launch_gemm_mx_t<Epi, 256>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st);
 }

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "../../include/lbw.h"
 
@@ -42,5 +43,25 @@ inline int group_rows(int M, int K, int elem_bytes) {
 }
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Tile width of the persistent GEMMs (128 x TBN tiles, one CTA per SM walking its share of them): the time is
+// set by the most tiles any CTA runs, and a 128-wide tile costs ~0.6 of a 256-wide one (B200, the block's bf16
+// and MXFP8 GEMMs at 1,350 / 2,700 / 10,800 rows: 0.58-0.63), so 128 wins when 0.6 x its per-CTA tile count
+// stays below 256's.
+inline bool prefer_narrow_tiles(long long m_tiles, long long n) {
+  const long long sms = num_sms();
+  const long long w256 = (m_tiles * ((n + 255) / 256) + sms - 1) / sms;
+  const long long w128 = (m_tiles * ((n + 127) / 128) + sms - 1) / sms;
+  return 3 * w128 < 5 * w256;
+}
+
+// Tile-width override of the persistent GEMMs for tuning sweeps: LBW_GEMM_TILE_N=128 or 256 forces that width
+// where the shape allows it; unset (or any other value) keeps the automatic choice.
+inline int tile_n_override() {
+  const char* s = getenv("LBW_GEMM_TILE_N");
+  if (!s) return 0;
+  const int v = atoi(s);
+  return (v == 128 || v == 256) ? v : 0;
+}
 
 }  // namespace lbw

@@ -281,3 +281,28 @@ class CausalWanModel(nn.Module):
         if sp.active():
             out = sp.gather_tokens(out)
         return [self.unpatchify(out, grid)]
+
+    @torch.no_grad()
+    def forward_fused(self, xa, ya, cam_a, ta, ta_key, chunk_a, xb, yb, cam_b, tb, tb_key, chunk_b, context, seq_len,
+                      kv_cache, crossattn_cache, frame_seqlen, max_attention_size=1_000_000):
+        """Chunk a's KV-cache commit (clean latent xa at ta = 0) and chunk b's first denoise step (xb at tb), the
+        reference's LINGBOT_FUSE_COMMIT forward (model_fast.py:3985-4097, called from image2video.py:1638-1649),
+        with its signature and result ([b's output]). The reference packs both chunks into one forward so that a
+        Trainium graph pays its per-block fixed costs once; here the two forwards run back to back on the stream
+        (every GEMM of a 10,800-token chunk is already compute-bound, and the key sets are the same: a attends to
+        its window before b's K/V overwrite the chunk b evicts, b to the shared chunks, fresh a and itself).
+        ta_key / tb_key (host-side timestep cache keys) are not needed: timestep embeddings are cached by value.
+        cam_a / cam_b: the c2ws_plucker_emb lists of the two chunks (or None)."""
+        def start(x, chunk):
+            return int(chunk) * (int(x.shape[1]) // self.patch_size[0]) * int(frame_seqlen)
+
+        def cond(cam):
+            return {"c2ws_plucker_emb": cam} if cam is not None else None
+        self.forward([xa], ta, context, seq_len, y=[ya] if ya is not None else None, dit_cond_dict=cond(cam_a),
+                     kv_cache=kv_cache, crossattn_cache=crossattn_cache, current_start=start(xa, chunk_a),
+                     max_attention_size=max_attention_size, frame_seqlen=frame_seqlen, cross_attn_first_call=False,
+                     skip_head=True)
+        return self.forward([xb], tb, context, seq_len, y=[yb] if yb is not None else None, dit_cond_dict=cond(cam_b),
+                            kv_cache=kv_cache, crossattn_cache=crossattn_cache, current_start=start(xb, chunk_b),
+                            max_attention_size=max_attention_size, frame_seqlen=frame_seqlen,
+                            cross_attn_first_call=False)

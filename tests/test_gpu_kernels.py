@@ -116,6 +116,35 @@ def test_chunk_attention(cuda_dev, lq, rows, heads, qscale):
     assert max_abs(out.view(lq, heads, 128), ref) < 5e-2
 
 
+@pytest.mark.parametrize("lq,rows,heads,bias", [
+    (70, [128, 77], 2, False),        # lone query tile: ping-pong over 2 key tiles, the odd one ragged
+    (70, [100], 1, False),            # one key tile: slot 1 stays empty
+    (128, [300, 300, 300], 2, True),  # full lone tile, 9 key tiles (odd count), key bias
+    (1350, [256] * 7, 2, False),      # 8-rank c4 rows per head: five two-tile CTAs + a 70-row lone tile
+])
+def test_chunk_attention_lone_tile_ping_pong(cuda_dev, lq, rows, heads, bias):
+    """A CTA whose second query tile is past the last row splits its key tiles between two softmax slots and
+    merges the two partial softmaxes; direct output and split-KV partials both match fp32."""
+    import lbw_b200.kernels as K
+    q, ks, vs = _attn_case(lq, rows, heads, 41 + lq, qscale=2.0)
+    kb = None
+    if bias:
+        kb = torch.zeros(sum(rows))
+        kb[::3] = math.log(5.0)
+    d = cuda_dev
+    kd, vd = [k.to(d) for k in ks], [v.to(d) for v in vs]
+    out = K.chunk_attention(q.to(d), kd, vd, key_bias=None if kb is None else kb.to(d))
+    ref = ob.attention(q, torch.cat(ks), torch.cat(vs), key_bias=kb)
+    assert rel_l2(out.view(lq, heads, 128), ref) < 1e-2 and max_abs(out.view(lq, heads, 128), ref) < 5e-2
+    if kb is None:
+        n_tiles = K.n_kv_tiles(rows)
+        for splits in sorted({min(2, n_tiles), n_tiles}):
+            po, pml = K.attention_workspace(splits, lq, heads, d)
+            K.chunk_attention_partial(q.to(d), kd, vd, splits, po, pml)
+            o2 = K.attention_merge(po, pml, splits, torch.empty_like(out))
+            assert rel_l2(o2.view(lq, heads, 128), ref) < 1e-2
+
+
 def test_chunk_attention_row_max_near_900(cuda_dev):
     """Real-weight hot heads reach row maxima of ~864 (the reference's const-max guard, model_fast.py:254-263):
     a key aligned with each query and scaled x80 sits in a late tile of a later chunk, so the running max jumps

@@ -88,3 +88,38 @@ def test_model_from_checkpoint_folder_vs_reference_golden(cuda_dev, tmp_path):
     cache, cc = _cache(case, inp, cuda_dev)
     o = _run(m, case, inp, cache, cc, cuda_dev)[0].float().cpu()
     assert rel_l2(o, g["out"]) < 1e-2 and max_abs(o, g["out"]) < 5e-2
+
+
+def test_forward_fused_equals_commit_then_step(cuda_dev):
+    """forward_fused (LINGBOT_FUSE_COMMIT's signature): chunk a's commit at t = 0, then chunk b's step, with the
+    same output and cache as the two forwards called one after the other."""
+    g = load_golden("model_forward")
+    case = ModelCase(**g["case"])
+    m, inp = _build(case, cuda_dev)
+    d, L = cuda_dev, case.lq
+    fs = L // case.grid[0]
+    xb = (inp["x"] * 0.5).to(d)
+    tb = torch.tensor([700.0], device=d)
+    ca, cb = [inp["cam"].to(d)], [(inp["cam"] * 0.9).to(d)]
+    a, b = case.chunk_index, case.chunk_index + 1
+    cache1, cc1 = _cache(case, inp, d)
+    cache2, cc2 = _cache(case, inp, d)
+    for cc in (cc1, cc2):   # the cross cache is filled by an earlier forward, as in the reference
+        m([inp["x"].to(d)], inp["t"].to(d), [inp["context"].to(d)], L, y=[inp["y"].to(d)],
+          kv_cache=_cache(case, inp, d)[0], crossattn_cache=cc, current_start=a * L, frame_seqlen=fs,
+          cross_attn_first_call=True, skip_head=True)
+    zero = torch.zeros(1, device=d)
+    out = m.forward_fused(inp["x"].to(d), inp["y"].to(d), ca, zero, 0.0, a, xb, inp["y"].to(d), cb, tb, 700.0, b,
+                          context=[inp["context"].to(d)], seq_len=L, kv_cache=cache1, crossattn_cache=cc1,
+                          frame_seqlen=fs)
+    assert m([inp["x"].to(d)], zero, [inp["context"].to(d)], L, y=[inp["y"].to(d)],
+             dit_cond_dict={"c2ws_plucker_emb": ca}, kv_cache=cache2, crossattn_cache=cc2, current_start=a * L,
+             frame_seqlen=fs, cross_attn_first_call=False, skip_head=True) is None
+    ref = m([xb], tb, [inp["context"].to(d)], L, y=[inp["y"].to(d)], dit_cond_dict={"c2ws_plucker_emb": cb},
+            kv_cache=cache2, crossattn_cache=cc2, current_start=b * L, frame_seqlen=fs, cross_attn_first_call=False)
+    torch.cuda.synchronize()
+    assert torch.equal(out[0], ref[0]) and torch.isfinite(out[0]).all()
+    for i in range(case.layers):
+        for key in ("k", "v"):
+            for s1, s2 in zip(cache1[i][key], cache2[i][key]):
+                assert torch.equal(s1, s2)
