@@ -10,8 +10,9 @@ runs its chunked-KV forward (kv_chunks path, exact attention -> SDPA) and saves 
 the destination-chunk K/V it writes and the outputs of self_attn / cross_attn / ffn. It also saves
 the reference's cross_dedup_bias + cross_attention_dedup (wan/modules/attention.py:516-554) on a
 duplicated-context case, the reference's RoPE grids, its camera FiLM MLP, and one whole
-WanModelFast.forward (model_fast.py:3283-3935) of a 2-block i2v model with the camera condition. Inputs are NOT stored: they are
-regenerated from the seed by oracle.inputs.make_case; a checksum guards against drift.
+WanModelFast.forward (model_fast.py:3283-3935) of a 2-block i2v model with the camera condition, and the
+Wan 2.1 VAE decode (wan/modules/vae2_1.py) of a small latent. Inputs are NOT stored (except the small VAE
+latent): they are regenerated from the seed by oracle.inputs / oracle.vae; a checksum guards against drift.
 
 Nothing at test or bench time reads the reference; only the .pt files produced here are used.
 """
@@ -216,6 +217,36 @@ def run_model(mf, ckv):
                 ctx_k=[c["k"][0].clone() for c in cc], ctx_v=[c["v"][0].clone() for c in cc])
 
 
+VAE_CFG = dict(dim=32)          # the Wan 2.1 decoder structure (dim_mult 1,2,4,4, 2 res blocks, temporal x4) at dim 32
+VAE_SEED = 5
+
+
+def run_vae():
+    """The reference's WanVAE_.decode (wan/modules/vae2_1.py:548-572) and decode_chunk over two calls (:574-596)
+    of a 3-frame 4x6 latent, with oracle.vae's seeded parameters, and the bf16 latent scale of Wan2_1_VAE."""
+    from oracle import vae as ov
+    with contextlib.redirect_stdout(sys.stderr):
+        import wan.modules.vae2_1 as v21
+    m = v21.WanVAE_(dim=VAE_CFG["dim"], z_dim=16, dim_mult=[1, 2, 4, 4], num_res_blocks=2, attn_scales=[],
+                    temperal_downsample=[False, True, True]).eval()
+    params = ov.make_params(VAE_SEED, **VAE_CFG)
+    sd = m.state_dict()
+    names = {k for k in sd if k.startswith("conv2.") or k.startswith("decoder.")}
+    assert names == set(params), sorted(names ^ set(params))[:5]
+    for k, v in params.items():
+        assert tuple(sd[k].shape) == tuple(v.shape), k
+        sd[k] = v
+    m.load_state_dict(sd)
+    z = torch.randn(16, 3, 4, 6, generator=torch.Generator().manual_seed(VAE_SEED))
+    scale = ov.latent_scale()
+    with torch.no_grad():
+        full = m.decode(z.unsqueeze(0), scale).float().clamp(-1, 1)[0]
+        a = m.decode_chunk(z[:, :2].unsqueeze(0), scale, True).float().clamp(-1, 1)[0]
+        b = m.decode_chunk(z[:, 2:].unsqueeze(0), scale, False).float().clamp(-1, 1)[0]
+    return dict(cfg=VAE_CFG, seed=VAE_SEED, z=z, out=full, out_chunks=torch.cat([a, b], dim=1),
+                checksum=sum(float(v.abs().sum()) for v in params.values()))
+
+
 def main():
     install_shims()
     with contextlib.redirect_stdout(sys.stderr):
@@ -237,6 +268,8 @@ def main():
     table = {(i, n): ckv.chunk_routing(i, n) for n in (1, 2, 3, 4, 7) for i in range(0, 12)}
     torch.save(table, os.path.join(HERE, "chunk_routing.pt"))
     print("chunk_routing saved")
+    torch.save(run_vae(), os.path.join(HERE, "vae_decode.pt"))
+    print("vae_decode saved")
 
 
 if __name__ == "__main__":

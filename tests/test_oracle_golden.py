@@ -68,3 +68,18 @@ def test_model_forward_matches_reference():
     for i in range(case.layers):
         assert rel_l2(k_dest[i], g["k_dest"][i]) < 1e-2 and rel_l2(v_dest[i], g["v_dest"][i]) < 1e-2
         assert rel_l2(ctx_k[i], g["ctx_k"][i]) < 1e-2 and rel_l2(ctx_v[i], g["ctx_v"][i]) < 1e-2
+
+
+def test_oracle_vae_decode_vs_reference_golden():
+    """oracle.vae (the Wan 2.1 decoder restated) against the reference's WanVAE_.decode and a two-call
+    decode_chunk of the same latent (tests/golden/vae_decode.pt)."""
+    from oracle import vae as ov
+    g = load_golden("vae_decode")
+    p = ov.make_params(g["seed"], **g["cfg"])
+    assert abs(sum(float(v.abs().sum()) for v in p.values()) - g["checksum"]) < 1e-3 * g["checksum"]
+    out, _ = ov.decode(p, g["z"], **g["cfg"])
+    assert out.shape == g["out"].shape == (3, 9, 32, 48)
+    assert rel_l2(out, g["out"]) < 1e-5
+    a, dec = ov.decode(p, g["z"][:, :2], **g["cfg"])
+    b, _ = ov.decode(p, g["z"][:, 2:], decoder=dec, **g["cfg"])
+    assert rel_l2(torch.cat([a, b], dim=1), g["out_chunks"]) < 1e-5
