@@ -240,6 +240,39 @@ int lbw_sp_kv_stage(void* const* bufs, int rank, int world, unsigned int epoch, 
 int lbw_sp_kv_gather(void* const* bufs, int rank, int world, unsigned int epoch, void* k_dest, void* v_dest,
                      long long ld, int local_rows, int cols, void* stream);
 
+/* ---- Wan 2.1 VAE decoder (wan/modules/vae2_1.py) -------------------------------------------
+ * Frames are stored channels-last with a one-pixel zero border: [frames][h + 2][w + 2][c] bf16 ("padded rows",
+ * P = (h + 2)(w + 2) rows per frame). */
+/* Causal 3-D / 2-D convolution as an implicit GEMM on the tcgen05 GEMM (CausalConv3d :16-35, the Resample Conv2d
+ * :71-78 with kt = 1, the 1x1x1 shortcut). x: in_rows padded rows of c_in channels (c_in % 64 == 0) holding
+ * kt - 1 history frames (the causal cache, or zeros) followed by `frames` input frames; w: [c_out, kt*kh*kw*c_in]
+ * bf16, K ordered (kt, kh, kw, c); out: frames * P padded rows of c_out channels (c_out % 32 == 0), border rows
+ * written as zeros; bias [c_out] and residual (same shape as out, added after rounding) may be NULL.
+ * kt in {1, 3}, kh = kw in {1, 3}. */
+int lbw_vae_conv(const void* x, long long in_rows, int c_in, const void* w, const void* bias, int c_out, int kt, int kh,
+                 int kw, int frames, int h, int wd, const void* residual, void* out, void* stream);
+/* out = RMS_norm(x) (x / max(||x||_2, 1e-12) * sqrt(c_real) * gamma, :38-53), then SiLU if silu != 0; one row
+ * per voxel, c channels (c % 8 == 0, <= 512; channels past c_real are zero), gamma fp32 [c]. */
+int lbw_vae_rms_silu(const void* x, long long rows, int c, int c_real, const float* gamma, int silu, void* out,
+                     void* stream);
+/* Nearest 2x upsampling in h and w ('nearest-exact', :56-62) of padded frames into padded frames of 2h x 2w. */
+int lbw_vae_upsample2x(const void* x, int frames, int h, int w, int c, void* out, void* stream);
+/* Resample upsample3d's frame interleave (:131-135): x [frames * frame_rows][2c] -> out [2 * frames * frame_rows][c],
+ * frame 2f from channels [0, c), frame 2f + 1 from [c, 2c). */
+int lbw_vae_time_interleave(const void* x, int frames, long long frame_rows, int c, void* out, void* stream);
+/* AttentionBlock (:222-267) helpers: interior rows of padded frames -> compact token rows, and
+ * out (padded) = resid + y (compact rows) inside, zero border. */
+int lbw_vae_gather(const void* x, int frames, int h, int w, int c, void* out, void* stream);
+int lbw_vae_scatter_add(const void* y, const void* resid, int frames, int h, int w, int c, void* out, void* stream);
+/* fp32-output GEMM: out[m, n] = sum_k a[m, k] w[n, k] (the mid-block attention scores). */
+int lbw_gemm_f32(const void* a, long long lda, const void* w, long long ldw, float* out, long long ldo, int m, int n,
+                 int k, void* stream);
+/* p[r, c] = softmax_c(scale * s[r, :n]) as bf16 for c < n, 0 for n <= c < n_pad. */
+int lbw_softmax_rows(const float* s, long long lds, int rows, int n, int n_pad, float scale, void* p, long long ldp,
+                     void* stream);
+/* out[c][r] = x[r][c] (bf16). */
+int lbw_transpose_bf16(const void* x, long long ldx, int rows, int cols, void* out, long long ldo, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

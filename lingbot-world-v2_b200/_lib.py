@@ -46,6 +46,15 @@ SIGNATURES = {
     "lbw_mx_linear_rowss": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "lbw_mx_linear_residual_film": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp], _i),
     "lbw_mx_linear_act": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
+    "lbw_vae_conv": ([_vp, _ll, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp], _i),
+    "lbw_vae_rms_silu": ([_vp, _ll, _i, _i, _vp, _i, _vp, _vp], _i),
+    "lbw_vae_upsample2x": ([_vp, _i, _i, _i, _i, _vp, _vp], _i),
+    "lbw_vae_time_interleave": ([_vp, _i, _ll, _i, _vp, _vp], _i),
+    "lbw_vae_gather": ([_vp, _i, _i, _i, _i, _vp, _vp], _i),
+    "lbw_vae_scatter_add": ([_vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
+    "lbw_gemm_f32": ([_vp, _ll, _vp, _ll, _vp, _ll, _i, _i, _i, _vp], _i),
+    "lbw_softmax_rows": ([_vp, _ll, _i, _i, _i, _f, _vp, _ll, _vp], _i),
+    "lbw_transpose_bf16": ([_vp, _ll, _i, _i, _vp, _ll, _vp], _i),
     "lbw_chunk_attention_gated": ([_vp, _ll, _i, _i, _vp, _vp, _vp, _i, _ll, _f, _vp, _ll, _i, _vp, _vp, _i, _vp,
                                    ctypes.c_uint, _i, _vp], _i),
     "lbw_peer_buffer_create": ([_ll, ctypes.POINTER(_vp), _vp], _i),

@@ -348,4 +348,75 @@ struct EpiGeluMX {
   LBW_DEV void tile_done(int, int, float) const {}
 };
 
+// VAE decoder convolution over frames with a one-pixel zero border ([frames][H + 2][W + 2][C] rows): bf16(acc + b),
+// then + residual rounded to bf16 (the ResidualBlock's shortcut add, wan/modules/vae2_1.py:219); border rows are
+// written as zeros so that the output is the next layer's padded input.
+struct EpiConv {
+  static constexpr int WARP_SMEM = 0;  // no warp-cooperative chunk()
+  __nv_bfloat16* out;                // [M, ldo]
+  long long ldo;
+  const __nv_bfloat16* bias;         // [N] nullable
+  const __nv_bfloat16* residual;     // [M, ldr] nullable
+  long long ldr;
+  int P, W2, H2;                     // rows per frame (H + 2)(W + 2), padded width and height
+
+  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
+    const int q = row % P, hp = q / W2, wp = q - hp * W2;
+    const bool border = hp == 0 || hp == H2 - 1 || wp == 0 || wp == W2 - 1;
+    uint32_t pk[16];
+    if (border) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) pk[e] = 0u;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; e += 8) {
+        float b[8], r[8];
+        if (bias) {
+          const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + col + e));
+          const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
+#pragma unroll
+          for (int q2 = 0; q2 < 8; ++q2) b[q2] = __bfloat162float(bp[q2]);
+        } else {
+#pragma unroll
+          for (int q2 = 0; q2 < 8; ++q2) b[q2] = 0.f;
+        }
+        if (residual) {
+          const uint4 rr = *reinterpret_cast<const uint4*>(residual + (long long)row * ldr + col + e);
+          const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(&rr);
+#pragma unroll
+          for (int q2 = 0; q2 < 8; ++q2) r[q2] = __bfloat162float(rp[q2]);
+        }
+#pragma unroll
+        for (int q2 = 0; q2 < 8; q2 += 2) {
+          float y0 = bf16_round(v[e + q2] + b[q2]), y1 = bf16_round(v[e + q2 + 1] + b[q2 + 1]);
+          if (residual) {
+            y0 = bf16_round(y0 + r[q2]);
+            y1 = bf16_round(y1 + r[q2 + 1]);
+          }
+          pk[(e + q2) / 2] = pack_bf16(y0, y1);
+        }
+      }
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(out + (long long)row * ldo + col);
+#pragma unroll
+    for (int q2 = 0; q2 < 4; ++q2) d4[q2] = make_uint4(pk[4 * q2], pk[4 * q2 + 1], pk[4 * q2 + 2], pk[4 * q2 + 3]);
+    return 0.f;
+  }
+  LBW_DEV void tile_done(int, int, float) const {}
+};
+
+// fp32 store of the accumulator (attention scores of the VAE's mid-block attention)
+struct EpiStoreF32 {
+  static constexpr int WARP_SMEM = 0;  // no warp-cooperative chunk()
+  float* out;
+  long long ldo;
+  LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
+    float4* d4 = reinterpret_cast<float4*>(out + (long long)row * ldo + col);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    return 0.f;
+  }
+  LBW_DEV void tile_done(int, int, float) const {}
+};
+
 }  // namespace lbw

@@ -20,6 +20,11 @@
 //   EpiGelu      GELU_tanh(bf16(acc) + b), optionally followed by an MXFP8 quantise-dequantise of each
 //                32-column block (the FFN-up epilogue, kernels/ffn_epi.py:15-37, and the activation
 //                quantisation of kernels/ffn_mx.py:159-182) for the bf16-pipe MX FFN variant.
+//
+// The same kernel is the implicit-GEMM convolution of the VAE decoder (ConvA): the activations are frames
+// stored channels-last with a one-pixel zero border, [frames][H + 2][W + 2][C], so that every tap (kt, kh, kw)
+// of a (kt x kh x kw) kernel reads the same rows shifted by a constant: the A tile of a 64-channel K block of
+// tap t is one TMA load at row m0 + off[t] (rows before the tensor or past its end read as zeros).
 #include <math.h>
 
 #include <mutex>
@@ -58,12 +63,30 @@ template <int TBN> struct Cfg {
 }  // namespace gemm
 
 // ------------------------------------------------------------------------------------------
+// A-operand addressing: the (column, row) TMA coordinates of the 64-wide K block starting at column k0 for the
+// tile rows starting at row0.
+// ------------------------------------------------------------------------------------------
+struct PlainA {
+  LBW_DEV void coords(int k0, int row0, int& x, int& y) const { x = k0; y = row0; }
+};
+constexpr int CONV_MAX_TAPS = 27;
+struct ConvA {
+  int cblocks;               // 64-channel blocks per tap
+  int off[CONV_MAX_TAPS];    // row offset of each tap's input rows (negative: reads before the tensor = 0)
+  LBW_DEV void coords(int k0, int row0, int& x, int& y) const {
+    const int kb = k0 >> 6, tap = kb / cblocks;
+    x = (kb - tap * cblocks) << 6;
+    y = row0 + off[tap];
+  }
+};
+
+// ------------------------------------------------------------------------------------------
 // kernel
 // ------------------------------------------------------------------------------------------
-template <class Epi, int TBN = 256>
+template <class Epi, int TBN = 256, class AMap = PlainA>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                     int K, int group_m, Epi epi, int* status) {
+                     int K, int group_m, Epi epi, int* status, const __grid_constant__ AMap amap) {
   using gemm::BM;
   using gemm::BK;
   using C = gemm::Cfg<TBN>;
@@ -120,7 +143,9 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           mbar_expect_tx(&full_bar[s], STAGE_BYTES);
 #pragma unroll
           for (int u = 0; u < C::KSUB; ++u) {
-            tma_load_2d(sa + u * C::A_SUB, &tmA, &full_bar[s], kb * C::BKS + u * BK, m_blk * BM);
+            int ax, ay;
+            amap.coords(kb * C::BKS + u * BK, m_blk * BM, ax, ay);
+            tma_load_2d(sa + u * C::A_SUB, &tmA, &full_bar[s], ax, ay);
             tma_load_2d(sa + C::A_STAGE + u * C::B_SUB, &tmB, &full_bar[s], kb * C::BKS + u * BK, n_blk * BN);
           }
           ++issued;
@@ -213,9 +238,9 @@ inline void fit_epi(EpiStore& e, int tbn) { e.ss_per_chunk = (e.region_cols % tb
 template <class Epi>
 inline void fit_epi(Epi&, int) {}
 
-template <class Epi, int TBN>
+template <class Epi, int TBN, class AMap = PlainA>
 static int launch_gemm_t(const CUtensorMap& tmA, const void* W, long long ldw, int M, int N, int K, Epi epi,
-                         cudaStream_t stream, int* st) {
+                         cudaStream_t stream, int* st, const AMap& amap = AMap{}, int a_cols = 0) {
   using C = gemm::Cfg<TBN>;
   CUtensorMap tmB;
   int err = make_tmap_2d(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldw, gemm::BK, TBN);
@@ -223,7 +248,8 @@ static int launch_gemm_t(const CUtensorMap& tmA, const void* W, long long ldw, i
   fit_epi(epi, TBN);
   static bool attr_set = false;  // one flag per instantiation
   if (!attr_set) {
-    err = cuda_check(cudaFuncSetAttribute(gemm_bf16_kernel<Epi, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    err = cuda_check(cudaFuncSetAttribute(gemm_bf16_kernel<Epi, TBN, AMap>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           C::SMEM_BYTES + gemm::EPI_WARPS * Epi::WARP_SMEM),
                      "gemm smem attribute");
     if (err) return err;
@@ -231,8 +257,10 @@ static int launch_gemm_t(const CUtensorMap& tmA, const void* W, long long ldw, i
   }
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + TBN - 1) / TBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_bf16_kernel<Epi, TBN><<<grid, gemm::THREADS, C::SMEM_BYTES + gemm::EPI_WARPS * Epi::WARP_SMEM, stream>>>(
-      tmA, tmB, M, N, K, group_rows(M, K, 2), epi, st);
+  // tile groups keep ~40 MB of A rows in L2: A's row width is K for a GEMM, the channel count for a convolution
+  const int group = group_rows(M, a_cols > 0 ? a_cols : K, 2);
+  gemm_bf16_kernel<Epi, TBN, AMap><<<grid, gemm::THREADS, C::SMEM_BYTES + gemm::EPI_WARPS * Epi::WARP_SMEM, stream>>>(
+      tmA, tmB, M, N, K, group, epi, st, amap);
   return cuda_check(cudaGetLastError(), "gemm launch");
 }
 
@@ -347,6 +375,65 @@ int lbw_linear_gelu(const void* a, const void* w, const void* bias, int m, int n
   return launch_gemm(a, k, w, k, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int lbw_gemm_f32(const void* a, long long lda, const void* w, long long ldw, float* out, long long ldo, int m, int n,
+                 int k, void* stream) {
+  if (!out) return set_error(LBW_ERR_INVALID, "lbw_gemm_f32: null output");
+  if (!ok16(out) || ldo % 4 || lda % 8 || ldw % 8) return set_error(LBW_ERR_ALIGN, "lbw_gemm_f32: alignment");
+  EpiStoreF32 e{};
+  e.out = out;
+  e.ldo = ldo;
+  return launch_gemm(a, lda, w, ldw, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_vae_conv(const void* x, long long in_rows, int c_in, const void* w, const void* bias, int c_out, int kt, int kh,
+                 int kw, int frames, int h, int wd, const void* residual, void* out, void* stream) {
+  using namespace gemm;
+  if (!x || !w || !out) return set_error(LBW_ERR_INVALID, "lbw_vae_conv: null pointer");
+  if ((kt != 1 && kt != 3) || kh != kw || (kh != 1 && kh != 3))
+    return set_error(LBW_ERR_SHAPE, "lbw_vae_conv: kernel %dx%dx%d (kt 1 or 3, kh = kw 1 or 3)", kt, kh, kw);
+  if (c_in <= 0 || c_in % 64 || c_out <= 0 || c_out % 32 || frames <= 0 || h <= 0 || wd <= 0)
+    return set_error(LBW_ERR_SHAPE, "lbw_vae_conv: channels %d -> %d (multiples of 64 / 32), %d frames of %dx%d",
+                     c_in, c_out, frames, h, wd);
+  const long long P = (long long)(h + 2) * (wd + 2);
+  const long long M = (long long)frames * P;
+  if (in_rows < (long long)(frames + kt - 1) * P)
+    return set_error(LBW_ERR_SHAPE, "lbw_vae_conv: %lld input rows, need %lld (%d history frames)", in_rows,
+                     (long long)(frames + kt - 1) * P, kt - 1);
+  if (M > (1LL << 30) || in_rows > (1LL << 31) - 1)
+    return set_error(LBW_ERR_SHAPE, "lbw_vae_conv: %lld rows exceed the kernel's int indexing", M);
+  if (!aligned(x, 16) || !aligned(w, 16) || !ok16(out) || !ok16(bias) || !ok16(residual))
+    return set_error(LBW_ERR_ALIGN, "lbw_vae_conv: alignment");
+  int err = 0;
+  int* st = device_status(&err);
+  if (!st) return err;
+  ConvA amap{};
+  amap.cblocks = c_in / 64;
+  int t = 0;
+  for (int a = 0; a < kt; ++a)
+    for (int b = 0; b < kh; ++b)
+      for (int c = 0; c < kw; ++c)
+        amap.off[t++] = (int)(a * P + (b - kh / 2) * (long long)(wd + 2) + (c - kw / 2));
+  const int K = t * c_in;
+  CUtensorMap tmA;
+  if ((err = make_tmap_2d(&tmA, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, in_rows, c_in, c_in, BK, BM))) return err;
+  EpiConv e{};
+  e.out = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ldo = c_out;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
+  e.ldr = c_out;
+  e.P = (int)P;
+  e.W2 = wd + 2;
+  e.H2 = h + 2;
+  const long long mt = (M + BM - 1) / BM;
+  const bool can128 = K % gemm::Cfg<128>::BKS == 0;
+  const int force = tile_n_override();
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (can128 && (force ? force == 128 : prefer_narrow_tiles(mt, c_out)))
+    return launch_gemm_t<EpiConv, 128, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
+  return launch_gemm_t<EpiConv, 256, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
+}
+
 int lbw_linear_act(const void* a, const void* w, const void* bias, const void* addend, int silu, int m, int n, int k,
                    void* out, void* stream) {
   if (!out) return set_error(LBW_ERR_INVALID, "lbw_linear_act: null output");
@@ -458,7 +545,8 @@ extern "C" int lbw_linear_rmsnorm_noalloc(const void* a, const void* w, const vo
   const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
   // No status word: a bounded-wait timeout still ends the kernel, but is not recorded for this call.
-  gemm_bf16_kernel<EpiStore><<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmB, m, n, k, group_rows(m, k, 2), e, nullptr);
+  gemm_bf16_kernel<EpiStore><<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmB, m, n, k, group_rows(m, k, 2), e, nullptr,
+                                                                PlainA{});
   if ((err = cuda_check(cudaGetLastError(), "noalloc gemm launch"))) return err;
   rms_gamma_inplace_kernel<<<m, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), ss,
                                              reinterpret_cast<const __nv_bfloat16*>(gamma), n, eps, n);

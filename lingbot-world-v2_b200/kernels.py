@@ -398,3 +398,96 @@ def mx_linear_act(a, a_s, w, w_s, bias=None, addend=None, silu=False, out=None):
     check(load().lbw_mx_linear_act(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), ptr(addend), int(bool(silu)), m, n,
                                    k, ptr(out), stream_of(a.device)), "mx_linear_act")
     return out
+
+
+# ---------------------------------------------------------------------------------------------- VAE decoder
+def _avail(t):
+    """Elements addressable from t.data_ptr() to the end of its storage (bounds of strided views)."""
+    return (t.untyped_storage().nbytes() - t.storage_offset() * t.element_size()) // t.element_size()
+
+
+def vae_conv(x, in_rows, c_in, w, bias, c_out, k, frames, h, wd, out, residual=None):
+    """Causal conv over padded frames (lbw_vae_conv); k = (kt, kh, kw)."""
+    require_cuda(x, w, bias, out, residual)
+    kt, kh, kw = k
+    P = (h + 2) * (wd + 2)
+    if x.numel() < in_rows * c_in or w.numel() != c_out * kt * kh * kw * c_in or out.numel() < frames * P * c_out:
+        raise ValueError("vae_conv: buffer sizes do not match the convolution")
+    if residual is not None and residual.numel() < frames * P * c_out:
+        raise ValueError("vae_conv: residual smaller than the output")
+    check(load().lbw_vae_conv(ptr(x), in_rows, c_in, ptr(w), ptr(bias), c_out, kt, kh, kw, frames, h, wd,
+                              ptr(residual), ptr(out), stream_of(x.device)), "vae_conv")
+    return out
+
+
+def vae_rms_silu(x, rows, c, c_real, gamma, silu, out):
+    require_cuda(x, gamma, out)
+    if x.numel() < rows * c or out.numel() < rows * c or gamma.numel() < c or gamma.dtype != torch.float32:
+        raise ValueError("vae_rms_silu: buffer sizes")
+    check(load().lbw_vae_rms_silu(ptr(x), rows, c, c_real, ptr(gamma), int(bool(silu)), ptr(out),
+                                  stream_of(x.device)), "vae_rms_silu")
+    return out
+
+
+def vae_upsample2x(x, frames, h, w, c, out):
+    require_cuda(x, out)
+    if x.numel() < frames * (h + 2) * (w + 2) * c or out.numel() < frames * (2 * h + 2) * (2 * w + 2) * c:
+        raise ValueError("vae_upsample2x: buffer sizes")
+    check(load().lbw_vae_upsample2x(ptr(x), frames, h, w, c, ptr(out), stream_of(x.device)), "vae_upsample2x")
+    return out
+
+
+def vae_time_interleave(x, frames, frame_rows, c, out):
+    require_cuda(x, out)
+    if x.numel() < frames * frame_rows * 2 * c or out.numel() < 2 * frames * frame_rows * c:
+        raise ValueError("vae_time_interleave: buffer sizes")
+    check(load().lbw_vae_time_interleave(ptr(x), frames, frame_rows, c, ptr(out), stream_of(x.device)),
+          "vae_time_interleave")
+    return out
+
+
+def vae_gather(x, frames, h, w, c, out):
+    require_cuda(x, out)
+    if x.numel() < frames * (h + 2) * (w + 2) * c or out.numel() < frames * h * w * c:
+        raise ValueError("vae_gather: buffer sizes")
+    check(load().lbw_vae_gather(ptr(x), frames, h, w, c, ptr(out), stream_of(x.device)), "vae_gather")
+    return out
+
+
+def vae_scatter_add(y, resid, frames, h, w, c, out):
+    require_cuda(y, resid, out)
+    P = (h + 2) * (w + 2)
+    if y.numel() < frames * h * w * c or resid.numel() < frames * P * c or out.numel() < frames * P * c:
+        raise ValueError("vae_scatter_add: buffer sizes")
+    check(load().lbw_vae_scatter_add(ptr(y), ptr(resid), frames, h, w, c, ptr(out), stream_of(y.device)),
+          "vae_scatter_add")
+    return out
+
+
+def gemm_f32(a, lda, w, ldw, out, ldo, m, n, k):
+    """out[m, n] (fp32) = a[m, :k] w[n, :k]^T with explicit row strides."""
+    require_cuda(a, w, out)
+    if out.dtype != torch.float32 or out.numel() < (m - 1) * ldo + n:
+        raise ValueError("gemm_f32: output")
+    if _avail(a) < (m - 1) * lda + k or _avail(w) < (n - 1) * ldw + k:
+        raise ValueError("gemm_f32: operand sizes")
+    check(load().lbw_gemm_f32(ptr(a), lda, ptr(w), ldw, ptr(out), ldo, m, n, k, stream_of(a.device)), "gemm_f32")
+    return out
+
+
+def softmax_rows(s, rows, n, n_pad, scale, p):
+    require_cuda(s, p)
+    lds, ldp = s.stride(0), p.stride(0)
+    if s.shape[0] < rows or p.shape[0] < rows or s.shape[1] < n or p.shape[1] < n_pad:
+        raise ValueError("softmax_rows: shapes")
+    check(load().lbw_softmax_rows(ptr(s), lds, rows, n, n_pad, ctypes.c_float(scale), ptr(p), ldp,
+                                  stream_of(s.device)), "softmax_rows")
+    return p
+
+
+def transpose_bf16(x, ldx, rows, cols, out, ldo):
+    require_cuda(x, out)
+    if _avail(x) < (rows - 1) * ldx + cols or _avail(out) < (cols - 1) * ldo + rows:
+        raise ValueError("transpose_bf16: sizes")
+    check(load().lbw_transpose_bf16(ptr(x), ldx, rows, cols, ptr(out), ldo, stream_of(x.device)), "transpose_bf16")
+    return out

@@ -191,3 +191,16 @@ def test_oracle_lin_mx_changes_only_the_named_linears():
                              film=inp["film"], mx_linears=B.MX_LINEAR_NAMES)
     d = (allmx - base).norm() / (base - inp["x"]).norm()
     assert 1e-3 < d < 0.1
+
+
+def test_vae_decoder_parameter_names_match_the_reference():
+    """WanVAEDecoder carries conv2.* + decoder.* with the reference's names and shapes (the list in oracle.vae is
+    checked against the reference's own WanVAE_ state dict when the golden is made), so a checkpoint loads as is."""
+    import lbw_b200.vae as V
+    from oracle import vae as ov
+    for dim in (32, 96):
+        m = V.WanVAEDecoder(dim=dim)
+        got = {n: tuple(p.shape) for n, p in m.named_parameters()}
+        assert got == {n: tuple(s) for n, s in ov.param_shapes(dim=dim)}
+    with pytest.raises(ValueError, match="CUDA"):
+        V.WanVAEDecoder(dim=32).prepare()
