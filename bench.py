@@ -381,6 +381,83 @@ def run_sweep(args):
     return 0
 
 
+def vae_flops(layout, h, w, t_steady=True):
+    """Algorithmic FLOPs of one Decoder3d pass on a latent frame of h x w (real channels): every convolution
+    2 * voxels * c_out * c_in * taps, the mid-block attention 4 * (hw)^2 * c plus its 1x1 projections."""
+    t, total = 1, 0.0
+    for kind, name, ci, co in layout:
+        vox = t * h * w
+        if kind == "conv":
+            total += 2.0 * vox * co * ci * 27
+        elif kind == "res":
+            total += 2.0 * vox * co * ci * 27 + 2.0 * vox * co * co * 27 + (2.0 * vox * co * ci if ci != co else 0)
+        elif kind == "attn":
+            total += 4.0 * (h * w) ** 2 * ci * t + 2.0 * vox * ci * 4 * ci
+        elif kind in ("up3d", "up2d"):
+            if kind == "up3d" and t_steady:
+                total += 2.0 * vox * 2 * ci * ci * 3
+                t *= 2
+            h, w = 2 * h, 2 * w
+            total += 2.0 * t * h * w * co * ci * 9
+        else:
+            total += 2.0 * vox * 3 * ci * 27
+    return total
+
+
+def run_vae(args):
+    """The Wan 2.1 VAE decode of 720p causal chunks (3 latent frames of 90 x 160 -> 12 frames of 720 x 1280 in
+    the steady state) with the production decoder (dim 96) and seeded random weights; one step = one
+    decode_chunk continuing the causal cache."""
+    import __graft_entry__
+    __graft_entry__.build()
+    import lbw_b200.vae as V
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    m = V.WanVAEDecoder(dim=96).to(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    with torch.no_grad():
+        for name, prm in m.named_parameters():
+            if name.endswith("gamma"):
+                prm.copy_(1 + 0.1 * torch.randn(prm.shape, generator=g, device=dev))
+            elif name.endswith("bias"):
+                prm.copy_(0.02 * torch.randn(prm.shape, generator=g, device=dev))
+            else:
+                prm.copy_(torch.randn(prm.shape, generator=g, device=dev) / math.sqrt(prm[0].numel()))
+    m.prepare()
+    lat_t, lat_h, lat_w = 3, 90, 160
+    z = torch.randn(16, lat_t, lat_h, lat_w, generator=g, device=dev)
+    m.decode_chunk(z, first=True)                      # the video's first chunk (its first frame is not upsampled)
+    for _ in range(args.warmup):
+        m.decode_chunk(z)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(0) as clk:
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            out = m.decode_chunk(z)
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    frames = out.shape[1]
+    assert torch.isfinite(out).all()
+    flops = vae_flops(m.layout, lat_h, lat_w) * lat_t
+    pk, src = peaks()
+    peak = pk.get("bf16_tflops_sustained") or pk["bf16_tflops"]
+    tf = flops / (ms / 1e3) / 1e12
+    print(json.dumps({
+        "metric": "VAE decode frames/s (720p)", "value": frames / (ms / 1e3), "unit": "frames/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "bf16 (fp32 accumulation)", "data": "synthetic (seeded N(0,1) latent, random init)",
+        "config": {"workload": "vae_decode_720p_chunk", "latent": [16, lat_t, lat_h, lat_w], "frames_out": frames,
+                   "dim": 96, "l2": "activations and per-layer caches >> 126 MB"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_bf16_kernel<EpiConv> (implicit-GEMM conv)", "achieved": tf,
+                     "peak": peak, "unit": "TFLOP/s", "frac": tf / peak, "flops_per_step": flops,
+                     "peak_source": f"{src} bf16_tflops_sustained", "traffic": None},
+        "clocks": clk.summary()}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -396,11 +473,15 @@ def main():
                     help="with --sweep: one family of points (gemm = the block's bf16 GEMMs at 10,800 and 1,350 rows)")
     ap.add_argument("--lin-mx", action="store_true",
                     help="every block Linear in MXFP8 (the reference's LINGBOT_LIN_MX option; not the headline config)")
+    ap.add_argument("--vae", action="store_true",
+                    help="the Wan 2.1 VAE decode of 720p chunks instead of the DiT step (one JSON line of its own)")
     ap.add_argument("--breakdown", action="store_true",
                     help="after the timed steps, time each phase of the block with CUDA event marks")
     args = ap.parse_args()
     if args.sweep:
         return run_sweep(args)
+    if args.vae:
+        return run_vae(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
