@@ -45,20 +45,23 @@ constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
 constexpr int THREADS = 320;
 constexpr int EPI_THREADS = THREADS - 64;
 constexpr int EPI_WARPS = EPI_THREADS / 32;
-// Tile width TBN (256, or 128 when 256-wide tiles would leave the last wave mostly idle): ring depth and
-// shared memory per tile width.
+// Tile width TBN (256, or 128 when 256-wide tiles would leave the last wave mostly idle; the VAE convolutions also
+// use 192 for 192 / 384 / 768 output channels and 64 for the 3-channel head): ring depth and shared memory per
+// tile width.
 // A 128-wide tile's MMAs (N = 128) take half as long as a 256-wide tile's, so its stages hold two 64-wide K
 // blocks: the MMA thread then waits once per 8 MMAs instead of once per 4 (each wait leaves the tensor pipe
 // idle for ~100 cycles, because the lone issuing thread has nothing else in flight).
 template <int TBN> struct Cfg {
-  static constexpr int KSUB = TBN == 256 ? 1 : 2;          // 64-wide K blocks per stage
+  static_assert(TBN == 64 || TBN == 128 || TBN == 192 || TBN == 256, "tile widths 64, 128, 192, 256");
+  static constexpr int KSUB = TBN >= 192 ? 1 : 2;           // 64-wide K blocks per stage
   static constexpr int BKS = BK * KSUB;                      // K per stage
   static constexpr int A_SUB = BM * BK * 2, B_SUB = TBN * BK * 2;
   static constexpr int A_STAGE = A_SUB * KSUB, B_STAGE = B_SUB * KSUB;
   static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
-  static constexpr int STAGES = TBN == 256 ? 4 : 3;
+  static constexpr int STAGES = TBN == 128 ? 3 : 4;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-  static constexpr uint32_t TMEM_COLS = 2 * TBN;
+  // two accumulators of TBN columns; the allocation is a power of two
+  static constexpr uint32_t TMEM_COLS = 2 * TBN <= 128 ? 128 : (2 * TBN <= 256 ? 256 : 512);
 };
 }  // namespace gemm
 
@@ -429,6 +432,11 @@ int lbw_vae_conv(const void* x, long long in_rows, int c_in, const void* w, cons
   const bool can128 = K % gemm::Cfg<128>::BKS == 0;
   const int force = tile_n_override();
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // tiles exactly as wide as the channels where a width divides them: no zero columns computed
+  if (!force && c_out % 192 == 0)
+    return launch_gemm_t<EpiConv, 192, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
+  if (!force && c_out <= 64 && K % gemm::Cfg<64>::BKS == 0)
+    return launch_gemm_t<EpiConv, 64, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
   if (can128 && (force ? force == 128 : prefer_narrow_tiles(mt, c_out)))
     return launch_gemm_t<EpiConv, 128, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
   return launch_gemm_t<EpiConv, 256, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);

@@ -14,47 +14,64 @@ namespace lbw {
 
 namespace vae {
 
-// One warp per row; lanes own 8-channel vectors. Border rows (all zeros) stay zero.
-__global__ void rms_silu_kernel(const __nv_bfloat16* __restrict__ x, long long rows, int C, float scale_c,
-                                const float* __restrict__ gamma, int silu, __nv_bfloat16* __restrict__ out) {
-  const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const __nv_bfloat16* xr = x + row * C;
+// A CTA takes RMS_ROWS consecutive rows, which are one contiguous span of memory: its 256 threads load the span
+// as 16-byte vectors (coalesced), leave each vector's sum of squares in shared memory, sum each row's partials
+// in a fixed order (deterministic), and write the scaled vectors back. Border rows (all zeros) stay zero.
+constexpr int RMS_ROWS = 32, RMS_THREADS = 256, RMS_MAXC = 512;
+constexpr int RMS_VPT = RMS_ROWS * (RMS_MAXC / 8) / RMS_THREADS;  // vectors per thread at the widest rows
+
+__global__ void __launch_bounds__(RMS_THREADS) rms_silu_kernel(const __nv_bfloat16* __restrict__ x, long long rows,
+                                                               int C, float scale_c, const float* __restrict__ gamma,
+                                                               int silu, __nv_bfloat16* __restrict__ out) {
+  __shared__ float part[RMS_ROWS * (RMS_MAXC / 8)];
+  __shared__ float inv_s[RMS_ROWS];
   const int nv = C >> 3;
-  constexpr int MAXV = 2;  // C <= 512: at most 2 vectors per lane
-  uint4 v[MAXV];
-  float ss = 0.f;
+  const long long row0 = (long long)blockIdx.x * RMS_ROWS;
+  const int nrows = (int)(rows - row0 < RMS_ROWS ? rows - row0 : RMS_ROWS);
+  const int nvec = nrows * nv;
+  const uint4* src = reinterpret_cast<const uint4*>(x + row0 * C);
+  uint4 v[RMS_VPT];
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int g = lane + 32 * i;
-    if (g < nv) {
-      v[i] = *reinterpret_cast<const uint4*>(xr + g * 8);
+  for (int i = 0; i < RMS_VPT; ++i) {
+    const int k = threadIdx.x + i * RMS_THREADS;
+    if (k < nvec) {
+      v[i] = src[k];
       const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v[i]);
+      float ss = 0.f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const float f = __bfloat162float(b[e]);
         ss += f * f;
       }
+      part[k] = ss;
     }
   }
+  __syncthreads();
+  if (threadIdx.x < nrows) {
+    float ss = 0.f;
+    for (int j = 0; j < nv; ++j) ss += part[threadIdx.x * nv + j];
+    inv_s[threadIdx.x] = scale_c / fmaxf(sqrtf(ss), 1e-12f);
+  }
+  __syncthreads();
+  uint4* dst = reinterpret_cast<uint4*>(out + row0 * C);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = scale_c / fmaxf(sqrtf(ss), 1e-12f);
-#pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int g = lane + 32 * i;
-    if (g < nv) {
+  for (int i = 0; i < RMS_VPT; ++i) {
+    const int k = threadIdx.x + i * RMS_THREADS;
+    if (k < nvec) {
+      const int r = k / nv, g = k - r * nv;
+      const float inv = inv_s[r];
       const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v[i]);
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + g * 8));
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + g * 8 + 4));
+      const float gm[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
       float y[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        float t = __bfloat162float(b[e]) * inv * __ldg(gamma + g * 8 + e);
+        float t = __bfloat162float(b[e]) * inv * gm[e];
         if (silu) t = t / (1.f + __expf(-t));
         y[e] = t;
       }
-      *reinterpret_cast<uint4*>(out + row * C + g * 8) =
-          make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+      dst[k] = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
     }
   }
 }
@@ -213,7 +230,8 @@ int lbw_vae_rms_silu(const void* x, long long rows, int c, int c_real, const flo
   if (rows <= 0 || c <= 0 || c % 8 || c > 512 || c_real <= 0 || c_real > c)
     return set_error(LBW_ERR_SHAPE, "lbw_vae_rms_silu: %d channels (%d real; a multiple of 8, <= 512)", c, c_real);
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(gamma, 16)) return set_error(LBW_ERR_ALIGN, "lbw_vae_rms_silu");
-  vae::rms_silu_kernel<<<vae::blocks_for(rows * 32, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  vae::rms_silu_kernel<<<vae::blocks_for(rows, vae::RMS_ROWS), vae::RMS_THREADS, 0,
+                          reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), rows, c, sqrtf((float)c_real), gamma, silu,
       reinterpret_cast<__nv_bfloat16*>(out));
   return cuda_check(cudaGetLastError(), "vae rms_silu launch");

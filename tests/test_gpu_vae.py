@@ -38,7 +38,10 @@ def _pack(wt, cip, cop):
 
 @pytest.mark.parametrize("k,t,ci,co,h,w", [((3, 3, 3), 2, 40, 70, 5, 7), ((3, 3, 3), 1, 64, 128, 9, 4),
                                            ((1, 3, 3), 3, 100, 50, 6, 6), ((1, 1, 1), 2, 64, 64, 3, 5),
-                                           ((3, 1, 1), 2, 64, 256, 4, 4)])
+                                           ((3, 1, 1), 2, 64, 256, 4, 4),
+                                           ((3, 3, 3), 2, 64, 192, 5, 6),    # 192-wide tiles
+                                           ((1, 1, 1), 1, 128, 384, 4, 4),   # two 192-wide tiles
+                                           ((3, 3, 3), 2, 96, 3, 4, 6)])     # the head: 64-wide tiles
 def test_vae_conv_vs_torch(cuda_dev, k, t, ci, co, h, w):
     import lbw_b200.kernels as K
     g = _g(ci + co + t)
