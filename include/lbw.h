@@ -244,9 +244,10 @@ int lbw_sp_kv_gather(void* const* bufs, int rank, int world, unsigned int epoch,
  * Frames are stored channels-last with a one-pixel zero border: [frames][h + 2][w + 2][c] bf16 ("padded rows",
  * P = (h + 2)(w + 2) rows per frame). */
 /* Causal 3-D / 2-D convolution as an implicit GEMM on the tcgen05 GEMM (CausalConv3d :16-35, the Resample Conv2d
- * :71-78 with kt = 1, the 1x1x1 shortcut). x: in_rows padded rows of c_in channels (c_in % 64 == 0) holding
- * kt - 1 history frames (the causal cache, or zeros) followed by `frames` input frames; w: [c_out, kt*kh*kw*c_in]
- * bf16, K ordered (kt, kh, kw, c); out: frames * P padded rows of c_out channels (c_out % 32 == 0), border rows
+ * :71-78 with kt = 1, the 1x1x1 shortcut). x: in_rows padded rows of c_in channels (c_in % 8 == 0) holding
+ * kt - 1 history frames (the causal cache, or zeros) followed by `frames` input frames; w: [c_out, kt*kh*kw*ck]
+ * bf16 with ck = c_in rounded up to a multiple of 64 (zero weights past c_in), K ordered (kt, kh, kw, c); out:
+ * frames * P padded rows of c_out channels (c_out % 32 == 0), border rows
  * written as zeros; bias [c_out] and residual (same shape as out, added after rounding) may be NULL.
  * kt in {1, 3}, kh = kw in {1, 3}. */
 int lbw_vae_conv(const void* x, long long in_rows, int c_in, const void* w, const void* bias, int c_out, int kt, int kh,

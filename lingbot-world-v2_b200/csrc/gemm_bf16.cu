@@ -394,8 +394,8 @@ int lbw_vae_conv(const void* x, long long in_rows, int c_in, const void* w, cons
   if (!x || !w || !out) return set_error(LBW_ERR_INVALID, "lbw_vae_conv: null pointer");
   if ((kt != 1 && kt != 3) || kh != kw || (kh != 1 && kh != 3))
     return set_error(LBW_ERR_SHAPE, "lbw_vae_conv: kernel %dx%dx%d (kt 1 or 3, kh = kw 1 or 3)", kt, kh, kw);
-  if (c_in <= 0 || c_in % 64 || c_out <= 0 || c_out % 32 || frames <= 0 || h <= 0 || wd <= 0)
-    return set_error(LBW_ERR_SHAPE, "lbw_vae_conv: channels %d -> %d (multiples of 64 / 32), %d frames of %dx%d",
+  if (c_in <= 0 || c_in % 8 || c_out <= 0 || c_out % 32 || frames <= 0 || h <= 0 || wd <= 0)
+    return set_error(LBW_ERR_SHAPE, "lbw_vae_conv: channels %d -> %d (multiples of 8 / 32), %d frames of %dx%d",
                      c_in, c_out, frames, h, wd);
   const long long P = (long long)(h + 2) * (wd + 2);
   const long long M = (long long)frames * P;
@@ -409,14 +409,16 @@ int lbw_vae_conv(const void* x, long long in_rows, int c_in, const void* w, cons
   int err = 0;
   int* st = device_status(&err);
   if (!st) return err;
+  // K blocks of 64 channels per tap; the channels past c_in of the last block lie outside the tensor map's
+  // columns, so TMA fills them with zeros (and the packed weights hold zeros there)
   ConvA amap{};
-  amap.cblocks = c_in / 64;
+  amap.cblocks = (c_in + 63) / 64;
   int t = 0;
   for (int a = 0; a < kt; ++a)
     for (int b = 0; b < kh; ++b)
       for (int c = 0; c < kw; ++c)
         amap.off[t++] = (int)(a * P + (b - kh / 2) * (long long)(wd + 2) + (c - kw / 2));
-  const int K = t * c_in;
+  const int K = t * amap.cblocks * 64;
   CUtensorMap tmA;
   if ((err = make_tmap_2d(&tmA, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, in_rows, c_in, c_in, BK, BM))) return err;
   EpiConv e{};

@@ -411,7 +411,8 @@ def vae_conv(x, in_rows, c_in, w, bias, c_out, k, frames, h, wd, out, residual=N
     require_cuda(x, w, bias, out, residual)
     kt, kh, kw = k
     P = (h + 2) * (wd + 2)
-    if x.numel() < in_rows * c_in or w.numel() != c_out * kt * kh * kw * c_in or out.numel() < frames * P * c_out:
+    ck = (c_in + 63) // 64 * 64             # K-space channels per tap (zero weights past c_in)
+    if x.numel() < in_rows * c_in or w.numel() != c_out * kt * kh * kw * ck or out.numel() < frames * P * c_out:
         raise ValueError("vae_conv: buffer sizes do not match the convolution")
     if residual is not None and residual.numel() < frames * P * c_out:
         raise ValueError("vae_conv: residual smaller than the output")

@@ -6,7 +6,8 @@ frame, every causal convolution continuing from the last two input frames of the
 feature cache), the first frame not time-upsampled ('Rep', :100-135).
 
 Layout: activations are frames stored channels-last with a one-pixel zero border, [frames][h + 2][w + 2][C]
-bf16, C padded to a multiple of 64 (zero channels). Every causal convolution (3x3x3, the (3,1,1) time_conv,
+bf16, C rounded up to a multiple of 32 (the 96-channel full-resolution level is stored at 96). Every causal
+convolution (3x3x3, the (3,1,1) time_conv,
 the 3x3 Resample conv, the 1x1x1 shortcut) is one implicit-GEMM launch of the tcgen05 GEMM (lbw_vae_conv): the
 kernel taps are constant row shifts of that layout, the two history frames sit in front of the current ones in
 a per-layer buffer, and the epilogue adds the bias and the shortcut and zeroes the border. RMS_norm + SiLU,
@@ -31,6 +32,11 @@ LATENT_STD = [2.8184, 1.4541, 2.3275, 2.6558, 1.2196, 1.7708, 2.6052, 2.0743,
 
 def _pad64(c):
     return (c + 63) // 64 * 64
+
+
+def _pad32(c):
+    """Stored channels of an activation: outputs are written in 32-column chunks."""
+    return (c + 31) // 32 * 32
 
 
 def decoder_layout(dim=96, z_dim=16, dim_mult=(1, 2, 4, 4), num_res_blocks=2, temperal_upsample=(True, True, False)):
@@ -141,8 +147,9 @@ class WanVAEDecoder(nn.Module):
     # ------------------------------------------------------------------ weights
     @torch.no_grad()
     def prepare(self):
-        """Pack every convolution as a [c_out_p, taps * c_in_p] bf16 matrix (K ordered kt, kh, kw, c), biases as
-        bf16 [c_out_p], RMS gammas as fp32 [c_p] (zero padding everywhere)."""
+        """Pack every convolution as a [c_out_p, taps * c_k] bf16 matrix (K ordered kt, kh, kw, c; c_k = the stored
+        input channels rounded up to 64, zero weights past them), biases as bf16 [c_out_p], RMS gammas as fp32
+        [c_p] (c_p, c_out_p: channels rounded up to 32; zero padding everywhere)."""
         sd = dict(self.named_parameters())
         dev = sd["conv2.weight"].device
         if dev.type != "cuda":
@@ -153,16 +160,16 @@ class WanVAEDecoder(nn.Module):
             if w.dim() == 4:
                 w = w.unsqueeze(2)                            # Conv2d -> kt = 1
             co, ci = w.shape[:2]
-            cip = _pad64(ci)
+            cip = _pad64(_pad32(ci))
             if halves:                                        # time_conv: [c | c] -> [c_p | c_p]
                 c = co // 2
-                cp = _pad64(c)
+                cp = _pad32(c)
                 wp = torch.zeros(2 * cp, cip, *w.shape[2:], device=dev)
                 wp[:c, :ci], wp[cp:cp + c, :ci] = w[:c], w[c:]
                 bp = torch.zeros(2 * cp, device=dev)
                 bp[:c], bp[cp:cp + c] = sd[bname][:c].float(), sd[bname][c:].float()
             else:
-                cop = cout_p or _pad64(co)
+                cop = cout_p or _pad32(co)
                 wp = torch.zeros(cop, cip, *w.shape[2:], device=dev)
                 wp[:co, :ci] = w
                 bp = torch.zeros(cop, device=dev)
@@ -172,7 +179,7 @@ class WanVAEDecoder(nn.Module):
 
         def gamma(name):
             g = sd[name].float().reshape(-1)
-            out = torch.zeros(_pad64(g.numel()), device=dev)
+            out = torch.zeros(_pad32(g.numel()), device=dev)
             out[:g.numel()] = g
             return out
 
@@ -188,7 +195,9 @@ class WanVAEDecoder(nn.Module):
                 if ci != co:
                     pk[f"{name}.sc"] = conv(f"{name}.shortcut.weight", f"{name}.shortcut.bias")
             elif kind == "attn":
-                c, cp = ci, _pad64(ci)
+                c, cp = ci, _pad64(ci)      # a GEMM operand: K = cp must be a multiple of 64
+                if cp != _pad32(ci):
+                    raise ValueError(f"the mid-block attention width {ci} must be a multiple of 64")
                 g = gamma(f"{name}.norm.gamma")
                 wq = sd[f"{name}.to_qkv.weight"].float().reshape(3 * c, c)
                 bq = sd[f"{name}.to_qkv.bias"].float()
@@ -228,20 +237,18 @@ class WanVAEDecoder(nn.Module):
     def _conv_causal(self, key, act, producer, tmax, residual=None):
         """producer(dest) writes the layer input for act.t frames into the history buffer; then the 3x3x3 conv."""
         wk, bk, ks = self._packed[key]
-        c_in_p = wk.shape[1] // (ks[0] * ks[1] * ks[2])
-        hist = self._hist_for(key, act, c_in_p, tmax)
+        hist = self._hist_for(key, act, act.cp, tmax)
         producer(hist.slot(act.t))
         out = torch.empty(act.t * act.P, wk.shape[0], dtype=BF16, device=act.data.device)
-        kernels.vae_conv(hist.buf, hist.rows(act.t), c_in_p, wk, bk, wk.shape[0], ks, act.t, act.h, act.w, out,
+        kernels.vae_conv(hist.buf, hist.rows(act.t), act.cp, wk, bk, wk.shape[0], ks, act.t, act.h, act.w, out,
                          residual=residual)
         hist.advance(act.t)
         return out
 
     def _conv_plain(self, key, data, t, h, w, residual=None):
         wk, bk, ks = self._packed[key]
-        c_in_p = wk.shape[1] // (ks[0] * ks[1] * ks[2])
         out = torch.empty(t * (h + 2) * (w + 2), wk.shape[0], dtype=BF16, device=data.device)
-        kernels.vae_conv(data, data.shape[0], c_in_p, wk, bk, wk.shape[0], ks, t, h, w, out, residual=residual)
+        kernels.vae_conv(data, data.shape[0], data.shape[1], wk, bk, wk.shape[0], ks, t, h, w, out, residual=residual)
         return out
 
     def _rms(self, src, gamma, c_real, silu):
@@ -333,7 +340,7 @@ class WanVAEDecoder(nn.Module):
         zc = z.to(dev).float() / scale[1].to(dev).view(-1, 1, 1, 1) + scale[0].to(dev).view(-1, 1, 1, 1)
         c, T, h, w = zc.shape
         P = (h + 2) * (w + 2)
-        zp = torch.zeros(T, h + 2, w + 2, _pad64(c), dtype=BF16, device=dev)      # padded rows of the latent
+        zp = torch.zeros(T, h + 2, w + 2, _pad32(c), dtype=BF16, device=dev)      # padded rows of the latent
         zp[:, 1:-1, 1:-1, :c] = zc.permute(1, 2, 3, 0).to(BF16)
         x2 = self._conv_plain("conv2", zp.view(T * P, -1), T, h, w)
         outs = []

@@ -41,7 +41,8 @@ def _pack(wt, cip, cop):
                                            ((3, 1, 1), 2, 64, 256, 4, 4),
                                            ((3, 3, 3), 2, 64, 192, 5, 6),    # 192-wide tiles
                                            ((1, 1, 1), 1, 128, 384, 4, 4),   # two 192-wide tiles
-                                           ((3, 3, 3), 2, 96, 3, 4, 6)])     # the head: 64-wide tiles
+                                           ((3, 3, 3), 2, 96, 3, 4, 6),      # the head: 64-wide tiles
+                                           ((3, 3, 3), 2, 16, 32, 3, 4)])    # 16 stored channels in a 64 block
 def test_vae_conv_vs_torch(cuda_dev, k, t, ci, co, h, w):
     import lbw_b200.kernels as K
     g = _g(ci + co + t)
@@ -50,15 +51,17 @@ def test_vae_conv_vs_torch(cuda_dev, k, t, ci, co, h, w):
     x = torch.randn(tin, ci, h, w, generator=g).to(BF).float()
     wt = (torch.randn(co, ci, kt, kh, kw, generator=g) / math.sqrt(ci * kt * kh * kw)).to(BF).float()
     b = (torch.randn(co, generator=g) * 0.1).to(BF)
-    cip, cop = (ci + 63) // 64 * 64, (co + 31) // 32 * 32
+    # stored channels: a multiple of 8; K blocks of 64 read past them as zeros (TMA out-of-bounds fill)
+    cis, cop = (ci + 7) // 8 * 8, (co + 31) // 32 * 32
+    cik = (cis + 63) // 64 * 64
     P = (h + 2) * (w + 2)
     d = cuda_dev
-    xr = _padded(x, cip).to(d)
+    xr = _padded(x, cis).to(d)
     res = torch.randn(t * P, cop, generator=g).to(BF)
     bp = torch.zeros(cop, dtype=BF)
     bp[:co] = b
     out = torch.full((t * P, cop), 7.0, dtype=BF, device=d)
-    K.vae_conv(xr, tin * P, cip, _pack(wt, cip, cop).to(d), bp.to(d), cop, k, t, h, w, out, residual=res.to(d))
+    K.vae_conv(xr, tin * P, cis, _pack(wt, cik, cop).to(d), bp.to(d), cop, k, t, h, w, out, residual=res.to(d))
     ref = F.conv3d(x.permute(1, 0, 2, 3).unsqueeze(0), wt, b.float(), padding=(0, kh // 2, kw // 2))[0]
     ref = ref.permute(1, 0, 2, 3)                                            # [t, co, h, w]
     got = _unpad(out.cpu(), t, h, w, co)
