@@ -1,7 +1,7 @@
 """Generate golden fixtures from the REFERENCE implementation's own PyTorch code.
 
-Run in the build container, where the reference checkout exists (default /root/reference, or
-$LBW_REFERENCE):   python tests/golden/make_golden.py
+Run where a checkout of the reference exists, naming it in $LBW_REFERENCE:
+    LBW_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 It imports yahavb/lingbot-world-v2's wan/modules/model_fast.py on CPU through small import shims
 (the Neuron-only packages diffusers/easydict/torch_neuronx are absent here), builds one
@@ -25,7 +25,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("LBW_REFERENCE", "/root/reference")
+REF = os.environ.get("LBW_REFERENCE", "")
 sys.path.insert(0, ROOT)
 
 from oracle.inputs import BlockCase, ModelCase, make_case, make_model_case  # noqa: E402
@@ -248,6 +248,8 @@ def run_vae():
 
 
 def main():
+    if not REF or not os.path.isdir(os.path.join(REF, "wan")):
+        raise SystemExit("set LBW_REFERENCE to the reference checkout (the directory holding wan/)")
     install_shims()
     with contextlib.redirect_stdout(sys.stderr):
         import wan.modules.model_fast as mf
