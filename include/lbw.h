@@ -252,6 +252,11 @@ int lbw_sp_kv_gather(void* const* bufs, int rank, int world, unsigned int epoch,
  * kt in {1, 3}, kh = kw in {1, 3}. */
 int lbw_vae_conv(const void* x, long long in_rows, int c_in, const void* w, const void* bias, int c_out, int kt, int kh,
                  int kw, int frames, int h, int wd, const void* residual, void* out, void* stream);
+/* lbw_vae_conv fused with the RMS_norm + SiLU that follows a ResidualBlock's first convolution (:189-192): out =
+ * silu(y / max(||y||_2, 1e-12) * sqrt(c_real) * gamma) with y = bf16(conv + bias) over each row's c_out channels
+ * (c_out <= 256: the row lies in one GEMM tile); gamma fp32 [c_out]; border rows zero. */
+int lbw_vae_conv_rms(const void* x, long long in_rows, int c_in, const void* w, const void* bias, int c_out, int kt,
+                     int kh, int kw, int frames, int h, int wd, const float* gamma, int c_real, void* out, void* stream);
 /* out = RMS_norm(x) (x / max(||x||_2, 1e-12) * sqrt(c_real) * gamma, :38-53), then SiLU if silu != 0; one row
  * per voxel, c channels (c % 8 == 0, <= 512; channels past c_real are zero), gamma fp32 [c]. */
 int lbw_vae_rms_silu(const void* x, long long rows, int c, int c_real, const float* gamma, int silu, void* out,

@@ -47,6 +47,7 @@ SIGNATURES = {
     "lbw_mx_linear_residual_film": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp], _i),
     "lbw_mx_linear_act": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
     "lbw_vae_conv": ([_vp, _ll, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp], _i),
+    "lbw_vae_conv_rms": ([_vp, _ll, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp], _i),
     "lbw_vae_rms_silu": ([_vp, _ll, _i, _i, _vp, _i, _vp, _vp], _i),
     "lbw_vae_upsample2x": ([_vp, _i, _i, _i, _i, _vp, _vp], _i),
     "lbw_vae_time_interleave": ([_vp, _i, _ll, _i, _vp, _vp], _i),

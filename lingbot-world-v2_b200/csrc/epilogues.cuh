@@ -11,10 +11,19 @@
 // bf16, wan/modules/model_fast.py:1403-1410, :1602-1610); without it bias and accumulator meet in fp32 once
 // (nn.Linear).
 #pragma once
+#include <type_traits>
+
 #include "lbw_common.cuh"
 #include "mx_common.cuh"
 
 namespace lbw {
+
+// Epilogues that normalise each output row over all of its columns declare ROW_NORM = true and provide sumsq()
+// and chunk_norm(); the GEMM then reads the whole row from TMEM before writing it.
+template <class E, class = void>
+struct row_norm : std::false_type {};
+template <class E>
+struct row_norm<E, std::void_t<decltype(E::ROW_NORM)>> : std::integral_constant<bool, E::ROW_NORM> {};
 
 struct EpiStore {
   static constexpr int WARP_SMEM = 0;  // no warp-cooperative chunk()
@@ -402,6 +411,74 @@ struct EpiConv {
     for (int q2 = 0; q2 < 4; ++q2) d4[q2] = make_uint4(pk[4 * q2], pk[4 * q2 + 1], pk[4 * q2 + 2], pk[4 * q2 + 3]);
     return 0.f;
   }
+  LBW_DEV void tile_done(int, int, float) const {}
+};
+
+// The VAE ResidualBlock's first convolution fused with the RMS_norm + SiLU that follows it (vae2_1.py:189-192):
+// y = bf16(acc + b), then silu(y / max(||y||, 1e-12) * sqrt(C) * gamma) over the row's N channels (the whole row
+// lies in one tile), written straight into the second convolution's input; border rows are written as zeros.
+struct EpiConvRms {
+  static constexpr int WARP_SMEM = 0;  // no warp-cooperative chunk()
+  static constexpr bool ROW_NORM = true;
+  __nv_bfloat16* out;                // [M, ldo]
+  long long ldo;
+  const __nv_bfloat16* bias;         // [N] nullable
+  const float* gamma;                // [N] (zero past the real channels)
+  float scale_c;                     // sqrt(real channels)
+  int P, W2, H2;
+
+  LBW_DEV bool border(int row) const {
+    const int q = row % P, hp = q / W2, wp = q - hp * W2;
+    return hp == 0 || hp == H2 - 1 || wp == 0 || wp == W2 - 1;
+  }
+  LBW_DEV void rounded(int col, const float (&v)[32], float (&y)[32]) const {
+#pragma unroll
+    for (int e = 0; e < 32; e += 8) {
+      float b[8];
+      if (bias) {
+        const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + col + e));
+        const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) b[q] = __bfloat162float(bp[q]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) b[q] = 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) y[e + q] = bf16_round(v[e + q] + b[q]);
+    }
+  }
+  LBW_DEV float sumsq(int row, int col, const float (&v)[32]) const {
+    if (border(row)) return 0.f;
+    float y[32];
+    rounded(col, v, y);
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) ss += y[e] * y[e];
+    return ss;
+  }
+  LBW_DEV void chunk_norm(int row, int col, const float (&v)[32], float ss) const {
+    uint32_t pk[16];
+    if (border(row)) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) pk[e] = 0u;
+    } else {
+      float y[32];
+      rounded(col, v, y);
+      const float inv = scale_c / fmaxf(sqrtf(ss), 1e-12f);
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float t0 = y[e] * inv * __ldg(gamma + col + e), t1 = y[e + 1] * inv * __ldg(gamma + col + e + 1);
+        t0 = t0 / (1.f + __expf(-t0));
+        t1 = t1 / (1.f + __expf(-t1));
+        pk[e >> 1] = pack_bf16(t0, t1);
+      }
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(out + (long long)row * ldo + col);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+  }
+  LBW_DEV float chunk(int, int, const float (&)[32]) const { return 0.f; }
   LBW_DEV void tile_done(int, int, float) const {}
 };
 

@@ -210,8 +210,31 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       const int row = m_blk * BM + quarter * 32 + lane;
       const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       float stat = 0.f;
+      if constexpr (row_norm<Epi>::value) {
+        // the row's sum of squares over every column chunk of the tile (both warps of the pair read all of them),
+        // then this warp's half of the columns normalised and written
+        float ss = 0.f;
 #pragma unroll 1
-      for (int c = c0; c < c0 + NCH; ++c) {
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col = n_blk * BN + c * 32;
+          if (col >= N) break;  // warp-uniform
+          uint32_t r[32];
+          tmem_ld32(tb + c * 32, r);
+          tmem_ld_wait();
+          if (row < M) ss += epi.sumsq(row, col, reinterpret_cast<const float(&)[32]>(r));
+        }
+#pragma unroll 1
+        for (int c = c0; c < c0 + NCH; ++c) {
+          const int col = n_blk * BN + c * 32;
+          if (col >= N) break;  // warp-uniform
+          uint32_t r[32];
+          tmem_ld32(tb + c * 32, r);
+          tmem_ld_wait();
+          if (row < M) epi.chunk_norm(row, col, reinterpret_cast<const float(&)[32]>(r), ss);
+        }
+      }
+#pragma unroll 1
+      for (int c = c0; c < c0 + NCH && !row_norm<Epi>::value; ++c) {
         const int col = n_blk * BN + c * 32;
         if (col >= N) break;  // warp-uniform
         uint32_t r[32];
@@ -442,6 +465,52 @@ int lbw_vae_conv(const void* x, long long in_rows, int c_in, const void* w, cons
   if (can128 && (force ? force == 128 : prefer_narrow_tiles(mt, c_out)))
     return launch_gemm_t<EpiConv, 128, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
   return launch_gemm_t<EpiConv, 256, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
+}
+
+int lbw_vae_conv_rms(const void* x, long long in_rows, int c_in, const void* w, const void* bias, int c_out, int kt,
+                     int kh, int kw, int frames, int h, int wd, const float* gamma, int c_real, void* out, void* stream) {
+  using namespace gemm;
+  if (!x || !w || !out || !gamma) return set_error(LBW_ERR_INVALID, "lbw_vae_conv_rms: null pointer");
+  if ((kt != 1 && kt != 3) || kh != kw || (kh != 1 && kh != 3))
+    return set_error(LBW_ERR_SHAPE, "lbw_vae_conv_rms: kernel %dx%dx%d (kt 1 or 3, kh = kw 1 or 3)", kt, kh, kw);
+  if (c_in <= 0 || c_in % 8 || c_out <= 0 || c_out % 32 || c_out > 256 || c_real <= 0 || c_real > c_out ||
+      frames <= 0 || h <= 0 || wd <= 0)
+    return set_error(LBW_ERR_SHAPE, "lbw_vae_conv_rms: channels %d -> %d (%d real; the row must fit one tile)", c_in,
+                     c_out, c_real);
+  const long long P = (long long)(h + 2) * (wd + 2);
+  const long long M = (long long)frames * P;
+  if (in_rows < (long long)(frames + kt - 1) * P || M > (1LL << 30) || in_rows > (1LL << 31) - 1)
+    return set_error(LBW_ERR_SHAPE, "lbw_vae_conv_rms: %lld input rows for %d frames", in_rows, frames);
+  if (!aligned(x, 16) || !aligned(w, 16) || !ok16(out) || !ok16(bias) || !aligned(gamma, 16))
+    return set_error(LBW_ERR_ALIGN, "lbw_vae_conv_rms: alignment");
+  int err = 0;
+  int* st = device_status(&err);
+  if (!st) return err;
+  ConvA amap{};
+  amap.cblocks = (c_in + 63) / 64;
+  int t = 0;
+  for (int a = 0; a < kt; ++a)
+    for (int b = 0; b < kh; ++b)
+      for (int c = 0; c < kw; ++c)
+        amap.off[t++] = (int)(a * P + (b - kh / 2) * (long long)(wd + 2) + (c - kw / 2));
+  const int K = t * amap.cblocks * 64;
+  CUtensorMap tmA;
+  if ((err = make_tmap_2d(&tmA, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, in_rows, c_in, c_in, BK, BM))) return err;
+  EpiConvRms e{};
+  e.out = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ldo = c_out;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.gamma = gamma;
+  e.scale_c = sqrtf((float)c_real);
+  e.P = (int)P;
+  e.W2 = wd + 2;
+  e.H2 = h + 2;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // one tile holds the whole row
+  if (c_out == 192) return launch_gemm_t<EpiConvRms, 192, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
+  if (c_out <= 128 && K % gemm::Cfg<128>::BKS == 0)
+    return launch_gemm_t<EpiConvRms, 128, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
+  return launch_gemm_t<EpiConvRms, 256, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
 }
 
 int lbw_linear_act(const void* a, const void* w, const void* bias, const void* addend, int silu, int m, int n, int k,

@@ -421,6 +421,21 @@ def vae_conv(x, in_rows, c_in, w, bias, c_out, k, frames, h, wd, out, residual=N
     return out
 
 
+def vae_conv_rms(x, in_rows, c_in, w, bias, c_out, k, frames, h, wd, gamma, c_real, out):
+    """vae_conv fused with the RMS_norm + SiLU of its output rows (c_out <= 256)."""
+    require_cuda(x, w, bias, gamma, out)
+    kt, kh, kw = k
+    P = (h + 2) * (wd + 2)
+    ck = (c_in + 63) // 64 * 64
+    if x.numel() < in_rows * c_in or w.numel() != c_out * kt * kh * kw * ck or out.numel() < frames * P * c_out:
+        raise ValueError("vae_conv_rms: buffer sizes do not match the convolution")
+    if gamma.dtype != torch.float32 or gamma.numel() < c_out:
+        raise ValueError("vae_conv_rms: gamma must be fp32 [c_out]")
+    check(load().lbw_vae_conv_rms(ptr(x), in_rows, c_in, ptr(w), ptr(bias), c_out, kt, kh, kw, frames, h, wd,
+                                  ptr(gamma), c_real, ptr(out), stream_of(x.device)), "vae_conv_rms")
+    return out
+
+
 def vae_rms_silu(x, rows, c, c_real, gamma, silu, out):
     require_cuda(x, gamma, out)
     if x.numel() < rows * c or out.numel() < rows * c or gamma.numel() < c or gamma.dtype != torch.float32:

@@ -235,10 +235,12 @@ class WanVAEDecoder(nn.Module):
         return h
 
     def _conv_causal(self, key, act, producer, tmax, residual=None):
-        """producer(dest) writes the layer input for act.t frames into the history buffer; then the 3x3x3 conv."""
+        """producer(dest) writes the layer input for act.t frames into the history buffer (None: already written
+        there); then the causal convolution."""
         wk, bk, ks = self._packed[key]
         hist = self._hist_for(key, act, act.cp, tmax)
-        producer(hist.slot(act.t))
+        if producer is not None:
+            producer(hist.slot(act.t))
         out = torch.empty(act.t * act.P, wk.shape[0], dtype=BF16, device=act.data.device)
         kernels.vae_conv(hist.buf, hist.rows(act.t), act.cp, wk, bk, wk.shape[0], ks, act.t, act.h, act.w, out,
                          residual=residual)
@@ -259,6 +261,19 @@ class WanVAEDecoder(nn.Module):
     def _res(self, name, ci, co, x, tmax):
         pk = self._packed
         h = self._conv_plain(f"{name}.sc", x.data, x.t, x.h, x.w) if ci != co else x.data
+        wa, ba, ka = pk[f"{name}.c0"]
+        cop = wa.shape[0]
+        if cop <= 256:
+            # the first convolution writes RMS + SiLU of its rows straight into the second one's input
+            ha = self._hist_for(f"{name}.c0", x, x.cp, tmax)
+            self._rms(x.data, pk[f"{name}.g0"], ci, True)(ha.slot(x.t))
+            ya = _Act(x.data, x.t, x.h, x.w, co)                         # (shape only: P, device)
+            hb = self._hist_for(f"{name}.c1", ya, cop, tmax)
+            kernels.vae_conv_rms(ha.buf, ha.rows(x.t), x.cp, wa, ba, cop, ka, x.t, x.h, x.w, pk[f"{name}.g1"], co,
+                                 hb.slot(x.t))
+            ha.advance(x.t)
+            out = self._conv_causal(f"{name}.c1", _Act(hb.slot(x.t), x.t, x.h, x.w, co), None, tmax, residual=h)
+            return _Act(out, x.t, x.h, x.w, co)
         y = self._conv_causal(f"{name}.c0", x, self._rms(x.data, pk[f"{name}.g0"], ci, True), tmax)
         ya = _Act(y, x.t, x.h, x.w, co)
         out = self._conv_causal(f"{name}.c1", ya, self._rms(y, pk[f"{name}.g1"], co, True), tmax, residual=h)

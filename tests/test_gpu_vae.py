@@ -71,6 +71,40 @@ def test_vae_conv_vs_torch(cuda_dev, k, t, ci, co, h, w):
     assert not rows[:, 0].any() and not rows[:, -1].any() and not rows[:, :, 0].any() and not rows[:, :, -1].any()
 
 
+@pytest.mark.parametrize("ci,co,t", [(96, 96, 2), (64, 192, 1), (16, 32, 2)])
+def test_vae_conv_rms_fused(cuda_dev, ci, co, t):
+    """The first ResidualBlock convolution with its RMS_norm + SiLU in the epilogue equals the convolution followed
+    by the separate RMS + SiLU kernel (128-, 192- and 256-wide tiles holding whole rows)."""
+    import lbw_b200.kernels as K
+    g = _g(ci + co)
+    h, w = 5, 6
+    x = torch.randn(t + 2, ci, h, w, generator=g).to(BF).float()
+    wt = (torch.randn(co, ci, 3, 3, 3, generator=g) / math.sqrt(ci * 27)).to(BF).float()
+    b = (torch.randn(co, generator=g) * 0.1).to(BF)
+    gamma = 1 + 0.1 * torch.randn(co, generator=g)
+    cis, cop = (ci + 7) // 8 * 8, (co + 31) // 32 * 32
+    cik = (cis + 63) // 64 * 64
+    P = (h + 2) * (w + 2)
+    d = cuda_dev
+    xr = _padded(x, cis).to(d)
+    wk = _pack(wt, cik, cop).to(d)
+    bp = torch.zeros(cop, dtype=BF)
+    bp[:co] = b
+    gp = torch.zeros(cop)
+    gp[:co] = gamma
+    fused = torch.full((t * P, cop), 3.0, dtype=BF, device=d)
+    K.vae_conv_rms(xr, (t + 2) * P, cis, wk, bp.to(d), cop, (3, 3, 3), t, h, w, gp.to(d), co, fused)
+    y = torch.empty(t * P, cop, dtype=BF, device=d)
+    K.vae_conv(xr, (t + 2) * P, cis, wk, bp.to(d), cop, (3, 3, 3), t, h, w, y)
+    sep = torch.empty_like(y)
+    K.vae_rms_silu(y, t * P, cop, co, gp.to(d), True, sep)
+    assert rel_l2(fused.float(), sep.float()) < 1e-2
+    ref = F.conv3d(x.permute(1, 0, 2, 3).unsqueeze(0), wt, b.float(), padding=(0, 1, 1))[0].permute(1, 0, 2, 3)
+    ref = F.silu(ov.rms_norm(ref.to(BF).float(), gamma))
+    assert rel_l2(_unpad(fused.cpu(), t, h, w, co), ref) < 2e-2
+    assert not fused.cpu().reshape(t, h + 2, w + 2, cop)[:, 0].any()
+
+
 def test_vae_rms_silu(cuda_dev):
     import lbw_b200.kernels as K
     g = _g(3)
