@@ -201,3 +201,19 @@ def test_vae_decode_chunk_streams_like_one_decode(cuda_dev):
     b = m.decode_chunk(g["z"][:, 2:], ov.latent_scale())
     assert torch.equal(torch.cat([a, b], dim=1), full)
     assert rel_l2(torch.cat([a, b], dim=1).clamp(-1, 1).cpu(), g["out_chunks"]) < 3e-2
+
+
+def test_wan21_vae_wrapper_decode(cuda_dev):
+    """Wan2_1_VAE (the reference's decode interface) from a full WanVAE_-style state dict: encoder entries are
+    ignored, the bf16 latent scale is applied, frames come back clamped to [-1, 1]."""
+    import lbw_b200.vae as V
+    g = load_golden("vae_decode")
+    sd = dict(ov.make_params(g["seed"], **g["cfg"]))
+    sd["encoder.conv1.weight"] = torch.zeros(4, 3, 3, 3, 3)       # present in the reference checkpoint, unused here
+    vae = V.Wan2_1_VAE(z_dim=16, dim=g["cfg"]["dim"], device=cuda_dev, state_dict=sd)
+    out = vae.decode([g["z"]])[0].cpu()
+    assert out.shape == g["out"].shape and float(out.abs().max()) <= 1.0
+    assert rel_l2(out, g["out"]) < 3e-2
+    a = vae.decode_chunk(g["z"][:, :2], True)
+    b = vae.decode_chunk(g["z"][:, 2:], False)
+    assert torch.equal(torch.cat([a, b], dim=1).cpu(), out)
