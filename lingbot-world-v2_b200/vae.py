@@ -322,7 +322,7 @@ class WanVAEDecoder(nn.Module):
         return _Act(out, x.t, h2, w2, c // 2)
 
     def _frame(self, xin):
-        """One Decoder3d pass (vae2_1.py:428-477) on one latent frame (padded rows, z channels padded to 64)."""
+        """One Decoder3d pass (vae2_1.py:428-477) on one latent frame (padded rows of conv2's output)."""
         pk = self._packed
         x = xin
         tmax = 1
