@@ -204,3 +204,21 @@ def test_vae_decoder_parameter_names_match_the_reference():
         assert got == {n: tuple(s) for n, s in ov.param_shapes(dim=dim)}
     with pytest.raises(ValueError, match="CUDA"):
         V.WanVAEDecoder(dim=32).prepare()
+
+
+def test_vae_history_buffer_keeps_the_last_two_frames():
+    """The per-layer causal buffer of the VAE decoder: after each call its frames 0-1 are the last two frames of
+    the layer's whole input series (zeros before the first frame), whatever the number of frames per call."""
+    import lbw_b200.vae as V
+    P, c = 3, 2
+    h = V._Hist(P, c, 4, "cpu")
+    series = [torch.zeros(P, c, dtype=torch.bfloat16), torch.zeros(P, c, dtype=torch.bfloat16)]
+    val = 1.0
+    for t in (1, 1, 2, 4, 1, 4, 2):
+        frames = [torch.full((P, c), val + i, dtype=torch.bfloat16) for i in range(t)]
+        val += t
+        h.slot(t).copy_(torch.cat(frames))
+        assert torch.equal(h.buf[:2 * P], torch.cat(series[-2:]))      # what the convolution reads in front
+        series += frames
+        h.advance(t)
+        assert torch.equal(h.buf[:2 * P], torch.cat(series[-2:]))
