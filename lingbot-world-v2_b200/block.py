@@ -20,7 +20,6 @@ One forward = 14 kernels of liblbw.so on the current stream:
 an mx_quantize of the attention output before each of the two o-projections).
 The fp32 residual is updated in place by the GEMM epilogues.
 """
-import math
 
 import torch
 import torch.nn as nn

@@ -16,7 +16,6 @@ hoisted camera FiLM) path, keeping the reference's dtypes:
   * the blocks (oracle.block.block_forward) on the fp32 residual (:3771, :3830-3852)
   * CausalHead: LN(x) * (1 + e1) + e0 with e = modulation + e, fp32 Linear (:3119-3148); unpatchify (:4419-4440)
 """
-import math
 
 import torch
 import torch.nn.functional as F
