@@ -11,6 +11,11 @@ On CUDA the gather is PeerKV.gather: each rank stages its shard in a CUDA-IPC bu
 with copy engines, synchronised by stream memory operations (liblbw's lbw_sp_kv_gather), so no SM is taken
 from the attention it overlaps. gather_rows_inplace (one in-place all_gather_into_tensor per tensor) is the
 same exchange through torch.distributed; the CPU (gloo) tests use it.
+
+Failure detection is on the host, between steps: Liveness announces each rank's step in the process group's
+store so that a rank learns of a failed, departed or stalled peer before it launches an exchange that would
+wait on it, and abort() tears the group down without the collective barrier. Collectives themselves end by
+the process group's timeout.
 """
 import ctypes
 
@@ -120,13 +125,15 @@ class PeerKV:
         self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
         self.epoch = 0
 
-    def close(self):
+    def close(self, collective=True):
         """Collective: every rank's pulls have completed (device synchronisation + barrier) before the peers'
-        mappings are closed and this rank's buffer is freed."""
+        mappings are closed and this rank's buffer is freed. collective=False skips the barrier (teardown after a
+        peer was lost, see abort())."""
         if self._ptrs is None:
             return
         torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
+        if collective:
+            dist.barrier(group=self.group)
         lib = self._lib.load()
         with torch.cuda.device(self.device):
             for r, p in enumerate(self._ptrs):
@@ -186,6 +193,107 @@ def close_peers():
     """Collective: release every copy-engine exchange of this process (before destroying its process group)."""
     for key in list(_PEERS):
         _PEERS.pop(key).close()
+
+
+class PeerLost(RuntimeError):
+    """A rank of the group stopped taking part: it reported a failure, left, or missed a step's deadline."""
+
+    def __init__(self, msg, ranks):
+        super().__init__(msg)
+        self.ranks = tuple(ranks)
+
+
+class Liveness:
+    """Between-step liveness of a group's ranks, kept in the process group's key-value store.
+
+    The copy-engine exchange has no time limit of its own (a stream waits on its peers' ready words), so a rank
+    must not launch the next step's exchange while a peer is gone. Each rank calls beat(step) before a step's
+    launches and wait(step) before its first exchange: wait returns once every rank has announced `step` (or a
+    later one) and raises PeerLost, naming the ranks, when one has reported a failure (fail), left (leave) or
+    not announced the step within `timeout_s`. Nothing here touches a GPU; only the store is used.
+    """
+
+    LEFT = -1
+
+    def __init__(self, timeout_s=30.0, prefix="lbw/live", store=None, poll_s=0.005):
+        import torch.distributed.distributed_c10d as c10d
+        if not dist.is_initialized():
+            raise RuntimeError("Liveness needs an initialised process group")
+        self.store = store if store is not None else c10d._get_default_store()
+        self.timeout_s, self.poll_s, self.prefix = float(timeout_s), float(poll_s), prefix
+        self.rank, self.world = rank(), world()
+        self._ranks = (dist.get_process_group_ranks(_GROUP) if _GROUP is not None else list(range(self.world)))
+
+    def _key(self, r, what="step"):
+        return f"{self.prefix}/{what}/{self._ranks[r]}"
+
+    def beat(self, step):
+        """This rank starts `step` (a non-negative step counter that only grows)."""
+        if step < 0:
+            raise ValueError(f"step {step} < 0")
+        self.store.set(self._key(self.rank), str(int(step)))
+
+    def leave(self):
+        """This rank leaves the group cleanly between steps; the others' next wait raises PeerLost."""
+        self.store.set(self._key(self.rank), str(self.LEFT))
+
+    def fail(self, reason):
+        """Report this rank's failure (an exception between steps) to the others, then leave."""
+        self.store.set(self._key(self.rank, "error"), str(reason)[:500])
+        self.leave()
+
+    def _peek(self, r):
+        k = self._key(r)
+        if not self.store.check([k]):
+            return None
+        return int(self.store.get(k))
+
+    def wait(self, step):
+        """Return when every rank has announced `step` or a later one; raise PeerLost otherwise (also when
+        the store itself is gone, e.g. with the process that hosted it)."""
+        try:
+            return self._wait(step)
+        except PeerLost:
+            raise
+        except (RuntimeError, OSError) as e:  # DistStoreError derives from RuntimeError
+            raise PeerLost(f"step {step}: key-value store unreachable ({e})", ()) from e
+
+    def _wait(self, step):
+        import time
+        deadline = time.monotonic() + self.timeout_s
+        pending = [r for r in range(self.world) if r != self.rank]
+        while True:
+            lost, behind = [], []
+            for r in pending:
+                s = self._peek(r)
+                if s == self.LEFT:
+                    lost.append(r)
+                elif s is None or s < step:
+                    behind.append(r)
+            if lost:
+                why = []
+                for r in lost:
+                    ek = self._key(r, "error")
+                    why.append(f"rank {r}: " + (self.store.get(ek).decode() if self.store.check([ek]) else "left"))
+                raise PeerLost(f"step {step}: " + "; ".join(why), lost)
+            if not behind:
+                return
+            if time.monotonic() > deadline:
+                raise PeerLost(f"step {step}: rank(s) {behind} did not reach it within {self.timeout_s:.1f} s",
+                               behind)
+            pending = behind
+            time.sleep(self.poll_s)
+
+
+def abort(group=None):
+    """Tear down after a PeerLost or a collective timeout: release the copy-engine exchanges without the
+    collective barrier (the lost ranks would never reach it) and abort the process group, so no rank waits on
+    a peer that is gone. Call between steps, with none of this rank's exchanges in flight."""
+    for key in list(_PEERS):
+        _PEERS.pop(key).close(collective=False)
+    if dist.is_initialized():
+        import torch.distributed.distributed_c10d as c10d
+        c10d._abort_process_group(group)
 
 
 def gather_kv_inplace(k2d, v2d, local_rows):
