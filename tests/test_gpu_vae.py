@@ -42,7 +42,11 @@ def _pack(wt, cip, cop):
                                            ((3, 3, 3), 2, 64, 192, 5, 6),    # 192-wide tiles
                                            ((1, 1, 1), 1, 128, 384, 4, 4),   # two 192-wide tiles
                                            ((3, 3, 3), 2, 96, 3, 4, 6),      # the head: 64-wide tiles
-                                           ((3, 3, 3), 2, 16, 32, 3, 4)])    # 16 stored channels in a 64 block
+                                           ((3, 3, 3), 2, 16, 32, 3, 4),     # 16 stored channels in a 64 block
+                                           ((3, 3, 3), 2, 96, 96, 6, 9),     # the full-resolution level (dim 96)
+                                           ((3, 3, 3), 1, 192, 96, 4, 5),    # upsampled 192 -> 96 channels
+                                           ((3, 3, 3), 1, 384, 384, 3, 4),   # the lowest levels (dim 96)
+                                           ((3, 3, 3), 2, 32, 32, 3, 4)])    # 32 channels (dim 32)
 def test_vae_conv_vs_torch(cuda_dev, k, t, ci, co, h, w):
     import lbw_b200.kernels as K
     g = _g(ci + co + t)
