@@ -1,0 +1,148 @@
+"""The chunk-attention kernel's barrier protocol (lingbot-world-v2_b200/csrc/attn.cu, chunk_attn_kernel) run in the
+discrete-event model of tests/protocol_model.py under random TMA / MMA latencies, delayed commit arrivals, ragged
+tiles and random O rescales: no aliased parity wait, no deadlock, and the hazards below hold where the kernel
+relies on them.
+
+The programs restate the kernel's synchronisation, step for step:
+  producer   Q once; per key tile j: wait k_empty[j % 2] (use j / 2), load K; wait v_empty, load V
+  issuer     S_0 = Q_0 K_0^T (and S_1 with two query tiles), commit s_full; commit k_empty[0]; per tile j:
+             wait v_full and p_ready[0][0] -> P_0 V (keys 0..63); wait p_ready[0][1] -> P_0 V (keys 64..127);
+             next S_0 (wait k_full), commit s_full[0]; then the same P_1 V for the second tile; commit v_empty;
+             next S_1, commit s_full[1]; commit k_empty; finally commit o_done
+  softmax i  per tile: wait s_full[i]; P over S; without a rescale and on a full tile it arrives p_ready[i][0]
+             once keys 0..63 of P are written, else after the rescale of O; then p_ready[i][1]
+Hazards: S is complete when read; P (j) is written only after the P V that read P (j - 1) completed; O is rescaled
+only while no P V of that query tile runs; a K or V ring slot is refilled only after every MMA that read it
+completed."""
+import random
+
+import pytest
+
+from protocol_model import Bar, Model
+
+
+def attention_v1(m, n_tiles, two, rescale_p, ragged_p):
+    nq = 2 if two else 1
+    q_full = Bar("q_full")
+    k_full, k_empty = [Bar(f"k_full{s}") for s in range(2)], [Bar(f"k_empty{s}") for s in range(2)]
+    v_full, v_empty = [Bar(f"v_full{s}") for s in range(2)], [Bar(f"v_empty{s}") for s in range(2)]
+    s_full = [Bar(f"s_full{i}") for i in range(2)]
+    p_ready = [[Bar(f"p_ready{i}{h}", 4) for h in range(2)] for i in range(2)]   # 4 warps per warpgroup
+    o_done = Bar("o_done")
+    MMA_S, MMA_PV = 512, 256                     # 128 x 128 x 128 S; P V over 64 keys
+
+    def producer():
+        yield ("tma", q_full, ("Q",))
+        for j in range(n_tiles):
+            s = j & 1
+            yield ("wait", k_empty[s], j >> 1)
+            if j >= 2:
+                for i in range(nq):
+                    assert m.complete(("S", i, j - 2)), ("K slot refilled while read", j)
+            yield ("tma", k_full[s], ("K", j))
+            yield ("wait", v_empty[s], j >> 1)
+            if j >= 2:
+                for i in range(nq):
+                    for h in range(2):
+                        assert m.complete(("PV", i, h, j - 2)), ("V slot refilled while read", j)
+            yield ("tma", v_full[s], ("V", j))
+
+    def issuer():
+        yield ("wait", q_full, 1)
+        yield ("wait", k_full[0], 1)
+        for i in range(nq):
+            yield ("mma", ("S", i, 0), MMA_S)
+            yield ("commit", s_full[i])
+        yield ("commit", k_empty[0])
+        for j in range(n_tiles):
+            s, more, s1 = j & 1, j + 1 < n_tiles, (j + 1) & 1
+            yield ("wait", v_full[s], (j >> 1) + 1)
+            yield ("wait", p_ready[0][0], j + 1)
+            yield ("mma", ("PV", 0, 0, j), MMA_PV)
+            yield ("wait", p_ready[0][1], j + 1)
+            yield ("mma", ("PV", 0, 1, j), MMA_PV)
+            if more:
+                yield ("wait", k_full[s1], ((j + 1) >> 1) + 1)
+                yield ("mma", ("S", 0, j + 1), MMA_S)
+                yield ("commit", s_full[0])
+            if two:
+                yield ("wait", p_ready[1][0], j + 1)
+                yield ("mma", ("PV", 1, 0, j), MMA_PV)
+                yield ("wait", p_ready[1][1], j + 1)
+                yield ("mma", ("PV", 1, 1, j), MMA_PV)
+            yield ("commit", v_empty[s])
+            if more:
+                if two:
+                    yield ("mma", ("S", 1, j + 1), MMA_S)
+                    yield ("commit", s_full[1])
+                yield ("commit", k_empty[s1])
+        yield ("commit", o_done)
+
+    def softmax(wg):
+        for j in range(n_tiles):
+            yield ("wait", s_full[wg], j + 1)
+            assert m.complete(("S", wg, j)), ("S read before complete", wg, j)
+            if j >= 1:
+                for h in range(2):
+                    assert m.complete(("PV", wg, h, j - 1)), ("P overwritten while read", wg, j)
+            rescale = j > 0 and m.rng.random() < rescale_p
+            full = m.rng.random() >= ragged_p
+            yield ("work", m.rng.uniform(300, 600))
+            if full and not rescale:
+                for _ in range(4):
+                    yield ("arrive", p_ready[wg][0])
+            yield ("work", m.rng.uniform(300, 600))
+            if rescale:
+                for tag in m.issued:
+                    if tag[0] == "PV" and tag[1] == wg:
+                        assert m.complete(tag), ("O rescaled while a P V runs", wg, j, tag)
+                yield ("work", 300)
+            if rescale or not full:
+                for _ in range(4):
+                    yield ("arrive", p_ready[wg][0])
+            for _ in range(4):
+                yield ("arrive", p_ready[wg][1])
+        yield ("wait", o_done, 1)
+        for tag in m.issued:
+            if tag[0] == "PV" and tag[1] == wg:
+                assert m.complete(tag), ("epilogue before the last P V", wg)
+
+    m.spawn(producer(), "producer")
+    m.spawn(issuer(), "issuer")
+    for wg in range(nq):
+        m.spawn(softmax(wg), f"softmax{wg}")
+
+
+@pytest.mark.parametrize("jitter", [0.0, 300.0, 3000.0])
+def test_attention_protocol_random_schedules(jitter):
+    for seed in range(400):
+        rng = random.Random(seed)
+        m = Model(seed, commit_jitter=jitter)
+        attention_v1(m, n_tiles=rng.randint(1, 7), two=rng.random() < 0.7, rescale_p=rng.choice([0.0, 0.3, 1.0]),
+                     ragged_p=rng.choice([0.0, 0.5]))
+        m.run()
+
+
+def test_model_catches_a_wrong_phase():
+    """A planted mistake in the model (the second query tile's issuer waits for the previous tile's P) must be
+    reported."""
+    def broken(m, n_tiles):
+        b = Bar("p_ready")
+
+        def softmax():
+            for j in range(n_tiles):
+                yield ("work", 10)
+                yield ("arrive", b)
+
+        def issuer():
+            for j in range(n_tiles):
+                yield ("work", 1000)
+                yield ("wait", b, j)        # should be j + 1: passes on an older phase
+        m.spawn(softmax(), "softmax")
+        m.spawn(issuer(), "issuer")
+
+    with pytest.raises(AssertionError):
+        for seed in range(20):
+            m = Model(seed)
+            broken(m, 4)
+            m.run()
