@@ -1,7 +1,10 @@
-"""The chunk-attention kernel's barrier protocol (lingbot-world-v2_b200/csrc/attn.cu, chunk_attn_kernel) run in the
-discrete-event model of tests/protocol_model.py under random TMA / MMA latencies, delayed commit arrivals, ragged
-tiles and random O rescales: no aliased parity wait, no deadlock, and the hazards below hold where the kernel
-relies on them.
+"""The barrier protocols of the chunk-attention kernel (lingbot-world-v2_b200/csrc/attn.cu, chunk_attn_kernel) and of
+the persistent GEMMs (csrc/gemm_bf16.cu gemm_bf16_kernel: two TMEM accumulators; csrc/gemm_mx.cu gemm_mx_kernel:
+one) run in the discrete-event model of tests/protocol_model.py under random TMA / MMA latencies, delayed commit
+arrivals, ragged tiles and random O rescales: no aliased parity wait, no deadlock, and the hazards below hold
+where the kernels rely on them.
+
+Attention:
 
 The programs restate the kernel's synchronisation, step for step:
   producer   Q once; per key tile j: wait k_empty[j % 2] (use j / 2), load K; wait v_empty, load V
@@ -13,7 +16,16 @@ The programs restate the kernel's synchronisation, step for step:
              once keys 0..63 of P are written, else after the rescale of O; then p_ready[i][1]
 Hazards: S is complete when read; P (j) is written only after the P V that read P (j - 1) completed; O is rescaled
 only while no P V of that query tile runs; a K or V ring slot is refilled only after every MMA that read it
-completed."""
+completed.
+
+Persistent GEMM (one CTA's tiles t = 0, 1, ...):
+  producer   per tile, per K stage: wait empty[s] (its previous use), load A and B into slot s
+  issuer     per tile: wait tempty[acc] (the epilogue has released that accumulator), per K stage wait full[s],
+             MMAs into the accumulator, commit empty[s]; then commit tfull[acc]; acc alternates (two accumulators)
+             or stays 0 (one)
+  epilogue   each of the 8 warps per tile: wait tfull[acc], read its rows of the accumulator, arrive tempty[acc]
+Hazards: the accumulator is read only after every MMA of its tile completed, and is written by the next tile's
+MMAs only after all 8 warps read it; a ring slot is refilled only after the MMAs that read it completed."""
 import random
 
 import pytest
@@ -146,3 +158,62 @@ def test_model_catches_a_wrong_phase():
             m = Model(seed)
             broken(m, 4)
             m.run()
+
+
+def persistent_gemm(m, tiles, n_k, stages, n_acc, epi_warps=8):
+    full, empty = [Bar(f"full{s}") for s in range(stages)], [Bar(f"empty{s}") for s in range(stages)]
+    tfull, tempty = [Bar(f"tfull{a}") for a in range(n_acc)], [Bar(f"tempty{a}", epi_warps) for a in range(n_acc)]
+    read = {}                      # tile -> number of epilogue warps that have read its accumulator
+
+    def producer():
+        use = [0] * stages
+        s = 0
+        for t in range(tiles):
+            for kb in range(n_k):
+                yield ("wait", empty[s], use[s])
+                if use[s] > 0:
+                    assert all(m.complete(tag) for tag in m.issued if tag[2] == (s, use[s] - 1)), "slot refilled"
+                yield ("tma", full[s], ("AB", t, kb))
+                use[s] += 1
+                s = (s + 1) % stages
+
+    def issuer():
+        use = [0] * stages
+        s = 0
+        for t in range(tiles):
+            acc = t % n_acc
+            yield ("wait", tempty[acc], t // n_acc)
+            if t >= n_acc:
+                assert read.get(t - n_acc, 0) == epi_warps, ("accumulator overwritten while read", t)
+            for kb in range(n_k):
+                yield ("wait", full[s], use[s] + 1)
+                yield ("mma", ("MMA", t, (s, use[s])), m.rng.uniform(100, 600))
+                yield ("commit", empty[s])
+                use[s] += 1
+                s = (s + 1) % stages
+            yield ("commit", tfull[acc])
+
+    def epilogue(w):
+        for t in range(tiles):
+            acc = t % n_acc
+            yield ("wait", tfull[acc], t // n_acc + 1)
+            assert all(m.complete(tag) for tag in m.issued if tag[1] == t), ("accumulator read early", t)
+            yield ("work", m.rng.uniform(50, 400))
+            read[t] = read.get(t, 0) + 1
+            yield ("arrive", tempty[acc])
+            yield ("work", m.rng.uniform(0, 800))      # epilogue math after the release (one-accumulator kernel)
+
+    m.spawn(producer(), "producer")
+    m.spawn(issuer(), "issuer")
+    for w in range(epi_warps):
+        m.spawn(epilogue(w), f"epilogue{w}")
+
+
+@pytest.mark.parametrize("n_acc,stages", [(2, 4), (2, 3), (1, 4), (1, 3)])
+@pytest.mark.parametrize("jitter", [0.0, 2000.0])
+def test_persistent_gemm_protocol_random_schedules(n_acc, stages, jitter):
+    for seed in range(150):
+        rng = random.Random(seed)
+        m = Model(seed, commit_jitter=jitter)
+        persistent_gemm(m, tiles=rng.randint(1, 6), n_k=rng.randint(1, 9), stages=stages, n_acc=n_acc)
+        m.run()
