@@ -3,7 +3,8 @@
 The kernels of this library coordinate their warps (TMA producer, MMA issuer, softmax / epilogue warps) through
 shared-memory mbarriers waited on by phase parity, and through tcgen05.commit, which arrives on an mbarrier once
 every MMA issued before it by the thread has completed. A protocol written as programs over these primitives
-(`wait`, `arrive`, `mma`, `commit`, `tma`, `work`) runs here under random latencies. The model checks:
+(`wait`, `arrive`, `mma`, `commit`, `tma`, `work`; for streams `waitge` / `write` on 32-bit flags and `copy`) runs
+here under random latencies. The model checks:
   * every parity wait returns exactly at the completion it intends (a wait that passes on an older or newer phase
     of the same parity is an aliasing bug that a GPU would turn into a rare data race);
   * no program is left waiting (deadlock);
@@ -29,6 +30,13 @@ class Bar:
         # it; c == 0 is a producer's first-use wait (parity 1 on a fresh barrier, passes at k = 0)
         par = ((c - 1) & 1) if c >= 1 else 1
         return (self.k & 1) != par
+
+
+class Flag:
+    """A 32-bit word waited on with ">= value" (a CUDA stream memory-operation flag, or an event's record count)."""
+
+    def __init__(self, name, value=0):
+        self.name, self.value, self.waiters = name, value, []
 
 
 class Model:
@@ -100,6 +108,33 @@ class Model:
                 t_arr = self._pipe_free + (self.rng.uniform(0, self.jitter) if self.jitter else 0.0)
                 self.at(max(t_arr, self.t), lambda: self._arrive(bar))
                 self.at(self.t + 1, step)
+            elif kind == "waitge":
+                flag, v = cmd[1], cmd[2]
+
+                def check_flag():
+                    if flag.value >= v:
+                        self.at(self.t, step)
+                    else:
+                        flag.waiters.append(check_flag)
+                check_flag()
+            elif kind == "write":
+                flag, v = cmd[1], cmd[2]
+                assert v >= flag.value, f"{name}: {flag.name} moved back from {flag.value} to {v}"
+                flag.value = v
+                waiters, flag.waiters = flag.waiters, []
+                for w in waiters:
+                    self.at(self.t, w)
+                self.at(self.t, step)
+            elif kind == "copy":
+                # ("copy", on_start, on_end, duration): a copy-engine transfer in stream order; the callbacks
+                # check and update the state of the buffers it reads and writes
+                cmd[1]()
+                end = cmd[2]
+
+                def finish():
+                    end()
+                    step()
+                self.at(self.t + cmd[3], finish)
             elif kind == "tma":
                 bar, tag = cmd[1], cmd[2]
 

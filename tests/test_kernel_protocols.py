@@ -25,12 +25,24 @@ Persistent GEMM (one CTA's tiles t = 0, 1, ...):
              or stays 0 (one)
   epilogue   each of the 8 warps per tile: wait tfull[acc], read its rows of the accumulator, arrive tempty[acc]
 Hazards: the accumulator is read only after every MMA of its tile completed, and is written by the next tile's
-MMAs only after all 8 warps read it; a ring slot is refilled only after the MMAs that read it completed."""
+MMAs only after all 8 warps read it; a ring slot is refilled only after the MMAs that read it completed.
+
+Sequence-parallel K/V exchange (csrc/peer.cu lbw_sp_kv_stage / lbw_sp_kv_gather, driven by block.py
+_self_attention), per rank and exchange e:
+  main stream    the block's kernels (which write this rank's rows of the destination chunk); stage: wait
+                 done[me][p] >= e - 1 from every peer, copy this rank's rows into its staging buffer, record an event;
+                 the gated attention (whose destination-chunk tiles wait for gathered >= e); wait for the comm stream
+  comm stream    wait that event; write ready[p][me] = e in every peer's buffer; wait ready[me][p] >= e; start the
+                 pulls; join them; write done[p][me] = e in every peer's buffer; write gathered[me] = e
+  pull streams   (one per peer) copy the peer's staging buffer into its rows of the destination chunk
+Hazards: a staging buffer is rewritten only after every peer's pull of it finished, and is pulled only once it
+holds the exchange's rows; the attention reads the destination chunk only when every rank's rows of this exchange
+have landed."""
 import random
 
 import pytest
 
-from protocol_model import Bar, Model
+from protocol_model import Bar, Flag, Model
 
 
 def attention_v1(m, n_tiles, two, rescale_p, ragged_p):
@@ -217,3 +229,94 @@ def test_persistent_gemm_protocol_random_schedules(n_acc, stages, jitter):
         m = Model(seed, commit_jitter=jitter)
         persistent_gemm(m, tiles=rng.randint(1, 6), n_k=rng.randint(1, 9), stages=stages, n_acc=n_acc)
         m.run()
+
+
+def peer_exchange(m, world, epochs, skip_done_wait=False):
+    ready = [[Flag(f"ready{x}{y}") for y in range(world)] for x in range(world)]   # in x's buffer, written by y
+    done = [[Flag(f"done{x}{y}") for y in range(world)] for x in range(world)]
+    gathered = [Flag(f"gathered{x}") for x in range(world)]
+    ev_staged, ev_pull, ev_comm = ([Flag(f"{n}{x}") for x in range(world)] for n in ("staged", "pull", "comm"))
+    ev_pulled = [[Flag(f"pulled{x}{y}") for y in range(world)] for x in range(world)]
+    staging = [{"epoch": 0, "version": 0, "busy": False, "readers": 0} for _ in range(world)]
+    dest = [[0] * world for _ in range(world)]      # exchange whose rows p sit in rank r's destination chunk
+    peers = lambda r: [p for p in range(world) if p != r]
+
+    def main(r):
+        for e in range(1, epochs + 1):
+            yield ("work", m.rng.uniform(100, 3000))       # the block's kernels; they write this rank's own rows
+            dest[r][r] = e
+            if e > 1 and not skip_done_wait:
+                for p in peers(r):
+                    yield ("waitge", done[r][p], e - 1)
+            st = staging[r]
+
+            def begin(st=st):
+                assert st["readers"] == 0, "staging buffer rewritten while a peer pulls it"
+                st["busy"], st["version"] = True, st["version"] + 1
+
+            def end(st=st, e=e):
+                st["busy"], st["epoch"] = False, e
+            yield ("copy", begin, end, m.rng.uniform(50, 400))
+            yield ("write", ev_staged[r], e)
+            yield ("work", m.rng.uniform(0, 2000))          # attention over the leading chunks
+            yield ("waitge", gathered[r], e)                # the gated tiles' poll
+            assert all(dest[r][p] == e for p in range(world)), ("destination read before it landed", r, e)
+            yield ("work", m.rng.uniform(0, 500))
+            yield ("waitge", ev_comm[r], e)
+
+    def comm(r):
+        for e in range(1, epochs + 1):
+            yield ("waitge", ev_staged[r], e)
+            for p in peers(r):
+                yield ("write", ready[p][r], e)
+            for p in peers(r):
+                yield ("waitge", ready[r][p], e)
+            yield ("write", ev_pull[r], e)
+            for p in peers(r):
+                yield ("waitge", ev_pulled[r][p], e)
+            for p in peers(r):
+                yield ("write", done[p][r], e)
+            yield ("write", gathered[r], e)
+            yield ("write", ev_comm[r], e)
+
+    def pull(r, p):
+        for e in range(1, epochs + 1):
+            yield ("waitge", ev_pull[r], e)
+            st = staging[p]
+            seen = {}
+
+            def begin(st=st, e=e):
+                assert not st["busy"] and st["epoch"] == e, ("pulled a staging buffer not holding the exchange", e)
+                st["readers"] += 1
+                seen["v"] = st["version"]
+
+            def end(st=st, e=e):
+                assert st["version"] == seen["v"], "staging buffer changed during a pull"
+                st["readers"] -= 1
+                dest[r][p] = e
+            yield ("copy", begin, end, m.rng.uniform(100, 1500))
+            yield ("write", ev_pulled[r][p], e)
+
+    for r in range(world):
+        m.spawn(main(r), f"main{r}")
+        m.spawn(comm(r), f"comm{r}")
+        for p in peers(r):
+            m.spawn(pull(r, p), f"pull{r}<-{p}")
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_peer_exchange_protocol_random_schedules(world):
+    for seed in range(60):
+        rng = random.Random(seed)
+        m = Model(seed)
+        peer_exchange(m, world, epochs=rng.randint(1, 6))
+        m.run()
+
+
+def test_peer_exchange_model_catches_a_missing_wait():
+    """Without the stage's wait for the peers' done flags a rank may rewrite its staging buffer under a pull."""
+    with pytest.raises(AssertionError):
+        for seed in range(200):
+            m = Model(seed)
+            peer_exchange(m, 4, epochs=6, skip_done_wait=True)
+            m.run()
