@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4] [--impl lbw|reference]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N   (sequence parallel)
 
-Workload (the headline): 40 blocks of the 14B geometry (dim 5120, 40 heads,
+Workload (benchmark configuration c4, the headline): 40 blocks of the 14B geometry (dim 5120, 40 heads,
 FFN 13824), one 720p chunk of 3 latent frames (45 x 80 tokens per frame, 10,800 query tokens) against a
 21-frame KV window (6 cached chunks + the destination chunk = 75,600 keys), 512 text tokens, hoisted
 camera FiLM, MXFP8 FFN. Synthetic seeded data with the benchmark distributions (no checkpoints here).
@@ -197,7 +197,7 @@ def run_reference(args):
 
 
 def run_sweep(args):
-    """BASELINE configs[4] (c5): kernel sweep on one GPU. Chunk attention with 40 heads x 128 over
+    """Benchmark configuration c5: kernel sweep on one GPU. Chunk attention with 40 heads x 128 over
     Lq in {1560, 4680, 10800} x Lkv in {4096, 16384, 32768, 75600, 131072}; MXFP8 FFN GEMMs (E4M3, E8M0 per
     32) M in {4680, 10800, 43200} for up (K 5120 -> N 13824) and down (13824 -> 5120). One JSON line per
     point: TFLOP/s from CUDA events around each launch (median of 5, an L2 flush before each launch) and the
@@ -468,7 +468,7 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=int(os.environ.get("LBW_CPU_ROWS", "1350")))
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--sweep", action="store_true", help="kernel sweep (BASELINE configs[4]) instead of the step")
+    ap.add_argument("--sweep", action="store_true", help="kernel sweep (benchmark configuration c5) instead of the step")
     ap.add_argument("--sweep-only", default="all", choices=["all", "attention", "mxfp8", "gemm", "linmx", "tiles"],
                     help="with --sweep: one family of points (gemm = the block's bf16 GEMMs at 10,800 and 1,350 rows)")
     ap.add_argument("--lin-mx", action="store_true",
