@@ -219,7 +219,12 @@ class Liveness:
         import torch.distributed.distributed_c10d as c10d
         if not dist.is_initialized():
             raise RuntimeError("Liveness needs an initialised process group")
-        self.store = store if store is not None else c10d._get_default_store()
+        if store is None:
+            get = getattr(c10d, "_get_default_store", None)   # the store init_process_group created
+            if get is None:
+                raise RuntimeError("Liveness: this torch.distributed has no default store; pass store=")
+            store = get()
+        self.store = store
         self.timeout_s, self.poll_s, self.prefix = float(timeout_s), float(poll_s), prefix
         self.rank, self.world = rank(), world()
         self._ranks = (dist.get_process_group_ranks(_GROUP) if _GROUP is not None else list(range(self.world)))
@@ -293,7 +298,11 @@ def abort(group=None):
         _PEERS.pop(key).close(collective=False)
     if dist.is_initialized():
         import torch.distributed.distributed_c10d as c10d
-        c10d._abort_process_group(group)
+        abort_pg = getattr(c10d, "_abort_process_group", None)
+        if abort_pg is not None:
+            abort_pg(group)          # ends the group's pending collectives without waiting for the lost ranks
+        else:
+            dist.destroy_process_group(group)
 
 
 def gather_kv_inplace(k2d, v2d, local_rows):
