@@ -504,14 +504,16 @@ static int launch_attention(const void* q, long long ldq, int q_rows, int heads,
   kv.n_tiles = n_tiles;
   if (n_splits < 1 || n_splits > n_tiles)
     return set_error(LBW_ERR_SHAPE, "chunk_attention: %d KV splits for %d key tiles", n_splits, n_tiles);
-  static bool attr[2] = {false, false};
+  static bool attr[64][2] = {};  // per device and variant
   const int hb = key_bias ? 1 : 0;
-  if (!attr[hb]) {
+  const int dix = device_index();
+  if (dix < 0) return set_error(LBW_ERR_CUDA, "chunk_attention: cudaGetDevice failed");
+  if (!attr[dix][hb]) {
     err = cuda_check(cudaFuncSetAttribute(hb ? chunk_attn_kernel<true> : chunk_attn_kernel<false>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
                      "attention smem attribute");
     if (err) return err;
-    attr[hb] = true;
+    attr[dix][hb] = true;
   }
   dim3 grid((q_rows + QT * BM - 1) / (QT * BM), heads, n_splits);
   const float scale_log2 = softmax_scale * 1.4426950408889634f;

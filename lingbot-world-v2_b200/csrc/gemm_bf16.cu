@@ -272,14 +272,16 @@ static int launch_gemm_t(const CUtensorMap& tmA, const void* W, long long ldw, i
   int err = make_tmap_2d(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldw, gemm::BK, TBN);
   if (err) return err;
   fit_epi(epi, TBN);
-  static bool attr_set = false;  // one flag per instantiation
-  if (!attr_set) {
+  static bool attr_set[64] = {};  // per instantiation and device
+  const int dix = device_index();
+  if (dix < 0) return set_error(LBW_ERR_CUDA, "gemm: cudaGetDevice failed");
+  if (!attr_set[dix]) {
     err = cuda_check(cudaFuncSetAttribute(gemm_bf16_kernel<Epi, TBN, AMap>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           C::SMEM_BYTES + gemm::EPI_WARPS * Epi::WARP_SMEM),
                      "gemm smem attribute");
     if (err) return err;
-    attr_set = true;
+    attr_set[dix] = true;
   }
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + TBN - 1) / TBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();

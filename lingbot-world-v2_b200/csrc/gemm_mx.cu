@@ -237,13 +237,15 @@ static int launch_gemm_mx_t(const CUtensorMap& tmA, const void* a_scales, const 
   CUtensorMap tmB;
   int err = make_tmap_2d(&tmB, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, mxg::BK, TBN);
   if (err) return err;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static bool attr_set[64] = {};  // per instantiation and device
+  const int dix = device_index();
+  if (dix < 0) return set_error(LBW_ERR_CUDA, "mx gemm: cudaGetDevice failed");
+  if (!attr_set[dix]) {
     err = cuda_check(cudaFuncSetAttribute(gemm_mx_kernel<Epi, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           smem_bytes),
                      "mx gemm smem attribute");
     if (err) return err;
-    attr_set = true;
+    attr_set[dix] = true;
   }
   const int tiles = ((M + mxg::BM - 1) / mxg::BM) * ((N + TBN - 1) / TBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();

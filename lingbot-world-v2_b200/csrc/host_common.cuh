@@ -55,6 +55,13 @@ inline bool prefer_narrow_tiles(long long m_tiles, long long n) {
   return 3 * w128 < 5 * w256;
 }
 
+// Index of the current device for per-device caches (function attributes such as a kernel's dynamic shared
+// memory limit belong to one device's context), or -1.
+inline int device_index() {
+  int d = 0;
+  return (cudaGetDevice(&d) == cudaSuccess && d >= 0 && d < 64) ? d : -1;
+}
+
 // Tile-width override of the persistent GEMMs for tuning sweeps: LBW_GEMM_TILE_N=128 or 256 forces that width
 // where the shape allows it; unset (or any other value) keeps the automatic choice.
 inline int tile_n_override() {
