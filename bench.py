@@ -8,12 +8,13 @@ FFN 13824), one 720p chunk of 3 latent frames (45 x 80 tokens per frame, 10,800 
 21-frame KV window (6 cached chunks + the destination chunk = 75,600 keys), 512 text tokens, hoisted
 camera FiLM, MXFP8 FFN. Synthetic seeded data with the benchmark distributions (no checkpoints here).
 A step = one forward of the whole block stack over the chunk; N ranks shard the query tokens (strong
-scaling) and all-gather each block's new K/V over NCCL.
+scaling) and all-gather each block's new K/V over NVLink (copy engines, CUDA IPC buffers).
 
 Printed JSON (rank 0): value = query tokens / step time (max over ranks), e2e = the same through host
 buffers (pinned H2D of x, D2H of the result), roofline of the dominant kernel (self-attention), the CPU
 baseline (the oracle port timed on a bounded sample on the host cores), clocks sampled during the
-timed region.
+timed region, and (after the timed region) the parity of the stack's first block against the CPU oracle on a
+sample of query rows.
 """
 import argparse
 import json
@@ -108,14 +109,32 @@ class Clocks:
                 "samples": len(rows)}
 
 
-def cpu_oracle_step(cfg_name, rows_sample, threads, blocks=1):
+def config_of(args, world):
+    """The `config` object both arms print (the same dict, so the two lines name the same workload)."""
+    c = CONFIGS[args.config]
+    m = MODELS[c["model"]]
+    f, gh, gw = c["grid"]
+    chunk = f * gh * gw
+    return {"workload": args.config, "model": c["model"], "blocks": c["layers"], "dim": m["dim"],
+            "heads": m["num_heads"], "ffn_dim": m["ffn_dim"], "query_tokens": chunk,
+            "kv_tokens": (c["n_lead"] + 1) * chunk, "text_tokens": TEXT_LEN, "parallelism": f"sp{world}",
+            "lin_mx": bool(getattr(args, "lin_mx", False)),
+            "l2": "inputs larger than L2 (KV cache and weights >> 126 MB)"}
+
+
+# wan/configs/wan_i2v_1_3B.py:21-33 and wan_i2v_A14B.py:16-33 (the same table as lbw_b200.model.CONFIGS; kept here
+# so that the CPU reference arm does not load the CUDA package)
+MODELS = {"1.3B": dict(dim=1536, ffn_dim=8960, num_heads=12), "14B": dict(dim=5120, ffn_dim=13824, num_heads=40)}
+
+
+def cpu_oracle_step(cfg_name, rows_sample, threads, blocks=1, mx=False):
     """One block of the oracle (CPU restatement of the reference block) at the workload's geometry on a
-    sample of the query rows; returns seconds."""
+    sample of the query rows; returns seconds. mx=False times the bf16 FFN: the reference has no CPU MX path,
+    so its CPU block runs the FFN in bf16 (the MX emulation is a parity checker, not a timed baseline)."""
     from oracle import block as ob
-    import lbw_b200.model as M
     torch.set_num_threads(threads)
     c = CONFIGS[cfg_name]
-    m = M.CONFIGS[c["model"]]
+    m = MODELS[c["model"]]
     C, H, F = m["dim"], m["num_heads"], m["ffn_dim"]
     f, gh, gw = c["grid"]
     chunk = f * gh * gw
@@ -146,7 +165,7 @@ def cpu_oracle_step(cfg_name, rows_sample, threads, blocks=1):
     t0 = time.perf_counter()
     for _ in range(blocks):
         ob.block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos[:rows_sample], sin[:rows_sample], film=film,
-                         mx=True)
+                         mx=mx)
     return time.perf_counter() - t0
 
 
@@ -162,16 +181,104 @@ def cpu_info():
     return os.cpu_count() or 1, model
 
 
+def parity_rows(chunk, world, rank_rows, seed=5, n_random=24):
+    """Query rows the parity check compares: on rank 0's shard the first and last rows, the rows on both sides
+    of the 256-row CTA and 128-row tile boundaries, the ragged last query tile, and seeded random rows; on every
+    other rank's shard a few rows (their K/V only, which rank 0 holds after the exchange)."""
+    own = {0, 1, 127, 128, 255, 256, rank_rows - 1, rank_rows - 2}
+    last_tile = (rank_rows - 1) // 128 * 128
+    own |= {last_tile, last_tile + 1, max(last_tile - 1, 0)}
+    g = torch.Generator().manual_seed(seed)
+    own |= set(torch.randint(0, rank_rows, (n_random,), generator=g).tolist())
+    own = sorted(r for r in own if 0 <= r < rank_rows)
+    others = []
+    for r in range(1, world):
+        base = r * rank_rows
+        others += [base, base + rank_rows // 2, base + rank_rows - 1]
+    return own, others
+
+
+def block_parity(stack, args, c, dims, dev, world, rank, L_loc, ks0, vs0, ctx, cache0, e0, freqs):
+    """Checks block 0 of the timed stack against the CPU oracle (oracle/block.py, pinned to the reference's
+    own block) on a sample of query rows: its output rows on rank 0, and the destination chunk's K and V rows of
+    every rank (gathered into rank 0's cache under sequence parallelism). The oracle's window is the cached
+    chunks plus the destination chunk as the GPU wrote it, with the sampled rows' K/V recomputed by the oracle
+    (attention has no token mask, so the key order does not matter). Tolerances: rel-L2 <= 1e-2 on the block
+    output (max-abs <= 0.15: the stack's FFN is MXFP8), rel-L2 <= 2e-2 on its update x_out - x, 1e-2 on K and V."""
+    import lbw_b200._lib as L
+    import lbw_b200.model as M
+    from oracle import block as ob
+    C, F, H = dims
+    chunk = L_loc * world
+    bf = torch.bfloat16
+    # block 0's weights again: the timed stack drew them first from the same seed
+    ref = M.BlockStack.synthetic(1, C, F, H, dev, seed=0, ffn_mx=True, lin_mx=args.lin_mx, free_sources=False)
+    b0, r0 = stack.blocks[0], ref.blocks[0]
+    same = all(torch.equal(a, b) if torch.is_tensor(a) else all(torch.equal(u, v) for u, v in zip(a, b))
+               for a, b in ((b0._packed[k], r0._packed[k]) for k in b0._packed))
+    p = {k: v.detach().cpu() for k, v in r0.state_dict().items() if not k.startswith("cam_")}
+    del ref, r0
+    gen = torch.Generator().manual_seed(1234)
+    x_full = torch.randn(chunk, C, generator=gen).to(bf).float()
+    fs_full = (torch.randn(chunk, C, generator=gen) * 0.1).to(bf)
+    ft_full = (torch.randn(chunk, C, generator=gen) * 0.1).to(bf)
+    a = rank * L_loc
+    xs = x_full[a:a + L_loc].to(dev).contiguous()
+    film = (fs_full[a:a + L_loc].to(dev).contiguous(), ft_full[a:a + L_loc].to(dev).contiguous())
+    b0.forward_inplace(xs, e0, ks0, vs0, ctx, cache0, c["grid"], c["start_frame"], freqs, film=film, ws=stack._ws)
+    torch.cuda.synchronize()
+    L.check_device_status()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    if rank != 0:
+        return None
+    own, others = parity_rows(chunk, world, L_loc)
+    rows = own + others
+    idx = torch.tensor(rows)
+    k_dst = ks0[-1].view(chunk, H, 128).cpu()
+    v_dst = vs0[-1].view(chunk, H, 128).cpu()
+    keep = torch.ones(chunk, dtype=torch.bool)
+    keep[idx] = False
+    k_lead = [k.view(-1, H, 128).cpu() for k in ks0[:-1]] + [k_dst[keep]]
+    v_lead = [v.view(-1, H, 128).cpu() for v in vs0[:-1]] + [v_dst[keep]]
+    cos, sin = ob.rope_grid(ob.rope_freqs(), c["grid"], c["start_frame"])
+    import lbw_b200.block as B
+    names = [n for n in B.MX_LINEAR_NAMES] if args.lin_mx else ()
+    ck, cv = ob.cross_kv(p, ctx.cpu(), mx_linears=names)
+    t0 = time.perf_counter()
+    r = ob.block_forward(p, x_full[idx], e0.cpu(), k_lead, v_lead, ck, cv, cos[idx], sin[idx],
+                         film=(fs_full[idx], ft_full[idx]), mx=True, return_all=True, mx_linears=names)
+    t_oracle = time.perf_counter() - t0
+    n = len(own)
+    got = xs.cpu()[torch.tensor(own)]
+    want, x_in = r["x"][:n], x_full[idx][:n]
+    rel = lambda u, v: float((u.float() - v.float()).norm() / v.float().norm().clamp_min(1e-30))  # noqa: E731
+    res = {"block": 0, "rows_checked": n, "kv_rows_checked": len(rows), "ranks_checked": world,
+           "rel_l2": rel(got, want), "max_abs": float((got - want).abs().max()),
+           "update_rel_l2": rel(got - x_in, want - x_in),
+           "k_rel_l2": rel(k_dst[idx], r["k"]), "v_rel_l2": rel(v_dst[idx], r["v"]),
+           "cross_k_rel_l2": rel(cache0["k"].view(-1, H, 128).cpu(), ck),
+           "weights_match_timed_stack": bool(same), "oracle_s": round(t_oracle, 2),
+           "oracle": "oracle/block.py (CPU restatement pinned to the reference block; MXFP8 FFN as OCP MX QDQ)",
+           # max-abs 5e-2 is the bar of the bf16 block output; through the MXFP8 FFN a ~1e-4 difference upstream
+           # moves single outputs by a few hundredths, so the MX block is held to rel-L2 and max-abs <= 0.15
+           "tolerance": {"rel_l2": 1e-2, "max_abs": 0.15, "update_rel_l2": 2e-2, "kv_rel_l2": 1e-2}}
+    res["ok"] = bool(same and res["rel_l2"] <= 1e-2 and res["max_abs"] <= 0.15 and res["update_rel_l2"] <= 2e-2
+                     and res["k_rel_l2"] <= 1e-2 and res["v_rel_l2"] <= 1e-2 and res["cross_k_rel_l2"] <= 1e-2)
+    return res
+
+
 def run_reference(args):
     """--impl reference: the reference path's CPU implementation (the oracle port, oracle/block.py) on the
     host cores, rank 0 only, each step one block over a bounded sample of the chunk's query rows."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import __graft_entry__
-    __graft_entry__.load_package()
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     c = CONFIGS[args.config]
     f, gh, gw = c["grid"]
+    chunk = f * gh * gw
     layers = c["layers"]
     threads, model = cpu_info()
     # Warm-up on a small sample (thread pools, allocator), which also calibrates the per-row cost so that
@@ -182,14 +289,21 @@ def run_reference(args):
     rows = int(budget / max(args.steps, 1) / max(t_probe / probe_rows, 1e-9))
     rows = max(probe_rows, min(args.cpu_rows, rows // 8 * 8))
     times = [cpu_oracle_step(args.config, rows, threads) for _ in range(args.steps)]
-    t_step = statistics.median(times) * layers          # one block timed, x blocks (identical cost)
-    value = rows / t_step
-    sample = (f"{rows} of {f * gh * gw} query rows, 1 of {layers} blocks (x{layers} extrapolated), "
-              f"full {(c['n_lead'] + 1) * f * gh * gw}-key window; CPU: {model}")
+    t_sample = statistics.median(times)                 # one timed step: 1 block over `rows` query rows
+    t_full = t_sample * (chunk / rows) * layers         # the whole chunk through all blocks (extrapolated)
+    value = chunk / t_full
+    sample = (f"{rows} of {chunk} query rows through 1 of {layers} blocks (bf16 FFN) against the full "
+              f"{(c['n_lead'] + 1) * chunk}-key window; CPU: {model}")
     out = {"metric": "chunk-forward tokens/s", "value": value, "unit": "tokens/s", "impl": "reference",
-           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3,
-           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32/bf16 (CPU torch)",
-           "data": "synthetic", "config": {"workload": args.config, "blocks": layers},
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           # a timed step is the bounded sample below; the whole chunk forward is extrapolated from it
+           "ms_per_step": t_sample * 1e3, "ms_per_step_kind": "measured sample (1 block, sample_rows rows)",
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           "dtype": "bf16 weights, fp32 residual and softmax (CPU torch)", "data": "synthetic",
+           "config": config_of(args, world),
+           "extrapolation": {"sample_rows": rows, "chunk_rows": chunk, "sample_blocks": 1, "blocks": layers,
+                             "ms_sample_step": t_sample * 1e3, "ms_chunk_forward_extrapolated": t_full * 1e3,
+                             "factor": (chunk / rows) * layers},
            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out))
@@ -468,6 +582,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=int(os.environ.get("LBW_CPU_ROWS", "1350")))
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the oracle check of the first block on a row sample (run after the timed steps)")
     ap.add_argument("--sweep", action="store_true", help="kernel sweep (benchmark configuration c5) instead of the step")
     ap.add_argument("--sweep-only", default="all", choices=["all", "attention", "mxfp8", "gemm", "linmx", "tiles"],
                     help="with --sweep: one family of points (gemm = the block's bf16 GEMMs at 10,800 and 1,350 rows)")
@@ -519,13 +635,15 @@ def main():
     lkv = n_chunks * chunk
 
     stack = M.BlockStack.synthetic(layers, C, F, H, dev, seed=0, ffn_mx=True, lin_mx=args.lin_mx)
-    g = torch.Generator(device=dev).manual_seed(1 + rank)
+    # the cached chunks and the text context are replicated: the same draws on every rank
+    gk = torch.Generator(device=dev).manual_seed(1)
     bf = torch.bfloat16
-    ks = [[torch.randn(1, chunk, H, 128, generator=g, device=dev, dtype=bf) for _ in range(n_chunks)]
+    ks = [[torch.randn(1, chunk, H, 128, generator=gk, device=dev, dtype=bf) for _ in range(n_chunks)]
           for _ in range(layers)]
-    vs = [[torch.randn(1, chunk, H, 128, generator=g, device=dev, dtype=bf) for _ in range(n_chunks)]
+    vs = [[torch.randn(1, chunk, H, 128, generator=gk, device=dev, dtype=bf) for _ in range(n_chunks)]
           for _ in range(layers)]
-    ctx = torch.randn(TEXT_LEN, C, generator=g, device=dev, dtype=bf)
+    ctx = torch.randn(TEXT_LEN, C, generator=gk, device=dev, dtype=bf)
+    g = torch.Generator(device=dev).manual_seed(2 + rank)
     caches = [{"k": torch.empty(TEXT_LEN, H, 128, dtype=bf, device=dev),
                "v": torch.empty(TEXT_LEN, H, 128, dtype=bf, device=dev)} for _ in range(layers)]
     films = [((torch.randn(L_loc, C, generator=g, device=dev) * 0.1).to(bf),
@@ -624,6 +742,17 @@ def main():
                "d2h_bytes_per_step": nbytes, "ms_per_step": ms_e2e}
     assert torch.isfinite(yh if e2e else xf).all(), "non-finite block output"
 
+    # Parity of the timed stack's first block against the CPU oracle on a row sample (outside the timed region)
+    parity = None
+    if not args.no_parity:
+        parity = block_parity(stack, args, c, (C, F, H), dev, world, rank, L_loc, ks[0], vs[0], ctx, caches[0], e0,
+                              freqs)
+    exchange = None
+    if world > 1:
+        pkv = [p for p in sp._PEERS.values()]
+        exchange = {"kind": "copy engines over CUDA IPC (stream memory operations), not NCCL", "world": world,
+                    "peers_opened": [p.world - 1 for p in pkv], "exchanges_per_step": layers}
+
     # DRAM traffic of one attention launch: an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of
     # the c2 self-attention, 4,680 queries x 32,760 keys, measured 987.5 MB; K/V (re-read from L2 by the query
     # blocks of a head) dominate it, so it is scaled by this workload's K/V bytes.
@@ -642,9 +771,7 @@ def main():
         "dtype": ("bf16 (attention) + mxfp8 e4m3/e8m0 (every Linear, LINGBOT_LIN_MX)" if args.lin_mx else
                   "bf16 (attention, projections) + mxfp8 e4m3/e8m0 (FFN)"),
         "data": "synthetic (seeded N(0,1) latents / KV, N(0,0.02) weights, random init)",
-        "config": {"workload": args.config, "model": c["model"], "blocks": layers, "query_tokens": chunk,
-                   "kv_tokens": lkv, "text_tokens": TEXT_LEN, "parallelism": f"sp{world}", "lin_mx": args.lin_mx,
-                   "l2": "inputs larger than L2 (KV cache and weights >> 126 MB)"},
+        "config": config_of(args, world),
         "latency_ms": ms,
         "tc_frac_of_peak": flops / (ms / 1e3) / (peak_tc * 1e12 * world),
         "roofline": {"bound": "tensor", "kernel": "chunk_attn_kernel", "achieved": attn_tf, "peak": peak_tc,
@@ -655,7 +782,10 @@ def main():
                      "ms_per_launch": attn_ms},
         "gpu_launches": launches,
         "e2e": e2e,
+        "parity": parity,
     }
+    if exchange is not None:
+        result["exchange"] = exchange
     if breakdown is not None:
         result["phases_ms_per_step"] = breakdown
     if rank == 0:
@@ -667,8 +797,9 @@ def main():
         t_cpu = cpu_oracle_step(args.config, rows, threads)
         cpu_value = rows / (t_cpu * layers)
         result["cpu_baseline"] = {"value": cpu_value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                  "sample": f"oracle block (oracle/block.py) on {rows} of {chunk} query rows, "
-                                            f"1 block x{layers} extrapolated, full {lkv}-key window; {model}"}
+                                  "sample": f"oracle block (oracle/block.py, bf16 FFN) on {rows} of {chunk} query "
+                                            f"rows, 1 block x{layers} extrapolated, full {lkv}-key window; {model}",
+                                  "sample_rows": rows, "extrapolation_factor": (chunk / rows) * layers}
     if rank == 0:
         print(json.dumps(result))
     if world > 1:

@@ -36,8 +36,9 @@ int lbw_version(void);
 /* Copies this thread's last error message into buf (always NUL-terminated). */
 int lbw_last_error(char* buf, size_t n);
 const char* lbw_status_string(int code);
-/* Synchronises `stream`, reads and clears the device status word of the current device.
- * Returns LBW_ERR_TIMEOUT (device_code = 0x100 | site) if a kernel wait ran out. */
+/* Synchronises `stream`, reads and clears the device status words of the current device (the library's, and
+ * the one of lbw_linear_rmsnorm_noalloc); allocates nothing. Returns LBW_ERR_TIMEOUT (device_code =
+ * 0x100 | site) if a kernel wait ran out. */
 int lbw_check_device_status(void* stream, int* device_code);
 
 /* ---- chunk attention ----------------------------------------------------------------
@@ -119,13 +120,14 @@ int lbw_linear_gelu(const void* a, const void* w, const void* bias, int m, int n
  * y = bf16(a w^T + bias) -- the result of lbw_linear_rowss followed by lbw_rmsnorm_rope without RoPE, but
  * the per-row sums of squares are kept in a fixed 256 KB array inside the library (m <= 65536 rows;
  * larger m returns LBW_ERR_SHAPE) instead of a caller buffer, and no device memory is ever allocated
- * (not even the status word: a bounded-wait timeout in this call is not reported). It exists for
- * callers that cannot allocate: runtimes that reserve all device memory for their own pool up front
+ * (its bounded-wait timeouts go to a second fixed word in the library, which lbw_check_device_status
+ * reads and clears without allocating; after a timeout the RMSNorm pass leaves out unchanged). It exists
+ * for callers that cannot allocate: runtimes that reserve all device memory for their own pool up front
  * and plugins hosted by another framework with no allocator to offer. Every GPU that loads the library
- * holds the array until the process exits. The first call on a device looks up the array's device
- * address (make that first call before any stream capture). All calls share the one array, so calls
- * that overlap on the GPU (other streams, other threads) race; serialise them. No counterpart in the
- * reference: it is an addition of this library. */
+ * holds the array until the process exits. The first call in each device context looks up the arrays'
+ * device addresses (make that first call before any stream capture). All calls share the one array, so
+ * calls that overlap on the GPU (other streams, other threads) race; serialise them. No counterpart in
+ * the reference: it is an addition of this library. */
 int lbw_linear_rmsnorm_noalloc(const void* a, const void* w, const void* bias, const void* gamma, int m, int n, int k,
                                float eps, void* out, void* stream);
 

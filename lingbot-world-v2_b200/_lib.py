@@ -12,8 +12,7 @@ import re
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-# LBW_LIB_PATH: another build of the same C ABI (an A/B of two builds in one session); default the in-tree one
-LIB_PATH = os.environ.get("LBW_LIB_PATH") or os.path.join(HERE, "liblbw.so")
+LIB_PATH = os.path.join(HERE, "liblbw.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "lbw.h")
 
 LBW_OK, LBW_ERR_INVALID, LBW_ERR_SHAPE, LBW_ERR_ALIGN, LBW_ERR_CUDA, LBW_ERR_TIMEOUT, LBW_ERR_UNSUPPORTED = range(7)

@@ -40,6 +40,13 @@ int* device_status(int* err) {
   return g_status[dev];
 }
 
+int* device_status_peek() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  return g_status[dev];
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -113,20 +120,24 @@ const char* lbw_status_string(int code) {
 }
 
 int lbw_check_device_status(void* stream, int* device_code) {
-  int err = 0;
-  int* st = lbw::device_status(&err);
-  if (!st) return err;
+  // Reads the library's status word and the allocation-free entry point's one; allocates neither.
+  int* words[2] = {lbw::device_status_peek(), lbw::noalloc_status_peek()};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  int v = 0;
-  int rc = lbw::cuda_check(cudaMemcpyAsync(&v, st, sizeof(int), cudaMemcpyDeviceToHost, s), "status read");
+  int v[2] = {0, 0};
+  for (int i = 0; i < 2; ++i) {
+    if (!words[i]) continue;
+    int rc = lbw::cuda_check(cudaMemcpyAsync(&v[i], words[i], sizeof(int), cudaMemcpyDeviceToHost, s), "status read");
+    if (rc) return rc;
+  }
+  int rc = lbw::cuda_check(cudaStreamSynchronize(s), "status sync");
   if (rc) return rc;
-  rc = lbw::cuda_check(cudaStreamSynchronize(s), "status sync");
-  if (rc) return rc;
-  if (device_code) *device_code = v;
-  if (v != 0) {
-    cudaMemsetAsync(st, 0, sizeof(int), s);
+  const int code = v[0] ? v[0] : v[1];
+  if (device_code) *device_code = code;
+  if (code != 0) {
+    for (int i = 0; i < 2; ++i)
+      if (v[i]) cudaMemsetAsync(words[i], 0, sizeof(int), s);
     cudaStreamSynchronize(s);
-    return lbw::set_error(LBW_ERR_TIMEOUT, "a kernel wait timed out (device code 0x%x)", v);
+    return lbw::set_error(LBW_ERR_TIMEOUT, "a kernel wait timed out (device code 0x%x)", code);
   }
   return LBW_OK;
 }

@@ -535,19 +535,24 @@ int lbw_linear_act(const void* a, const void* w, const void* bias, const void* a
 // lbw_rmsnorm_rope without RoPE). Some hosts cannot hand this library a scratch buffer or let it
 // call cudaMalloc: runtimes that reserve the whole device memory for their own pool up front (a
 // serving engine sizing its KV cache to fill HBM) and plugins loaded by another framework that
-// exposes no allocator to them. For those callers the row sums of squares live in the fixed array
-// below, which every GPU that loads the library keeps until the process exits.
+// exposes no allocator to them. For those callers the row sums of squares, and the status word
+// that records a timed-out wait of the GEMM, live in the fixed arrays below, which every GPU that
+// loads the library keeps until the process exits.
 // ------------------------------------------------------------------------------------------
 namespace lbw {
 
 constexpr int NOALLOC_MAX_ROWS = 65536;  // 256 KB of fp32 row sums per device
 static __device__ __align__(256) float g_noalloc_rowss[NOALLOC_MAX_ROWS];
+// Bounded-wait timeouts of the call's GEMM (LBW_DEV_TIMEOUT | site); read and cleared by lbw_check_device_status.
+static __device__ int g_noalloc_status;
 
 // y[row, :] = bf16(bf16(y * rsqrt(ss[row] / C + eps)) * gamma), in place (the same rounding points as
-// rmsnorm_rope_kernel without the rotation). Each thread reads and rewrites its own 8 values.
+// rmsnorm_rope_kernel without the rotation). Each thread reads and rewrites its own 8 values. Nothing is
+// written when the GEMM before it recorded a timeout (its output is incomplete).
 __global__ void __launch_bounds__(128) rms_gamma_inplace_kernel(__nv_bfloat16* y, const float* ss,
                                                                 const __nv_bfloat16* __restrict__ gamma, int C,
-                                                                float eps, long long ldy) {
+                                                                float eps, long long ldy, const int* status) {
+  if (*(volatile const int*)status != 0) return;
   const long long row = blockIdx.x;
   const float r = 1.f / sqrtf(ss[row] / (float)C + eps);
   __nv_bfloat16* yr = y + row * ldy;
@@ -564,29 +569,85 @@ __global__ void __launch_bounds__(128) rms_gamma_inplace_kernel(__nv_bfloat16* y
   }
 }
 
-// Device address of g_noalloc_rowss for the current device, looked up once per device.
-static float* noalloc_rowss_ptr(int* err) {
-  static std::mutex mu;
-  static float* ptrs[64] = {nullptr};
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// Device addresses of the two arrays in the CUDA context current on this thread, looked up once per context
+// (a module's globals have a different address in every context that loads it).
+struct NoallocSlot {
+  CUcontext ctx = nullptr;
+  int dev = -1;
+  float* rowss = nullptr;
+  int* status = nullptr;
+};
+static std::mutex g_noalloc_mu;
+static NoallocSlot g_noalloc_slots[64];
+
+static CUcontext current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  CUcontext c = nullptr;
+  if (fn) fn(&c);
+  return c;
+}
+
+static const NoallocSlot* noalloc_slot(int* err) {
   int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
     *err = set_error(LBW_ERR_CUDA, "lbw_linear_rmsnorm_noalloc: cudaGetDevice failed");
     return nullptr;
   }
-  std::lock_guard<std::mutex> lk(mu);
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_rowss);
-    if (e != cudaSuccess || p == nullptr) {
+  CUcontext ctx = current_context();
+  if (!ctx) {  // no context on this thread yet: bind the device's primary context, as the runtime would
+    if (cudaSetDevice(dev) != cudaSuccess || !(ctx = current_context())) {
+      *err = set_error(LBW_ERR_CUDA, "lbw_linear_rmsnorm_noalloc: no CUDA context");
+      return nullptr;
+    }
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  for (auto& s : g_noalloc_slots)
+    if (s.rowss && s.ctx == ctx && s.dev == dev) {
+      *err = LBW_OK;
+      return &s;
+    }
+  for (auto& s : g_noalloc_slots) {
+    if (s.rowss) continue;
+    void* pr = nullptr;
+    void* ps = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&pr, g_noalloc_rowss);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&ps, g_noalloc_status);
+    if (e != cudaSuccess || !pr || !ps) {
       *err = set_error(LBW_ERR_CUDA, "lbw_linear_rmsnorm_noalloc: cudaGetSymbolAddress failed: %s",
                        cudaGetErrorString(e));
       return nullptr;
     }
-    ptrs[dev] = static_cast<float*>(p);
+    s.ctx = ctx;
+    s.dev = dev;
+    s.rowss = static_cast<float*>(pr);
+    s.status = static_cast<int*>(ps);
+    *err = LBW_OK;
+    return &s;
   }
-  *err = LBW_OK;
-  return ptrs[dev];
+  *err = set_error(LBW_ERR_UNSUPPORTED, "lbw_linear_rmsnorm_noalloc: more than 64 device contexts");
+  return nullptr;
+}
+
+// The allocation-free status word of the current device and context, or null when the entry point has not been
+// used there (lbw_check_device_status reads it without looking anything up).
+int* noalloc_status_peek() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  const CUcontext ctx = current_context();
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  for (auto& s : g_noalloc_slots)
+    if (s.rowss && s.ctx == ctx && s.dev == dev) return s.status;
+  return nullptr;
 }
 
 }  // namespace lbw
@@ -601,35 +662,27 @@ extern "C" int lbw_linear_rmsnorm_noalloc(const void* a, const void* w, const vo
                      m, NOALLOC_MAX_ROWS);
   if (n <= 0 || n % 32 || k <= 0 || k % BK)
     return set_error(LBW_ERR_SHAPE, "lbw_linear_rmsnorm_noalloc: N=%d must be a multiple of 32 and K=%d of %d", n, k, BK);
-  if (!ok16(out) || !ok16(bias) || !ok16(gamma))
+  if (!aligned(a, 16) || !aligned(w, 16) || !ok16(out) || !ok16(bias) || !ok16(gamma))
     return set_error(LBW_ERR_ALIGN, "lbw_linear_rmsnorm_noalloc: alignment");
   int err = 0;
-  float* ss = noalloc_rowss_ptr(&err);
-  if (!ss) return err;
+  const NoallocSlot* slot = noalloc_slot(&err);
+  if (!slot) return err;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // The array keeps the previous call's sums: clear this call's rows first.
-  if ((err = cuda_check(cudaMemsetAsync(ss, 0, sizeof(float) * (size_t)m, s), "noalloc scratch clear"))) return err;
-  CUtensorMap tmA, tmB;
+  if ((err = cuda_check(cudaMemsetAsync(slot->rowss, 0, sizeof(float) * (size_t)m, s), "noalloc scratch clear")))
+    return err;
+  CUtensorMap tmA;
   if ((err = make_tmap_2d(&tmA, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, k, k, BK, BM))) return err;
-  if ((err = make_tmap_2d(&tmB, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, k, k, BK, BN))) return err;
   EpiStore e{};
   e.out[0] = e.out[1] = e.out[2] = reinterpret_cast<__nv_bfloat16*>(out);
   e.ld[0] = e.ld[1] = e.ld[2] = n;
-  e.ss[0] = ss;
+  e.ss[0] = slot->rowss;
   e.region_cols = n;
-  e.ss_per_chunk = (n % BN) != 0;
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
-  if ((err = cuda_check(cudaFuncSetAttribute(gemm_bf16_kernel<EpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SMEM_BYTES),
-                        "gemm smem attribute")))
-    return err;
-  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  // No status word: a bounded-wait timeout still ends the kernel, but is not recorded for this call.
-  gemm_bf16_kernel<EpiStore><<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmB, m, n, k, group_rows(m, k, 2), e, nullptr,
-                                                                PlainA{});
-  if ((err = cuda_check(cudaGetLastError(), "noalloc gemm launch"))) return err;
-  rms_gamma_inplace_kernel<<<m, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), ss,
-                                             reinterpret_cast<const __nv_bfloat16*>(gamma), n, eps, n);
+  // the 256-wide tile launch of the allocating GEMMs (its shared-memory attribute is set once per device), with
+  // the library's own status word replaced by the fixed one
+  if ((err = launch_gemm_t<EpiStore, 256>(tmA, w, k, m, n, k, e, s, slot->status))) return err;
+  rms_gamma_inplace_kernel<<<m, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), slot->rowss,
+                                             reinterpret_cast<const __nv_bfloat16*>(gamma), n, eps, n, slot->status);
   return cuda_check(cudaGetLastError(), "noalloc rms launch");
 }

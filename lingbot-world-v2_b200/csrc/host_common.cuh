@@ -17,6 +17,11 @@ int set_error(int code, const char* fmt, ...);
 // Device status word of the current device (zeroed on first use). Kernels that wait on
 // mbarriers record timeouts there; lbw_check_device_status() reads and clears it.
 int* device_status(int* err);
+// The status word of the current device if device_status() has created it, else null (allocates nothing).
+int* device_status_peek();
+// The status word of lbw_linear_rmsnorm_noalloc in the current device and context, or null when that entry
+// point has not run there.
+int* noalloc_status_peek();
 
 // cudaError_t -> LBW_ERR_CUDA with the CUDA error string.
 inline int cuda_check(cudaError_t e, const char* what) {

@@ -18,14 +18,17 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   float inner = k0 * (x + k1 * x * x * x);
   return 0.5f * x * (1.f + tanhf(inner));
 }
-// Same formula with the SFU's tanh.approx.f32 (relative error ~2^-11, below the bf16 rounding the
-// result gets): a handful of instructions instead of the long tanhf sequence, for GEMM epilogues.
+// The same function through the identity 0.5 x (1 + tanh(z)) = x / (1 + e^(-2z)), with the SFU's ex2.approx
+// (relative error ~2^-22) and a fast division: a few instructions, and accurate to a few fp32 ulps, so that the
+// bf16 rounding of the result (and the MXFP8 code chosen from it) rarely differs from the fp32 GELU's
+// (tanh.approx.f32 has a relative error of ~2^-11, a quarter of a bf16 ulp). For x -> -inf the exponential
+// overflows and the quotient is -0.
 __device__ __forceinline__ float gelu_tanh_fast(float x) {
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
   const float inner = k0 * fmaf(k1 * x, x * x, x);
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
-  return 0.5f * x * (1.f + t);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-2.8853900817779268f * inner));  // e^(-2 inner)
+  return __fdividef(x, 1.f + e);
 }
 // 2^e as a float for e in [-126, 127] (exact).
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }

@@ -50,9 +50,11 @@ class BlockStack(nn.Module):
         return xf
 
     @classmethod
-    def synthetic(cls, num_layers, dim, ffn_dim, num_heads, device, seed=0, ffn_mx=True, peaked=False, lin_mx=False):
+    def synthetic(cls, num_layers, dim, ffn_dim, num_heads, device, seed=0, ffn_mx=True, peaked=False, lin_mx=False,
+                  free_sources=True):
         """Build on the meta device, materialise bf16 weights on `device`, fill with the benchmark
-        distributions and pack them for the kernels (source copies freed)."""
+        distributions and pack them for the kernels (source copies freed unless free_sources=False). The
+        generator draws block by block, so the first blocks of two stacks built with the same seed are equal."""
         with torch.device("meta"):
             st = cls(num_layers, dim, ffn_dim, num_heads, ffn_mx=ffn_mx, lin_mx=lin_mx)
         st = st.to(torch.bfloat16).to_empty(device=device)
@@ -63,7 +65,7 @@ class BlockStack(nn.Module):
         g = torch.Generator(device=device).manual_seed(seed)
         init_synthetic_(st, g, peaked=peaked)
         for blk in st.blocks:
-            blk.prepare(free_sources=True, with_cam=False)   # the benchmark feeds hoisted FiLM tensors
+            blk.prepare(free_sources=free_sources, with_cam=False)   # the benchmark feeds hoisted FiLM tensors
         return st
 
 

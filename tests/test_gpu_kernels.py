@@ -299,6 +299,27 @@ def test_gated_attention_matches_ungated(cuda_dev):
         K.chunk_attention_gated(q, ks, vs, flag.data_ptr(), 7, 3, out=out)
 
 
+def test_gated_attention_times_out_on_a_gate_that_never_opens(cuda_dev):
+    """A gate word that nothing ever raises: every CTA's bounded gate wait (2^31 SM clocks, about a second) runs
+    out, the kernel drains its copies and MMAs and returns, and the host reads the timeout (0x100 | 0x23, the gate
+    site) from the device status word; the context stays usable for the next launch. One wave of CTAs (2 heads x
+    one 256-row query block), so the wait is paid once."""
+    import lbw_b200._lib as L
+    import lbw_b200.kernels as K
+    d = cuda_dev
+    q, ks, vs = _attn_case(256, [256, 200], 2, 37)
+    q, ks, vs = q.to(d), [k.to(d) for k in ks], [v.to(d) for v in vs]
+    flag = torch.zeros(4, dtype=torch.int32, device=d)       # stays 0; the kernel waits for 1
+    out = torch.zeros(256, 256, dtype=BF, device=d)
+    K.chunk_attention_gated(q, ks, vs, flag.data_ptr(), 1, 1, out=out)
+    with pytest.raises(L.LbwError, match="0x123"):
+        L.check_device_status()
+    assert L.check_device_status() == 0                      # read and cleared
+    ref = K.chunk_attention(q, ks, vs)                       # the context still runs kernels
+    torch.cuda.synchronize()
+    assert rel_l2(ref.view(256, 2, 128), ob.attention(q.cpu(), torch.cat(ks).cpu(), torch.cat(vs).cpu())) < 1e-2
+
+
 def test_split_count_is_validated(cuda_dev):
     import lbw_b200.kernels as K
     q, ks, vs = _attn_case(128, [100], 1, 23)
