@@ -12,6 +12,10 @@
 //   warps 0-3 / 4-7  softmax of query tile 0 / 1 (thread = query row = TMEM lane)
 //   warp 8           TMA producer: Q once, then K/V tiles through a 2-deep ring
 //   warp 9           UMMA issuer, TMEM owner (512 columns: S0 | S1 | O0 | O1, 128 each)
+//   warp 10          watches the K/V ring for the issuer: its arrivals fold "V(j) landed" into p_ready[0][0] and
+//                    "K(j + 1) landed" into p_ready[0][1], so the issuing thread waits on four barriers per key
+//                    tile instead of six (every shared-memory read of the issuing thread, an mbarrier test
+//                    included, first waits for the MMAs it has issued to be taken by the tensor pipe)
 // S_i = Q_i Kᵀ lands in TMEM; the softmax warps read it (tcgen05.ld), write bf16 P_i back over
 // the first 64 columns of S_i (tcgen05.st, signalled per half tile so that P V on keys 0..63 starts
 // while the exponentials of keys 64..127 are computed) and the MMA warp accumulates O_i += P_i V from TMEM
@@ -41,7 +45,7 @@ constexpr int BM = 128, BN = 128, D = 128, QT = 2, STAGES = 2, MAX_CHUNKS = 8;
 constexpr int HALF = 128 * 64 * 2;  // 128 rows x 64 bf16 (one 128-byte swizzled box)
 constexpr int TILE = 2 * HALF;      // 128 rows x 128 bf16
 constexpr int SMEM_BYTES = (QT + 2 * STAGES) * TILE + 1024;
-constexpr int THREADS = 320;
+constexpr int THREADS = 352;
 }  // namespace attn
 
 struct KVMaps {
@@ -133,8 +137,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     }
     for (int i = 0; i < QT; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_ready[i][0], 128);  // P of keys 0..63 written
-      mbar_init(&p_ready[i][1], 128);  // P of keys 64..127 written
+      mbar_init(&p_ready[i][0], 128 + (i == 0));  // P of keys 0..63 written (+ V(j) landed, for tile 0)
+      mbar_init(&p_ready[i][1], 128 + (i == 0));  // P of keys 64..127 written (+ K(j + 1) landed, for tile 0)
     }
     mbar_init(&o_done, 1);
     mbar_init(&done_bar, 1);
@@ -229,19 +233,16 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tc_commit(&k_empty[0]);
         for (int j = 0; j < n_tiles && ok; ++j) {
           const int s = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
           const bool more = j + 1 < n_tiles;
           const int s1 = (j + 1) & 1;
-          const uint32_t ph1 = ((j + 1) >> 1) & 1;
-          if (!mbar_wait(&v_full[s], ph, ab, 0x33) || !mbar_wait(&p_ready[0][0], j & 1, ab, 0x34)) { ok = false; break; }
+          // p_ready[0][0] also means V(j) landed, p_ready[0][1] also K(j + 1) (the watcher's arrivals)
+          if (!mbar_wait(&p_ready[0][0], j & 1, ab, 0x34)) { ok = false; break; }
           tc_fence_after();
           issue_pv(0, s, j == 0, 0);
           if (!mbar_wait(&p_ready[0][1], j & 1, ab, 0x37)) { ok = false; break; }
           tc_fence_after();
           issue_pv(0, s, j == 0, 1);
           if (more) {
-            if (!mbar_wait(&k_full[s1], ph1, ab, 0x35)) { ok = false; break; }
-            tc_fence_after();
             issue_s(0, s1);
             tc_commit(&s_full[0]);
           }
@@ -266,6 +267,22 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       }
       tc_commit(&done_bar);
       mbar_wait_drain(&done_bar, 0);
+    }
+  } else if (warp == 10) {
+    // ---------------- K/V watcher ----------------
+    // Observes every landing in order (K(0) first), so none of its parity waits runs a phase ahead, and waits for
+    // each p_ready[0][h] phase to complete before arriving for the next key tile: an early arrival would count
+    // toward the current phase and release P V before every softmax thread had written its part of P.
+    if (lane == 0) {
+      const int n_tiles = g_end - g_begin;
+      bool ok = mbar_wait(&k_full[0], 0, ab, 0x60);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, ab, 0x61)) break;
+        mbar_arrive(&p_ready[0][0]);
+        if (j + 1 < n_tiles && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, ab, 0x62)) break;
+        mbar_arrive(&p_ready[0][1]);
+        if (!mbar_wait(&p_ready[0][0], j & 1, ab, 0x63) || !mbar_wait(&p_ready[0][1], j & 1, ab, 0x64)) break;
+      }
     }
   } else {
     // ---------------- softmax / correction / epilogue ----------------

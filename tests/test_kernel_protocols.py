@@ -8,15 +8,18 @@ Attention:
 
 The programs restate the kernel's synchronisation, step for step:
   producer   Q once; per key tile j: wait k_empty[j % 2] (use j / 2), load K; wait v_empty, load V
+  watcher    K(0) landed; per tile j: V(j) landed -> arrive p_ready[0][0]; K(j + 1) landed -> arrive p_ready[0][1];
+             then wait for both phases of tile j to complete (so its next arrivals cannot land in them)
   issuer     S_0 = Q_0 K_0^T (and S_1 with two query tiles), commit s_full; commit k_empty[0]; per tile j:
-             wait v_full and p_ready[0][0] -> P_0 V (keys 0..63); wait p_ready[0][1] -> P_0 V (keys 64..127);
-             next S_0 (wait k_full), commit s_full[0]; then the same P_1 V for the second tile; commit v_empty;
-             next S_1, commit s_full[1]; commit k_empty; finally commit o_done
+             wait p_ready[0][0] (P_0 keys 0..63 and V(j)) -> P_0 V (keys 0..63); wait p_ready[0][1] (P_0 keys
+             64..127 and K(j + 1)) -> P_0 V (keys 64..127); next S_0, commit s_full[0]; then the same P_1 V for the
+             second tile; commit v_empty; next S_1, commit s_full[1]; commit k_empty; finally commit o_done
   softmax i  per tile: wait s_full[i]; P over S; without a rescale and on a full tile it arrives p_ready[i][0]
              once keys 0..63 of P are written, else after the rescale of O; then p_ready[i][1]
-Hazards: S is complete when read; P (j) is written only after the P V that read P (j - 1) completed; O is rescaled
-only while no P V of that query tile runs; a K or V ring slot is refilled only after every MMA that read it
-completed.
+Hazards: S is complete when read; P V starts only after every softmax warp wrote its part of P and V landed; the next
+S only after K landed; P (j) is written only after the P V that read P (j - 1) completed; O is rescaled only while
+no P V of that query tile runs; a K or V ring slot is refilled only after every MMA that read it completed; every
+arrival lands in the phase it is meant for.
 
 Persistent GEMM (one CTA's tiles t = 0, 1, ...):
   producer   per tile, per K stage: wait empty[s] (its previous use), load A and B into slot s
@@ -45,15 +48,17 @@ import pytest
 from protocol_model import Bar, Flag, Model
 
 
-def attention_v1(m, n_tiles, two, rescale_p, ragged_p):
+def attention_v1(m, n_tiles, two, rescale_p, ragged_p, watcher_phase_wait=True):
     nq = 2 if two else 1
     q_full = Bar("q_full")
     k_full, k_empty = [Bar(f"k_full{s}") for s in range(2)], [Bar(f"k_empty{s}") for s in range(2)]
     v_full, v_empty = [Bar(f"v_full{s}") for s in range(2)], [Bar(f"v_empty{s}") for s in range(2)]
     s_full = [Bar(f"s_full{i}") for i in range(2)]
-    p_ready = [[Bar(f"p_ready{i}{h}", 4) for h in range(2)] for i in range(2)]   # 4 warps per warpgroup
+    # 4 softmax warps per warpgroup; query tile 0's two barriers also take the watcher's arrival
+    p_ready = [[Bar(f"p_ready{i}{h}", 4 + (i == 0)) for h in range(2)] for i in range(2)]
     o_done = Bar("o_done")
     MMA_S, MMA_PV = 512, 256                     # 128 x 128 x 128 S; P V over 64 keys
+    p_written = {}                               # (query tile, key tile, half) -> softmax warps that wrote it
 
     def producer():
         yield ("tma", q_full, ("Q",))
@@ -71,6 +76,20 @@ def attention_v1(m, n_tiles, two, rescale_p, ragged_p):
                         assert m.complete(("PV", i, h, j - 2)), ("V slot refilled while read", j)
             yield ("tma", v_full[s], ("V", j))
 
+    def watcher():
+        yield ("wait", k_full[0], 1)             # every landing observed in order, K(0) first
+        for j in range(n_tiles):
+            yield ("wait", v_full[j & 1], (j >> 1) + 1)
+            assert p_ready[0][0].k == j, ("watcher arrival in another phase", j)
+            yield ("arrive", p_ready[0][0])
+            if j + 1 < n_tiles:
+                yield ("wait", k_full[(j + 1) & 1], ((j + 1) >> 1) + 1)
+            assert p_ready[0][1].k == j, ("watcher arrival in another phase", j)
+            yield ("arrive", p_ready[0][1])
+            if watcher_phase_wait:
+                yield ("wait", p_ready[0][0], j + 1)
+                yield ("wait", p_ready[0][1], j + 1)
+
     def issuer():
         yield ("wait", q_full, 1)
         yield ("wait", k_full[0], 1)
@@ -80,19 +99,21 @@ def attention_v1(m, n_tiles, two, rescale_p, ragged_p):
         yield ("commit", k_empty[0])
         for j in range(n_tiles):
             s, more, s1 = j & 1, j + 1 < n_tiles, (j + 1) & 1
-            yield ("wait", v_full[s], (j >> 1) + 1)
             yield ("wait", p_ready[0][0], j + 1)
+            assert ("V", j) in m.loaded and p_written.get((0, j, 0), 0) == 4, ("P V before V / P", 0, j)
             yield ("mma", ("PV", 0, 0, j), MMA_PV)
             yield ("wait", p_ready[0][1], j + 1)
+            assert (not more or ("K", j + 1) in m.loaded) and p_written.get((0, j, 1), 0) == 4, ("S before K", j)
             yield ("mma", ("PV", 0, 1, j), MMA_PV)
             if more:
-                yield ("wait", k_full[s1], ((j + 1) >> 1) + 1)
                 yield ("mma", ("S", 0, j + 1), MMA_S)
                 yield ("commit", s_full[0])
             if two:
                 yield ("wait", p_ready[1][0], j + 1)
+                assert p_written.get((1, j, 0), 0) == 4, ("P V before P", 1, j)
                 yield ("mma", ("PV", 1, 0, j), MMA_PV)
                 yield ("wait", p_ready[1][1], j + 1)
+                assert p_written.get((1, j, 1), 0) == 4, ("P V before P", 1, j)
                 yield ("mma", ("PV", 1, 1, j), MMA_PV)
             yield ("commit", v_empty[s])
             if more:
@@ -101,6 +122,12 @@ def attention_v1(m, n_tiles, two, rescale_p, ragged_p):
                     yield ("commit", s_full[1])
                 yield ("commit", k_empty[s1])
         yield ("commit", o_done)
+
+    def release(wg, j, h):
+        for _ in range(4):
+            p_written[(wg, j, h)] = p_written.get((wg, j, h), 0) + 1
+            assert p_ready[wg][h].k == j, ("softmax arrival in another phase", wg, j, h)
+            yield ("arrive", p_ready[wg][h])
 
     def softmax(wg):
         for j in range(n_tiles):
@@ -111,27 +138,26 @@ def attention_v1(m, n_tiles, two, rescale_p, ragged_p):
                     assert m.complete(("PV", wg, h, j - 1)), ("P overwritten while read", wg, j)
             rescale = j > 0 and m.rng.random() < rescale_p
             full = m.rng.random() >= ragged_p
-            yield ("work", m.rng.uniform(300, 600))
+            # each half of the softmax from much shorter to much longer than the other tile's MMAs
+            yield ("work", m.rng.uniform(150, 1300))
             if full and not rescale:
-                for _ in range(4):
-                    yield ("arrive", p_ready[wg][0])
-            yield ("work", m.rng.uniform(300, 600))
+                yield from release(wg, j, 0)
+            yield ("work", m.rng.uniform(150, 1300))
             if rescale:
                 for tag in m.issued:
                     if tag[0] == "PV" and tag[1] == wg:
                         assert m.complete(tag), ("O rescaled while a P V runs", wg, j, tag)
                 yield ("work", 300)
             if rescale or not full:
-                for _ in range(4):
-                    yield ("arrive", p_ready[wg][0])
-            for _ in range(4):
-                yield ("arrive", p_ready[wg][1])
+                yield from release(wg, j, 0)
+            yield from release(wg, j, 1)
         yield ("wait", o_done, 1)
         for tag in m.issued:
             if tag[0] == "PV" and tag[1] == wg:
                 assert m.complete(tag), ("epilogue before the last P V", wg)
 
     m.spawn(producer(), "producer")
+    m.spawn(watcher(), "watcher")
     m.spawn(issuer(), "issuer")
     for wg in range(nq):
         m.spawn(softmax(wg), f"softmax{wg}")
@@ -145,6 +171,20 @@ def test_attention_protocol_random_schedules(jitter):
         attention_v1(m, n_tiles=rng.randint(1, 7), two=rng.random() < 0.7, rescale_p=rng.choice([0.0, 0.3, 1.0]),
                      ragged_p=rng.choice([0.0, 0.5]))
         m.run()
+
+
+def test_model_catches_a_watcher_running_ahead():
+    """Without its wait for each p_ready[0][h] phase, the watcher's arrival for the next key tile can land in the
+    current phase (P V would start before every softmax warp has written P): the model must report it."""
+    caught = 0
+    for seed in range(50):
+        m = Model(seed, tma_latency=(10.0, 20.0))
+        attention_v1(m, n_tiles=5, two=True, rescale_p=0.0, ragged_p=0.0, watcher_phase_wait=False)
+        try:
+            m.run()
+        except AssertionError:
+            caught += 1
+    assert caught > 0
 
 
 def test_model_catches_a_wrong_phase():
