@@ -312,8 +312,9 @@ def run_reference(args):
 
 def run_sweep(args):
     """Benchmark configuration c5: kernel sweep on one GPU. Chunk attention with 40 heads x 128 over
-    Lq in {1560, 4680, 10800} x Lkv in {4096, 16384, 32768, 75600, 131072}; MXFP8 FFN GEMMs (E4M3, E8M0 per
-    32) M in {4680, 10800, 43200} for up (K 5120 -> N 13824) and down (13824 -> 5120). One JSON line per
+    Lq in {1560, 4680, 10800} x Lkv in {4096, 16384, 32768, 75600, 131072}; block-scaled FFN GEMMs (MXFP8 E4M3
+    and E5M2, MXFP4 E2M1, E8M0 per 32) M in {4680, 10800, 43200} for up (K 5120 -> N 13824) and down
+    (13824 -> 5120). One JSON line per
     point: TFLOP/s from CUDA events around each launch (median of 5, an L2 flush before each launch) and the
     fraction of the measured bf16 peak (burst: each kernel is timed alone)."""
     import __graft_entry__
@@ -363,19 +364,25 @@ def run_sweep(args):
             print(json.dumps({"sweep": "chunk_attention", "q_rows": lq, "kv_rows": lkv, "heads": H, "kv_splits": splits,
                               "ms": ms, "tflops": tf, "frac_of_peak": tf / peak, "peak": f"{src} bf16_tflops {peak}"}))
             del ks, vs, parts
-    for m in ((4680, 10800, 43200) if only in ("all", "mxfp8") else ()):
-        for kk, nn in ((5120, 13824), (13824, 5120)):
-            a = torch.randn(m, kk, generator=g, device=dev, dtype=bf)
-            w = (torch.randn(nn, kk, generator=g, device=dev) * 0.02).to(bf)
-            ad, as_, _ = K.mx_quantize(a)
-            wd, ws, _ = K.mx_quantize(w)
-            o = torch.empty(m, nn, dtype=bf, device=dev)
-            ms = timed(lambda: K.mx_linear(ad, as_, wd, ws, None, o))
-            tf = 2.0 * m * kk * nn / (ms / 1e3) / 1e12
-            print(json.dumps({"sweep": "mxfp8_gemm", "m": m, "k": kk, "n": nn, "ms": ms, "tflops": tf,
-                              "frac_of_bf16_peak": tf / peak, "frac_of_2x_bf16_peak": tf / (2 * peak),
-                              "peak": f"{src} bf16_tflops {peak}"}))
-            del a, w, ad, as_, wd, ws, o
+    # block-scaled FFN GEMMs: MXFP8 E4M3 (the reference's default), E5M2 (its LINGBOT_MX_FP8 option) and MXFP4 E2M1;
+    # the nominal dense rates are 2x (FP8) and 4x (FP4) the bf16 rate, so each point is also given against 2x / 4x
+    # the measured bf16 peak
+    fmts = {"mxfp8": ("e4m3", "e5m2", "e2m1"), "mxfp4": ("e2m1",), "all": ("e4m3", "e5m2", "e2m1")}.get(only, ())
+    for fmt in fmts:
+        mult = 4 if fmt == "e2m1" else 2
+        for m in (4680, 10800, 43200):
+            for kk, nn in ((5120, 13824), (13824, 5120)):
+                a = torch.randn(m, kk, generator=g, device=dev, dtype=bf)
+                w = (torch.randn(nn, kk, generator=g, device=dev) * 0.02).to(bf)
+                ad, as_, _ = K.mx_quantize(a, fmt=fmt)
+                wd, ws, _ = K.mx_quantize(w, fmt=fmt)
+                o = torch.empty(m, nn, dtype=bf, device=dev)
+                ms = timed(lambda: K.mx_linear(ad, as_, wd, ws, None, o, fmt=fmt))
+                tf = 2.0 * m * kk * nn / (ms / 1e3) / 1e12
+                print(json.dumps({"sweep": "mx_gemm", "format": fmt, "m": m, "k": kk, "n": nn, "ms": ms, "tflops": tf,
+                                  "frac_of_bf16_peak": tf / peak, f"frac_of_{mult}x_bf16_peak": tf / (mult * peak),
+                                  "peak": f"{src} bf16_tflops {peak}"}))
+                del a, w, ad, as_, wd, ws, o
     # the block's bf16 GEMMs (q|k|v with the row sums of squares; o-projection with the gated residual + FiLM) at
     # the 1- and 8-GPU row counts of c4; 3 untimed launches first (an ncu capture can skip them with -s)
     for m in ((10800, 1350) if only in ("all", "gemm") else ()):
@@ -585,7 +592,8 @@ def main():
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the oracle check of the first block on a row sample (run after the timed steps)")
     ap.add_argument("--sweep", action="store_true", help="kernel sweep (benchmark configuration c5) instead of the step")
-    ap.add_argument("--sweep-only", default="all", choices=["all", "attention", "mxfp8", "gemm", "linmx", "tiles"],
+    ap.add_argument("--sweep-only", default="all",
+                    choices=["all", "attention", "mxfp8", "mxfp4", "gemm", "linmx", "tiles"],
                     help="with --sweep: one family of points (gemm = the block's bf16 GEMMs at 10,800 and 1,350 rows)")
     ap.add_argument("--lin-mx", action="store_true",
                     help="every block Linear in MXFP8 (the reference's LINGBOT_LIN_MX option; not the headline config)")

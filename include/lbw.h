@@ -177,12 +177,28 @@ int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, i
  * the in-kernel activation quantisation of ffn_mx.mm. */
 int lbw_mx_quantize(const void* x, int rows, int k, void* data, void* scales, void* dequant, void* stream);
 
+/* Element formats of the block-scaled path (OCP MX v1.0, one E8M0 scale per 32 elements along k). */
+enum lbw_mx_format {
+  LBW_MX_E4M3 = 0, /* MXFP8 E4M3: the reference's default (kernels/ffn_mx.py:18) */
+  LBW_MX_E5M2 = 1, /* MXFP8 E5M2: LINGBOT_MX_FP8=float8_e5m2 (kernels/ffn_mx.py:8, :18) */
+  LBW_MX_E2M1 = 2  /* MXFP4 E2M1: two elements per byte, element 2i in the low nibble (k % 256 == 0 for GEMMs);
+                      not in the reference, the benchmark's block-scaled GEMM sweep asks for it */
+};
+/* lbw_mx_quantize in any lbw_mx_format: data [rows, k] bytes (E2M1: [rows, k / 2], packed), scales as above.
+ * Replaces ffn_mx.prequantize_weight with LINGBOT_MX_FP8 (kernels/ffn_mx.py:8-18, :44-47). */
+int lbw_mx_quantize_fmt(const void* x, int rows, int k, int fmt, void* data, void* scales, void* dequant, void* stream);
+
 /* Block-scaled tcgen05 GEMMs (kind::mxf8f6f4, E4M3 x E4M3, E8M0 scale per 32 along K, fp32 accumulate).
  * a: codes [m, k] + tiled scales (rows padded to 128); w: codes [n, k] + tiled scales; k % 128 == 0,
  * n % 128 == 0. Replaces ffn_mx.mm (kernels/ffn_mx.py:159-182, nkilib matmul_mxfp8). */
 /* Every epilogue rounds a w^T to bf16 before adding the bias, as ffn_mx.mm's bf16 result + bias does in the
  * reference (_mx_matmul, model_fast.py:1403-1410; _ffn_mx :1589-1610). */
 /* out[m, n] = bf16(bf16(a w^T) + bias) (bias may be NULL). */
+int lbw_mx_linear_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                      int m, int n, int k, int fmt, void* out, void* stream);
+/* lbw_mx_linear_fmt in the element format lbw_mx_format fmt (E4M3 / E5M2: kind::mxf8f6f4; E2M1: kind::mxf4, K = 64
+ * per MMA, k % 256 == 0); a and w as lbw_mx_quantize_fmt writes them. Replaces ffn_mx.mm (kernels/ffn_mx.py:159-182)
+ * under LINGBOT_MX_FP8. */
 int lbw_mx_linear(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias, int m,
                   int n, int k, void* out, void* stream);
 /* FFN up: GELU_tanh(bf16(a w^T) + bias) quantised to MXFP8 codes out[m, n] + tiled scales out_scales

@@ -33,6 +33,8 @@ SIGNATURES = {
     "lbw_layernorm_mod": ([_vp, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _vp, _vp], _i),
     "lbw_rmsnorm_rope": ([_vp, _vp, _vp, _i, _i, _f, _vp, _vp, _i, _i, _i, _i, _vp, _ll, _i, _vp], _i),
     "lbw_mx_quantize": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
+    "lbw_mx_quantize_fmt": ([_vp, _i, _i, _i, _vp, _vp, _vp, _vp], _i),
+    "lbw_mx_linear_fmt": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
     "lbw_linear_rmsnorm_noalloc": ([_vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp], _i),
     "lbw_chunk_attention_partial": ([_vp, _ll, _i, _i, _vp, _vp, _vp, _i, _ll, _vp, _f, _i, _vp, _vp, _i, _vp], _i),
     "lbw_attention_merge": ([_vp, _vp, _i, _i, _i, _vp, _ll, _vp], _i),

@@ -26,32 +26,37 @@
 namespace lbw {
 
 namespace mxg {
-constexpr int BM = 128, BK = 128;
+constexpr int BM = 128, BK = 128;  // BK: bytes of one K block per row (one 128-byte swizzled TMA box row)
 constexpr int A_BYTES = BM * BK;   // 16 KB
 constexpr int SFA_BYTES = 512;
 constexpr int THREADS = 320;
 constexpr int EPI_WARPS = 8;
 constexpr int SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per CTA on sm_100
 // Tile width TBN = 256 (default) or 128 (when 256-wide tiles would leave the last wave mostly idle).
-// A 128-wide tile's MMAs take half as long as a 256-wide tile's, so its stages hold two 128-code K blocks (and
+// A 128-wide tile's MMAs take half as long as a 256-wide tile's, so its stages hold two K blocks (and
 // their scale atoms): the lone MMA-issuing thread then waits once per 8 MMAs instead of once per 4.
-template <int TBN> struct Cfg {
-  static constexpr int KSUB = TBN == 256 ? 1 : 2;                 // 128-code K blocks per stage
+// FMT: element format (MX_E4M3 / MX_E5M2: a K block is 128 elements, one byte each, one 512-byte scale atom per
+// 128 rows; MX_E2M1: 256 elements as packed nibbles, two scale atoms per 128 rows).
+template <int TBN, int FMT = MX_E4M3> struct Cfg {
+  static constexpr int KSUB = TBN == 256 ? 1 : 2;                 // K blocks per stage
+  static constexpr int KE = FMT == MX_E2M1 ? 256 : 128;           // elements of one K block
+  static constexpr int SFPB = KE / 128;                           // scale atoms per K block and 128 rows
   static constexpr int B_SUB = TBN * BK;
   static constexpr int A_STAGE = A_BYTES * KSUB, B_STAGE = B_SUB * KSUB;
   static constexpr int B_BYTES = B_STAGE;
-  static constexpr int SFA_STAGE = SFA_BYTES * KSUB;
-  static constexpr int SFB_STAGE = TBN / 128 * 512 * KSUB;
+  static constexpr int SFA_STAGE = SFA_BYTES * SFPB * KSUB;
+  static constexpr int SFB_STAGE = TBN / 128 * 512 * SFPB * KSUB;
   static constexpr int SF_BYTES = SFA_STAGE + SFB_STAGE;
   static constexpr int TX_BYTES = A_STAGE + B_STAGE + SF_BYTES;
   static constexpr int STAGES = TBN == 256 ? 4 : 3;
   static constexpr int SMEM_BYTES = STAGES * TX_BYTES + 1024;
-  // scale columns right after the accumulator: 4 per K block for A, then 4 per K block and 128-row W block
-  static constexpr uint32_t SFA_COL = TBN, SFB_COL = TBN + 4 * KSUB;
+  // scale columns right after the accumulator: 4 per scale atom for A (SFPB per K block), then the same per
+  // 128-row W block
+  static constexpr uint32_t SFA_COL = TBN, SFB_COL = TBN + 4 * SFPB * KSUB;
 };
 }  // namespace mxg
 
-template <class Epi, int TBN = 256>
+template <class Epi, int TBN = 256, int FMT = MX_E4M3>
 __global__ void __launch_bounds__(mxg::THREADS, 1)
     gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, int M, int N, int K, int group_m,
@@ -60,7 +65,8 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
   using mxg::BM;
   using mxg::BK;
   using mxg::A_BYTES;
-  using Cf = mxg::Cfg<TBN>;
+  using Cf = mxg::Cfg<TBN, FMT>;
+  constexpr int SFPB = Cf::SFPB;
   constexpr int BN = TBN, STAGES = Cf::STAGES, B_BYTES = Cf::B_BYTES, SF_BYTES = Cf::SF_BYTES;
   constexpr int TX_BYTES = Cf::TX_BYTES;
   constexpr uint32_t SFA_COL = Cf::SFA_COL, SFB_COL = Cf::SFB_COL;
@@ -98,7 +104,8 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
   const uint32_t tmem = tmem_slot;
   const Abort ab{status, &abort_flag};
 
-  const int nM = (M + BM - 1) / BM, nN = (N + BN - 1) / BN, nK = K / BK, nS = nK / KSUB;
+  const int nM = (M + BM - 1) / BM, nN = (N + BN - 1) / BN, nK = K / Cf::KE, nS = nK / KSUB;
+  const int nAtom = K / 128;  // scale atoms per 128 rows (4 scales of 32 elements each)
   const int n_sf_blocks = (N + 127) / 128;  // 128-row scale blocks of W that exist
   const int tiles = nM * nN;
 
@@ -123,12 +130,14 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
             tma_load_2d(sB + s * B_BYTES + u * Cf::B_SUB, &tmB, &full_bar[s], (kb + u) * BK, n_blk * BN);
           }
           // scale atoms of consecutive K blocks are consecutive 512-byte atoms
-          bulk_load(sf, sfa + ((long long)m_blk * nK + kb) * 512, 512 * KSUB, &full_bar[s]);
+          bulk_load(sf, sfa + ((long long)m_blk * nAtom + kb * SFPB) * 512, 512 * SFPB * KSUB, &full_bar[s]);
           if (BN == 256) {
-            bulk_load(sf + 512, sfb + ((long long)b0 * nK + kb) * 512, 512, &full_bar[s]);
-            bulk_load(sf + 1024, sfb + ((long long)b1 * nK + kb) * 512, 512, &full_bar[s]);
+            bulk_load(sf + Cf::SFA_STAGE, sfb + ((long long)b0 * nAtom + kb * SFPB) * 512, 512 * SFPB, &full_bar[s]);
+            bulk_load(sf + Cf::SFA_STAGE + 512 * SFPB, sfb + ((long long)b1 * nAtom + kb * SFPB) * 512, 512 * SFPB,
+                      &full_bar[s]);
           } else {
-            bulk_load(sf + Cf::SFA_STAGE, sfb + ((long long)n_blk * nK + kb) * 512, 512 * KSUB, &full_bar[s]);
+            bulk_load(sf + Cf::SFA_STAGE, sfb + ((long long)n_blk * nAtom + kb * SFPB) * 512, 512 * SFPB * KSUB,
+                      &full_bar[s]);
           }
           ++issued;
           if (++s == STAGES) { s = 0; ph ^= 1; }
@@ -154,24 +163,37 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
           tc_fence_after();
           const uint64_t da = dA + (uint64_t)((s * A_STAGE) >> 4), db = dB + (uint64_t)((s * B_BYTES) >> 4);
           const uint64_t ds = dS + (uint64_t)((s * SF_BYTES) >> 4);
-          if (BN == 256) {
-            tmem_cp_32x128b_x4(tmem + SFA_COL, ds);
-            tmem_cp_32x128b_x4(tmem + SFB_COL, ds + (uint64_t)(512 >> 4));
-            tmem_cp_32x128b_x4(tmem + SFB_COL + 4, ds + (uint64_t)(1024 >> 4));
-          } else {
+          // scale atoms into TMEM: A's atoms of the stage's K blocks, then per 128-row W block its atoms
 #pragma unroll
-            for (int u = 0; u < KSUB; ++u) {
-              tmem_cp_32x128b_x4(tmem + SFA_COL + 4 * u, ds + (uint64_t)((u * 512) >> 4));
-              tmem_cp_32x128b_x4(tmem + SFB_COL + 4 * u, ds + (uint64_t)((Cf::SFA_STAGE + u * 512) >> 4));
-            }
+          for (int a = 0; a < SFPB * KSUB; ++a)
+            tmem_cp_32x128b_x4(tmem + SFA_COL + 4 * a, ds + (uint64_t)((a * 512) >> 4));
+          // W: the stage holds each 128-row W block's atoms in turn; in TMEM the scales of one atom for all of
+          // the tile's TBN rows are consecutive (4 columns per 128 rows), atom after atom
+#pragma unroll
+          for (int i = 0; i < Cf::SFB_STAGE / 512; ++i) {
+            const int b = i / (SFPB * KSUB), t = i % (SFPB * KSUB);
+            tmem_cp_32x128b_x4(tmem + SFB_COL + (BN / 128) * 4 * t + 4 * b,
+                               ds + (uint64_t)((Cf::SFA_STAGE + i * 512) >> 4));
           }
+          // 4 MMAs per 128-byte K block (32 bytes each: K = 32 E4M3 / E5M2 or K = 64 E2M1 elements). An MMA's
+          // scales are consecutive bytes of a 32-bit TMEM scale column: FP8 reads byte kk of the block's atom,
+          // E2M1 reads bytes 2 (kk % 2) .. +1 of atom kk / 2.
 #pragma unroll
           for (int u = 0; u < KSUB; ++u)
 #pragma unroll
-            for (int kk = 0; kk < BK / 32; ++kk)
-              mma_mxf8_ss(tmem, da + (uint64_t)((u * A_BYTES) >> 4) + (uint64_t)(kk * 2),
-                          db + (uint64_t)((u * Cf::B_SUB) >> 4) + (uint64_t)(kk * 2), idesc_mxf8(BM, BN, kk),
-                          (ks | u | kk) != 0, tmem + SFA_COL + 4 * u, tmem + SFB_COL + 4 * u);
+            for (int kk = 0; kk < 4; ++kk) {
+              const int atom = u * SFPB + (FMT == MX_E2M1 ? (kk >> 1) : 0);
+              const uint32_t sf_id = FMT == MX_E2M1 ? 2 * (kk & 1) : kk;
+              const uint64_t a_d = da + (uint64_t)((u * A_BYTES) >> 4) + (uint64_t)(kk * 2);
+              const uint64_t b_d = db + (uint64_t)((u * Cf::B_SUB) >> 4) + (uint64_t)(kk * 2);
+              const uint32_t acc = (ks | u | kk) != 0;
+              if (FMT == MX_E2M1)
+                mma_mxf4_ss(tmem, a_d, b_d, idesc_mxf4(BM, BN, sf_id), acc, tmem + SFA_COL + 4 * atom,
+                            tmem + SFB_COL + (BN / 128) * 4 * atom);
+              else
+                mma_mxf8_ss(tmem, a_d, b_d, idesc_mxf8(BM, BN, sf_id, FMT == MX_E5M2 ? 1 : 0), acc,
+                            tmem + SFA_COL + 4 * atom, tmem + SFB_COL + (BN / 128) * 4 * atom);
+            }
           tc_commit(&empty_bar[s]);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
@@ -228,20 +250,21 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-template <class Epi, int TBN>
+template <class Epi, int TBN, int FMT = MX_E4M3>
 static int launch_gemm_mx_t(const CUtensorMap& tmA, const void* a_scales, const void* w, const void* w_scales, int M,
                             int N, int K, const Epi& epi, cudaStream_t stream, int* st) {
-  using C = mxg::Cfg<TBN>;
+  using C = mxg::Cfg<TBN, FMT>;
   constexpr int smem_bytes = C::SMEM_BYTES + mxg::EPI_WARPS * Epi::WARP_SMEM;
   static_assert(smem_bytes <= mxg::SMEM_LIMIT, "operand ring + epilogue staging exceed the shared memory of a CTA");
+  const int row_bytes = K / 32 * mx_block_bytes(FMT);
   CUtensorMap tmB;
-  int err = make_tmap_2d(&tmB, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, mxg::BK, TBN);
+  int err = make_tmap_2d(&tmB, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, row_bytes, row_bytes, mxg::BK, TBN);
   if (err) return err;
   static bool attr_set[64] = {};  // per instantiation and device
   const int dix = device_index();
   if (dix < 0) return set_error(LBW_ERR_CUDA, "mx gemm: cudaGetDevice failed");
   if (!attr_set[dix]) {
-    err = cuda_check(cudaFuncSetAttribute(gemm_mx_kernel<Epi, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    err = cuda_check(cudaFuncSetAttribute(gemm_mx_kernel<Epi, TBN, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           smem_bytes),
                      "mx gemm smem attribute");
     if (err) return err;
@@ -249,32 +272,37 @@ static int launch_gemm_mx_t(const CUtensorMap& tmA, const void* a_scales, const 
   }
   const int tiles = ((M + mxg::BM - 1) / mxg::BM) * ((N + TBN - 1) / TBN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_mx_kernel<Epi, TBN><<<grid, mxg::THREADS, smem_bytes, stream>>>(
+  gemm_mx_kernel<Epi, TBN, FMT><<<grid, mxg::THREADS, smem_bytes, stream>>>(
       tmA, tmB, reinterpret_cast<const uint8_t*>(a_scales), reinterpret_cast<const uint8_t*>(w_scales), M, N, K,
-      group_rows(M, K, 1), epi, st);
+      group_rows(M, row_bytes, 1), epi, st);
   return cuda_check(cudaGetLastError(), "mx gemm launch");
 }
 
-template <class Epi>
+// fmt: MX_E4M3 (the reference's default), MX_E5M2 (LINGBOT_MX_FP8=float8_e5m2) or MX_E2M1 (MXFP4). A and W hold
+// K / 32 blocks per row: 32 bytes each for the FP8 formats, 16 (packed nibbles) for E2M1.
+template <class Epi, int FMT = MX_E4M3>
 static int launch_gemm_mx(const void* a, const void* a_scales, const void* w, const void* w_scales, int M, int N, int K,
                           const Epi& epi, cudaStream_t stream) {
   using namespace mxg;
+  constexpr int fmt = FMT;
+  const int ke = fmt == MX_E2M1 ? 256 : 128;  // elements of one 128-byte K block
   if (M <= 0 || N <= 0 || K <= 0) return set_error(LBW_ERR_SHAPE, "mx gemm: empty problem %d x %d x %d", M, N, K);
-  if (K % BK) return set_error(LBW_ERR_SHAPE, "mx gemm: K=%d must be a multiple of %d", K, BK);
+  if (K % ke) return set_error(LBW_ERR_SHAPE, "mx gemm: K=%d must be a multiple of %d", K, ke);
   if (N % 128) return set_error(LBW_ERR_SHAPE, "mx gemm: N=%d must be a multiple of 128", N);
   if (!a || !w || !a_scales || !w_scales) return set_error(LBW_ERR_INVALID, "mx gemm: null operand");
   if (!aligned(a_scales, 16) || !aligned(w_scales, 16)) return set_error(LBW_ERR_ALIGN, "mx gemm: scales alignment");
   int err = 0;
   int* st = device_status(&err);
   if (!st) return err;
+  const int row_bytes = K / 32 * mx_block_bytes(fmt);
   CUtensorMap tmA;
-  if ((err = make_tmap_2d(&tmA, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, BK, BM))) return err;
+  if ((err = make_tmap_2d(&tmA, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, row_bytes, row_bytes, BK, BM))) return err;
   const long long mt = (M + BM - 1) / BM;
-  const bool can128 = (K / BK) % mxg::Cfg<128>::KSUB == 0;
+  const bool can128 = (K / ke) % 2 == 0;  // 128-wide tiles stage two K blocks
   const int force = tile_n_override();
-  if (can128 && (force ? force == 128 : prefer_narrow_tiles(mt, N)))
-    return launch_gemm_mx_t<Epi, 128>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st);
-  return launch_gemm_mx_t<Epi, 256>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st);
+  const bool narrow = can128 && (force ? force == 128 : prefer_narrow_tiles(mt, N));
+  return narrow ? launch_gemm_mx_t<Epi, 128, FMT>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st)
+                : launch_gemm_mx_t<Epi, 256, FMT>(tmA, a_scales, w, w_scales, M, N, K, epi, stream, st);
 }
 
 static bool ok16mx(const void* p) { return p == nullptr || aligned(p, 16); }
@@ -296,6 +324,23 @@ int lbw_mx_linear(const void* a, const void* a_scales, const void* w, const void
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   e.round_acc = 1;
   return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_mx_linear_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                      int m, int n, int k, int fmt, void* out, void* stream) {
+  if (!out) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_fmt: null output");
+  if (!ok16mx(out) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_fmt: alignment");
+  EpiStore e{};
+  e.out[0] = e.out[1] = e.out[2] = reinterpret_cast<__nv_bfloat16*>(out);
+  e.ld[0] = e.ld[1] = e.ld[2] = n;
+  e.region_cols = n;
+  e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  e.round_acc = 1;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (fmt == MX_E4M3) return launch_gemm_mx<EpiStore, MX_E4M3>(a, a_scales, w, w_scales, m, n, k, e, s);
+  if (fmt == MX_E5M2) return launch_gemm_mx<EpiStore, MX_E5M2>(a, a_scales, w, w_scales, m, n, k, e, s);
+  if (fmt == MX_E2M1) return launch_gemm_mx<EpiStore, MX_E2M1>(a, a_scales, w, w_scales, m, n, k, e, s);
+  return set_error(LBW_ERR_INVALID, "lbw_mx_linear_fmt: element format %d", fmt);
 }
 
 int lbw_mx_linear_gelu(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,

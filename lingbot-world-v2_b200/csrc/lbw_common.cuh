@@ -172,6 +172,17 @@ LBW_DEV void mma_mxf8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
 }
+// D(tmem) (+)= (A * SFA) * (B * SFB), kind::mxf4 (E2M1 pairs per byte) with E8M0 scales, two per MMA (K = 64).
+LBW_DEV void mma_mxf4_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate,
+                         uint32_t sfa_tmem, uint32_t sfb_tmem) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
 // Shared memory (32 rows x 16 bytes) -> TMEM, broadcast to the four 32-lane quarters.
 LBW_DEV void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
@@ -250,15 +261,25 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn_major, 
          | ((uint32_t)(N >> 3) << 17)   // N
          | ((uint32_t)(M >> 4) << 24);  // M
 }
-// Instruction descriptor, kind::mxf8f6f4 block-scaled: E4M3 x E4M3 with UE8M0 scales,
-// K-major operands; sf_id selects the byte of the 32-bit TMEM scale column.
-__host__ __device__ constexpr uint32_t idesc_mxf8(int M, int N, uint32_t sf_id) {
+// Instruction descriptor, kind::mxf8f6f4 block-scaled: both operands E4M3 (fmt 0) or both E5M2 (fmt 1) with UE8M0
+// scales, K-major operands; sf_id selects the byte of the 32-bit TMEM scale column.
+__host__ __device__ constexpr uint32_t idesc_mxf8(int M, int N, uint32_t sf_id, uint32_t fmt = 0) {
   return (sf_id << 4)                  // B scale-factor id
-         | (0u << 7) | (0u << 10)      // A, B = E4M3
+         | (fmt << 7) | (fmt << 10)    // A, B element format (0 = E4M3, 1 = E5M2)
          | ((uint32_t)(N >> 3) << 17)  // N
          | (1u << 23)                  // scale format UE8M0
          | ((uint32_t)(M >> 4) << 24)  // M
          | (sf_id << 29);              // A scale-factor id
+}
+// Instruction descriptor, kind::mxf4 block-scaled (E2M1 x E2M1, packed two per byte, one UE8M0 scale per 32
+// elements, K = 64 per MMA): sf_id is the first of the two consecutive scale bytes the MMA reads (0 or 2).
+__host__ __device__ constexpr uint32_t idesc_mxf4(int M, int N, uint32_t sf_id) {
+  return (sf_id << 4)                  // B scale-factor id
+         | (1u << 7) | (1u << 10)      // A, B element format E2M1 (the kind::mxf4 encoding)
+         | ((uint32_t)(N >> 3) << 17)  // N
+         | (1u << 23)                  // scale format UE8M0
+         | ((uint32_t)(M >> 4) << 24)  // M
+         | (sf_id << 29);              // A scale-factor id; bit 31 = 0: K = 64
 }
 
 // ------------------------------------------------------------------------------------------

@@ -7,6 +7,7 @@
 // An all-zero block gets s = -127.
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 #include <stdint.h>
 
@@ -66,6 +67,56 @@ __device__ __forceinline__ uint8_t mx_quant32(const float (&v)[32], uint8_t (&q)
     q[i + 1] = (uint8_t)(p >> 8);
   }
   return (uint8_t)(s + 127);
+}
+
+// ---- element formats of the block-scaled path (OCP MX v1.0): E4M3 (emax 8), E5M2 (emax 15), E2M1 (emax 2) ----
+enum MxFmt : int { MX_E4M3 = 0, MX_E5M2 = 1, MX_E2M1 = 2 };
+__host__ __device__ constexpr int mx_emax(int fmt) { return fmt == MX_E5M2 ? 15 : (fmt == MX_E2M1 ? 2 : 8); }
+// bytes of one 32-value block's elements (E2M1: two per byte, element 2i in the low nibble)
+__host__ __device__ constexpr int mx_block_bytes(int fmt) { return fmt == MX_E2M1 ? 16 : 32; }
+
+// Shared exponent floor(log2(amax)) - emax, clamped to the E8M0 range [-127, 127]; -127 for an all-zero block.
+__device__ __forceinline__ int mx_shared_exp_fmt(float amax, int emax) {
+  if (!(amax > 0.f)) return -127;
+  int e = (int)((__float_as_uint(amax) >> 23) & 0xFF);
+  int fl = (e == 0) ? -127 : e - 127;
+  int s = fl - emax;
+  return s < -127 ? -127 : (s > 127 ? 127 : s);
+}
+
+// Quantise 32 values to format FMT: element bytes into q (mx_block_bytes(FMT) of them), returns the E8M0 byte.
+// Elements are round-to-nearest-even of v / 2^s, saturated to the format's largest finite value.
+template <int FMT>
+__device__ __forceinline__ uint8_t mx_quant32_fmt(const float (&v)[32], uint8_t* q) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const int s = mx_shared_exp_fmt(amax, mx_emax(FMT));
+  // v * 2^-s is exact: -s lies in [-125, 127], so 2^-s is a normal float
+  const float inv = exp2i(-s);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    const float2 f = make_float2(v[i] * inv, v[i + 1] * inv);
+    if (FMT == MX_E2M1) {
+      q[i >> 1] = (uint8_t)__nv_cvt_float2_to_fp4x2(f, __NV_E2M1, cudaRoundNearest);
+    } else {
+      const __nv_fp8x2_storage_t p = __nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, FMT == MX_E5M2 ? __NV_E5M2 : __NV_E4M3);
+      q[i] = (uint8_t)(p & 0xFF);
+      q[i + 1] = (uint8_t)(p >> 8);
+    }
+  }
+  return (uint8_t)(s + 127);
+}
+
+// Element i of a block (bytes q) as a float, before the shared scale.
+template <int FMT>
+__device__ __forceinline__ float mx_elem(const uint8_t* q, int i) {
+  if (FMT == MX_E2M1) {
+    const __nv_fp4_storage_t c = (__nv_fp4_storage_t)((q[i >> 1] >> ((i & 1) * 4)) & 0xF);
+    return __half2float(__half(__nv_cvt_fp4_to_halfraw(c, __NV_E2M1)));
+  }
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)q[i], FMT == MX_E5M2 ? __NV_E5M2 : __NV_E4M3);
+  return __half2float(__half(h));
 }
 
 // Quantise-dequantise 32 values and pack the (exactly representable) results as bf16 pairs.

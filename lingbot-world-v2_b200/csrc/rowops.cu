@@ -146,10 +146,13 @@ __global__ void __launch_bounds__(ROW_THREADS) rmsnorm_rope_kernel(
   }
 }
 
-// One thread per 32-value block; rows up to the next multiple of 128 get zero scales.
+// One thread per 32-value block; rows up to the next multiple of 128 get zero scales. FMT: MX_E4M3 / MX_E5M2
+// (one byte per element, row pitch K) or MX_E2M1 (packed nibbles, row pitch K / 2).
+template <int FMT>
 __global__ void mx_quantize_kernel(const __nv_bfloat16* __restrict__ x, int rows, int K, int rows_pad,
                                    uint8_t* __restrict__ data, uint8_t* __restrict__ scales,
                                    __nv_bfloat16* __restrict__ deq) {
+  constexpr int BB = mx_block_bytes(FMT);
   const int nb = K >> 5;
   const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (id >= (long long)rows_pad * nb) return;
@@ -167,19 +170,19 @@ __global__ void mx_quantize_kernel(const __nv_bfloat16* __restrict__ x, int rows
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[q * 8 + e] = __bfloat162float(b[e]);
   }
-  uint8_t qb[32];
-  const uint8_t sb = mx_quant32(v, qb);
+  __align__(16) uint8_t qb[32];
+  const uint8_t sb = mx_quant32_fmt<FMT>(v, qb);
   scales[mx_sf_offset(r, j, K)] = sb;
-  uint4* dp = reinterpret_cast<uint4*>(data + (long long)r * K + j * 32);
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(qb);
-  dp[0] = make_uint4(w[0], w[1], w[2], w[3]);
-  dp[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  uint4* dp = reinterpret_cast<uint4*>(data + (long long)r * (K / 32 * BB) + j * BB);
+  const uint4* w = reinterpret_cast<const uint4*>(qb);
+#pragma unroll
+  for (int q = 0; q < BB / 16; ++q) dp[q] = w[q];
   if (deq) {
     const int se = (int)sb - 127;
     uint32_t pk[16];
 #pragma unroll
     for (int e = 0; e < 32; e += 2)
-      pk[e >> 1] = pack_bf16(ldexpf(mx_from_e4m3(qb[e]), se), ldexpf(mx_from_e4m3(qb[e + 1]), se));
+      pk[e >> 1] = pack_bf16(ldexpf(mx_elem<FMT>(qb, e), se), ldexpf(mx_elem<FMT>(qb, e + 1), se));
     uint4* d4 = reinterpret_cast<uint4*>(deq + (long long)r * K + j * 32);
 #pragma unroll
     for (int q = 0; q < 4; ++q) d4[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
@@ -258,18 +261,29 @@ int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, i
   return cuda_check(cudaGetLastError(), "rmsnorm_rope launch");
 }
 
-int lbw_mx_quantize(const void* x, int rows, int k, void* data, void* scales, void* dequant, void* stream) {
+int lbw_mx_quantize_fmt(const void* x, int rows, int k, int fmt, void* data, void* scales, void* dequant,
+                        void* stream) {
   if (!x || !data || !scales) return set_error(LBW_ERR_INVALID, "mx_quantize: null pointer");
+  if (fmt < MX_E4M3 || fmt > MX_E2M1) return set_error(LBW_ERR_INVALID, "mx_quantize: element format %d", fmt);
   if (rows <= 0 || k <= 0 || k % 128) return set_error(LBW_ERR_SHAPE, "mx_quantize: K=%d must be a multiple of 128", k);
   if (!aligned(x, 16) || !aligned(data, 16) || (dequant && !aligned(dequant, 16)))
     return set_error(LBW_ERR_ALIGN, "mx_quantize: alignment");
   const int rows_pad = (rows + 127) / 128 * 128;
   const long long n = (long long)rows_pad * (k / 32);
   const int threads = 256;
-  mx_quantize_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x), rows, k, rows_pad, reinterpret_cast<uint8_t*>(data),
-      reinterpret_cast<uint8_t*>(scales), reinterpret_cast<__nv_bfloat16*>(dequant));
+  const unsigned blocks = (unsigned)((n + threads - 1) / threads);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  uint8_t *d = reinterpret_cast<uint8_t*>(data), *sc = reinterpret_cast<uint8_t*>(scales);
+  __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(dequant);
+  if (fmt == MX_E4M3) mx_quantize_kernel<MX_E4M3><<<blocks, threads, 0, s>>>(xb, rows, k, rows_pad, d, sc, dq);
+  else if (fmt == MX_E5M2) mx_quantize_kernel<MX_E5M2><<<blocks, threads, 0, s>>>(xb, rows, k, rows_pad, d, sc, dq);
+  else mx_quantize_kernel<MX_E2M1><<<blocks, threads, 0, s>>>(xb, rows, k, rows_pad, d, sc, dq);
   return cuda_check(cudaGetLastError(), "mx_quantize launch");
+}
+
+int lbw_mx_quantize(const void* x, int rows, int k, void* data, void* scales, void* dequant, void* stream) {
+  return lbw_mx_quantize_fmt(x, rows, k, MX_E4M3, data, scales, dequant, stream);
 }
 
 }  // extern "C"

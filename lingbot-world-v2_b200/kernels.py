@@ -264,31 +264,43 @@ def rmsnorm_rope(x, ss, gamma, eps, out, rope=None, grid=None, tok0=0, out_row_o
     return out
 
 
-def mx_quantize(x, dequant=False, data=None, scales=None):
-    """x [rows, K] bf16 -> (data uint8 [rows, K] E4M3 codes, scales uint8 tiled, dequant bf16 or None).
-    data / scales: optional output buffers (mx_buffers(rows, K))."""
+MX_FORMATS = {"e4m3": 0, "e5m2": 1, "e2m1": 2}   # lbw_mx_format (include/lbw.h)
+
+
+def mx_row_bytes(k, fmt="e4m3"):
+    """Bytes of one row of k elements: k for the MXFP8 formats, k / 2 for E2M1 (packed nibbles)."""
+    return k // 2 if fmt == "e2m1" else k
+
+
+def mx_quantize(x, dequant=False, data=None, scales=None, fmt="e4m3"):
+    """x [rows, K] bf16 -> (data uint8 [rows, K] codes ([rows, K / 2] packed for fmt "e2m1"), scales uint8 tiled,
+    dequant bf16 or None). fmt: "e4m3" (default), "e5m2" or "e2m1". data / scales: optional output buffers
+    (mx_buffers(rows, K, fmt=fmt))."""
     require_cuda(x, data, scales)
     _c(x, BF16)
+    if fmt not in MX_FORMATS:
+        raise ValueError(f"mx_quantize: element format {fmt!r} (one of {sorted(MX_FORMATS)})")
     rows, k = x.shape
     rows_pad = (rows + 127) // 128 * 128
+    rb = mx_row_bytes(k, fmt)
     if (data is None) != (scales is None):
         raise ValueError("mx_quantize: give both data and scales, or neither")
     if data is None:
-        data = torch.empty(rows, k, dtype=torch.uint8, device=x.device)
+        data = torch.empty(rows, rb, dtype=torch.uint8, device=x.device)
         scales = torch.empty(rows_pad * (k // 32), dtype=torch.uint8, device=x.device)
-    elif (data.shape != (rows, k) or data.dtype != torch.uint8 or not data.is_contiguous()
+    elif (data.shape != (rows, rb) or data.dtype != torch.uint8 or not data.is_contiguous()
           or scales.dtype != torch.uint8 or scales.numel() < rows_pad * (k // 32)):
         raise ValueError("mx_quantize: output buffers do not match x")
     deq = torch.empty_like(x) if dequant else None
-    check(load().lbw_mx_quantize(ptr(x), rows, k, ptr(data), ptr(scales), ptr(deq), stream_of(x.device)),
-          "mx_quantize")
+    check(load().lbw_mx_quantize_fmt(ptr(x), rows, k, MX_FORMATS[fmt], ptr(data), ptr(scales), ptr(deq),
+                                     stream_of(x.device)), "mx_quantize")
     return data, scales, deq
 
 
-def mx_buffers(rows, k, device):
-    """Zeroed MXFP8 operand buffers: codes [rows, k] uint8 and tiled scales (rows padded to 128)."""
+def mx_buffers(rows, k, device, fmt="e4m3"):
+    """Zeroed MX operand buffers: codes [rows, row bytes] uint8 and tiled scales (rows padded to 128)."""
     rows_pad = (rows + 127) // 128 * 128
-    return (torch.zeros(rows, k, dtype=torch.uint8, device=device),
+    return (torch.zeros(rows, mx_row_bytes(k, fmt), dtype=torch.uint8, device=device),
             torch.zeros(rows_pad * (k // 32), dtype=torch.uint8, device=device))
 
 
@@ -315,23 +327,28 @@ def layernorm_affine_mx(x, eps, weight, bias, data, scales):
     return data, scales
 
 
-def _mx_check(a, a_s, w, w_s):
+def _mx_check(a, a_s, w, w_s, fmt="e4m3"):
+    """(m, n, k) of an MX GEMM, k in elements (a row of E2M1 codes holds k / 2 bytes)."""
     require_cuda(a, a_s, w, w_s)
-    m, k = a.shape
+    m, kb = a.shape
     n = w.shape[0]
-    if a.dtype != torch.uint8 or w.dtype != torch.uint8 or w.shape[1] != k:
-        raise ValueError("mx gemm: codes must be uint8 [m, k] and [n, k]")
+    k = kb * 2 if fmt == "e2m1" else kb
+    if a.dtype != torch.uint8 or w.dtype != torch.uint8 or w.shape[1] != kb:
+        raise ValueError("mx gemm: codes must be uint8 [m, k] and [n, k] (k / 2 bytes per row for e2m1)")
     if a_s.numel() < (m + 127) // 128 * 128 * (k // 32) or w_s.numel() < (n + 127) // 128 * 128 * (k // 32):
         raise ValueError("mx gemm: scale buffers too small")
     return m, n, k
 
 
-def mx_linear(a, a_s, w, w_s, bias=None, out=None):
-    m, n, k = _mx_check(a, a_s, w, w_s)
+def mx_linear(a, a_s, w, w_s, bias=None, out=None, fmt="e4m3"):
+    """out [m, n] = bf16(bf16(a w^T) + bias) on the block-scaled GEMM; a, w as mx_quantize(..., fmt=fmt) made them."""
+    if fmt not in MX_FORMATS:
+        raise ValueError(f"mx_linear: element format {fmt!r} (one of {sorted(MX_FORMATS)})")
+    m, n, k = _mx_check(a, a_s, w, w_s, fmt)
     if out is None:
         out = torch.empty(m, n, dtype=BF16, device=a.device)
-    check(load().lbw_mx_linear(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(out), stream_of(a.device)),
-          "mx_linear")
+    check(load().lbw_mx_linear_fmt(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, MX_FORMATS[fmt], ptr(out),
+                                   stream_of(a.device)), "mx_linear")
     return out
 
 

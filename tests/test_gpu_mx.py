@@ -196,3 +196,57 @@ def test_layernorm_affine_mx(cuda_dev, c):
     q, se = omx.quantize(h)
     got = omx.dequantize(dq.cpu().view(torch.float8_e4m3fn), _untile(ds.cpu(), m, c))
     assert rel_l2(got, omx.dequantize(q, se)) < 2e-3
+
+
+# ---- the other element formats: E5M2 (LINGBOT_MX_FP8=float8_e5m2, kernels/ffn_mx.py:8, :18) and E2M1 (MXFP4) ----
+
+def _codes(q, fmt):
+    """Oracle element values -> the bytes the GPU stores (E2M1: packed nibbles, element 2i low)."""
+    if fmt == "e2m1":
+        return omx.e2m1_pack(omx.e2m1_codes(q))
+    return q.view(torch.uint8)
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "e2m1"])
+def test_mx_quantize_formats_bit_exact(cuda_dev, fmt):
+    """Codes, E8M0 scales (tiled) and dequantised values bit-exact with the OCP MX emulation, over 6 decades of
+    magnitude, an all-zero block and a block that saturates the element format."""
+    import lbw_b200.kernels as K
+    g = torch.Generator().manual_seed(41)
+    rows, k = 300, 512
+    x = (torch.randn(rows, k, generator=g) * torch.logspace(-3, 3, rows).view(-1, 1)).to(BF)
+    x[5] = 0
+    x[7, :32] = 1000.0
+    x[9, 64:96] = torch.linspace(-7.0, 7.0, 32)     # E2M1 ties and the +-6 saturation
+    data, scales, deq = K.mx_quantize(x.to(cuda_dev), dequant=True, fmt=fmt)
+    q, s = omx.quantize(x, fmt)
+    assert torch.equal(data.cpu(), _codes(q, fmt))
+    assert torch.equal(scales.cpu(), omx.scales_tiled(s, k))
+    assert torch.equal(deq.cpu().float(), omx.dequantize(q, s))
+
+
+@pytest.mark.parametrize("fmt", ["e5m2", "e2m1"])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 256), (300, 512, 768), (77, 384, 512), (1350, 1024, 1024),
+                                   (1000, 1536, 1536)])
+def test_mx_linear_formats_vs_emulation(cuda_dev, fmt, m, n, k):
+    """The block-scaled GEMM in E5M2 (kind::mxf8f6f4) and E2M1 (kind::mxf4) against the emulation: the same
+    quantised operands, so only the fp32 summation order differs before the bf16 rounding."""
+    import lbw_b200.kernels as K
+    a, w, b = _ab(m, n, k, 7 * m + n + k)
+    d = cuda_dev
+    ad, as_, _ = K.mx_quantize(a.to(d), fmt=fmt)
+    wd, ws, _ = K.mx_quantize(w.to(d), fmt=fmt)
+    out = K.mx_linear(ad, as_, wd, ws, b.to(d), fmt=fmt)
+    ref = (omx.mx_linear(a, w, fmt).float() + b.float()).to(BF)
+    assert rel_l2(out, ref) < 4e-3
+
+
+def test_mx_formats_reject_bad_shapes(cuda_dev):
+    import lbw_b200.kernels as K
+    d = cuda_dev
+    a = torch.zeros(128, 384, dtype=BF, device=d)
+    ad, as_, _ = K.mx_quantize(a, fmt="e2m1")      # 384 % 128 == 0: fine for the quantiser
+    with pytest.raises(ValueError, match="multiple of 256"):
+        K.mx_linear(ad, as_, ad, as_, fmt="e2m1")      # ... but an E2M1 GEMM needs k % 256 == 0
+    with pytest.raises(ValueError, match="element format"):
+        K.mx_quantize(a, fmt="e3m2")
