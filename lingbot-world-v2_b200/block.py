@@ -24,7 +24,7 @@ The fp32 residual is updated in place by the GEMM epilogues.
 import torch
 import torch.nn as nn
 
-from . import kernels, rope, sp
+from . import kernels, ops, rope, sp  # noqa: F401  (ops registers the kernels as torch.ops.lbw.*)
 from .attention import cross_dedup_bias
 
 BF16 = torch.bfloat16
@@ -72,13 +72,23 @@ class Workspace:
         self.h = mk(rows, dim)
         self.q_raw = mk(rows, dim)
         self.k_raw = mk(rows, dim)
-        self.ss = mk(2, rows, dt=torch.float32)
+        # row sums of squares of q and k (two tensors: an operator may not write two views of one)
+        self.ss_q = mk(rows, dt=torch.float32)
+        self.ss_k = mk(rows, dt=torch.float32)
         self.q = mk(rows, dim)
         self.attn = mk(rows, dim)
         self.u = mk(rows, ffn_dim)
         # MXFP8 operands of the FFN: codes + tiled E8M0 scales (rows padded to 128)
         self.hq, self.hs = kernels.mx_buffers(rows, dim, device)
         self.uq, self.us = kernels.mx_buffers(rows, ffn_dim, device)
+
+    def new_kv(self, chunk_rows):
+        """Scratch K and V of the new chunk [chunk_rows, dim] bf16 for kv_write=False (the cache slot is left as it
+        is), allocated on first use."""
+        if getattr(self, "_new_kv", None) is None or self._new_kv[0].shape[0] != chunk_rows:
+            self._new_kv = (torch.empty(chunk_rows, self.dim, dtype=BF16, device=self.h.device),
+                            torch.empty(chunk_rows, self.dim, dtype=BF16, device=self.h.device))
+        return self._new_kv
 
     def attn_parts(self, slots, heads):
         """Split-KV workspace (fp32 partial outputs + (m, l)), grown on demand."""
@@ -319,13 +329,13 @@ class CausalWanAttentionBlock(nn.Module):
                 kv_write_end=None, kv_roll_dst=0, kv_roll_src=0, kv_roll_len=0, kv_current_end=None,
                 kv_chunks=None, grid_ints=None, fused=None, kv_write=True, kv_only=False):
         """x [1, L, C] fp32 (this rank's token shard under sequence parallelism), e [1, 1, 6, C] fp32
-        -> new x (fp32). Writes the chunk's roped K and V into kv_chunks[0][-1] / kv_chunks[1][-1]."""
+        -> new x (fp32). Writes the chunk's roped K and V into kv_chunks[0][-1] / kv_chunks[1][-1]; with
+        kv_write=False (LINGBOT_STEP_NOWRITE: the denoise steps, model_fast.py:2135-2143, :3821-3835) the new
+        chunk's K and V are attended from scratch and the destination slot is left unchanged."""
         if kv_chunks is None:
             raise ValueError("the B200 block serves the chunked KV cache: pass kv_chunks=(k_chunks, v_chunks)")
         if fused is not None or kv_roll_len:
             raise ValueError("fused commit/roll variants of the Trainium path are not part of the B200 block")
-        if not kv_write:
-            raise ValueError("kv_write=False (LINGBOT_STEP_NOWRITE) is not supported by the B200 block")
         if crossattn_cache is None or context is None:
             raise ValueError("pass the text context and its crossattn_cache dict")
         out = x.detach().float().reshape(-1, self.dim).clone()
@@ -344,7 +354,7 @@ class CausalWanAttentionBlock(nn.Module):
                 raise ValueError("dit_cond_dict must carry the hoisted 'cam_film' (scale, shift)")
             film = dit_cond_dict["cam_film"]
         self.forward_inplace(out, e, kv_chunks[0], kv_chunks[1], context, crossattn_cache, grid, start_frame,
-                             freqs, film=film, fill_cross=bool(first), kv_only=kv_only)
+                             freqs, film=film, fill_cross=bool(first), kv_only=kv_only, kv_write=kv_write)
         return out.view(x.shape) if x.dtype == torch.float32 else out.view(x.shape).to(x.dtype)
 
     @staticmethod
@@ -360,10 +370,12 @@ class CausalWanAttentionBlock(nn.Module):
         return tuple(int(v) for v in g)
 
     def forward_inplace(self, xf, e, k_chunks, v_chunks, context, crossattn_cache, grid, start_frame, freqs,
-                        film=None, fill_cross=False, kv_only=False, ws=None, attn_events=None, phases=None):
+                        film=None, fill_cross=False, kv_only=False, ws=None, attn_events=None, phases=None,
+                        kv_write=True):
         """The block on the fp32 residual xf [L_local, C] (updated in place). attn_events: optional list
         that receives a (start, end) pair of CUDA events around the self-attention kernel. phases: optional
-        list that receives (name, event) marks after each step, for per-phase timing."""
+        list that receives (name, event) marks after each step, for per-phase timing. kv_write=False: the new
+        chunk's K/V go to workspace scratch instead of the destination chunk, which is not modified."""
         mark = (lambda name: phases.append((name, _event()))) if phases is not None else (lambda name: None)
         mark("start")
         if self._packed is None:
@@ -378,6 +390,11 @@ class CausalWanAttentionBlock(nn.Module):
         em = (pk["mod"] + e.reshape(6, C).float()).contiguous()
         k_dst, v_dst = k_chunks[-1], v_chunks[-1]
         chunk_rows = k_dst.numel() // C
+        if not kv_write:
+            if kv_only:
+                raise ValueError("kv_only computes the cache entries: it needs kv_write=True")
+            k_dst, v_dst = ws.new_kv(chunk_rows)
+            k_chunks, v_chunks = list(k_chunks[:-1]) + [k_dst], list(v_chunks[:-1]) + [v_dst]
         p = sp.world() if sp.active() else 1
         if chunk_rows != L * p:
             raise ValueError(f"destination chunk holds {chunk_rows} tokens, expected {L} x {p} ranks")
@@ -387,7 +404,7 @@ class CausalWanAttentionBlock(nn.Module):
             raise ValueError(f"grid {grid} does not match the chunk's {chunk_rows} tokens")
         cos, sin = rope.rope_tables(freqs, grid, start_frame, dev)
         rp = (cos, sin, f)
-        ss_q, ss_k = ws.ss[0], ws.ss[1]
+        ss_q, ss_k = ws.ss_q, ws.ss_k
 
         # self-attention
         if "wqkv_mx" in pk:

@@ -16,6 +16,17 @@ BF16 = torch.bfloat16
 HEAD_DIM = 128
 
 
+def _tracing(eager):
+    """True while torch.compile traces a graph (and the caller is not the operator's own implementation): the
+    wrapper then calls the torch.ops.lbw operator (lbw_b200.ops) so that the kernel becomes a graph node."""
+    return not eager and torch.compiler.is_compiling()
+
+
+def _op(name):
+    """torch.ops.lbw.<name> (registered when lbw_b200.ops is imported, as lbw_b200.block does)."""
+    return getattr(torch.ops.lbw, name)
+
+
 def _c(t, dtype=None):
     if dtype is not None and t.dtype != dtype:
         raise ValueError(f"expected {dtype}, got {t.dtype}")
@@ -30,9 +41,16 @@ def _rows(t):
     return t.reshape(-1, t.shape[-2] * t.shape[-1]) if t.dim() >= 3 else t
 
 
-def chunk_attention(q, k_chunks, v_chunks, key_bias=None, out=None, softmax_scale=None):
+def chunk_attention(q, k_chunks, v_chunks, key_bias=None, out=None, softmax_scale=None, _eager=False):
     """q [Lq, H, 128] (or [1, Lq, H, 128] / [Lq, H*128]) bf16; chunks [L_i, H, 128]-like bf16 ->
     out [Lq, H*128] bf16 = softmax(q kᵀ * scale + bias) v over the concatenated chunks."""
+    if _tracing(_eager):
+        if out is None:
+            out = torch.empty(q.numel() // (q.shape[-1] * (q.shape[-2] if q.dim() >= 3 else 1)),
+                              q.shape[-1] * (q.shape[-2] if q.dim() >= 3 else 1), dtype=BF16, device=q.device)
+        scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(HEAD_DIM)
+        _op("chunk_attention")(q, list(k_chunks), list(v_chunks), key_bias, float(scale), out)
+        return out
     require_cuda(q, *k_chunks, *v_chunks, key_bias, out)
     q2 = _rows(_c(q, BF16))
     lq, cols = q2.shape
@@ -75,8 +93,13 @@ def attention_workspace(n_slots, q_rows, heads, device):
 
 
 def chunk_attention_partial(q, k_chunks, v_chunks, n_splits, part_o, part_ml, slot0=0, key_bias=None,
-                            softmax_scale=None):
+                            softmax_scale=None, _eager=False):
     """Split-KV attention into workspace slots slot0 .. slot0 + n_splits - 1 (see lbw.h)."""
+    if _tracing(_eager):
+        scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(HEAD_DIM)
+        _op("chunk_attention_partial")(q, list(k_chunks), list(v_chunks), int(n_splits), part_o, part_ml, int(slot0),
+                                       key_bias, float(scale))
+        return
     require_cuda(q, *k_chunks, *v_chunks, key_bias, part_o, part_ml)
     q2 = _rows(_c(q, BF16))
     lq, cols = q2.shape
@@ -133,7 +156,10 @@ def chunk_attention_gated(q, k_chunks, v_chunks, gate_flag_ptr, gate_value, gate
     return out
 
 
-def attention_merge(part_o, part_ml, n_slots, out):
+def attention_merge(part_o, part_ml, n_slots, out, _eager=False):
+    if _tracing(_eager):
+        _op("attention_merge")(part_o, part_ml, int(n_slots), out)
+        return out
     require_cuda(part_o, part_ml, out)
     _, lq, heads, _ = part_o.shape
     o2 = _rows(_c(out, BF16))
@@ -172,7 +198,10 @@ def gemm_bf16(a, w, bias=None, out=None):
     return out
 
 
-def qkv_proj(h, w_qkv, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, v_row_off=0):
+def qkv_proj(h, w_qkv, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, v_row_off=0, _eager=False):
+    if _tracing(_eager):
+        _op("qkv_proj")(h, w_qkv, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, int(v_row_off))
+        return
     require_cuda(h, w_qkv, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out)
     m, c = h.shape
     v2 = _rows(v_out)
@@ -184,7 +213,10 @@ def qkv_proj(h, w_qkv, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, v_row_off=0):
                               ptr(v2), v2.stride(0), v_row_off, stream_of(h.device)), "qkv_proj")
 
 
-def linear_rowss(a, w, bias, out, ss):
+def linear_rowss(a, w, bias, out, ss, _eager=False):
+    if _tracing(_eager):
+        _op("linear_rowss")(a, w, bias, out, ss)
+        return out
     require_cuda(a, w, bias, out, ss)
     m, k = a.shape
     n = w.shape[0]
@@ -195,7 +227,10 @@ def linear_rowss(a, w, bias, out, ss):
     return out
 
 
-def linear_residual(a, w, bias, x, gate=None, film_scale=None, film_shift=None):
+def linear_residual(a, w, bias, x, gate=None, film_scale=None, film_shift=None, _eager=False):
+    if _tracing(_eager):
+        _op("linear_residual")(a, w, bias, x, gate, film_scale, film_shift)
+        return x
     require_cuda(a, w, bias, x, gate, film_scale, film_shift)
     m, k = a.shape
     n = w.shape[0]
@@ -226,7 +261,10 @@ def linear_act(a, w, bias=None, addend=None, silu=False, out=None):
     return out
 
 
-def linear_gelu(a, w, bias, out, mx_qdq):
+def linear_gelu(a, w, bias, out, mx_qdq, _eager=False):
+    if _tracing(_eager):
+        _op("linear_gelu")(a, w, bias, out, bool(mx_qdq))
+        return out
     require_cuda(a, w, bias, out)
     m, k = a.shape
     n = w.shape[0]
@@ -237,7 +275,10 @@ def linear_gelu(a, w, bias, out, mx_qdq):
     return out
 
 
-def layernorm_mod(x, eps, out, scale=None, shift=None, weight=None, bias=None, mx_qdq=False):
+def layernorm_mod(x, eps, out, scale=None, shift=None, weight=None, bias=None, mx_qdq=False, _eager=False):
+    if _tracing(_eager):
+        _op("layernorm_mod")(x, float(eps), out, scale, shift, weight, bias, bool(mx_qdq))
+        return out
     require_cuda(x, out)
     _c(x, torch.float32)
     m, c = x.shape
@@ -246,8 +287,15 @@ def layernorm_mod(x, eps, out, scale=None, shift=None, weight=None, bias=None, m
     return out
 
 
-def rmsnorm_rope(x, ss, gamma, eps, out, rope=None, grid=None, tok0=0, out_row_off=0):
+def rmsnorm_rope(x, ss, gamma, eps, out, rope=None, grid=None, tok0=0, out_row_off=0, _eager=False):
     """rope = (cos, sin, n_frames) from rope.rope_tables; grid = (f, h, w)."""
+    if _tracing(_eager):
+        if rope is not None:
+            _op("rmsnorm_rope")(x, ss, gamma, float(eps), out, rope[0], rope[1], int(rope[2]), int(grid[1]),
+                                int(grid[2]), int(tok0), int(out_row_off))
+        else:
+            _op("rmsnorm_rope")(x, ss, gamma, float(eps), out, None, None, 0, 0, 0, int(tok0), int(out_row_off))
+        return out
     require_cuda(x, ss, gamma, out)
     m, c = x.shape
     o2 = _rows(out)
@@ -272,10 +320,16 @@ def mx_row_bytes(k, fmt="e4m3"):
     return k // 2 if fmt == "e2m1" else k
 
 
-def mx_quantize(x, dequant=False, data=None, scales=None, fmt="e4m3"):
+def mx_quantize(x, dequant=False, data=None, scales=None, fmt="e4m3", _eager=False):
     """x [rows, K] bf16 -> (data uint8 [rows, K] codes ([rows, K / 2] packed for fmt "e2m1"), scales uint8 tiled,
     dequant bf16 or None). fmt: "e4m3" (default), "e5m2" or "e2m1". data / scales: optional output buffers
     (mx_buffers(rows, K, fmt=fmt))."""
+    if _tracing(_eager) and not dequant:
+        if data is None and scales is None:
+            d, sc = _op("mx_quantize")(x, fmt)
+            return d, sc, None
+        _op("mx_quantize_into")(x, data, scales, fmt)
+        return data, scales, None
     require_cuda(x, data, scales)
     _c(x, BF16)
     if fmt not in MX_FORMATS:
@@ -304,7 +358,10 @@ def mx_buffers(rows, k, device, fmt="e4m3"):
             torch.zeros(rows_pad * (k // 32), dtype=torch.uint8, device=device))
 
 
-def layernorm_mod_mx(x, eps, scale, shift, data, scales):
+def layernorm_mod_mx(x, eps, scale, shift, data, scales, _eager=False):
+    if _tracing(_eager):
+        _op("layernorm_mod_mx")(x, float(eps), scale, shift, data, scales)
+        return data, scales
     require_cuda(x, scale, shift, data, scales)
     _c(x, torch.float32)
     m, c = x.shape
@@ -315,8 +372,11 @@ def layernorm_mod_mx(x, eps, scale, shift, data, scales):
     return data, scales
 
 
-def layernorm_affine_mx(x, eps, weight, bias, data, scales):
+def layernorm_affine_mx(x, eps, weight, bias, data, scales, _eager=False):
     """MXFP8 codes + tiled scales of LN(x) * weight + bias (norm3 before an MXFP8 cross_attn.q)."""
+    if _tracing(_eager):
+        _op("layernorm_affine_mx")(x, float(eps), weight, bias, data, scales)
+        return data, scales
     require_cuda(x, weight, bias, data, scales)
     _c(x, torch.float32), _c(weight, torch.float32), _c(bias, torch.float32)
     m, c = x.shape
@@ -340,8 +400,14 @@ def _mx_check(a, a_s, w, w_s, fmt="e4m3"):
     return m, n, k
 
 
-def mx_linear(a, a_s, w, w_s, bias=None, out=None, fmt="e4m3"):
+def mx_linear(a, a_s, w, w_s, bias=None, out=None, fmt="e4m3", _eager=False):
     """out [m, n] = bf16(bf16(a w^T) + bias) on the block-scaled GEMM; a, w as mx_quantize(..., fmt=fmt) made them."""
+    if _tracing(_eager):
+        y = _op("mx_linear")(a, a_s, w, w_s, bias, fmt)
+        if out is None:
+            return y
+        out.copy_(y)
+        return out
     if fmt not in MX_FORMATS:
         raise ValueError(f"mx_linear: element format {fmt!r} (one of {sorted(MX_FORMATS)})")
     m, n, k = _mx_check(a, a_s, w, w_s, fmt)
@@ -352,7 +418,10 @@ def mx_linear(a, a_s, w, w_s, bias=None, out=None, fmt="e4m3"):
     return out
 
 
-def mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales):
+def mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales, _eager=False):
+    if _tracing(_eager):
+        _op("mx_linear_gelu")(a, a_s, w, w_s, bias, out, out_scales)
+        return out, out_scales
     m, n, k = _mx_check(a, a_s, w, w_s)
     if out.shape != (m, n) or out.dtype != torch.uint8:
         raise ValueError("mx_linear_gelu: out must be uint8 [m, n]")
@@ -361,7 +430,10 @@ def mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales):
     return out, out_scales
 
 
-def mx_linear_residual(a, a_s, w, w_s, bias, x, gate=None, film_scale=None, film_shift=None):
+def mx_linear_residual(a, a_s, w, w_s, bias, x, gate=None, film_scale=None, film_shift=None, _eager=False):
+    if _tracing(_eager):
+        _op("mx_linear_residual")(a, a_s, w, w_s, bias, x, gate, film_scale, film_shift)
+        return x
     m, n, k = _mx_check(a, a_s, w, w_s)
     require_cuda(x, gate, film_scale, film_shift)
     if x.shape != (m, n) or x.dtype != torch.float32:

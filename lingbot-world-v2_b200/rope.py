@@ -40,16 +40,22 @@ def rope_tables(freqs, grid, start_frame, device):
     """(cos, sin) fp32 device tables [f*22 + h*21 + w*21] for a chunk of grid (f, h, w) whose first
     frame is `start_frame` (= current_start // frame_seqlen)."""
     f, h, w = (int(v) for v in grid)
+    if torch.compiler.is_compiling():   # no host-side cache inside a traced graph
+        return _tables(freqs, f, h, w, int(start_frame), device)
     key = (id(freqs), tuple(freqs.shape), f, h, w, int(start_frame), str(device))
     hit = _CACHE.get(key)
     if hit is not None and hit[0] is freqs:
         return hit[1]
+    out = _tables(freqs, f, h, w, int(start_frame), device)
+    _CACHE[key] = (freqs, out)
+    return out
+
+
+def _tables(freqs, f, h, w, start_frame, device):
     fc = freqs.detach().cpu().float()
     s0, s1 = split_sizes(fc)
     if (s0, s1) != (22, 21):
         raise ValueError(f"rope tables are laid out for head_dim 128 (22/21/21 pairs), got {s0}/{s1}/{s1}")
     ang = torch.cat([fc[start_frame:start_frame + f, :s0].reshape(-1), fc[:h, s0:s0 + s1].reshape(-1),
                      fc[:w, s0 + s1:].reshape(-1)])
-    out = (torch.cos(ang).to(device), torch.sin(ang).to(device))
-    _CACHE[key] = (freqs, out)
-    return out
+    return torch.cos(ang).to(device), torch.sin(ang).to(device)
