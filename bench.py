@@ -651,12 +651,12 @@ def main():
     vs = [[torch.randn(1, chunk, H, 128, generator=gk, device=dev, dtype=bf) for _ in range(n_chunks)]
           for _ in range(layers)]
     ctx = torch.randn(TEXT_LEN, C, generator=gk, device=dev, dtype=bf)
+    e0 = torch.randn(6, C, generator=gk, device=dev) * 0.1      # the step's time embedding: the same on every rank
     g = torch.Generator(device=dev).manual_seed(2 + rank)
     caches = [{"k": torch.empty(TEXT_LEN, H, 128, dtype=bf, device=dev),
                "v": torch.empty(TEXT_LEN, H, 128, dtype=bf, device=dev)} for _ in range(layers)]
     films = [((torch.randn(L_loc, C, generator=g, device=dev) * 0.1).to(bf),
               (torch.randn(L_loc, C, generator=g, device=dev) * 0.1).to(bf)) for _ in range(layers)]
-    e0 = torch.randn(6, C, generator=g, device=dev) * 0.1
     x0 = torch.randn(L_loc, C, generator=g, device=dev).to(bf).float()
     xf = x0.clone()
     freqs = R.rope_freqs()

@@ -243,20 +243,30 @@ int lbw_peer_buffer_create(long long bytes, void** ptr, void* ipc_handle);
 int lbw_peer_buffer_open(const void* ipc_handle, void** ptr);
 /* owned = 1 for the caller's own buffer (freed), 0 for an opened peer buffer (unmapped). */
 int lbw_peer_buffer_close(void* ptr, int owned);
+/* The exchange's flag words: one LBW_SP_FLAG_BLOCK-byte block per rank in host memory that every rank of the node
+ * maps (a POSIX shared-memory segment, say) and registers here: page-aligned, a whole number of pages. *dev = the
+ * device address of `host` in this process. Block r holds ready[64] (byte 0), done[64] (byte 256) and a copy of
+ * the gathered epoch (byte 512) of rank r. A rank's streams wait only on its own block, so a host thread can end
+ * any of those waits by writing the awaited epoch there (the limit a stream memory operation does not have). */
+#define LBW_SP_FLAG_BLOCK 1024
+int lbw_host_flags_register(void* host, long long bytes, void** dev);
+int lbw_host_flags_unregister(void* host);
 /* One exchange = lbw_sp_kv_stage then lbw_sp_kv_gather with the same arguments (they may go on different
- * streams; stage first in stream order). Rank r's rows [r*local_rows, (r+1)*local_rows) of k_dest and v_dest
- * ([world*local_rows, ld] bf16, row stride ld elements, cols used) are sent to every peer, and the peers'
- * rows are received. bufs[p] = rank p's buffer as mapped in this process (bufs[rank] = own).
+ * streams; the second on a stream ordered after the first). This rank's rows [rank*local_rows, +local_rows) of
+ * k_dest / v_dest ([world*local_rows, ld] bf16, row stride ld elements, cols used) are sent to every peer, and
+ * the peers' rows are received. bufs[p] = rank p's buffer as mapped in this process (bufs[rank] = own); flags =
+ * the device address (lbw_host_flags_register) of rank 0's flag block, rank r's at flags + r*LBW_SP_FLAG_BLOCK.
  * epoch = 1, 2, ...: the number of this exchange on these buffers, the same on every rank.
  * stage: waits until every peer has finished reading the previous epoch, then copies this rank's rows into
- * its buffer. gather: announces them, waits (without a timeout) until every peer has staged the same epoch,
- * pulls the peers' rows with copy engines (helper streams joined back into `stream`), and, when all rows
- * have landed, sets the 32-bit word at byte 512 of the own buffer to epoch (the gate of
- * lbw_chunk_attention_gated). */
-int lbw_sp_kv_stage(void* const* bufs, int rank, int world, unsigned int epoch, void* k_dest, void* v_dest,
-                    long long ld, int local_rows, int cols, void* stream);
-int lbw_sp_kv_gather(void* const* bufs, int rank, int world, unsigned int epoch, void* k_dest, void* v_dest,
-                     long long ld, int local_rows, int cols, void* stream);
+ * its buffer. gather: announces them, waits until every peer has staged the same epoch (or the host writes the
+ * epoch into this rank's flag block), pulls the peers' rows with copy engines (helper streams joined back into
+ * `stream`), and, when all rows have landed, sets the 32-bit word at byte 512 of the own buffer to epoch (the
+ * gate of lbw_chunk_attention_gated) and its copy in the own flag block. Replaces the K/V all-gather
+ * (wan/modules/model_fast.py:2066-2108 _gather_new, wan/distributed/tensor_parallel.py:106-139). */
+int lbw_sp_kv_stage(void* const* bufs, void* flags, int rank, int world, unsigned int epoch, void* k_dest,
+                    void* v_dest, long long ld, int local_rows, int cols, void* stream);
+int lbw_sp_kv_gather(void* const* bufs, void* flags, int rank, int world, unsigned int epoch, void* k_dest,
+                     void* v_dest, long long ld, int local_rows, int cols, void* stream);
 
 /* ---- Wan 2.1 VAE decoder (wan/modules/vae2_1.py) -------------------------------------------
  * Frames are stored channels-last with a one-pixel zero border: [frames][h + 2][w + 2][c] bf16 ("padded rows",

@@ -63,8 +63,10 @@ SIGNATURES = {
     "lbw_peer_buffer_create": ([_ll, ctypes.POINTER(_vp), _vp], _i),
     "lbw_peer_buffer_open": ([_vp, ctypes.POINTER(_vp)], _i),
     "lbw_peer_buffer_close": ([_vp, _i], _i),
-    "lbw_sp_kv_stage": ([ctypes.POINTER(_vp), _i, _i, ctypes.c_uint, _vp, _vp, _ll, _i, _i, _vp], _i),
-    "lbw_sp_kv_gather": ([ctypes.POINTER(_vp), _i, _i, ctypes.c_uint, _vp, _vp, _ll, _i, _i, _vp], _i),
+    "lbw_host_flags_register": ([_vp, _ll, ctypes.POINTER(_vp)], _i),
+    "lbw_host_flags_unregister": ([_vp], _i),
+    "lbw_sp_kv_stage": ([ctypes.POINTER(_vp), _vp, _i, _i, ctypes.c_uint, _vp, _vp, _ll, _i, _i, _vp], _i),
+    "lbw_sp_kv_gather": ([ctypes.POINTER(_vp), _vp, _i, _i, ctypes.c_uint, _vp, _vp, _ll, _i, _i, _vp], _i),
 }
 
 _lib = None

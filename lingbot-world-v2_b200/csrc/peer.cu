@@ -7,12 +7,18 @@
 // own). Nothing of the exchange occupies an SM, so it runs under the attention of the cached chunks instead
 // of competing with it for SMs the way a collective kernel does.
 //
-// Buffer layout (one per rank, same size on every rank):
-//   [0, 256)      ready[64]: ready[p] = epoch when rank p has staged its shard for that epoch
-//   [256, 512)    done[64]:  done[p]  = epoch when rank p has finished pulling this rank's shard
+// Buffer layout (one per rank, same size on every rank, in device memory shared through CUDA IPC):
 //   [512, 516)    gathered:  epoch of the last exchange whose rows have all landed in this rank's destination
 //                 (read by the gated attention kernel, lbw_chunk_attention_gated)
 //   [4096, ...)   K shard [rows, cols] bf16, then V shard [rows, cols] bf16
+// Flag blocks (one per rank, LBW_SP_FLAG_BLOCK bytes each, in host memory that every rank of the node maps and
+// registers with CUDA, so that the host can also write them):
+//   [0, 256)      ready[64]: ready[p] = epoch when rank p has staged its shard for that epoch
+//   [256, 512)    done[64]:  done[p]  = epoch when rank p has finished pulling this rank's shard
+//   [512, 516)    gathered, as above (a copy the host's watchdog reads)
+// A rank's streams wait only on words of its own flag block, so a host thread can always release them (by
+// writing the awaited epochs there) when a peer stops taking part: the waits have a limit even though stream
+// memory operations have none.
 // Epochs count the exchanges on a buffer (1, 2, ...); every rank runs the same sequence of exchanges.
 #include <string.h>
 
@@ -24,6 +30,7 @@ namespace lbw {
 
 constexpr int PEER_MAX = 64;
 constexpr size_t PEER_FLAGS = 4096;
+constexpr size_t FLAG_BLOCK = LBW_SP_FLAG_BLOCK;
 
 typedef CUresult (*StreamValueFn)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
 
@@ -118,6 +125,26 @@ int lbw_peer_buffer_close(void* ptr, int owned) {
   return LBW_OK;
 }
 
+int lbw_host_flags_register(void* host, long long bytes, void** dev) {
+  if (!host || !dev || bytes <= 0) return set_error(LBW_ERR_INVALID, "host_flags_register: bad arguments");
+  if (!aligned(host, 4096) || bytes % 4096) return set_error(LBW_ERR_ALIGN, "host_flags_register: page alignment");
+  cudaError_t e = cudaHostRegister(host, (size_t)bytes, cudaHostRegisterMapped | cudaHostRegisterPortable);
+  if (e != cudaSuccess) return set_error(LBW_ERR_CUDA, "host_flags_register: %s", cudaGetErrorString(e));
+  e = cudaHostGetDevicePointer(dev, host, 0);
+  if (e != cudaSuccess) {
+    cudaHostUnregister(host);
+    return set_error(LBW_ERR_CUDA, "host_flags_register: device pointer: %s", cudaGetErrorString(e));
+  }
+  return LBW_OK;
+}
+
+int lbw_host_flags_unregister(void* host) {
+  if (!host) return LBW_OK;
+  cudaError_t e = cudaHostUnregister(host);
+  if (e != cudaSuccess) return set_error(LBW_ERR_CUDA, "host_flags_unregister: %s", cudaGetErrorString(e));
+  return LBW_OK;
+}
+
 }  // extern "C"
 
 namespace lbw {
@@ -129,11 +156,13 @@ struct Exchange {
   CUstream cs = nullptr;
   size_t row = 0, pitch = 0, shard = 0;
   uint8_t *mine = nullptr, *kd = nullptr, *vd = nullptr;
+  uint8_t* flags = nullptr;  // device address (this process's mapping) of rank 0's flag block
 };
 
-static int exchange_setup(Exchange* x, void* const* bufs, int rank, int world, unsigned int epoch, void* k_dest,
-                          void* v_dest, long long ld, int local_rows, int cols, void* stream, const char* who) {
-  if (!bufs || !k_dest || !v_dest) return set_error(LBW_ERR_INVALID, "%s: null pointer", who);
+static int exchange_setup(Exchange* x, void* const* bufs, void* flags, int rank, int world, unsigned int epoch,
+                          void* k_dest, void* v_dest, long long ld, int local_rows, int cols, void* stream,
+                          const char* who) {
+  if (!bufs || !flags || !k_dest || !v_dest) return set_error(LBW_ERR_INVALID, "%s: null pointer", who);
   if (world < 2 || world > PEER_MAX || rank < 0 || rank >= world || epoch == 0 || local_rows <= 0 || cols <= 0 ||
       ld < cols)
     return set_error(LBW_ERR_SHAPE, "%s: rank %d of %d, epoch %u, %d x %d rows (ld %lld)", who, rank, world, epoch,
@@ -149,14 +178,18 @@ static int exchange_setup(Exchange* x, void* const* bufs, int rank, int world, u
   x->pitch = (size_t)ld * 2;
   x->shard = x->row * (size_t)local_rows;
   x->mine = static_cast<uint8_t*>(bufs[rank]);
+  x->flags = static_cast<uint8_t*>(flags);
   x->kd = static_cast<uint8_t*>(k_dest);
   x->vd = static_cast<uint8_t*>(v_dest);
   return LBW_OK;
 }
 
-static CUdeviceptr flag_at(void* base, int which, int p) {
-  return reinterpret_cast<CUdeviceptr>(static_cast<uint8_t*>(base) + which * 256 + 4 * p);
+// word `p` of region `which` (0 ready, 1 done, 2 gathered) of rank `owner`'s flag block
+static CUdeviceptr flag_at(const Exchange& x, int owner, int which, int p) {
+  return reinterpret_cast<CUdeviceptr>(x.flags + (size_t)owner * FLAG_BLOCK + which * 256 + 4 * p);
 }
+// the gathered word the gated attention reads, in this rank's device buffer
+static CUdeviceptr gathered_at(const Exchange& x) { return reinterpret_cast<CUdeviceptr>(x.mine + 512); }
 
 static int ck(CUresult r, const char* what) {
   return r == CUDA_SUCCESS ? LBW_OK : set_error(LBW_ERR_CUDA, "sp_kv exchange: %s (%d)", what, (int)r);
@@ -174,15 +207,17 @@ static int copy_rows(uint8_t* dst, size_t dpitch, const uint8_t* src, size_t spi
 
 extern "C" {
 
-int lbw_sp_kv_stage(void* const* bufs, int rank, int world, unsigned int epoch, void* k_dest, void* v_dest,
-                    long long ld, int local_rows, int cols, void* stream) {
+int lbw_sp_kv_stage(void* const* bufs, void* flags, int rank, int world, unsigned int epoch, void* k_dest,
+                    void* v_dest, long long ld, int local_rows, int cols, void* stream) {
   Exchange x;
-  int err = exchange_setup(&x, bufs, rank, world, epoch, k_dest, v_dest, ld, local_rows, cols, stream, "sp_kv_stage");
+  int err = exchange_setup(&x, bufs, flags, rank, world, epoch, k_dest, v_dest, ld, local_rows, cols, stream,
+                           "sp_kv_stage");
   if (err) return err;
   // every peer has finished pulling this rank's previous shard before it is overwritten
   if (epoch > 1)
     for (int p = 0; p < world; ++p)
-      if (p != rank && (err = ck(x.wt(x.cs, flag_at(x.mine, 1, p), epoch - 1, CU_STREAM_WAIT_VALUE_GEQ), "wait done")))
+      if (p != rank &&
+          (err = ck(x.wt(x.cs, flag_at(x, rank, 1, p), epoch - 1, CU_STREAM_WAIT_VALUE_GEQ), "wait done")))
         return err;
   const size_t own = (size_t)rank * local_rows * x.pitch;
   if ((err = copy_rows(x.mine + PEER_FLAGS, x.row, x.kd + own, x.pitch, x.row, local_rows, x.s))) return err;
@@ -190,18 +225,20 @@ int lbw_sp_kv_stage(void* const* bufs, int rank, int world, unsigned int epoch, 
   return cuda_check(cudaGetLastError(), "sp_kv_stage");
 }
 
-int lbw_sp_kv_gather(void* const* bufs, int rank, int world, unsigned int epoch, void* k_dest, void* v_dest,
-                     long long ld, int local_rows, int cols, void* stream) {
+int lbw_sp_kv_gather(void* const* bufs, void* flags, int rank, int world, unsigned int epoch, void* k_dest,
+                     void* v_dest, long long ld, int local_rows, int cols, void* stream) {
   Exchange x;
-  int err = exchange_setup(&x, bufs, rank, world, epoch, k_dest, v_dest, ld, local_rows, cols, stream, "sp_kv_gather");
+  int err = exchange_setup(&x, bufs, flags, rank, world, epoch, k_dest, v_dest, ld, local_rows, cols, stream,
+                           "sp_kv_gather");
   if (err) return err;
   PullStreams* ps = nullptr;
   if ((err = pull_streams(&ps))) return err;
   for (int p = 0; p < world; ++p)
-    if (p != rank && (err = ck(x.wr(x.cs, flag_at(bufs[p], 0, rank), epoch, CU_STREAM_WRITE_VALUE_DEFAULT), "signal ready")))
+    if (p != rank && (err = ck(x.wr(x.cs, flag_at(x, p, 0, rank), epoch, CU_STREAM_WRITE_VALUE_DEFAULT), "signal ready")))
       return err;
   for (int p = 0; p < world; ++p)
-    if (p != rank && (err = ck(x.wt(x.cs, flag_at(x.mine, 0, p), epoch, CU_STREAM_WAIT_VALUE_GEQ), "wait ready"))) return err;
+    if (p != rank && (err = ck(x.wt(x.cs, flag_at(x, rank, 0, p), epoch, CU_STREAM_WAIT_VALUE_GEQ), "wait ready")))
+      return err;
   // pull every peer's shard on its own stream (copy engines in parallel), join, then release the peers' buffers
   if (cudaEventRecord(ps->ev[PEER_MAX], x.s) != cudaSuccess) return set_error(LBW_ERR_CUDA, "sp_kv_gather: event record");
   for (int p = 0; p < world; ++p) {
@@ -217,9 +254,11 @@ int lbw_sp_kv_gather(void* const* bufs, int rank, int world, unsigned int epoch,
       return set_error(LBW_ERR_CUDA, "sp_kv_gather: join of the pull from rank %d failed", p);
   }
   for (int p = 0; p < world; ++p)
-    if (p != rank && (err = ck(x.wr(x.cs, flag_at(bufs[p], 1, rank), epoch, CU_STREAM_WRITE_VALUE_DEFAULT), "signal done")))
+    if (p != rank && (err = ck(x.wr(x.cs, flag_at(x, p, 1, rank), epoch, CU_STREAM_WRITE_VALUE_DEFAULT), "signal done")))
       return err;
-  if ((err = ck(x.wr(x.cs, flag_at(x.mine, 2, 0), epoch, CU_STREAM_WRITE_VALUE_DEFAULT), "signal gathered"))) return err;
+  if ((err = ck(x.wr(x.cs, gathered_at(x), epoch, CU_STREAM_WRITE_VALUE_DEFAULT), "signal gathered"))) return err;
+  if ((err = ck(x.wr(x.cs, flag_at(x, rank, 2, 0), epoch, CU_STREAM_WRITE_VALUE_DEFAULT), "signal gathered (host)")))
+    return err;
   return cuda_check(cudaGetLastError(), "sp_kv_gather");
 }
 

@@ -12,10 +12,11 @@ with copy engines, synchronised by stream memory operations (liblbw's lbw_sp_kv_
 from the attention it overlaps. gather_rows_inplace (one in-place all_gather_into_tensor per tensor) is the
 same exchange through torch.distributed; the CPU (gloo) tests use it.
 
-Failure detection is on the host, between steps: Liveness announces each rank's step in the process group's
-store so that a rank learns of a failed, departed or stalled peer before it launches an exchange that would
-wait on it, and abort() tears the group down without the collective barrier. Collectives themselves end by
-the process group's timeout.
+Failure detection is on the host: Liveness announces each rank's step in the process group's store so that a
+rank learns of a failed, departed or stalled peer before it launches an exchange that would wait on it; an
+exchange already waiting on a peer that stopped is released by PeerKV's watchdog after its timeout (PeerLost);
+abort() tears the group down without the collective barrier. Collectives themselves end by the process group's
+timeout.
 """
 import ctypes
 
@@ -95,16 +96,31 @@ def write_and_gather(shard, dest):
     return dest
 
 
+FLAG_BLOCK = 1024          # bytes of one rank's flag block (LBW_SP_FLAG_BLOCK in include/lbw.h)
+_READY, _DONE, _GATHERED = 0, 64, 128   # word offsets inside a block
+
+
 class PeerKV:
     """The copy-engine K/V exchange of one process group: this rank's IPC buffer plus the peers' buffers
-    mapped into this process. Created collectively (every rank, same shapes); reused by every block."""
+    mapped into this process, and the group's flag blocks in a shared-memory segment of the node that every
+    rank maps and registers with CUDA. Created collectively (every rank, same shapes); reused by every block.
 
-    def __init__(self, local_rows, cols, device, group=None):
+    The streams of an exchange wait on flag words of this rank's own block (stream memory operations, which
+    have no time limit of their own). A watchdog thread gives them one: when an exchange has been pending for
+    timeout_s (LBW_SP_TIMEOUT_S, default 60) without any progress, it writes the awaited epochs into this rank's
+    block, which lets the streams run on (the step's result is then invalid), and records PeerLost naming the
+    ranks whose flags lagged; the next stage() / finish() / check() raises it, and abort() tears down."""
+
+    def __init__(self, local_rows, cols, device, group=None, timeout_s=None):
+        import mmap
+        import os
+        import threading
         from . import _lib
         self._lib = _lib
         lib = _lib.load()
         self.rows, self.cols, self.device, self.group = local_rows, cols, device, group
         self.rank, self.world = rank(), world()
+        self.timeout_s = float(timeout_s if timeout_s is not None else os.environ.get("LBW_SP_TIMEOUT_S", "60"))
         nbytes = 4096 + 2 * local_rows * cols * 2
         own = ctypes.c_void_p()
         handle = (ctypes.c_char * 64)()
@@ -123,23 +139,102 @@ class PeerKV:
                            f"peer_buffer_open(rank {r})", 0)
                 ptrs.append(p.value)
         self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        # flag blocks: a /dev/shm file made by the group's first rank, mapped by all, unlinked once all have it
+        fbytes = max(4096, (self.world * FLAG_BLOCK + 4095) // 4096 * 4096)
+        names = [None] * self.world
+        name = f"/dev/shm/lbw_sp_{os.getpid()}_{id(self):x}" if self.rank == 0 else None
+        if self.rank == 0:
+            fd = os.open(name, os.O_CREAT | os.O_EXCL | os.O_RDWR, 0o600)
+            os.ftruncate(fd, fbytes)
+            os.close(fd)
+        dist.all_gather_object(names, name, group=group)
+        fd = os.open(names[0], os.O_RDWR)
+        self._mm = mmap.mmap(fd, fbytes)
+        os.close(fd)
+        dist.barrier(group=group)
+        if self.rank == 0:
+            os.unlink(names[0])
+        self._words = (ctypes.c_uint32 * (fbytes // 4)).from_buffer(self._mm)
+        self._host = ctypes.addressof(self._words)
+        dev_flags = ctypes.c_void_p()
+        _lib.check(lib.lbw_host_flags_register(ctypes.c_void_p(self._host), fbytes, ctypes.byref(dev_flags)),
+                   "host_flags_register", 0)
+        self._flags = dev_flags
         self.epoch = 0
+        self.failed = None
+        self._stop = threading.Event()
+        self._watchdog = threading.Thread(target=self._watch, name=f"lbw-sp-watchdog-{self.rank}", daemon=True)
+        self._watchdog.start()
 
-    def close(self, collective=True):
-        """Collective: every rank's pulls have completed (device synchronisation + barrier) before the peers'
-        mappings are closed and this rank's buffer is freed. collective=False skips the barrier (teardown after a
-        peer was lost, see abort())."""
+    def _word(self, owner, region, p):
+        return owner * (FLAG_BLOCK // 4) + region + p
+
+    def _release(self, epoch):
+        """Write `epoch` into every ready/done word of this rank's block that is below it (host stores)."""
+        for p in range(self.world):
+            if p == self.rank:
+                continue
+            for region in (_READY, _DONE):
+                i = self._word(self.rank, region, p)
+                if self._words[i] < epoch:
+                    self._words[i] = epoch
+
+    def _watch(self):
+        import time
+        last, t_last = -1, time.monotonic()
+        while not self._stop.wait(0.02):
+            done = self._words[self._word(self.rank, _GATHERED, 0)]
+            pending = self.epoch
+            now = time.monotonic()
+            if done != last or pending <= done:
+                last, t_last = done, now
+                continue
+            if now - t_last > self.timeout_s and self.failed is None:
+                lag = [p for p in range(self.world) if p != self.rank and
+                       (self._words[self._word(self.rank, _READY, p)] < pending or
+                        self._words[self._word(self.rank, _DONE, p)] < pending - 1)]
+                self._release(pending)
+                self.failed = PeerLost(f"K/V exchange {pending}: no progress for {self.timeout_s:.1f} s, waiting on "
+                                       f"rank(s) {lag}; the pending exchanges were released (their results are "
+                                       f"invalid)", lag)
+            elif self.failed is not None:
+                self._release(pending)   # exchanges enqueued after the failure must not wait either
+
+    def check(self):
+        """Raise the PeerLost the watchdog recorded, if any."""
+        if self.failed is not None:
+            raise self.failed
+
+    def close(self, collective=True, timeout_s=30.0):
+        """Release the exchange. collective=True: every rank's pulls have completed (device synchronisation +
+        barrier) before the peers' mappings are closed and this rank's buffer is freed. collective=False (teardown
+        after a lost peer, see abort()): no barrier; this rank's pending waits are released first and the device
+        is waited for at most timeout_s; if it is still busy the buffers are left to the process's exit."""
+        import threading
         if self._ptrs is None:
             return
-        torch.cuda.synchronize(self.device)
+        self._stop.set()
+        self._watchdog.join(timeout=5)
         if collective:
+            torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
+        else:
+            self._release(max(self.epoch, 1))
+            t = threading.Thread(target=torch.cuda.synchronize, args=(self.device,), daemon=True)
+            t.start()
+            t.join(timeout=timeout_s)
+            if t.is_alive():
+                self._ptrs = None
+                return
         lib = self._lib.load()
         with torch.cuda.device(self.device):
             for r, p in enumerate(self._ptrs):
                 self._lib.check(lib.lbw_peer_buffer_close(ctypes.c_void_p(p), int(r == self.rank)),
                                 "peer_buffer_close", 0)
+            self._lib.check(lib.lbw_host_flags_unregister(ctypes.c_void_p(self._host)), "host_flags_unregister", 0)
         self._ptrs = None
+        del self._words
+        self._mm.close()
 
     @property
     def gathered_flag(self):
@@ -151,13 +246,14 @@ class PeerKV:
 
     def _call(self, fn, k2d, v2d, stream):
         self._lib.check(getattr(self._lib.load(), fn)(
-            self._ptrs, self.rank, self.world, ctypes.c_uint(self.epoch), ctypes.c_void_p(k2d.data_ptr()),
-            ctypes.c_void_p(v2d.data_ptr()), k2d.stride(0), self.rows, self.cols,
+            self._ptrs, self._flags, self.rank, self.world, ctypes.c_uint(self.epoch),
+            ctypes.c_void_p(k2d.data_ptr()), ctypes.c_void_p(v2d.data_ptr()), k2d.stride(0), self.rows, self.cols,
             ctypes.c_void_p(stream.cuda_stream)), fn, 0)
 
     def stage(self, k2d, v2d):
         """Start an exchange: this rank's rows of k2d, v2d ([world * local_rows, cols] bf16, row stride
         k2d.stride(0)) are copied to its buffer, in order on the current stream."""
+        self.check()
         if k2d.shape != v2d.shape or k2d.shape[0] != self.rows * self.world or k2d.shape[1] != self.cols \
                 or k2d.stride(0) != v2d.stride(0):
             raise ValueError(f"PeerKV: K/V {tuple(k2d.shape)} do not match {self.world} x {self.rows} rows")
@@ -166,6 +262,7 @@ class PeerKV:
 
     def finish(self, k2d, v2d):
         """Complete the exchange begun by stage() on the current stream: the peers' rows land in k2d, v2d."""
+        self.check()
         self._call("lbw_sp_kv_gather", k2d, v2d, torch.cuda.current_stream(self.device))
 
     def gather(self, k2d, v2d):
@@ -195,6 +292,13 @@ def close_peers():
         _PEERS.pop(key).close()
 
 
+def check_peers():
+    """Raise PeerLost if the watchdog of an exchange of this process released a stalled exchange (its step's
+    results are invalid); call after a step, before using its output."""
+    for pk in _PEERS.values():
+        pk.check()
+
+
 class PeerLost(RuntimeError):
     """A rank of the group stopped taking part: it reported a failure, left, or missed a step's deadline."""
 
@@ -206,8 +310,8 @@ class PeerLost(RuntimeError):
 class Liveness:
     """Between-step liveness of a group's ranks, kept in the process group's key-value store.
 
-    The copy-engine exchange has no time limit of its own (a stream waits on its peers' ready words), so a rank
-    must not launch the next step's exchange while a peer is gone. Each rank calls beat(step) before a step's
+    A copy-engine exchange that a peer never joins is ended by PeerKV's watchdog (after its timeout, with an invalid
+    step), but a rank should not launch the next step's exchange while a peer is known to be gone. Each rank calls beat(step) before a step's
     launches and wait(step) before its first exchange: wait returns once every rank has announced `step` (or a
     later one) and raises PeerLost, naming the ranks, when one has reported a failure (fail), left (leave) or
     not announced the step within `timeout_s`. Nothing here touches a GPU; only the store is used.
@@ -292,8 +396,9 @@ class Liveness:
 
 def abort(group=None):
     """Tear down after a PeerLost or a collective timeout: release the copy-engine exchanges without the
-    collective barrier (the lost ranks would never reach it) and abort the process group, so no rank waits on
-    a peer that is gone. Call between steps, with none of this rank's exchanges in flight."""
+    collective barrier (the lost ranks would never reach it; exchanges still waiting on them are released and
+    the device is waited for with a limit) and abort the process group, so no rank waits on a peer that is
+    gone."""
     for key in list(_PEERS):
         _PEERS.pop(key).close(collective=False)
     if dist.is_initialized():
