@@ -31,8 +31,8 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-ATTN_TRAFFIC_C2_BYTES = 804.108288e6 + 183.372544e6   # ncu, chunk_attn_kernel, c2 (see the profiles folder)
-ATTN_KV_BYTES_C2 = 4.0 * 32760 * 5120
+ATTN_TRAFFIC_C4_BYTES = 2114.584832e6 + 122.817024e6  # ncu dram bytes, one chunk_attn_kernel launch at c4
+ATTN_KV_BYTES_C4 = 4.0 * 75600 * 5120
 
 CONFIGS = {
     # name: (model, frames, grid_h, grid_w, lead chunks, start_frame, layers override)
@@ -342,11 +342,14 @@ def run_sweep(args):
 
     H, C = 40, 5120
     only = args.sweep_only
-    for lq in ((1560, 4680, 10800) if only in ("all", "attention") else ()):
+    # attn_c4: the headline step's self-attention launch alone (10,800 queries, 7 chunks of 10,800 keys), for
+    # profiling one launch
+    att = {"all": (1560, 4680, 10800), "attention": (1560, 4680, 10800), "attn_c4": (10800,)}.get(only, ())
+    for lq in att:
         q = torch.randn(lq, C, generator=g, device=dev, dtype=bf)
         out = torch.empty(lq, C, dtype=bf, device=dev)
-        for lkv in (4096, 16384, 32768, 75600, 131072):
-            n_chunks = max(1, -(-lkv // 18900))
+        for lkv in ((75600,) if only == "attn_c4" else (4096, 16384, 32768, 75600, 131072)):
+            n_chunks = 7 if only == "attn_c4" else max(1, -(-lkv // 18900))
             rows = [lkv // n_chunks + (1 if i < lkv % n_chunks else 0) for i in range(n_chunks)]
             ks = [torch.randn(r, C, generator=g, device=dev, dtype=bf) for r in rows]
             vs = [torch.randn(r, C, generator=g, device=dev, dtype=bf) for r in rows]
@@ -593,7 +596,7 @@ def main():
                     help="skip the oracle check of the first block on a row sample (run after the timed steps)")
     ap.add_argument("--sweep", action="store_true", help="kernel sweep (benchmark configuration c5) instead of the step")
     ap.add_argument("--sweep-only", default="all",
-                    choices=["all", "attention", "mxfp8", "mxfp4", "gemm", "linmx", "tiles"],
+                    choices=["all", "attention", "attn_c4", "mxfp8", "mxfp4", "gemm", "linmx", "tiles"],
                     help="with --sweep: one family of points (gemm = the block's bf16 GEMMs at 10,800 and 1,350 rows)")
     ap.add_argument("--lin-mx", action="store_true",
                     help="every block Linear in MXFP8 (the reference's LINGBOT_LIN_MX option; not the headline config)")
@@ -762,10 +765,11 @@ def main():
                     "peers_opened": [p.world - 1 for p in pkv], "exchanges_per_step": layers}
 
     # DRAM traffic of one attention launch: an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of
-    # the c2 self-attention, 4,680 queries x 32,760 keys, measured 987.5 MB; K/V (re-read from L2 by the query
-    # blocks of a head) dominate it, so it is scaled by this workload's K/V bytes.
+    # the c4 self-attention alone, 10,800 queries x 75,600 keys, measured 2,237.4 MB. K/V (re-read from L2 by
+    # the query blocks of a head) dominate it, so another window is scaled by its K/V bytes; at N>1 a rank's
+    # launch has fewer query blocks per head and no capture of its own, so the field is null there.
     kv_bytes = 4.0 * lkv * C
-    attn_traffic = ATTN_TRAFFIC_C2_BYTES * kv_bytes / ATTN_KV_BYTES_C2 / world if world == 1 else None
+    attn_traffic = ATTN_TRAFFIC_C4_BYTES * kv_bytes / ATTN_KV_BYTES_C4 if world == 1 else None
     pk, src = peaks()
     fb, fm = flops_per_block(chunk, lkv, C, F)
     flops = (fb + fm) * layers
@@ -784,7 +788,7 @@ def main():
         "tc_frac_of_peak": flops / (ms / 1e3) / (peak_tc * 1e12 * world),
         "roofline": {"bound": "tensor", "kernel": "chunk_attn_kernel", "achieved": attn_tf, "peak": peak_tc,
                      "unit": "TFLOP/s", "frac": attn_tf / peak_tc, "traffic": attn_traffic,
-                     "traffic_source": "ncu dram bytes of the c2 launch scaled by K/V bytes" if attn_traffic else None,
+                     "traffic_source": "ncu dram bytes of one c4 launch, scaled by K/V bytes" if attn_traffic else None,
                      "algorithmic_bytes": 2.0 * L_loc * C * 2 + kv_bytes,
                      "peak_source": f"{src} bf16_tflops_sustained", "flops_per_launch": attn_flops,
                      "ms_per_launch": attn_ms},
