@@ -40,6 +40,19 @@ const char* lbw_status_string(int code);
  * the one of lbw_linear_rmsnorm_noalloc); allocates nothing. Returns LBW_ERR_TIMEOUT (device_code =
  * 0x100 | site) if a kernel wait ran out. */
 int lbw_check_device_status(void* stream, int* device_code);
+/* Per-device setup, optional (the per-device handle the port plans as lbw_init(device, nccl_comm); the
+ * sequence-parallel exchange here runs over CUDA IPC, so no communicator is passed). Creates on `device`, now
+ * instead of on first use, what the library keeps per device: the device status word (a 64-byte allocation)
+ * and the peer pull streams and events, so that a caller which later hands the rest of device memory to a
+ * pool of its own has the library's allocations made first. Idempotent; the caller's current context is
+ * current again on return. LBW_ERR_INVALID for a device that does not exist.
+ * Replaces: nothing in the reference (its NKI kernels keep no per-device state); planned boundary item. */
+int lbw_init(int device);
+/* Waits for `device` (cudaDeviceSynchronize: no exchange may still be waiting on a peer), then frees the
+ * status word and destroys the pull streams and events. The next call that needs them creates them again.
+ * Peer buffers and registered flag blocks belong to the caller (lbw_peer_buffer_close,
+ * lbw_host_flags_unregister). */
+int lbw_destroy(int device);
 
 /* ---- chunk attention ----------------------------------------------------------------
  * out[q, h*128:(h+1)*128] = softmax(scale * Q_h K_hᵀ + bias) V_h over the concatenation of
@@ -70,7 +83,10 @@ int lbw_chunk_attention_partial(const void* q, long long ldq, int q_rows, int he
  * gate_value (wrap-safe) before its first load from them. gate_flag is written by a stream memory operation
  * on another stream once copy engines have filled those chunks (lbw_sp_kv_gather writes it), so the gather of
  * the new chunk's K/V runs under the attention of the cached chunks without a separate launch for the new
- * chunk (the reference overlaps the same way, wan/modules/model_fast.py:2033-2110). No key bias. */
+ * chunk (the reference overlaps the same way, wan/modules/model_fast.py:2033-2110). No key bias.
+ * The wait's limit is LBW_GATE_TIMEOUT_S seconds of the GPU's global timer (environment, read per call; default
+ * 120, above the exchange watchdog's default 60 s, whose release of a lost peer's flags opens the gate first);
+ * when it runs out the kernel returns and lbw_check_device_status reports device code 0x123. */
 int lbw_chunk_attention_gated(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
                               const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
                               float softmax_scale, void* out, long long ldo, int n_splits, float* part_o,

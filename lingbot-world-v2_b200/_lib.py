@@ -24,6 +24,8 @@ SIGNATURES = {
     "lbw_last_error": ([ctypes.c_char_p, ctypes.c_size_t], _i),
     "lbw_status_string": ([_i], ctypes.c_char_p),
     "lbw_check_device_status": ([_vp, ctypes.POINTER(_i)], _i),
+    "lbw_init": ([_i], _i),
+    "lbw_destroy": ([_i], _i),
     "lbw_chunk_attention": ([_vp, _ll, _i, _i, _vp, _vp, _vp, _i, _ll, _vp, _f, _vp, _ll, _vp], _i),
     "lbw_gemm_bf16": ([_vp, _ll, _vp, _ll, _vp, _vp, _ll, _i, _i, _i, _vp], _i),
     "lbw_qkv_proj": ([_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _ll, _i, _vp], _i),
@@ -111,7 +113,7 @@ CALLS = [0]
 def check(rc, what, launches=1):
     """Raises on a non-zero status; on success counts `launches` kernels enqueued by the call."""
     if rc == LBW_OK:
-        if what != "device status":
+        if what not in ("device status", "lbw_init", "lbw_destroy"):
             CALLS[0] += launches
         return
     msg = f"{what}: {last_error()} (status {rc})"
@@ -142,3 +144,15 @@ def require_cuda(*tensors):
     for t in tensors:
         if t is not None and not t.is_cuda:
             raise ValueError("lbw ops take CUDA tensors only (there is no CPU path)")
+
+
+def init_device(device=None):
+    """lbw_init: makes the library's per-device state (status word, peer pull streams) on `device` now."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    check(load().lbw_init(dev.index if dev.index is not None else torch.cuda.current_device()), "lbw_init")
+
+
+def destroy_device(device=None):
+    """lbw_destroy: waits for `device`, then releases the library's per-device state there."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    check(load().lbw_destroy(dev.index if dev.index is not None else torch.cuda.current_device()), "lbw_destroy")

@@ -83,15 +83,24 @@ __global__ void attn_merge_kernel(const float* __restrict__ part_o, const float*
 
 // Bounded wait until *flag has reached value (wrap-safe), for K/V rows that a stream memory operation on
 // another stream announces once its copy engines have written them; then order the TMA loads that follow
-// after the flag.
-__device__ __forceinline__ bool gate_wait(const unsigned int* flag, unsigned int value, const Abort& ab, int site) {
-  const long long t0 = clock64();
+// after the flag. The limit is in nanoseconds of the global timer (set by the host: a peer may legitimately be
+// late by more than the mbarrier limit, and the exchange's own watchdog, which opens this gate when a peer is
+// lost, acts after its timeout).
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool gate_wait(const unsigned int* flag, unsigned int value, long long limit_ns,
+                                          const Abort& ab, int site) {
+  const unsigned long long t0 = global_ns();
   while (true) {
     unsigned int v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
     if ((int)(v - value) >= 0) break;
     if (*ab.flag) return false;
-    if (clock64() - t0 > LBW_WAIT_CYCLES) {
+    if ((long long)(global_ns() - t0) > limit_ns) {
       *ab.flag = 1;
       if (ab.status) atomicCAS(ab.status, 0, LBW_DEV_TIMEOUT | site);
       return false;
@@ -107,7 +116,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     chunk_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KVMaps kv, int q_rows,
                       float scale_log2, const float* __restrict__ key_bias, __nv_bfloat16* __restrict__ out,
                       long long ldo, float* __restrict__ part_o, float* __restrict__ part_ml, int slot0,
-                      const unsigned int* gate_flag, unsigned int gate_value, int gate_chunk, int* status) {
+                      const unsigned int* gate_flag, unsigned int gate_value, int gate_chunk, long long gate_limit_ns,
+                      int* status) {
   using namespace attn;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -168,7 +178,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         for (int t0 = 0; t0 < rows && g < g_end; t0 += BN, ++g) {
           if (g < g_begin) continue;
           if (c >= gate_chunk && !gated) {  // chunks from gate_chunk on are still being filled by copy engines
-            if (!gate_wait(gate_flag, gate_value, ab, 0x23)) { ok = false; break; }
+            if (!gate_wait(gate_flag, gate_value, gate_limit_ns, ab, 0x23)) { ok = false; break; }
             gated = true;
           }
           const int s = j & 1;
@@ -476,6 +486,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 
 using namespace lbw;
 
+// Limit of the gate wait: LBW_GATE_TIMEOUT_S seconds (default 120, more than the exchange watchdog's default
+// 60 s, so that a lost peer is reported as PeerLost by the host rather than as a device timeout), read per call.
+static long long gate_timeout_ns() {
+  double s = 120.0;
+  if (const char* e = getenv("LBW_GATE_TIMEOUT_S")) {
+    const double v = atof(e);
+    if (v > 0) s = v;
+  }
+  if (s > 3600.0) s = 3600.0;
+  return (long long)(s * 1e9);
+}
+
 static int launch_attention(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
                             const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
                             const float* key_bias, float softmax_scale, void* out, long long ldo, int n_splits,
@@ -534,13 +556,14 @@ static int launch_attention(const void* q, long long ldq, int q_rows, int heads,
   }
   dim3 grid((q_rows + QT * BM - 1) / (QT * BM), heads, n_splits);
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
+  const long long gate_ns = gate_chunk < n_chunks ? gate_timeout_ns() : 0;
   __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
   if (hb)
     chunk_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, key_bias, o, ldo, part_o,
-                                                              part_ml, slot0, gate_flag, gate_value, gate_chunk, st);
+                                                              part_ml, slot0, gate_flag, gate_value, gate_chunk, gate_ns, st);
   else
     chunk_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, nullptr, o, ldo, part_o,
-                                                               part_ml, slot0, gate_flag, gate_value, gate_chunk, st);
+                                                               part_ml, slot0, gate_flag, gate_value, gate_chunk, gate_ns, st);
   return cuda_check(cudaGetLastError(), "attention launch");
 }
 

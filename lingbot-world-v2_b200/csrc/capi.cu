@@ -119,6 +119,73 @@ const char* lbw_status_string(int code) {
   }
 }
 
+// The per-device state is keyed by device ordinal and is made on first use; lbw_init / lbw_destroy create and
+// release it at a time the caller picks. Both switch to `device` for the call and then make the caller's
+// context current again (cudaSetDevice alone would leave the device's primary context current, which is not
+// the caller's when it runs in a context of its own).
+typedef CUresult (*CtxGetFn)(CUcontext*);
+typedef CUresult (*CtxSetFn)(CUcontext);
+
+static void* driver_entry(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return p;
+}
+
+struct DeviceScope {
+  CUcontext prev = nullptr;
+  CtxSetFn set = nullptr;
+  int err = LBW_OK;
+  explicit DeviceScope(int device, const char* who) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+      err = lbw::set_error(LBW_ERR_CUDA, "%s: cudaGetDeviceCount failed", who);
+      return;
+    }
+    if (device < 0 || device >= n || device >= 64) {
+      err = lbw::set_error(LBW_ERR_INVALID, "%s: device %d out of range (%d devices)", who, device, n);
+      return;
+    }
+    auto get = reinterpret_cast<CtxGetFn>(driver_entry("cuCtxGetCurrent"));
+    set = reinterpret_cast<CtxSetFn>(driver_entry("cuCtxSetCurrent"));
+    if (!get || !set || get(&prev) != CUDA_SUCCESS) {
+      err = lbw::set_error(LBW_ERR_CUDA, "%s: driver context entry points unavailable", who);
+      return;
+    }
+    err = lbw::cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  }
+  ~DeviceScope() {
+    if (set && prev) set(prev);
+  }
+};
+
+int lbw_init(int device) {
+  DeviceScope scope(device, "lbw_init");
+  if (scope.err) return scope.err;
+  int err = LBW_OK;
+  lbw::device_status(&err);
+  if (err) return err;
+  return lbw::pull_streams_init();
+}
+
+int lbw_destroy(int device) {
+  DeviceScope scope(device, "lbw_destroy");
+  if (scope.err) return scope.err;
+  int err = lbw::cuda_check(cudaDeviceSynchronize(), "lbw_destroy: device synchronize");
+  {
+    std::lock_guard<std::mutex> lk(lbw::g_mu);
+    if (lbw::g_status[device]) {
+      const int e = lbw::cuda_check(cudaFree(lbw::g_status[device]), "lbw_destroy: status word free");
+      if (!err) err = e;
+      lbw::g_status[device] = nullptr;
+    }
+  }
+  lbw::pull_streams_release(device);
+  return err;
+}
+
 int lbw_check_device_status(void* stream, int* device_code) {
   // Reads the library's status word and the allocation-free entry point's one; allocates neither.
   int* words[2] = {lbw::device_status_peek(), lbw::noalloc_status_peek()};

@@ -22,6 +22,11 @@ int* device_status_peek();
 // The status word of lbw_linear_rmsnorm_noalloc in the current device and context, or null when that entry
 // point has not run there.
 int* noalloc_status_peek();
+// Creates the current device's peer pull streams and events now (lbw_init); they are otherwise made on the first
+// exchange.
+int pull_streams_init();
+// Destroys device `dev`'s pull streams and events (lbw_destroy); the next exchange creates them again.
+void pull_streams_release(int dev);
 
 // cudaError_t -> LBW_ERR_CUDA with the CUDA error string.
 inline int cuda_check(cudaError_t e, const char* what) {

@@ -63,26 +63,49 @@ struct PullStreams {
   bool ready = false;
 };
 
+static std::mutex g_pull_mu;
+static PullStreams g_pull[64];
+
 static int pull_streams(PullStreams** out) {
-  static std::mutex mu;
-  static PullStreams per_dev[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return set_error(LBW_ERR_CUDA, "cudaGetDevice failed");
-  std::lock_guard<std::mutex> lk(mu);
-  PullStreams& p = per_dev[dev];
+  std::lock_guard<std::mutex> lk(g_pull_mu);
+  PullStreams& p = g_pull[dev];
   if (!p.ready) {
     int lo = 0, hi = 0;
     if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess) return set_error(LBW_ERR_CUDA, "stream priority range");
     for (int i = 0; i < PEER_MAX; ++i)
-      if (cudaStreamCreateWithPriority(&p.s[i], cudaStreamNonBlocking, hi) != cudaSuccess)
+      if (!p.s[i] && cudaStreamCreateWithPriority(&p.s[i], cudaStreamNonBlocking, hi) != cudaSuccess)
         return set_error(LBW_ERR_CUDA, "peer pull stream creation failed");
     for (int i = 0; i <= PEER_MAX; ++i)
-      if (cudaEventCreateWithFlags(&p.ev[i], cudaEventDisableTiming) != cudaSuccess)
+      if (!p.ev[i] && cudaEventCreateWithFlags(&p.ev[i], cudaEventDisableTiming) != cudaSuccess)
         return set_error(LBW_ERR_CUDA, "peer pull event creation failed");
     p.ready = true;
   }
   *out = &p;
   return LBW_OK;
+}
+
+int pull_streams_init() {
+  PullStreams* p = nullptr;
+  return pull_streams(&p);
+}
+
+void pull_streams_release(int dev) {
+  if (dev < 0 || dev >= 64) return;
+  std::lock_guard<std::mutex> lk(g_pull_mu);
+  PullStreams& p = g_pull[dev];
+  for (int i = 0; i < PEER_MAX; ++i)
+    if (p.s[i]) {
+      cudaStreamDestroy(p.s[i]);
+      p.s[i] = nullptr;
+    }
+  for (int i = 0; i <= PEER_MAX; ++i)
+    if (p.ev[i]) {
+      cudaEventDestroy(p.ev[i]);
+      p.ev[i] = nullptr;
+    }
+  p.ready = false;
 }
 
 }  // namespace lbw

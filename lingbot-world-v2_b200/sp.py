@@ -310,11 +310,12 @@ class PeerLost(RuntimeError):
 class Liveness:
     """Between-step liveness of a group's ranks, kept in the process group's key-value store.
 
-    A copy-engine exchange that a peer never joins is ended by PeerKV's watchdog (after its timeout, with an invalid
-    step), but a rank should not launch the next step's exchange while a peer is known to be gone. Each rank calls beat(step) before a step's
-    launches and wait(step) before its first exchange: wait returns once every rank has announced `step` (or a
-    later one) and raises PeerLost, naming the ranks, when one has reported a failure (fail), left (leave) or
-    not announced the step within `timeout_s`. Nothing here touches a GPU; only the store is used.
+    A copy-engine exchange that a peer never joins is ended by PeerKV's watchdog (after its timeout, with an
+    invalid step), but a rank should not launch the next step's exchange while a peer is known to be gone. Each
+    rank calls beat(step) before a step's launches and wait(step) before its first exchange: wait returns once
+    every rank has announced `step` (or a later one) and raises PeerLost, naming the ranks, when one has reported
+    a failure (fail), left (leave) or not announced the step within `timeout_s`. Nothing here touches a GPU; only
+    the store is used.
     """
 
     LEFT = -1

@@ -299,21 +299,26 @@ def test_gated_attention_matches_ungated(cuda_dev):
         K.chunk_attention_gated(q, ks, vs, flag.data_ptr(), 7, 3, out=out)
 
 
-def test_gated_attention_times_out_on_a_gate_that_never_opens(cuda_dev):
-    """A gate word that nothing ever raises: every CTA's bounded gate wait (2^31 SM clocks, about a second) runs
-    out, the kernel drains its copies and MMAs and returns, and the host reads the timeout (0x100 | 0x23, the gate
-    site) from the device status word; the context stays usable for the next launch. One wave of CTAs (2 heads x
-    one 256-row query block), so the wait is paid once."""
+def test_gated_attention_times_out_on_a_gate_that_never_opens(cuda_dev, monkeypatch):
+    """A gate word that nothing ever raises: every CTA's bounded gate wait (LBW_GATE_TIMEOUT_S, set to one second
+    here; 120 s by default) runs out, the kernel drains its copies and MMAs and returns, and the host reads the
+    timeout (0x100 | 0x23, the gate site) from the device status word; the context stays usable for the next
+    launch. One wave of CTAs (2 heads x one 256-row query block), so the wait is paid once."""
+    import time
     import lbw_b200._lib as L
     import lbw_b200.kernels as K
+    monkeypatch.setenv("LBW_GATE_TIMEOUT_S", "1")
     d = cuda_dev
     q, ks, vs = _attn_case(256, [256, 200], 2, 37)
     q, ks, vs = q.to(d), [k.to(d) for k in ks], [v.to(d) for v in vs]
     flag = torch.zeros(4, dtype=torch.int32, device=d)       # stays 0; the kernel waits for 1
     out = torch.zeros(256, 256, dtype=BF, device=d)
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
     K.chunk_attention_gated(q, ks, vs, flag.data_ptr(), 1, 1, out=out)
     with pytest.raises(L.LbwError, match="0x123"):
         L.check_device_status()
+    assert 0.9 < time.monotonic() - t0 < 30
     assert L.check_device_status() == 0                      # read and cleared
     ref = K.chunk_attention(q, ks, vs)                       # the context still runs kernels
     torch.cuda.synchronize()
@@ -349,3 +354,27 @@ def test_small_m_residual_and_qkv_use_narrow_tiles(cuda_dev):
     xd = x.to(d)
     K.linear_residual(h.to(d), wo.to(d), None, xd)
     assert rel_l2(xd - x.to(d), ob.linear(h, wo, None).float()) < 5e-3
+
+
+def test_device_init_destroy(cuda_dev):
+    """lbw_init makes the per-device state up front (idempotent, a missing device is a ValueError, the caller's
+    device stays current); lbw_destroy releases it after the device is idle, and the next call recreates it:
+    the same attention before and after gives the same bits and a clean status."""
+    import lbw_b200._lib as L
+    import lbw_b200.kernels as K
+    d = cuda_dev
+    L.init_device(d)
+    L.init_device(d)
+    with pytest.raises(ValueError):
+        L.init_device(torch.device("cuda", 63))
+    assert torch.cuda.current_device() == d.index
+    q, ks, vs = _attn_case(200, [256, 130], 2, 41)
+    q, ks, vs = q.to(d), [k.to(d) for k in ks], [v.to(d) for v in vs]
+    ref = K.chunk_attention(q, ks, vs)
+    assert L.check_device_status() == 0
+    L.destroy_device(d)
+    assert torch.cuda.current_device() == d.index
+    assert L.check_device_status() == 0          # no status word now: nothing to read, nothing allocated
+    out = K.chunk_attention(q, ks, vs)           # recreates the status word
+    assert torch.equal(out, ref)
+    assert L.check_device_status() == 0

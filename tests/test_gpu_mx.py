@@ -90,13 +90,15 @@ def test_layernorm_mod_mx(cuda_dev, c):
     assert rel_l2(got, omx.dequantize(q, se)) < 2e-3
 
 
-def test_ffn_mx_mm_interface(cuda_dev):
+@pytest.mark.parametrize("fmt", [None, "e5m2", "e2m1"])
+def test_ffn_mx_mm_interface(cuda_dev, fmt):
+    """ffn_mx.prequantize_weight / mm (the reference's operator names); fmt None = LINGBOT_MX_FP8's default E4M3."""
     import lbw_b200.ffn_mx as FM
     m, n, k = 200, 384, 512
     a, w, _ = _ab(m, n, k, 13)
-    data, scales = FM.prequantize_weight(w.to(cuda_dev))
-    out = FM.mm(a.to(cuda_dev), data, scales)
-    assert rel_l2(out, omx.mx_linear(a, w)) < 4e-3
+    data, scales = FM.prequantize_weight(w.to(cuda_dev), fmt=fmt)
+    out = FM.mm(a.to(cuda_dev), data, scales, fmt=fmt)
+    assert rel_l2(out, omx.mx_linear(a, w, fmt or "e4m3")) < 4e-3
 
 
 def test_mx_linear_residual_narrow_tiles(cuda_dev):

@@ -28,3 +28,23 @@ def test_e2m1_pack_round_trip():
     packed = omx.e2m1_pack(omx.e2m1_codes(q))
     assert packed.shape == (4, 32) and packed.dtype == torch.uint8
     assert torch.equal(omx.e2m1_unpack(packed), q)
+
+
+def test_ffn_mx_reads_lingbot_mx_fp8():
+    """ffn_mx takes its element format from LINGBOT_MX_FP8 at import, as the reference's kernels/ffn_mx.py:8,18
+    does, and rejects a value the reference does not accept."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import __graft_entry__; __graft_entry__.load_package(); import lbw_b200.ffn_mx as FM; print(FM.FMT)")
+    for val, want in (("float8_e5m2", "e5m2"), ("float8_e4m3fn", "e4m3"), (None, "e4m3")):
+        env = dict(os.environ)
+        env.pop("LINGBOT_MX_FP8", None)
+        if val:
+            env["LINGBOT_MX_FP8"] = val
+        out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True)
+        assert out.returncode == 0 and out.stdout.strip() == want, out.stderr
+    env = dict(os.environ, LINGBOT_MX_FP8="float16")
+    out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True)
+    assert out.returncode != 0 and "LINGBOT_MX_FP8" in out.stderr
