@@ -670,9 +670,9 @@ def main():
     torch.cuda.synchronize()
     L.check_device_status()
 
-    def step(ev=None, phases=None):
-        stack.forward_chunk(xf, e0, (ks, vs), ctx, caches, c["grid"], c["start_frame"], freqs, films=films,
-                            attn_events=ev, phases=phases)
+    def step(ev=None, phases=None, x=None):
+        stack.forward_chunk(xf if x is None else x, e0, (ks, vs), ctx, caches, c["grid"], c["start_frame"], freqs,
+                            films=films, attn_events=ev, phases=phases)
 
     def barrier():
         if world > 1:
@@ -725,23 +725,45 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         breakdown = {n: round(float(v), 3) for n, v in zip(names, t)}
 
-    # end to end through host buffers: pinned x in, result out, every step
+    # End to end through host buffers, pipelined as a serving loop runs it: step i's input is copied in (pinned
+    # host -> device, on a copy stream) while step i - 1 computes, and its result is copied out while step i + 1
+    # computes (two residual buffers). Every step's copies are inside the timed region, which ends when the last
+    # result has reached the host.
     e2e = None
     if not args.no_e2e:
         xh = x0.cpu().pin_memory()
         yh = torch.empty_like(xh).pin_memory()
-        for _ in range(2):
-            xf.copy_(xh, non_blocking=True)
-            step()
-            yh.copy_(xf, non_blocking=True)
+        bufs = [xf, torch.empty_like(xf)]
+        cs = torch.cuda.Stream(device=dev)
+        main = torch.cuda.current_stream(dev)
+
+        def run_e2e(n):
+            ev_in = [torch.cuda.Event() for _ in range(2)]
+            ev_step = [torch.cuda.Event() for _ in range(2)]
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(main)
+            cs.wait_event(start)
+            with torch.cuda.stream(cs):
+                bufs[0].copy_(xh, non_blocking=True)
+                ev_in[0].record(cs)
+            for i in range(n):
+                b = i & 1
+                main.wait_event(ev_in[b])
+                step(x=bufs[b])
+                ev_step[b].record(main)
+                with torch.cuda.stream(cs):
+                    if i + 1 < n:   # after the previous read-back of that buffer, in copy-stream order
+                        bufs[b ^ 1].copy_(xh, non_blocking=True)
+                        ev_in[b ^ 1].record(cs)
+                    cs.wait_event(ev_step[b])
+                    yh.copy_(bufs[b], non_blocking=True)
+            main.wait_stream(cs)
+            end.record(main)
+            return start, end
+
+        run_e2e(2)
         barrier()
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record()
-        for _ in range(args.steps):
-            xf.copy_(xh, non_blocking=True)
-            step()
-            yh.copy_(xf, non_blocking=True)
-        e2.record()
+        s2, e2 = run_e2e(args.steps)
         barrier()
         ms_e2e = s2.elapsed_time(e2) / args.steps
         t = torch.tensor([ms_e2e], device=dev)
@@ -750,7 +772,8 @@ def main():
         ms_e2e = float(t[0])
         nbytes = xh.numel() * xh.element_size() * world
         e2e = {"value": chunk / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
-               "d2h_bytes_per_step": nbytes, "ms_per_step": ms_e2e}
+               "d2h_bytes_per_step": nbytes, "ms_per_step": ms_e2e,
+               "pipeline": "copy stream: step i's input in during step i - 1, its result out during step i + 1"}
     assert torch.isfinite(yh if e2e else xf).all(), "non-finite block output"
 
     # Parity of the timed stack's first block against the CPU oracle on a row sample (outside the timed region)

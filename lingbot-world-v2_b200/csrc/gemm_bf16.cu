@@ -46,13 +46,13 @@ constexpr int THREADS = 320;
 constexpr int EPI_THREADS = THREADS - 64;
 constexpr int EPI_WARPS = EPI_THREADS / 32;
 // Tile width TBN (256, or 128 when 256-wide tiles would leave the last wave mostly idle; the VAE convolutions also
-// use 192 for 192 / 384 / 768 output channels and 64 for the 3-channel head): ring depth and shared memory per
-// tile width.
+// use 192 for 192 / 384 / 768 output channels, 96 for 96 and 64 for the 3-channel head): ring depth and shared
+// memory per tile width.
 // A 128-wide tile's MMAs (N = 128) take half as long as a 256-wide tile's, so its stages hold two 64-wide K
 // blocks: the MMA thread then waits once per 8 MMAs instead of once per 4 (each wait leaves the tensor pipe
 // idle for ~100 cycles, because the lone issuing thread has nothing else in flight).
 template <int TBN> struct Cfg {
-  static_assert(TBN == 64 || TBN == 128 || TBN == 192 || TBN == 256, "tile widths 64, 128, 192, 256");
+  static_assert(TBN == 64 || TBN == 96 || TBN == 128 || TBN == 192 || TBN == 256, "tile widths 64, 96, 128, 192, 256");
   static constexpr int KSUB = TBN >= 192 ? 1 : 2;           // 64-wide K blocks per stage
   static constexpr int BKS = BK * KSUB;                      // K per stage
   static constexpr int A_SUB = BM * BK * 2, B_SUB = TBN * BK * 2;
@@ -60,8 +60,12 @@ template <int TBN> struct Cfg {
   static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
   static constexpr int STAGES = TBN == 128 ? 3 : 4;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-  // two accumulators of TBN columns; the allocation is a power of two
-  static constexpr uint32_t TMEM_COLS = 2 * TBN <= 128 ? 128 : (2 * TBN <= 256 ? 256 : 512);
+  // two accumulators of TBN columns, the second at column ACC (96 columns are kept 128 apart); the allocation is
+  // a power of two
+  static constexpr uint32_t ACC = TBN == 96 ? 128 : TBN;
+  static constexpr uint32_t TMEM_COLS = 2 * ACC <= 128 ? 128 : (2 * ACC <= 256 ? 256 : 512);
+  static constexpr int NCHUNK = TBN / 32;                 // 32-column epilogue chunks per tile row
+  static constexpr int NCH = (NCHUNK + 1) / 2;            // per warp of a lane-quarter pair (the second may get fewer)
 };
 }  // namespace gemm
 
@@ -172,7 +176,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
         if (!mbar_wait(&tempty_bar[acc], aph ^ 1, ab, 2)) break;
         tc_fence_after();
-        const uint32_t d = tmem + acc * BN;
+        const uint32_t d = tmem + acc * C::ACC;
         bool ok = true;
         for (int kb = 0; kb < nK; ++kb) {
           if (!mbar_wait(&full_bar[s], ph, ab, 3)) { ok = false; break; }
@@ -198,7 +202,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     }
   } else {
     const int quarter = warp & 3;          // warps 2..9 -> TMEM lane quarters 2,3,0,1,2,3,0,1
-    constexpr int NCH = BN / 32 / 2;       // 32-column chunks per warp
+    constexpr int NCH = C::NCH;            // 32-column chunks per warp
     const int c0 = ((warp - 2) >> 2) * NCH;
     int acc = 0;
     uint32_t aph = 0;
@@ -208,7 +212,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       if (!mbar_wait(&tfull_bar[acc], aph, ab, 4)) break;
       tc_fence_after();
       const int row = m_blk * BM + quarter * 32 + lane;
-      const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + acc * C::ACC;
       float stat = 0.f;
       if constexpr (row_norm<Epi>::value) {
         // the row's sum of squares over every column chunk of the tile (both warps of the pair read all of them),
@@ -224,7 +228,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           if (row < M) ss += epi.sumsq(row, col, reinterpret_cast<const float(&)[32]>(r));
         }
 #pragma unroll 1
-        for (int c = c0; c < c0 + NCH; ++c) {
+        for (int c = c0; c < c0 + NCH && c < C::NCHUNK; ++c) {
           const int col = n_blk * BN + c * 32;
           if (col >= N) break;  // warp-uniform
           uint32_t r[32];
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         }
       }
 #pragma unroll 1
-      for (int c = c0; c < c0 + NCH && !row_norm<Epi>::value; ++c) {
+      for (int c = c0; c < c0 + NCH && c < C::NCHUNK && !row_norm<Epi>::value; ++c) {
         const int col = n_blk * BN + c * 32;
         if (col >= N) break;  // warp-uniform
         uint32_t r[32];
@@ -462,6 +466,8 @@ int lbw_vae_conv(const void* x, long long in_rows, int c_in, const void* w, cons
   // tiles exactly as wide as the channels where a width divides them: no zero columns computed
   if (!force && c_out % 192 == 0)
     return launch_gemm_t<EpiConv, 192, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
+  if (!force && c_out == 96 && K % gemm::Cfg<96>::BKS == 0)
+    return launch_gemm_t<EpiConv, 96, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
   if (!force && c_out <= 64 && K % gemm::Cfg<64>::BKS == 0)
     return launch_gemm_t<EpiConv, 64, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
   if (can128 && (force ? force == 128 : prefer_narrow_tiles(mt, c_out)))
@@ -510,6 +516,8 @@ int lbw_vae_conv_rms(const void* x, long long in_rows, int c_in, const void* w, 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // one tile holds the whole row
   if (c_out == 192) return launch_gemm_t<EpiConvRms, 192, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
+  if (c_out == 96 && K % gemm::Cfg<96>::BKS == 0)
+    return launch_gemm_t<EpiConvRms, 96, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
   if (c_out <= 128 && K % gemm::Cfg<128>::BKS == 0)
     return launch_gemm_t<EpiConvRms, 128, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);
   return launch_gemm_t<EpiConvRms, 256, ConvA>(tmA, w, K, (int)M, c_out, K, e, s, st, amap, c_in);

@@ -94,3 +94,44 @@ def test_kv_write_false_leaves_the_slot(cuda_dev):
     assert torch.equal(got, ref)                                          # the same K/V were attended
     ws = blk._ws.new_kv(case.lq)
     assert torch.equal(ws[0].view_as(k_new), k_new) and torch.equal(ws[1].view_as(v_new), v_new)
+
+
+def _opcheck_cases(d):
+    import lbw_b200.kernels as K
+    g = torch.Generator(device=d).manual_seed(61)
+    r = lambda *s, dt=torch.float32, std=1.0: (torch.randn(*s, generator=g, device=d) * std).to(dt)  # noqa: E731
+    m, c, n = 200, 512, 256
+    ops = torch.ops.lbw
+    x = r(m, c)
+    a, w, b = r(m, c, dt=BF), r(n, c, dt=BF, std=0.05), r(n, dt=BF, std=0.05)
+    q, k, v = r(m, 2, 128, dt=BF), r(300, 2, 128, dt=BF), r(300, 2, 128, dt=BF)
+    wd, ws, _ = K.mx_quantize(w)
+    ad, as_, _ = K.mx_quantize(a)
+    cases = {
+        "layernorm_mod": (ops.layernorm_mod, (x, 1e-6, torch.empty(m, c, dtype=BF, device=d), r(c, std=0.1),
+                                              r(c, std=0.1), None, None, False)),
+        "linear_residual": (ops.linear_residual, (a, w, b, r(m, n), r(n, std=0.1), r(m, n, dt=BF, std=0.1),
+                                                  r(m, n, dt=BF, std=0.1))),
+        "linear_rowss": (ops.linear_rowss, (a, w, b, torch.empty(m, n, dtype=BF, device=d),
+                                            torch.zeros(m, device=d))),
+        "chunk_attention": (ops.chunk_attention, (q, [k], [v], None, 128 ** -0.5,
+                                                  torch.empty(m, 256, dtype=BF, device=d))),
+        "rmsnorm_rope": (ops.rmsnorm_rope, (a, (a.float() ** 2).sum(1), r(c, dt=BF), 1e-6,
+                                            torch.empty(m, c, dtype=BF, device=d), None, None, 0, 0, 0, 0, 0)),
+        "mx_quantize": (ops.mx_quantize, (a, "e4m3")),
+        "mx_quantize_into": (ops.mx_quantize_into, (a, torch.empty_like(ad), torch.empty_like(as_), "e4m3")),
+        "mx_linear": (ops.mx_linear, (ad, as_, wd, ws, b, "e4m3")),
+    }
+    return cases
+
+
+@pytest.mark.parametrize("name", ["layernorm_mod", "linear_residual", "linear_rowss", "chunk_attention",
+                                  "rmsnorm_rope", "mx_quantize", "mx_quantize_into", "mx_linear"])
+def test_opcheck(cuda_dev, name):
+    """torch.library.opcheck: each operator's schema (the tensors it declares it writes are the ones it writes, new
+    outputs are new), its fake implementation (same output metadata as the real kernel) and its behaviour under
+    compilation with dynamic shapes."""
+    op, args = _opcheck_cases(cuda_dev)[name]
+    res = torch.library.opcheck(op, args, test_utils=("test_schema", "test_faketensor", "test_aot_dispatch_dynamic"),
+                                raise_exception=False)
+    assert all(v == "SUCCESS" for v in res.values()), res
