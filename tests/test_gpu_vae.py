@@ -46,7 +46,9 @@ def _pack(wt, cip, cop):
                                            ((3, 3, 3), 2, 96, 96, 6, 9),     # the full-resolution level (dim 96)
                                            ((3, 3, 3), 1, 192, 96, 4, 5),    # upsampled 192 -> 96 channels
                                            ((3, 3, 3), 1, 384, 384, 3, 4),   # the lowest levels (dim 96)
-                                           ((3, 3, 3), 2, 32, 32, 3, 4)])    # 32 channels (dim 32)
+                                           ((3, 3, 3), 2, 32, 32, 3, 4),     # 32 channels (dim 32)
+                                           ((3, 3, 3), 1, 96, 192, 4, 5),    # 96 -> 192 channels, 192-wide tiles
+                                           ((1, 1, 1), 2, 32, 256, 9, 9)])   # 32 stored channels in a 64 block
 def test_vae_conv_vs_torch(cuda_dev, k, t, ci, co, h, w):
     import lbw_b200.kernels as K
     g = _g(ci + co + t)
