@@ -185,6 +185,14 @@ int lbw_layernorm_affine_mx(const float* x, int m, int c, float eps, const float
 int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, int c, float eps,
                      const float* rope_cos, const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0,
                      void* out, long long ldo, int out_row_off, void* stream);
+/* lbw_rmsnorm_rope of q and k of the same m tokens in ONE launch: q_out rows q_row_off.. (stride ldq) get q_raw's
+ * normalised and rotated rows (ss_q, gamma_q), k_out rows k_row_off.. (stride ldk) k_raw's (ss_k, gamma_k); the
+ * same RoPE tables and token numbering for both. Replaces: qk_post.qk_norm_rope (kernels/qk_post.py:37-413), which
+ * normalises and rotates q and k together. */
+int lbw_qk_rmsnorm_rope(const void* q_raw, const float* ss_q, const void* gamma_q, void* q_out, long long ldq,
+                        int q_row_off, const void* k_raw, const float* ss_k, const void* gamma_k, void* k_out,
+                        long long ldk, int k_row_off, int m, int c, float eps, const float* rope_cos,
+                        const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0, void* stream);
 
 /* ---- MXFP8 -------------------------------------------------------------------------------- */
 /* Quantise bf16 x [rows, k] (k % 128 == 0) to E4M3 data [rows, k] and E8M0 scales in the tiled

@@ -34,6 +34,8 @@ SIGNATURES = {
     "lbw_linear_gelu": ([_vp, _vp, _vp, _i, _i, _i, _vp, _i, _vp], _i),
     "lbw_layernorm_mod": ([_vp, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _vp, _vp], _i),
     "lbw_rmsnorm_rope": ([_vp, _vp, _vp, _i, _i, _f, _vp, _vp, _i, _i, _i, _i, _vp, _ll, _i, _vp], _i),
+    "lbw_qk_rmsnorm_rope": ([_vp, _vp, _vp, _vp, _ll, _i, _vp, _vp, _vp, _vp, _ll, _i, _i, _i, _f, _vp, _vp, _i, _i,
+                             _i, _i, _vp], _i),
     "lbw_mx_quantize": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
     "lbw_mx_quantize_fmt": ([_vp, _i, _i, _i, _vp, _vp, _vp, _vp], _i),
     "lbw_mx_linear_fmt": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),

@@ -9,9 +9,9 @@ MXFP8 FFN (ffn_mx=True, LINGBOT_FFN_MX) or the bf16 FFN. lin_mx=True (LINGBOT_LI
 :1442-1494) puts the other block Linears on the MXFP8 GEMM too, except those named in lin_mx_skip
 (LINGBOT_LIN_MX_SKIP): their inputs are quantised by the producing LayerNorm kernel or by mx_quantize.
 
-One forward = 14 kernels of liblbw.so on the current stream:
+One forward = 13 kernels of liblbw.so on the current stream:
   layernorm_mod(norm1 + adaLN) -> qkv_proj (v straight into the destination chunk) ->
-  rmsnorm_rope(q) -> rmsnorm_rope(k into the destination chunk) -> [sequence-parallel K/V all-gather]
+  qk_rmsnorm_rope(q, and k into the destination chunk, one launch) -> [sequence-parallel K/V all-gather]
   -> chunk_attention -> linear_residual(o-proj, gate e2, FiLM) -> layernorm(norm3 affine) ->
   linear_rowss(cross q) -> rmsnorm(cross q) -> chunk_attention(cross, optional dedup bias) ->
   linear_residual(cross o) -> layernorm_mod(norm2 + adaLN, MX QDQ) -> linear_gelu(ffn.0 + GELU, MX QDQ)
@@ -417,8 +417,8 @@ class CausalWanAttentionBlock(nn.Module):
             mark("ln1")
             kernels.qkv_proj(ws.h, pk["wqkv"], pk["bqkv"], ws.q_raw, ws.k_raw, ss_q, ss_k, v_dst, v_row_off=row0)
         mark("qkv")
-        kernels.rmsnorm_rope(ws.q_raw, ss_q, pk["gq"], eps, ws.q, rope=rp, grid=grid, tok0=row0)
-        kernels.rmsnorm_rope(ws.k_raw, ss_k, pk["gk"], eps, k_dst, rope=rp, grid=grid, tok0=row0, out_row_off=row0)
+        kernels.qk_rmsnorm_rope(ws.q_raw, ss_q, pk["gq"], ws.q, ws.k_raw, ss_k, pk["gk"], k_dst, eps, rp, grid,
+                                tok0=row0, k_row_off=row0)
         mark("qk_norm_rope")
         if kv_only:
             if p > 1:
@@ -486,4 +486,4 @@ class CausalWanAttentionBlock(nn.Module):
         return xf
 
 
-KERNELS_PER_BLOCK = 14
+KERNELS_PER_BLOCK = 13

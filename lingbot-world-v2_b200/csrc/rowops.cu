@@ -4,6 +4,7 @@
 //                   wan/modules/model.py:145-156; kernels/glue.py:69-166
 //   rmsnorm_rope    bf16(bf16(x * rsqrt(mean(x^2) + eps)) * gamma), then the 3-D RoPE rotation
 //                   wan/modules/model.py:126-143; model_fast.py:878-979; kernels/qk_post.py:37-413
+//                   (qk_rmsnorm_rope: q and k of the same tokens in one launch)
 //   mx_quantize     bf16 -> E4M3 + E8M0 scales (tiled layout), kernels/ffn_mx.py:44-47
 #include "host_common.cuh"
 #include "lbw_common.cuh"
@@ -110,11 +111,12 @@ __global__ void __launch_bounds__(ROW_THREADS) layernorm_mod_kernel(const float*
   }
 }
 
-__global__ void __launch_bounds__(ROW_THREADS) rmsnorm_rope_kernel(
-    const __nv_bfloat16* __restrict__ x, const float* __restrict__ ss, const __nv_bfloat16* __restrict__ gamma, int C,
-    float eps, const float* __restrict__ rcos, const float* __restrict__ rsin, int n_frames, int gh, int gw, int tok0,
-    __nv_bfloat16* __restrict__ out, long long ldo, int out_row_off) {
-  const long long row = blockIdx.x;
+// One row of RMSNorm (+ RoPE): thread t owns the 8-value groups t, t + 128, ... of the row.
+__device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* __restrict__ x, const float* __restrict__ ss,
+                                                 const __nv_bfloat16* __restrict__ gamma, int C, float eps,
+                                                 const float* __restrict__ rcos, const float* __restrict__ rsin,
+                                                 int n_frames, int gh, int gw, int tok0, __nv_bfloat16* __restrict__ out,
+                                                 long long ldo, int out_row_off, long long row) {
   const float r = 1.f / sqrtf(ss[row] / (float)C + eps);
   const int tok = tok0 + (int)row;
   const int f = tok / (gh * gw), hh = (tok / gw) % gh, ww = tok % gw;
@@ -144,6 +146,33 @@ __global__ void __launch_bounds__(ROW_THREADS) rmsnorm_rope_kernel(
     uint4 o = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
     *reinterpret_cast<uint4*>(orow + g * 8) = o;
   }
+}
+
+__global__ void __launch_bounds__(ROW_THREADS) rmsnorm_rope_kernel(
+    const __nv_bfloat16* __restrict__ x, const float* __restrict__ ss, const __nv_bfloat16* __restrict__ gamma, int C,
+    float eps, const float* __restrict__ rcos, const float* __restrict__ rsin, int n_frames, int gh, int gw, int tok0,
+    __nv_bfloat16* __restrict__ out, long long ldo, int out_row_off) {
+  rmsnorm_rope_row(x, ss, gamma, C, eps, rcos, rsin, n_frames, gh, gw, tok0, out, ldo, out_row_off, blockIdx.x);
+}
+
+// q and k of the same tokens in one launch (blocks 0..m-1: q rows, m..2m-1: k rows), as the reference's
+// qk_post.qk_norm_rope treats them together; each has its own gamma, row sums of squares and destination.
+struct QKRows {
+  const __nv_bfloat16* x[2];
+  const float* ss[2];
+  const __nv_bfloat16* gamma[2];
+  __nv_bfloat16* out[2];
+  long long ldo[2];
+  int out_row_off[2];
+};
+
+__global__ void __launch_bounds__(ROW_THREADS) qk_rmsnorm_rope_kernel(const __grid_constant__ QKRows t, int m, int C,
+                                                                      float eps, const float* __restrict__ rcos,
+                                                                      const float* __restrict__ rsin, int n_frames,
+                                                                      int gh, int gw, int tok0) {
+  const int w = blockIdx.x >= (unsigned)m;
+  rmsnorm_rope_row(t.x[w], t.ss[w], t.gamma[w], C, eps, rcos, rsin, n_frames, gh, gw, tok0, t.out[w], t.ldo[w],
+                   t.out_row_off[w], (long long)blockIdx.x - (w ? m : 0));
 }
 
 // One thread per 32-value block; rows up to the next multiple of 128 get zero scales. FMT: MX_E4M3 / MX_E5M2
@@ -259,6 +288,43 @@ int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, i
       rope_sin, n_frames, grid_h > 0 ? grid_h : 1, grid_w > 0 ? grid_w : 1, tok0,
       reinterpret_cast<__nv_bfloat16*>(out), ldo, out_row_off);
   return cuda_check(cudaGetLastError(), "rmsnorm_rope launch");
+}
+
+int lbw_qk_rmsnorm_rope(const void* q_raw, const float* ss_q, const void* gamma_q, void* q_out, long long ldq,
+                        int q_row_off, const void* k_raw, const float* ss_k, const void* gamma_k, void* k_out,
+                        long long ldk, int k_row_off, int m, int c, float eps, const float* rope_cos,
+                        const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0, void* stream) {
+  if (!q_raw || !ss_q || !gamma_q || !q_out || !k_raw || !ss_k || !gamma_k || !k_out)
+    return set_error(LBW_ERR_INVALID, "qk_rmsnorm_rope: null pointer");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return set_error(LBW_ERR_INVALID, "qk_rmsnorm_rope: cos/sin pair");
+  if (m <= 0 || c <= 0 || c % 128 || c > RR_MAXIT * ROW_THREADS * 8 || m > (1 << 30))
+    return set_error(LBW_ERR_SHAPE, "qk_rmsnorm_rope: %d rows of width %d (a multiple of 128, <= %d)", m, c,
+                     RR_MAXIT * ROW_THREADS * 8);
+  if (rope_cos && (grid_h <= 0 || grid_w <= 0 || rope_frames <= 0 || tok0 < 0 ||
+                   (tok0 + m - 1) / (grid_h * grid_w) >= rope_frames))
+    return set_error(LBW_ERR_SHAPE, "qk_rmsnorm_rope: tokens %d..%d outside a %d-frame %dx%d grid", tok0, tok0 + m - 1,
+                     rope_frames, grid_h, grid_w);
+  if (q_row_off < 0 || k_row_off < 0) return set_error(LBW_ERR_INVALID, "qk_rmsnorm_rope: negative row offset");
+  if (!aligned(q_raw, 16) || !aligned(k_raw, 16) || !aligned(gamma_q, 16) || !aligned(gamma_k, 16) ||
+      !aligned(q_out, 16) || !aligned(k_out, 16) || ldq % 8 || ldk % 8 || ldq < c || ldk < c)
+    return set_error(LBW_ERR_ALIGN, "qk_rmsnorm_rope: alignment or row stride");
+  QKRows t{};
+  t.x[0] = reinterpret_cast<const __nv_bfloat16*>(q_raw);
+  t.x[1] = reinterpret_cast<const __nv_bfloat16*>(k_raw);
+  t.ss[0] = ss_q;
+  t.ss[1] = ss_k;
+  t.gamma[0] = reinterpret_cast<const __nv_bfloat16*>(gamma_q);
+  t.gamma[1] = reinterpret_cast<const __nv_bfloat16*>(gamma_k);
+  t.out[0] = reinterpret_cast<__nv_bfloat16*>(q_out);
+  t.out[1] = reinterpret_cast<__nv_bfloat16*>(k_out);
+  t.ldo[0] = ldq;
+  t.ldo[1] = ldk;
+  t.out_row_off[0] = q_row_off;
+  t.out_row_off[1] = k_row_off;
+  const int n_frames = rope_cos ? rope_frames : 0;
+  qk_rmsnorm_rope_kernel<<<2 * m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      t, m, c, eps, rope_cos, rope_sin, n_frames, grid_h > 0 ? grid_h : 1, grid_w > 0 ? grid_w : 1, tok0);
+  return cuda_check(cudaGetLastError(), "qk_rmsnorm_rope launch");
 }
 
 int lbw_mx_quantize_fmt(const void* x, int rows, int k, int fmt, void* data, void* scales, void* dequant,

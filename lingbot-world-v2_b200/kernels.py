@@ -312,6 +312,30 @@ def rmsnorm_rope(x, ss, gamma, eps, out, rope=None, grid=None, tok0=0, out_row_o
     return out
 
 
+def qk_rmsnorm_rope(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out, eps, rope, grid, tok0=0, q_row_off=0,
+                    k_row_off=0, _eager=False):
+    """rmsnorm_rope of q and k of the same tokens in one launch (lbw_qk_rmsnorm_rope, the reference's
+    qk_post.qk_norm_rope): q_out rows q_row_off.., k_out rows k_row_off.. get the normalised, rotated rows."""
+    if _tracing(_eager):
+        _op("qk_rmsnorm_rope")(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out, float(eps), rope[0],
+                               rope[1], int(rope[2]), int(grid[1]), int(grid[2]), int(tok0), int(q_row_off),
+                               int(k_row_off))
+        return q_out, k_out
+    require_cuda(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out)
+    m, c = q_raw.shape
+    qo, ko = _rows(q_out), _rows(k_out)
+    if k_raw.shape != (m, c) or ss_q.numel() < m or ss_k.numel() < m or qo.shape[1] != c or ko.shape[1] != c:
+        raise ValueError("qk_rmsnorm_rope: q and k rows do not match")
+    if q_row_off < 0 or q_row_off + m > qo.shape[0] or k_row_off < 0 or k_row_off + m > ko.shape[0]:
+        raise ValueError("qk_rmsnorm_rope: rows outside an output")
+    cos, sin, nf = rope
+    check(load().lbw_qk_rmsnorm_rope(ptr(q_raw), ptr(ss_q), ptr(gamma_q), ptr(qo), qo.stride(0), q_row_off,
+                                     ptr(k_raw), ptr(ss_k), ptr(gamma_k), ptr(ko), ko.stride(0), k_row_off, m, c,
+                                     ctypes.c_float(eps), ptr(cos), ptr(sin), nf, int(grid[1]), int(grid[2]), tok0,
+                                     stream_of(q_raw.device)), "qk_rmsnorm_rope")
+    return q_out, k_out
+
+
 MX_FORMATS = {"e4m3": 0, "e5m2": 1, "e2m1": 2}   # lbw_mx_format (include/lbw.h)
 
 

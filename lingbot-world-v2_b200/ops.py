@@ -111,6 +111,22 @@ def _(x, ss, gamma, eps, out, cos, sin, n_frames, grid_h, grid_w, tok0, out_row_
     return None
 
 
+@torch.library.custom_op("lbw::qk_rmsnorm_rope", mutates_args=("q_out", "k_out"))
+def qk_rmsnorm_rope(q_raw: torch.Tensor, ss_q: torch.Tensor, gamma_q: torch.Tensor, q_out: torch.Tensor,
+                    k_raw: torch.Tensor, ss_k: torch.Tensor, gamma_k: torch.Tensor, k_out: torch.Tensor, eps: float,
+                    cos: torch.Tensor, sin: torch.Tensor, n_frames: int, grid_h: int, grid_w: int, tok0: int,
+                    q_row_off: int, k_row_off: int) -> None:
+    """q and k RMSNorm + RoPE in one launch (kernels/qk_post.py qk_norm_rope)."""
+    K.qk_rmsnorm_rope(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out, eps, (cos, sin, n_frames),
+                      (n_frames, grid_h, grid_w), tok0=tok0, q_row_off=q_row_off, k_row_off=k_row_off, _eager=True)
+
+
+@qk_rmsnorm_rope.register_fake
+def _(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out, eps, cos, sin, n_frames, grid_h, grid_w, tok0,
+      q_row_off, k_row_off):
+    return None
+
+
 @torch.library.custom_op("lbw::linear_residual", mutates_args=("x",))
 def linear_residual(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], x: torch.Tensor,
                     gate: Optional[torch.Tensor], film_scale: Optional[torch.Tensor],
@@ -208,5 +224,5 @@ def _(a, a_s, w, w_s, bias, fmt):
 
 
 OPS = ("chunk_attention", "chunk_attention_partial", "attention_merge", "layernorm_mod", "layernorm_mod_mx",
-       "layernorm_affine_mx", "qkv_proj", "rmsnorm_rope", "linear_residual", "linear_rowss", "linear_gelu",
+       "layernorm_affine_mx", "qkv_proj", "rmsnorm_rope", "qk_rmsnorm_rope", "linear_residual", "linear_rowss", "linear_gelu",
        "mx_linear_gelu", "mx_linear_residual", "mx_quantize_into", "mx_quantize", "mx_linear")

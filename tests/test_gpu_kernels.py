@@ -243,6 +243,27 @@ def test_rmsnorm_rope(cuda_dev, grid, start, tok0, m, c):
     assert rel_l2(out[8:].view(m, -1, 128), ref) < 2e-3
 
 
+@pytest.mark.parametrize("grid,start,tok0,m,c", [((3, 4, 6), 6, 0, 72, 512), ((3, 30, 52), 18, 1170, 1170, 512)])
+def test_qk_rmsnorm_rope_equals_two_launches(cuda_dev, grid, start, tok0, m, c):
+    """The fused q + k launch gives the bits of the two separate rmsnorm_rope launches (own gammas, row sums and
+    destinations; k written at a row offset into a wider chunk, as into the destination cache slot)."""
+    import lbw_b200.kernels as K
+    import lbw_b200.rope as R
+    g = _g(19)
+    d = cuda_dev
+    q, k = torch.randn(m, c, generator=g).to(BF).to(d), torch.randn(m, c, generator=g).to(BF).to(d)
+    gq, gk = [(1 + 0.02 * torch.randn(c, generator=g)).to(BF).to(d) for _ in range(2)]
+    ssq, ssk = q.float().pow(2).sum(1), k.float().pow(2).sum(1)
+    cos, sin = R.rope_tables(R.rope_freqs(), grid, start, d)
+    rp = (cos, sin, grid[0])
+    q1, k1 = torch.empty(m, c, dtype=BF, device=d), torch.full((m + 16, c), 3.0, dtype=BF, device=d)
+    K.rmsnorm_rope(q, ssq, gq, 1e-6, q1, rope=rp, grid=grid, tok0=tok0)
+    K.rmsnorm_rope(k, ssk, gk, 1e-6, k1, rope=rp, grid=grid, tok0=tok0, out_row_off=16)
+    q2, k2 = torch.empty(m, c, dtype=BF, device=d), torch.full((m + 16, c), 3.0, dtype=BF, device=d)
+    K.qk_rmsnorm_rope(q, ssq, gq, q2, k, ssk, gk, k2, 1e-6, rp, grid, tok0=tok0, k_row_off=16)
+    assert torch.equal(q1, q2) and torch.equal(k1, k2)
+
+
 def test_mx_quantize_bit_exact(cuda_dev):
     import lbw_b200.kernels as K
     g = _g(17)

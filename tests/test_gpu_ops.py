@@ -107,6 +107,8 @@ def _opcheck_cases(d):
     q, k, v = r(m, 2, 128, dt=BF), r(300, 2, 128, dt=BF), r(300, 2, 128, dt=BF)
     wd, ws, _ = K.mx_quantize(w)
     ad, as_, _ = K.mx_quantize(a)
+    import lbw_b200.rope as R
+    rope = R.rope_tables(R.rope_freqs(), (9, 4, 6), 6, d)   # a 216-token grid holds the m = 200 rows
     cases = {
         "layernorm_mod": (ops.layernorm_mod, (x, 1e-6, torch.empty(m, c, dtype=BF, device=d), r(c, std=0.1),
                                               r(c, std=0.1), None, None, False)),
@@ -118,6 +120,11 @@ def _opcheck_cases(d):
                                                   torch.empty(m, 256, dtype=BF, device=d))),
         "rmsnorm_rope": (ops.rmsnorm_rope, (a, (a.float() ** 2).sum(1), r(c, dt=BF), 1e-6,
                                             torch.empty(m, c, dtype=BF, device=d), None, None, 0, 0, 0, 0, 0)),
+        "qk_rmsnorm_rope": (ops.qk_rmsnorm_rope, (a, (a.float() ** 2).sum(1), r(c, dt=BF),
+                                                  torch.empty(m, c, dtype=BF, device=d), a.flip(0).contiguous(),
+                                                  (a.float() ** 2).sum(1).flip(0).contiguous(), r(c, dt=BF),
+                                                  torch.empty(m + 8, c, dtype=BF, device=d), 1e-6, *rope,
+                                                  9, 4, 6, 0, 0, 8)),
         "mx_quantize": (ops.mx_quantize, (a, "e4m3")),
         "mx_quantize_into": (ops.mx_quantize_into, (a, torch.empty_like(ad), torch.empty_like(as_), "e4m3")),
         "mx_linear": (ops.mx_linear, (ad, as_, wd, ws, b, "e4m3")),
@@ -126,7 +133,8 @@ def _opcheck_cases(d):
 
 
 @pytest.mark.parametrize("name", ["layernorm_mod", "linear_residual", "linear_rowss", "chunk_attention",
-                                  "rmsnorm_rope", "mx_quantize", "mx_quantize_into", "mx_linear"])
+                                  "rmsnorm_rope", "qk_rmsnorm_rope", "mx_quantize", "mx_quantize_into",
+                                  "mx_linear"])
 def test_opcheck(cuda_dev, name):
     """torch.library.opcheck: each operator's schema (the tensors it declares it writes are the ones it writes, new
     outputs are new), its fake implementation (same output metadata as the real kernel) and its behaviour under
