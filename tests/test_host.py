@@ -222,3 +222,43 @@ def test_vae_history_buffer_keeps_the_last_two_frames():
         series += frames
         h.advance(t)
         assert torch.equal(h.buf[:2 * P], torch.cat(series[-2:]))
+
+
+def _p(v=256):
+    return ctypes.c_void_p(v)   # a 256-byte-aligned stand-in address: never dereferenced, the checks come first
+
+
+@pytest.mark.parametrize("case", ["qk_null", "qk_width", "qk_grid", "rr_pair", "mx_fmt", "mx_k", "noalloc_rows",
+                                  "noalloc_k", "vae_kernel", "vae_channels"])
+def test_entry_points_validate_before_any_cuda_call(lib, case):
+    """Each entry point rejects bad arguments with its status code and a message, before it touches CUDA (the
+    reference's wrappers raise ValueError / RuntimeError the same way, wan/modules/attention.py:86-90)."""
+    f, c, s = ctypes.c_float, ctypes.c_longlong, None
+    calls = {
+        "qk_null": (lambda: lib.lbw_qk_rmsnorm_rope(None, _p(), _p(), _p(), c(512), 0, _p(), _p(), _p(), _p(), c(512),
+                                                     0, 4, 512, f(1e-6), None, None, 0, 0, 0, 0, s),
+                    L.LBW_ERR_INVALID, "null"),
+        "qk_width": (lambda: lib.lbw_qk_rmsnorm_rope(_p(), _p(), _p(), _p(), c(500), 0, _p(), _p(), _p(), _p(), c(500),
+                                                      0, 4, 500, f(1e-6), None, None, 0, 0, 0, 0, s),
+                     L.LBW_ERR_SHAPE, "multiple of 128"),
+        "qk_grid": (lambda: lib.lbw_qk_rmsnorm_rope(_p(), _p(), _p(), _p(), c(512), 0, _p(), _p(), _p(), _p(), c(512), 0,
+                                                     100, 512, f(1e-6), _p(), _p(), 3, 4, 6, 0, s),
+                    L.LBW_ERR_SHAPE, "outside"),
+        "rr_pair": (lambda: lib.lbw_rmsnorm_rope(_p(), _p(), _p(), 4, 512, f(1e-6), _p(), None, 1, 1, 1, 0, _p(),
+                                                 c(512), 0, s),
+                    L.LBW_ERR_INVALID, "cos/sin"),
+        "mx_fmt": (lambda: lib.lbw_mx_quantize_fmt(_p(), 4, 128, 7, _p(), _p(), None, s), L.LBW_ERR_INVALID, "format"),
+        "mx_k": (lambda: lib.lbw_mx_quantize_fmt(_p(), 4, 100, 0, _p(), _p(), None, s), L.LBW_ERR_SHAPE, "multiple"),
+        "noalloc_rows": (lambda: lib.lbw_linear_rmsnorm_noalloc(_p(), _p(), None, _p(), 65537, 256, 256, f(1e-6),
+                                                                _p(), s),
+                         L.LBW_ERR_SHAPE, "at most 65536"),
+        "noalloc_k": (lambda: lib.lbw_linear_rmsnorm_noalloc(_p(), _p(), None, _p(), 8, 256, 100, f(1e-6), _p(), s),
+                      L.LBW_ERR_SHAPE, "K=100"),
+        "vae_kernel": (lambda: lib.lbw_vae_conv(_p(), 1000, 64, _p(), None, 64, 2, 3, 3, 1, 4, 4, None, _p(), s),
+                       L.LBW_ERR_SHAPE, "kernel"),
+        "vae_channels": (lambda: lib.lbw_vae_conv(_p(), 1000, 60, _p(), None, 64, 3, 3, 3, 1, 4, 4, None, _p(), s),
+                         L.LBW_ERR_SHAPE, "channels"),
+    }
+    fn, code, text = calls[case]
+    assert fn() == code
+    assert text in L.last_error()
