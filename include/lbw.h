@@ -168,6 +168,10 @@ int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scal
  * h = (LN(x)(1 + e4) + e3).to(bf16) (model_fast.py:3101) quantised for the MXFP8 FFN (kernels/ffn_mx.py:159-182). */
 int lbw_layernorm_mod_mx(const float* x, int m, int c, float eps, const float* scale, const float* shift, void* data,
                          void* scales, void* stream);
+/* lbw_layernorm_mod_mx with the codes in element format fmt: LBW_MX_E4M3 or LBW_MX_E5M2 (the reference's
+ * LINGBOT_MX_FP8=float8_e5m2, kernels/ffn_mx.py:8,18). */
+int lbw_layernorm_mod_mx_fmt(const float* x, int m, int c, float eps, const float* scale, const float* shift, int fmt,
+                             void* data, void* scales, void* stream);
 /* As lbw_layernorm_mod_mx with the affine weight/bias of norm3 (fp32 [c]) instead of the modulation: the
  * cross-attention q input LN(x) * w3 + b3 (model_fast.py:2865-2867) quantised for an MXFP8 cross_attn.q
  * (LINGBOT_LIN_MX, model_fast.py:1266-1269). */
@@ -229,10 +233,17 @@ int lbw_mx_linear(const void* a, const void* a_scales, const void* w, const void
  * (the down projection's A operand). Replaces ffn_mx.mm + ffn_epi.bias_gelu_pad (kernels/ffn_epi.py:15-37). */
 int lbw_mx_linear_gelu(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
                        int m, int n, int k, void* out, void* out_scales, void* stream);
+/* lbw_mx_linear_gelu with operands and output codes in element format fmt (LBW_MX_E4M3 or LBW_MX_E5M2). */
+int lbw_mx_linear_gelu_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                           int m, int n, int k, int fmt, void* out, void* out_scales, void* stream);
 /* FFN down + gated residual: x[m, n] (fp32, in place) += bf16(a w^T + bias) * gate[n] (gate may be NULL).
  * Replaces ffn_mx.mm + bias and x + y * e5 (model_fast.py:1584-1611, :3110-3111). */
 int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, const void* w_scales,
                            const void* bias, int m, int n, int k, float* x, const float* gate, void* stream);
+/* lbw_mx_linear_residual with operands in element format fmt (LBW_MX_E4M3 or LBW_MX_E5M2). */
+int lbw_mx_linear_residual_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales,
+                               const void* bias, int m, int n, int k, int fmt, float* x, const float* gate,
+                               void* stream);
 
 /* The block's other Linears in MXFP8 (LINGBOT_LIN_MX=1, model_fast.py:1266-1269; _prequantize_linears_mx
  * :1442-1494 quantises each weight once, _mx_linear_forward :1413-1416 runs y = _mx_matmul(x) + b). */

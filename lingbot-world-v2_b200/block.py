@@ -24,6 +24,7 @@ The fp32 residual is updated in place by the GEMM epilogues.
 import torch
 import torch.nn as nn
 
+from . import ffn_mx as _ffn_mx
 from . import kernels, ops, rope, sp  # noqa: F401  (ops registers the kernels as torch.ops.lbw.*)
 from .attention import cross_dedup_bias
 
@@ -103,7 +104,9 @@ class Workspace:
 class CausalWanAttentionBlock(nn.Module):
     def __init__(self, dim, ffn_dim, num_heads, local_attn_size=-1, sink_size=0, qk_norm=True,
                  cross_attn_norm=False, eps=1e-6, ffn_mx=True, cross_dedup=0, mx_pipe="mxf8", lin_mx=False,
-                 lin_mx_skip=()):
+                 lin_mx_skip=(), mx_fp8=None):
+        """mx_fp8: element format of the MX FFN, "float8_e4m3fn" or "float8_e5m2" (the reference's LINGBOT_MX_FP8,
+        kernels/ffn_mx.py:8,18); None takes LINGBOT_MX_FP8 as lbw_b200.ffn_mx read it at import (default E4M3)."""
         super().__init__()
         if dim % num_heads or dim // num_heads != HEAD_DIM:
             raise ValueError("the B200 kernels are built for head_dim 128")
@@ -128,6 +131,13 @@ class CausalWanAttentionBlock(nn.Module):
             if mx_pipe != "mxf8":
                 raise ValueError("lin_mx runs on the block-scaled tcgen05 GEMM (mx_pipe='mxf8')")
             self.ffn_mx = True   # LINGBOT_LIN_MX implies LINGBOT_FFN_MX (model_fast.py:1270)
+        fp8 = mx_fp8 or _ffn_mx.FP8
+        if fp8 not in _ffn_mx._FMT_OF_DTYPE:
+            raise ValueError(f"mx_fp8={fp8!r}: expected one of {sorted(_ffn_mx._FMT_OF_DTYPE)}")
+        self.mx_fmt = _ffn_mx._FMT_OF_DTYPE[fp8]
+        if self.mx_fmt != "e4m3" and self.ffn_mx and (self.lin_mx or mx_pipe != "mxf8"):
+            raise ValueError("float8_e5m2 runs the MX FFN on the block-scaled GEMM (mx_pipe='mxf8'); lin_mx and the "
+                             "bf16-pipe variant take E4M3 only")
         self.cross_dedup = int(cross_dedup)
         self.norm1 = nn.Identity()
         self.self_attn = _AttnParams(dim, num_heads, qk_norm, eps)
@@ -174,9 +184,9 @@ class CausalWanAttentionBlock(nn.Module):
         pk["mod"] = self.modulation.detach().float().reshape(6, self.dim).contiguous()
         w1, w2 = b(self.ffn[0].weight), b(self.ffn[2].weight)
         if self.ffn_mx and self.mx_pipe == "mxf8":
-            # MXFP8 weights: E4M3 codes + E8M0 scales read by the block-scaled tcgen05 GEMM
-            pk["w1_mx"] = kernels.mx_quantize(w1)[:2]
-            pk["w2_mx"] = kernels.mx_quantize(w2)[:2]
+            # MXFP8 weights: E4M3 (or E5M2) codes + E8M0 scales read by the block-scaled tcgen05 GEMM
+            pk["w1_mx"] = kernels.mx_quantize(w1, fmt=self.mx_fmt)[:2]
+            pk["w2_mx"] = kernels.mx_quantize(w2, fmt=self.mx_fmt)[:2]
         elif self.ffn_mx:
             # bf16-pipe variant: the GEMM reads the exact bf16 dequantisation of the MXFP8 weights
             pk["w1"] = kernels.mx_quantize(w1, dequant=True)[2]
@@ -473,11 +483,12 @@ class CausalWanAttentionBlock(nn.Module):
 
         # FFN
         if self.ffn_mx and self.mx_pipe == "mxf8":
-            kernels.layernorm_mod_mx(xf, eps, em[4], em[3], ws.hq, ws.hs)
+            fmt = self.mx_fmt
+            kernels.layernorm_mod_mx(xf, eps, em[4], em[3], ws.hq, ws.hs, fmt=fmt)
             mark("ln2")
-            kernels.mx_linear_gelu(ws.hq, ws.hs, *pk["w1_mx"], pk["b1"], ws.uq, ws.us)
+            kernels.mx_linear_gelu(ws.hq, ws.hs, *pk["w1_mx"], pk["b1"], ws.uq, ws.us, fmt=fmt)
             mark("ffn_up")
-            kernels.mx_linear_residual(ws.uq, ws.us, *pk["w2_mx"], pk["b2"], xf, gate=em[5])
+            kernels.mx_linear_residual(ws.uq, ws.us, *pk["w2_mx"], pk["b2"], xf, gate=em[5], fmt=fmt)
         else:
             kernels.layernorm_mod(xf, eps, ws.h, scale=em[4], shift=em[3], mx_qdq=self.ffn_mx)
             kernels.linear_gelu(ws.h, pk["w1"], pk["b1"], ws.u, mx_qdq=self.ffn_mx)

@@ -327,11 +327,12 @@ struct EpiAct {
 
 struct EpiGeluMX {
   static constexpr int WARP_SMEM = 0;  // no warp-cooperative chunk()
-  uint8_t* data;     // [M, ld] E4M3 codes of GELU(u + b)
+  uint8_t* data;     // [M, ld] E4M3 (or E5M2, fmt) codes of GELU(u + b)
   uint8_t* scales;   // E8M0 scales in the tiled layout of a [M, sf_cols] matrix (mx_sf_offset)
   long long ld;
   int sf_cols;
   const __nv_bfloat16* bias;
+  int fmt;           // MX_E4M3 (0) or MX_E5M2
 
   LBW_DEV float chunk(int row, int col, const float (&v)[32]) const {
     float g[32];
@@ -345,8 +346,8 @@ struct EpiGeluMX {
         g[e + q] = bf16_round(gelu_tanh_fast(u));
       }
     }
-    uint8_t qb[32];
-    const uint8_t sb = mx_quant32(g, qb);
+    __align__(16) uint8_t qb[32];
+    const uint8_t sb = fmt == MX_E5M2 ? mx_quant32_fmt<MX_E5M2>(g, qb) : mx_quant32(g, qb);
     const uint32_t* w = reinterpret_cast<const uint32_t*>(qb);
     uint4* dp = reinterpret_cast<uint4*>(data + (long long)row * ld + col);
     dp[0] = make_uint4(w[0], w[1], w[2], w[3]);

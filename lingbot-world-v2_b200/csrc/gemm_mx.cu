@@ -345,7 +345,14 @@ int lbw_mx_linear_fmt(const void* a, const void* a_scales, const void* w, const 
 
 int lbw_mx_linear_gelu(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
                        int m, int n, int k, void* out, void* out_scales, void* stream) {
+  return lbw_mx_linear_gelu_fmt(a, a_scales, w, w_scales, bias, m, n, k, MX_E4M3, out, out_scales, stream);
+}
+
+int lbw_mx_linear_gelu_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                           int m, int n, int k, int fmt, void* out, void* out_scales, void* stream) {
   if (!out || !out_scales || !bias) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_gelu: null pointer");
+  if (fmt != MX_E4M3 && fmt != MX_E5M2)
+    return set_error(LBW_ERR_INVALID, "lbw_mx_linear_gelu: element format %d (E4M3 or E5M2)", fmt);
   if (!ok16mx(out) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_gelu: alignment");
   EpiGeluMX e{};
   e.data = reinterpret_cast<uint8_t*>(out);
@@ -353,12 +360,23 @@ int lbw_mx_linear_gelu(const void* a, const void* a_scales, const void* w, const
   e.ld = n;
   e.sf_cols = n;
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
-  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+  e.fmt = fmt;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (fmt == MX_E5M2) return launch_gemm_mx<EpiGeluMX, MX_E5M2>(a, a_scales, w, w_scales, m, n, k, e, s);
+  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, s);
 }
 
 int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, const void* w_scales,
                            const void* bias, int m, int n, int k, float* x, const float* gate, void* stream) {
+  return lbw_mx_linear_residual_fmt(a, a_scales, w, w_scales, bias, m, n, k, MX_E4M3, x, gate, stream);
+}
+
+int lbw_mx_linear_residual_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales,
+                               const void* bias, int m, int n, int k, int fmt, float* x, const float* gate,
+                               void* stream) {
   if (!x) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual: null residual");
+  if (fmt != MX_E4M3 && fmt != MX_E5M2)
+    return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual: element format %d (E4M3 or E5M2)", fmt);
   if (!ok16mx(x) || !ok16mx(gate) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_residual: alignment");
   EpiResidualT<false, 16> e{};
   e.x = x;
@@ -366,7 +384,9 @@ int lbw_mx_linear_residual(const void* a, const void* a_scales, const void* w, c
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   e.gate = gate;
   e.round_acc = 1;
-  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (fmt == MX_E5M2) return launch_gemm_mx<EpiResidualT<false, 16>, MX_E5M2>(a, a_scales, w, w_scales, m, n, k, e, s);
+  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, s);
 }
 
 // ---- the other block Linears in MXFP8 (LINGBOT_LIN_MX, wan/modules/model_fast.py:1266-1269, :1442-1494): each is

@@ -36,7 +36,7 @@ __global__ void __launch_bounds__(ROW_THREADS) layernorm_mod_kernel(const float*
                                                                     const float* __restrict__ bias, int mx,
                                                                     __nv_bfloat16* __restrict__ out,
                                                                     uint8_t* __restrict__ mx_data,
-                                                                    uint8_t* __restrict__ mx_scales) {
+                                                                    uint8_t* __restrict__ mx_scales, int mx_fmt) {
   __shared__ float red[4];
   const long long row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + row * C);
@@ -90,12 +90,14 @@ __global__ void __launch_bounds__(ROW_THREADS) layernorm_mod_kernel(const float*
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-      const int se = mx_shared_exp(amax);
-      if (mx_data) {  // E4M3 codes + E8M0 scale (tiled layout): the next MXFP8 GEMM's A operand
+      const bool e5 = mx_data && mx_fmt == MX_E5M2;
+      const int se = e5 ? mx_shared_exp_fmt(amax, mx_emax(MX_E5M2)) : mx_shared_exp(amax);
+      if (mx_data) {  // E4M3 (or E5M2) codes + E8M0 scale (tiled layout): the next MX GEMM's A operand
         // y * 2^-se is exact: se lies in [-127, 119] for bf16-range values, so 2^-se is a normal float
         const float inv = exp2i(-se);
-        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(y[0] * inv, y[1] * inv), __NV_SATFINITE, __NV_E4M3);
-        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(y[2] * inv, y[3] * inv), __NV_SATFINITE, __NV_E4M3);
+        const __nv_fp8_interpretation_t kind = e5 ? __NV_E5M2 : __NV_E4M3;
+        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(y[0] * inv, y[1] * inv), __NV_SATFINITE, kind);
+        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(y[2] * inv, y[3] * inv), __NV_SATFINITE, kind);
         if (g < G) {
           *reinterpret_cast<uint32_t*>(mx_data + row * C + g * 4) = lo | (hi << 16);
           if ((g & 7) == 0) mx_scales[mx_sf_offset(row, g >> 3, C)] = (uint8_t)(se + 127);
@@ -234,7 +236,7 @@ int lbw_layernorm_affine_mx(const float* x, int m, int c, float eps, const float
     return set_error(LBW_ERR_ALIGN, "layernorm_affine_mx: x, data, weight and bias need 16-byte alignment");
   layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, c, eps, nullptr, nullptr, weight, bias, 1, nullptr, reinterpret_cast<uint8_t*>(data),
-      reinterpret_cast<uint8_t*>(scales));
+      reinterpret_cast<uint8_t*>(scales), MX_E4M3);
   return cuda_check(cudaGetLastError(), "layernorm_affine_mx launch");
 }
 
@@ -250,13 +252,21 @@ int lbw_layernorm_mod(const float* x, int m, int c, float eps, const float* scal
       !aligned(bias, 16))
     return set_error(LBW_ERR_ALIGN, "layernorm_mod: x, out and the modulation vectors need 16-byte alignment");
   layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, c, eps, scale, shift, weight, bias, mx_qdq, reinterpret_cast<__nv_bfloat16*>(out), nullptr, nullptr);
+      x, c, eps, scale, shift, weight, bias, mx_qdq, reinterpret_cast<__nv_bfloat16*>(out), nullptr, nullptr,
+      MX_E4M3);
   return cuda_check(cudaGetLastError(), "layernorm_mod launch");
 }
 
 int lbw_layernorm_mod_mx(const float* x, int m, int c, float eps, const float* scale, const float* shift, void* data,
                          void* scales, void* stream) {
+  return lbw_layernorm_mod_mx_fmt(x, m, c, eps, scale, shift, MX_E4M3, data, scales, stream);
+}
+
+int lbw_layernorm_mod_mx_fmt(const float* x, int m, int c, float eps, const float* scale, const float* shift, int fmt,
+                             void* data, void* scales, void* stream) {
   if (!x || !data || !scales || !scale || !shift) return set_error(LBW_ERR_INVALID, "layernorm_mod_mx: null pointer");
+  if (fmt != MX_E4M3 && fmt != MX_E5M2)
+    return set_error(LBW_ERR_INVALID, "layernorm_mod_mx: element format %d (E4M3 or E5M2)", fmt);
   if (m <= 0 || c <= 0 || c % 128 || c > LN_MAXV * ROW_THREADS * 4)
     return set_error(LBW_ERR_SHAPE, "layernorm_mod_mx: width %d must be a multiple of 128 and <= %d", c,
                      LN_MAXV * ROW_THREADS * 4);
@@ -264,7 +274,7 @@ int lbw_layernorm_mod_mx(const float* x, int m, int c, float eps, const float* s
     return set_error(LBW_ERR_ALIGN, "layernorm_mod_mx: x, data and the modulation vectors need 16-byte alignment");
   layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, c, eps, scale, shift, nullptr, nullptr, 1, nullptr, reinterpret_cast<uint8_t*>(data),
-      reinterpret_cast<uint8_t*>(scales));
+      reinterpret_cast<uint8_t*>(scales), fmt);
   return cuda_check(cudaGetLastError(), "layernorm_mod_mx launch");
 }
 

@@ -382,17 +382,25 @@ def mx_buffers(rows, k, device, fmt="e4m3"):
             torch.zeros(rows_pad * (k // 32), dtype=torch.uint8, device=device))
 
 
-def layernorm_mod_mx(x, eps, scale, shift, data, scales, _eager=False):
+def _fp8_fmt(fmt, who):
+    if fmt not in ("e4m3", "e5m2"):
+        raise ValueError(f"{who}: element format {fmt!r} (e4m3 or e5m2)")
+    return MX_FORMATS[fmt]
+
+
+def layernorm_mod_mx(x, eps, scale, shift, data, scales, fmt="e4m3", _eager=False):
+    """LN(x) * (1 + scale) + shift -> MX codes (E4M3, or E5M2 with fmt="e5m2") + tiled E8M0 scales."""
     if _tracing(_eager):
-        _op("layernorm_mod_mx")(x, float(eps), scale, shift, data, scales)
+        _op("layernorm_mod_mx")(x, float(eps), scale, shift, data, scales, fmt)
         return data, scales
     require_cuda(x, scale, shift, data, scales)
     _c(x, torch.float32)
     m, c = x.shape
     if data.shape != (m, c) or scales.numel() < (m + 127) // 128 * 128 * (c // 32):
         raise ValueError("layernorm_mod_mx: output buffers do not match x")
-    check(load().lbw_layernorm_mod_mx(ptr(x), m, c, ctypes.c_float(eps), ptr(scale), ptr(shift), ptr(data),
-                                      ptr(scales), stream_of(x.device)), "layernorm_mod_mx")
+    check(load().lbw_layernorm_mod_mx_fmt(ptr(x), m, c, ctypes.c_float(eps), ptr(scale), ptr(shift),
+                                          _fp8_fmt(fmt, "layernorm_mod_mx"), ptr(data), ptr(scales),
+                                          stream_of(x.device)), "layernorm_mod_mx")
     return data, scales
 
 
@@ -442,30 +450,37 @@ def mx_linear(a, a_s, w, w_s, bias=None, out=None, fmt="e4m3", _eager=False):
     return out
 
 
-def mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales, _eager=False):
+def mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales, fmt="e4m3", _eager=False):
+    """FFN-up: GELU(bf16(a w^T) + bias) -> MX codes + scales, operands and output in fmt (e4m3 or e5m2)."""
     if _tracing(_eager):
-        _op("mx_linear_gelu")(a, a_s, w, w_s, bias, out, out_scales)
+        _op("mx_linear_gelu")(a, a_s, w, w_s, bias, out, out_scales, fmt)
         return out, out_scales
     m, n, k = _mx_check(a, a_s, w, w_s)
     if out.shape != (m, n) or out.dtype != torch.uint8:
         raise ValueError("mx_linear_gelu: out must be uint8 [m, n]")
-    check(load().lbw_mx_linear_gelu(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(out), ptr(out_scales),
-                                    stream_of(a.device)), "mx_linear_gelu")
+    check(load().lbw_mx_linear_gelu_fmt(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k,
+                                        _fp8_fmt(fmt, "mx_linear_gelu"), ptr(out), ptr(out_scales),
+                                        stream_of(a.device)), "mx_linear_gelu")
     return out, out_scales
 
 
-def mx_linear_residual(a, a_s, w, w_s, bias, x, gate=None, film_scale=None, film_shift=None, _eager=False):
+def mx_linear_residual(a, a_s, w, w_s, bias, x, gate=None, film_scale=None, film_shift=None, fmt="e4m3",
+                       _eager=False):
+    """x += bf16(bf16(a w^T) + bias) * gate (then the FiLM, E4M3 only), operands in fmt (e4m3 or e5m2)."""
     if _tracing(_eager):
-        _op("mx_linear_residual")(a, a_s, w, w_s, bias, x, gate, film_scale, film_shift)
+        _op("mx_linear_residual")(a, a_s, w, w_s, bias, x, gate, film_scale, film_shift, fmt)
         return x
     m, n, k = _mx_check(a, a_s, w, w_s)
     require_cuda(x, gate, film_scale, film_shift)
     if x.shape != (m, n) or x.dtype != torch.float32:
         raise ValueError("mx_linear_residual: x must be fp32 [m, n]")
     if film_scale is None and film_shift is None:
-        check(load().lbw_mx_linear_residual(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(x), ptr(gate),
-                                            stream_of(a.device)), "mx_linear_residual")
+        check(load().lbw_mx_linear_residual_fmt(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k,
+                                                _fp8_fmt(fmt, "mx_linear_residual"), ptr(x), ptr(gate),
+                                                stream_of(a.device)), "mx_linear_residual")
         return x
+    if fmt != "e4m3":
+        raise ValueError("mx_linear_residual: the FiLM epilogue takes E4M3 operands only")
     for t in (film_scale, film_shift):
         if t is None or t.shape != (m, n) or t.dtype != BF16 or not t.is_contiguous():
             raise ValueError("mx_linear_residual: FiLM tensors must both be contiguous bf16 [m, n]")

@@ -66,12 +66,12 @@ def _(x, eps, out, scale, shift, weight, bias, mx_qdq):
 
 @torch.library.custom_op("lbw::layernorm_mod_mx", mutates_args=("data", "scales"))
 def layernorm_mod_mx(x: torch.Tensor, eps: float, scale: torch.Tensor, shift: torch.Tensor, data: torch.Tensor,
-                     scales: torch.Tensor) -> None:
-    K.layernorm_mod_mx(x, eps, scale, shift, data, scales, _eager=True)
+                     scales: torch.Tensor, fmt: str) -> None:
+    K.layernorm_mod_mx(x, eps, scale, shift, data, scales, fmt=fmt, _eager=True)
 
 
 @layernorm_mod_mx.register_fake
-def _(x, eps, scale, shift, data, scales):
+def _(x, eps, scale, shift, data, scales, fmt):
     return None
 
 
@@ -162,25 +162,25 @@ def _(a, w, bias, out, mx_qdq):
 
 @torch.library.custom_op("lbw::mx_linear_gelu", mutates_args=("out", "out_scales"))
 def mx_linear_gelu(a: torch.Tensor, a_s: torch.Tensor, w: torch.Tensor, w_s: torch.Tensor, bias: torch.Tensor,
-                   out: torch.Tensor, out_scales: torch.Tensor) -> None:
-    K.mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales, _eager=True)
+                   out: torch.Tensor, out_scales: torch.Tensor, fmt: str) -> None:
+    K.mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales, fmt=fmt, _eager=True)
 
 
 @mx_linear_gelu.register_fake
-def _(a, a_s, w, w_s, bias, out, out_scales):
+def _(a, a_s, w, w_s, bias, out, out_scales, fmt):
     return None
 
 
 @torch.library.custom_op("lbw::mx_linear_residual", mutates_args=("x",))
 def mx_linear_residual(a: torch.Tensor, a_s: torch.Tensor, w: torch.Tensor, w_s: torch.Tensor,
                        bias: Optional[torch.Tensor], x: torch.Tensor, gate: Optional[torch.Tensor],
-                       film_scale: Optional[torch.Tensor], film_shift: Optional[torch.Tensor]) -> None:
-    K.mx_linear_residual(a, a_s, w, w_s, bias, x, gate=gate, film_scale=film_scale, film_shift=film_shift,
+                       film_scale: Optional[torch.Tensor], film_shift: Optional[torch.Tensor], fmt: str) -> None:
+    K.mx_linear_residual(a, a_s, w, w_s, bias, x, gate=gate, film_scale=film_scale, film_shift=film_shift, fmt=fmt,
                          _eager=True)
 
 
 @mx_linear_residual.register_fake
-def _(a, a_s, w, w_s, bias, x, gate, film_scale, film_shift):
+def _(a, a_s, w, w_s, bias, x, gate, film_scale, film_shift, fmt):
     return None
 
 

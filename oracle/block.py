@@ -84,9 +84,10 @@ def linear(x, w, b):
     return y.to(torch.bfloat16)
 
 
-def mx_matmul(x, w, b):
-    """_mx_matmul (model_fast.py:1403-1410): the MXFP8 matmul's bf16 result, then + bias in bf16."""
-    y = mxo.mx_linear(x.to(torch.bfloat16), w)
+def mx_matmul(x, w, b, fmt="e4m3"):
+    """_mx_matmul (model_fast.py:1403-1410): the MXFP8 matmul's bf16 result, then + bias in bf16; fmt is the element
+    format LINGBOT_MX_FP8 selects (kernels/ffn_mx.py:8,18)."""
+    y = mxo.mx_linear(x.to(torch.bfloat16), w, fmt)
     return y if b is None else (y.float() + b.float()).to(torch.bfloat16)
 
 
@@ -147,10 +148,11 @@ def cross_kv(p, context, eps=1e-6, mx_linears=()):
 
 
 def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, mx=False, eps=1e-6,
-                  dedup_kc=None, return_all=False, mx_linears=()):
+                  dedup_kc=None, return_all=False, mx_linears=(), mx_fmt="e4m3"):
     """One block. x [Lq, C] fp32; e0 [6, C] fp32; k_lead/v_lead lists of [L_i, H, d] bf16;
     ctx_k/ctx_v [T, H, d] bf16; cos/sin [Lq, 64] fp32; film = (scale, shift) [Lq, C] bf16; mx: MXFP8 FFN;
-    mx_linears: names of the other Linears in MXFP8 (LINGBOT_LIN_MX).
+    mx_linears: names of the other Linears in MXFP8 (LINGBOT_LIN_MX); mx_fmt: the FFN's element format ("e4m3",
+    or "e5m2" for LINGBOT_MX_FP8=float8_e5m2, kernels/ffn_mx.py:8,18).
     Returns x_out (and, with return_all, the intermediates)."""
     lin = lambda name, t: block_linear(p, name, t, mx_linears)  # noqa: E731
     Lq, C = x.shape
@@ -187,9 +189,9 @@ def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, m
     # FFN
     h2 = (layer_norm(x2, eps) * (1 + e[4]) + e[3]).to(torch.bfloat16)
     if mx or mx_linears:
-        u = mx_matmul(h2, p["ffn.0.weight"], p["ffn.0.bias"])
+        u = mx_matmul(h2, p["ffn.0.weight"], p["ffn.0.bias"], mx_fmt)
         g = F.gelu(u.float(), approximate="tanh").to(torch.bfloat16)
-        y2 = mx_matmul(g, p["ffn.2.weight"], p["ffn.2.bias"])
+        y2 = mx_matmul(g, p["ffn.2.weight"], p["ffn.2.bias"], mx_fmt)
     else:
         u = linear(h2, p["ffn.0.weight"], p["ffn.0.bias"])
         g = F.gelu(u.float(), approximate="tanh").to(torch.bfloat16)

@@ -35,21 +35,38 @@ def test_mx_linear_vs_emulation(cuda_dev, m, n, k):
     assert rel_l2(out, ob.mx_matmul(a, w, b)) < 4e-3
 
 
-def test_mx_linear_gelu_emits_mx_codes(cuda_dev):
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_mx_linear_gelu_emits_mx_codes(cuda_dev, fmt):
     import lbw_b200.kernels as K
     m, n, k = 333, 768, 512
     a, w, b = _ab(m, n, k, 5)
     d = cuda_dev
-    ad, as_, _ = K.mx_quantize(a.to(d))
-    wd, ws, _ = K.mx_quantize(w.to(d))
+    ad, as_, _ = K.mx_quantize(a.to(d), fmt=fmt)
+    wd, ws, _ = K.mx_quantize(w.to(d), fmt=fmt)
     oq, os_ = K.mx_buffers(m, n, d)
-    K.mx_linear_gelu(ad, as_, wd, ws, b.to(d), oq, os_)
-    u = ((omx.qdq(a) @ omx.qdq(w).t()).to(BF) + b).to(BF)
+    K.mx_linear_gelu(ad, as_, wd, ws, b.to(d), oq, os_, fmt=fmt)
+    u = ((omx.qdq(a, fmt) @ omx.qdq(w, fmt).t()).to(BF) + b).to(BF)
     g = F.gelu(u.float(), approximate="tanh").to(BF)
-    q, s = omx.quantize(g)
-    got = omx.dequantize(oq.cpu().view(torch.float8_e4m3fn), _untile(os_.cpu(), m, n))
-    assert rel_l2(got, omx.dequantize(q, s)) < 1e-2
+    q, s = omx.quantize(g, fmt)
+    dt = torch.float8_e4m3fn if fmt == "e4m3" else torch.float8_e5m2
+    got = omx.dequantize(oq.cpu().view(dt), _untile(os_.cpu(), m, n))
+    assert rel_l2(got, omx.dequantize(q, s)) < (1e-2 if fmt == "e4m3" else 2e-2)
     assert (_untile(os_.cpu(), m, n) == s).float().mean() > 0.99
+
+
+def test_mx_linear_residual_e5m2(cuda_dev):
+    import lbw_b200.kernels as K
+    m, n, k = 260, 512, 768
+    a, w, b = _ab(m, n, k, 9)
+    d = cuda_dev
+    x = torch.randn(m, n)
+    gate = torch.randn(n) * 0.1
+    ad, as_, _ = K.mx_quantize(a.to(d), fmt="e5m2")
+    wd, ws, _ = K.mx_quantize(w.to(d), fmt="e5m2")
+    xd = x.to(d)
+    K.mx_linear_residual(ad, as_, wd, ws, b.to(d), xd, gate=gate.to(d), fmt="e5m2")
+    y = ob.mx_matmul(a, w, b, "e5m2")
+    assert rel_l2(xd.cpu() - x, y.float() * gate) < 5e-3
 
 
 def _untile(tiled, rows, k):
@@ -75,19 +92,21 @@ def test_mx_linear_residual(cuda_dev):
     assert rel_l2(xd - x.to(d), ref - x) < 5e-3
 
 
-@pytest.mark.parametrize("c", [128, 1536, 5120])
-def test_layernorm_mod_mx(cuda_dev, c):
+@pytest.mark.parametrize("c,fmt", [(128, "e4m3"), (1536, "e4m3"), (5120, "e4m3"), (1536, "e5m2")])
+def test_layernorm_mod_mx(cuda_dev, c, fmt):
     import lbw_b200.kernels as K
     g = torch.Generator().manual_seed(11)
     m = 257
     x = torch.randn(m, c, generator=g) * 2 + 0.5
     s, t = torch.randn(c, generator=g) * 0.1, torch.randn(c, generator=g) * 0.1
     dq, ds = K.mx_buffers(m, c, cuda_dev)
-    K.layernorm_mod_mx(x.to(cuda_dev), 1e-6, s.to(cuda_dev), t.to(cuda_dev), dq, ds)
+    K.layernorm_mod_mx(x.to(cuda_dev), 1e-6, s.to(cuda_dev), t.to(cuda_dev), dq, ds, fmt=fmt)
     h = (ob.layer_norm(x, 1e-6) * (1 + s) + t).to(BF)
-    q, se = omx.quantize(h)
-    got = omx.dequantize(dq.cpu().view(torch.float8_e4m3fn), _untile(ds.cpu(), m, c))
-    assert rel_l2(got, omx.dequantize(q, se)) < 2e-3
+    q, se = omx.quantize(h, fmt)
+    dt = torch.float8_e4m3fn if fmt == "e4m3" else torch.float8_e5m2
+    got = omx.dequantize(dq.cpu().view(dt), _untile(ds.cpu(), m, c))
+    assert rel_l2(got, omx.dequantize(q, se)) < (2e-3 if fmt == "e4m3" else 4e-3)
+    assert (_untile(ds.cpu(), m, c) == se).float().mean() > 0.99
 
 
 @pytest.mark.parametrize("fmt", [None, "e5m2", "e2m1"])
