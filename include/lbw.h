@@ -177,6 +177,9 @@ int lbw_layernorm_mod_mx_fmt(const float* x, int m, int c, float eps, const floa
  * (LINGBOT_LIN_MX, model_fast.py:1266-1269). */
 int lbw_layernorm_affine_mx(const float* x, int m, int c, float eps, const float* weight, const float* bias,
                             void* data, void* scales, void* stream);
+/* lbw_layernorm_affine_mx with the codes in element format fmt (LBW_MX_E4M3 or LBW_MX_E5M2). */
+int lbw_layernorm_affine_mx_fmt(const float* x, int m, int c, float eps, const float* weight, const float* bias,
+                                int fmt, void* data, void* scales, void* stream);
 
 /* RMSNorm (+ 3-D RoPE) of projected rows: y = bf16(bf16(x * rsqrt(ss/c + eps)) * gamma), then,
  * if rope_cos != NULL, the interleaved-pair rotation with per-token angles of (frame, h, w).
@@ -253,19 +256,33 @@ int lbw_mx_linear_residual_fmt(const void* a, const void* a_scales, const void* 
 int lbw_mx_qkv_proj(const void* h, const void* h_scales, const void* w_qkv, const void* w_qkv_scales,
                     const void* b_qkv, int m, int c, void* q_raw, void* k_raw, float* ss_q, float* ss_k, void* v_out,
                     long long ldv, int v_row_off, void* stream);
+/* lbw_mx_qkv_proj with operands in element format fmt (LBW_MX_E4M3 or LBW_MX_E5M2, LINGBOT_MX_FP8). */
+int lbw_mx_qkv_proj_fmt(const void* h, const void* h_scales, const void* w_qkv, const void* w_qkv_scales,
+                        const void* b_qkv, int m, int c, int fmt, void* q_raw, void* k_raw, float* ss_q, float* ss_k,
+                        void* v_out, long long ldv, int v_row_off, void* stream);
 /* out[m, n] = bf16(bf16(a w^T) + bias) with row sums of squares ss[m] (cleared here): cross_attn.q and, at the
  * first call, cross_attn.k on the text context (model_fast.py:2755-2798). */
 int lbw_mx_linear_rowss(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
                         int m, int n, int k, void* out, float* ss, void* stream);
+/* lbw_mx_linear_rowss with operands in element format fmt (LBW_MX_E4M3 or LBW_MX_E5M2). */
+int lbw_mx_linear_rowss_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                            int m, int n, int k, int fmt, void* out, float* ss, void* stream);
 /* self_attn.o + gate + camera FiLM: x += bf16(bf16(a w^T) + bias) * gate, then x = (1 + s) * x + t (film_scale,
  * film_shift bf16 [m, n], both or neither). The MXFP8 counterpart of lbw_linear_residual (:3056-3089). */
 int lbw_mx_linear_residual_film(const void* a, const void* a_scales, const void* w, const void* w_scales,
                                 const void* bias, int m, int n, int k, float* x, const float* gate,
                                 const void* film_scale, const void* film_shift, void* stream);
+/* lbw_mx_linear_residual_film with operands in element format fmt (LBW_MX_E4M3 or LBW_MX_E5M2). */
+int lbw_mx_linear_residual_film_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales,
+                                    const void* bias, int m, int n, int k, int fmt, float* x, const float* gate,
+                                    const void* film_scale, const void* film_shift, void* stream);
 /* Camera FiLM MLP layer: out = bf16(act(bf16(bf16(a w^T) + bias))) [+ addend, rounded to bf16], act = SiLU if silu
  * else identity. The MXFP8 counterpart of lbw_linear_act (cam_film, model_fast.py:2882-2891, :606-616). */
 int lbw_mx_linear_act(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
                       const void* addend, int silu, int m, int n, int k, void* out, void* stream);
+/* lbw_mx_linear_act with operands in element format fmt (LBW_MX_E4M3 or LBW_MX_E5M2). */
+int lbw_mx_linear_act_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                          const void* addend, int silu, int m, int n, int k, int fmt, void* out, void* stream);
 
 /* ---- sequence-parallel K/V exchange (one process per GPU, same node, NVLink) ----------------
  * Replaces the all-gather of the new chunk's K/V shards into every rank's destination cache chunk

@@ -48,6 +48,11 @@ SIGNATURES = {
     "lbw_mx_linear_gelu": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "lbw_mx_linear_residual": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "lbw_layernorm_mod_mx_fmt": ([_vp, _i, _i, _f, _vp, _vp, _i, _vp, _vp, _vp], _i),
+    "lbw_layernorm_affine_mx_fmt": ([_vp, _i, _i, _f, _vp, _vp, _i, _vp, _vp, _vp], _i),
+    "lbw_mx_qkv_proj_fmt": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _ll, _i, _vp], _i),
+    "lbw_mx_linear_rowss_fmt": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp], _i),
+    "lbw_mx_linear_residual_film_fmt": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp], _i),
+    "lbw_mx_linear_act_fmt": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp], _i),
     "lbw_mx_linear_gelu_fmt": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp], _i),
     "lbw_mx_linear_residual_fmt": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp], _i),
     "lbw_layernorm_affine_mx": ([_vp, _i, _i, _f, _vp, _vp, _vp, _vp, _vp], _i),

@@ -135,9 +135,9 @@ class CausalWanAttentionBlock(nn.Module):
         if fp8 not in _ffn_mx._FMT_OF_DTYPE:
             raise ValueError(f"mx_fp8={fp8!r}: expected one of {sorted(_ffn_mx._FMT_OF_DTYPE)}")
         self.mx_fmt = _ffn_mx._FMT_OF_DTYPE[fp8]
-        if self.mx_fmt != "e4m3" and self.ffn_mx and (self.lin_mx or mx_pipe != "mxf8"):
-            raise ValueError("float8_e5m2 runs the MX FFN on the block-scaled GEMM (mx_pipe='mxf8'); lin_mx and the "
-                             "bf16-pipe variant take E4M3 only")
+        if self.mx_fmt != "e4m3" and self.ffn_mx and mx_pipe != "mxf8":
+            raise ValueError("float8_e5m2 runs on the block-scaled GEMM (mx_pipe='mxf8'); the bf16-pipe variant "
+                             "takes E4M3 only")
         self.cross_dedup = int(cross_dedup)
         self.norm1 = nn.Identity()
         self.self_attn = _AttnParams(dim, num_heads, qk_norm, eps)
@@ -170,7 +170,7 @@ class CausalWanAttentionBlock(nn.Module):
         wqkv = torch.cat([b(sa.q.weight), b(sa.k.weight), b(sa.v.weight)]).contiguous()
         if "self_attn.q" in mx:
             # quantised per row along K, so the fused [Wq; Wk; Wv] codes equal the three quantised separately
-            pk["wqkv_mx"] = kernels.mx_quantize(wqkv)[:2]
+            pk["wqkv_mx"] = kernels.mx_quantize(wqkv, fmt=self.mx_fmt)[:2]
         else:
             pk["wqkv"] = wqkv
         pk["bqkv"] = torch.cat([b(sa.q.bias), b(sa.k.bias), b(sa.v.bias)]).contiguous()
@@ -216,7 +216,7 @@ class CausalWanAttentionBlock(nn.Module):
         """pk["w" + key] bf16 weight, or pk["w" + key + "_mx"] its MXFP8 codes + scales (quantised once, as
         _mx_quantize_linear does at load, model_fast.py:1384-1400); pk["b" + key] the bf16 bias."""
         if self._mx_name(key) in self.mx_linears:
-            pk["w" + key + "_mx"] = kernels.mx_quantize(b(lin.weight))[:2]
+            pk["w" + key + "_mx"] = kernels.mx_quantize(b(lin.weight), fmt=self.mx_fmt)[:2]
         else:
             pk["w" + key] = b(lin.weight)
         pk["b" + key] = b(lin.bias)
@@ -225,8 +225,8 @@ class CausalWanAttentionBlock(nn.Module):
         """One camera-FiLM MLP layer on the bf16 GEMM or, under lin_mx, on the MXFP8 GEMM."""
         pk = self._packed
         if "w" + key + "_mx" in pk:
-            xq, xs, _ = kernels.mx_quantize(x)
-            return kernels.mx_linear_act(xq, xs, *pk["w" + key + "_mx"], pk["b" + key], **kw)
+            xq, xs, _ = kernels.mx_quantize(x, fmt=self.mx_fmt)
+            return kernels.mx_linear_act(xq, xs, *pk["w" + key + "_mx"], pk["b" + key], fmt=self.mx_fmt, **kw)
         return kernels.linear_act(x, pk["w" + key], pk["b" + key], **kw)
 
     @torch.no_grad()
@@ -266,14 +266,15 @@ class CausalWanAttentionBlock(nn.Module):
         vc = crossattn_cache["v"].view(T, C)
         k_raw = torch.empty(T, C, dtype=BF16, device=ctx.device)
         ss = torch.empty(T, dtype=torch.float32, device=ctx.device)
-        cq = kernels.mx_quantize(ctx)[:2] if ("wck_mx" in pk or "wcv_mx" in pk) else None
+        fmt = self.mx_fmt
+        cq = kernels.mx_quantize(ctx, fmt=fmt)[:2] if ("wck_mx" in pk or "wcv_mx" in pk) else None
         if "wck_mx" in pk:
-            kernels.mx_linear_rowss(*cq, *pk["wck_mx"], pk["bck"], k_raw, ss)
+            kernels.mx_linear_rowss(*cq, *pk["wck_mx"], pk["bck"], k_raw, ss, fmt=fmt)
         else:
             kernels.linear_rowss(ctx, pk["wck"], pk["bck"], k_raw, ss)
         kernels.rmsnorm_rope(k_raw, ss, pk["gck"], self.eps, kc)
         if "wcv_mx" in pk:
-            kernels.mx_linear(*cq, *pk["wcv_mx"], pk["bcv"], out=vc)
+            kernels.mx_linear(*cq, *pk["wcv_mx"], pk["bcv"], out=vc, fmt=fmt)
         else:
             kernels.gemm_bf16(ctx, pk["wcv"], pk["bcv"], out=vc)
         if self.cross_dedup:
@@ -417,11 +418,12 @@ class CausalWanAttentionBlock(nn.Module):
         ss_q, ss_k = ws.ss_q, ws.ss_k
 
         # self-attention
+        fmt = self.mx_fmt
         if "wqkv_mx" in pk:
-            kernels.layernorm_mod_mx(xf, eps, em[1], em[0], ws.hq, ws.hs)
+            kernels.layernorm_mod_mx(xf, eps, em[1], em[0], ws.hq, ws.hs, fmt=fmt)
             mark("ln1")
             kernels.mx_qkv_proj(ws.hq, ws.hs, *pk["wqkv_mx"], pk["bqkv"], ws.q_raw, ws.k_raw, ss_q, ss_k, v_dst,
-                                v_row_off=row0)
+                                v_row_off=row0, fmt=fmt)
         else:
             kernels.layernorm_mod(xf, eps, ws.h, scale=em[1], shift=em[0])
             mark("ln1")
@@ -446,8 +448,8 @@ class CausalWanAttentionBlock(nn.Module):
         if fs is not None:
             fs, ft = fs.to(BF16).contiguous(), ft.to(BF16).contiguous()
         if "wo_mx" in pk:
-            kernels.mx_quantize(ws.attn, data=ws.hq, scales=ws.hs)
-            kernels.mx_linear_residual(ws.hq, ws.hs, *pk["wo_mx"], pk["bo"], xf, gate=em[2], film_scale=fs,
+            kernels.mx_quantize(ws.attn, data=ws.hq, scales=ws.hs, fmt=fmt)
+            kernels.mx_linear_residual(ws.hq, ws.hs, *pk["wo_mx"], pk["bo"], xf, gate=em[2], film_scale=fs, fmt=fmt,
                                        film_shift=ft)
         else:
             kernels.linear_residual(ws.attn, pk["wo"], pk["bo"], xf, gate=em[2], film_scale=fs, film_shift=ft)
@@ -457,9 +459,9 @@ class CausalWanAttentionBlock(nn.Module):
         if not self.cross_attn_norm:
             raise ValueError("cross_attn_norm=False is not supported by the B200 block")
         if "wcq_mx" in pk:
-            kernels.layernorm_affine_mx(xf, eps, pk["n3w"], pk["n3b"], ws.hq, ws.hs)
+            kernels.layernorm_affine_mx(xf, eps, pk["n3w"], pk["n3b"], ws.hq, ws.hs, fmt=fmt)
             mark("ln3")
-            kernels.mx_linear_rowss(ws.hq, ws.hs, *pk["wcq_mx"], pk["bcq"], ws.q_raw, ss_q)
+            kernels.mx_linear_rowss(ws.hq, ws.hs, *pk["wcq_mx"], pk["bcq"], ws.q_raw, ss_q, fmt=fmt)
         else:
             kernels.layernorm_mod(xf, eps, ws.h, weight=pk["n3w"], bias=pk["n3b"])
             mark("ln3")
@@ -475,15 +477,14 @@ class CausalWanAttentionBlock(nn.Module):
         kernels.chunk_attention(ws.q, [kc], [vc], key_bias=bias, out=ws.attn)
         mark("cross_attn")
         if "wco_mx" in pk:
-            kernels.mx_quantize(ws.attn, data=ws.hq, scales=ws.hs)
-            kernels.mx_linear_residual(ws.hq, ws.hs, *pk["wco_mx"], pk["bco"], xf)
+            kernels.mx_quantize(ws.attn, data=ws.hq, scales=ws.hs, fmt=fmt)
+            kernels.mx_linear_residual(ws.hq, ws.hs, *pk["wco_mx"], pk["bco"], xf, fmt=fmt)
         else:
             kernels.linear_residual(ws.attn, pk["wco"], pk["bco"], xf)
         mark("cross_o")
 
         # FFN
         if self.ffn_mx and self.mx_pipe == "mxf8":
-            fmt = self.mx_fmt
             kernels.layernorm_mod_mx(xf, eps, em[4], em[3], ws.hq, ws.hs, fmt=fmt)
             mark("ln2")
             kernels.mx_linear_gelu(ws.hq, ws.hs, *pk["w1_mx"], pk["b1"], ws.uq, ws.us, fmt=fmt)

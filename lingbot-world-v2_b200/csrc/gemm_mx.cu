@@ -307,6 +307,18 @@ static int launch_gemm_mx(const void* a, const void* a_scales, const void* w, co
 
 static bool ok16mx(const void* p) { return p == nullptr || aligned(p, 16); }
 
+// The MXFP8 element formats of the block Linears (LINGBOT_MX_FP8): E4M3 or E5M2.
+static int mx_fp8_fmt_ok(int fmt, const char* who) {
+  if (fmt == MX_E4M3 || fmt == MX_E5M2) return LBW_OK;
+  return set_error(LBW_ERR_INVALID, "%s: element format %d (E4M3 or E5M2)", who, fmt);
+}
+template <class Epi>
+static int launch_gemm_mx_fp8(int fmt, const void* a, const void* a_scales, const void* w, const void* w_scales, int M,
+                              int N, int K, const Epi& epi, cudaStream_t stream) {
+  if (fmt == MX_E5M2) return launch_gemm_mx<Epi, MX_E5M2>(a, a_scales, w, w_scales, M, N, K, epi, stream);
+  return launch_gemm_mx<Epi, MX_E4M3>(a, a_scales, w, w_scales, M, N, K, epi, stream);
+}
+
 }  // namespace lbw
 
 using namespace lbw;
@@ -395,6 +407,14 @@ int lbw_mx_linear_residual_fmt(const void* a, const void* a_scales, const void* 
 int lbw_mx_qkv_proj(const void* h, const void* h_scales, const void* w_qkv, const void* w_qkv_scales,
                     const void* b_qkv, int m, int c, void* q_raw, void* k_raw, float* ss_q, float* ss_k, void* v_out,
                     long long ldv, int v_row_off, void* stream) {
+  return lbw_mx_qkv_proj_fmt(h, h_scales, w_qkv, w_qkv_scales, b_qkv, m, c, MX_E4M3, q_raw, k_raw, ss_q, ss_k, v_out,
+                             ldv, v_row_off, stream);
+}
+
+int lbw_mx_qkv_proj_fmt(const void* h, const void* h_scales, const void* w_qkv, const void* w_qkv_scales,
+                        const void* b_qkv, int m, int c, int fmt, void* q_raw, void* k_raw, float* ss_q, float* ss_k,
+                        void* v_out, long long ldv, int v_row_off, void* stream) {
+  if (int err = mx_fp8_fmt_ok(fmt, "lbw_mx_qkv_proj")) return err;
   if (!q_raw || !k_raw || !v_out || !ss_q || !ss_k) return set_error(LBW_ERR_INVALID, "lbw_mx_qkv_proj: null pointer");
   if (c % mxg::BK) return set_error(LBW_ERR_SHAPE, "lbw_mx_qkv_proj: dim %d must be a multiple of %d", c, mxg::BK);
   if (!ok16mx(q_raw) || !ok16mx(k_raw) || !ok16mx(v_out) || !ok16mx(b_qkv) || ldv % 8 || v_row_off < 0)
@@ -414,11 +434,17 @@ int lbw_mx_qkv_proj(const void* h, const void* h_scales, const void* w_qkv, cons
   e.ss_per_chunk = (c % 256) != 0;   // a region boundary inside a 256-column tile: sums per 32-column chunk
   e.bias = reinterpret_cast<const __nv_bfloat16*>(b_qkv);
   e.round_acc = 1;
-  return launch_gemm_mx(h, h_scales, w_qkv, w_qkv_scales, m, 3 * c, c, e, s);
+  return launch_gemm_mx_fp8(fmt, h, h_scales, w_qkv, w_qkv_scales, m, 3 * c, c, e, s);
 }
 
 int lbw_mx_linear_rowss(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
                         int m, int n, int k, void* out, float* ss, void* stream) {
+  return lbw_mx_linear_rowss_fmt(a, a_scales, w, w_scales, bias, m, n, k, MX_E4M3, out, ss, stream);
+}
+
+int lbw_mx_linear_rowss_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                            int m, int n, int k, int fmt, void* out, float* ss, void* stream) {
+  if (int err = mx_fp8_fmt_ok(fmt, "lbw_mx_linear_rowss")) return err;
   if (!out || !ss) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_rowss: null pointer");
   if (!ok16mx(out) || !ok16mx(bias)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_rowss: alignment");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -432,12 +458,20 @@ int lbw_mx_linear_rowss(const void* a, const void* a_scales, const void* w, cons
   e.ss_per_chunk = (n % 256) != 0;
   e.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   e.round_acc = 1;
-  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, s);
+  return launch_gemm_mx_fp8(fmt, a, a_scales, w, w_scales, m, n, k, e, s);
 }
 
 int lbw_mx_linear_residual_film(const void* a, const void* a_scales, const void* w, const void* w_scales,
                                 const void* bias, int m, int n, int k, float* x, const float* gate,
                                 const void* film_scale, const void* film_shift, void* stream) {
+  return lbw_mx_linear_residual_film_fmt(a, a_scales, w, w_scales, bias, m, n, k, MX_E4M3, x, gate, film_scale,
+                                         film_shift, stream);
+}
+
+int lbw_mx_linear_residual_film_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales,
+                                    const void* bias, int m, int n, int k, int fmt, float* x, const float* gate,
+                                    const void* film_scale, const void* film_shift, void* stream) {
+  if (int err = mx_fp8_fmt_ok(fmt, "lbw_mx_linear_residual_film")) return err;
   if (!x) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual_film: null residual");
   if ((film_scale == nullptr) != (film_shift == nullptr))
     return set_error(LBW_ERR_INVALID, "lbw_mx_linear_residual_film: FiLM needs both scale and shift");
@@ -452,11 +486,17 @@ int lbw_mx_linear_residual_film(const void* a, const void* a_scales, const void*
   e.film_shift = reinterpret_cast<const __nv_bfloat16*>(film_shift);
   e.ldf = n;
   e.round_acc = 1;
-  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+  return launch_gemm_mx_fp8(fmt, a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int lbw_mx_linear_act(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
                       const void* addend, int silu, int m, int n, int k, void* out, void* stream) {
+  return lbw_mx_linear_act_fmt(a, a_scales, w, w_scales, bias, addend, silu, m, n, k, MX_E4M3, out, stream);
+}
+
+int lbw_mx_linear_act_fmt(const void* a, const void* a_scales, const void* w, const void* w_scales, const void* bias,
+                          const void* addend, int silu, int m, int n, int k, int fmt, void* out, void* stream) {
+  if (int err = mx_fp8_fmt_ok(fmt, "lbw_mx_linear_act")) return err;
   if (!out) return set_error(LBW_ERR_INVALID, "lbw_mx_linear_act: null output");
   if (!ok16mx(out) || !ok16mx(bias) || !ok16mx(addend)) return set_error(LBW_ERR_ALIGN, "lbw_mx_linear_act: alignment");
   EpiAct e{};
@@ -466,7 +506,7 @@ int lbw_mx_linear_act(const void* a, const void* a_scales, const void* w, const 
   e.addend = reinterpret_cast<const __nv_bfloat16*>(addend);
   e.silu = silu;
   e.round_acc = 1;
-  return launch_gemm_mx(a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
+  return launch_gemm_mx_fp8(fmt, a, a_scales, w, w_scales, m, n, k, e, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -228,7 +228,14 @@ extern "C" {
 
 int lbw_layernorm_affine_mx(const float* x, int m, int c, float eps, const float* weight, const float* bias,
                             void* data, void* scales, void* stream) {
+  return lbw_layernorm_affine_mx_fmt(x, m, c, eps, weight, bias, MX_E4M3, data, scales, stream);
+}
+
+int lbw_layernorm_affine_mx_fmt(const float* x, int m, int c, float eps, const float* weight, const float* bias,
+                                int fmt, void* data, void* scales, void* stream) {
   if (!x || !data || !scales || !weight || !bias) return set_error(LBW_ERR_INVALID, "layernorm_affine_mx: null pointer");
+  if (fmt != MX_E4M3 && fmt != MX_E5M2)
+    return set_error(LBW_ERR_INVALID, "layernorm_affine_mx: element format %d (E4M3 or E5M2)", fmt);
   if (m <= 0 || c <= 0 || c % 128 || c > LN_MAXV * ROW_THREADS * 4)
     return set_error(LBW_ERR_SHAPE, "layernorm_affine_mx: width %d must be a multiple of 128 and <= %d", c,
                      LN_MAXV * ROW_THREADS * 4);
@@ -236,7 +243,7 @@ int lbw_layernorm_affine_mx(const float* x, int m, int c, float eps, const float
     return set_error(LBW_ERR_ALIGN, "layernorm_affine_mx: x, data, weight and bias need 16-byte alignment");
   layernorm_mod_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, c, eps, nullptr, nullptr, weight, bias, 1, nullptr, reinterpret_cast<uint8_t*>(data),
-      reinterpret_cast<uint8_t*>(scales), MX_E4M3);
+      reinterpret_cast<uint8_t*>(scales), fmt);
   return cuda_check(cudaGetLastError(), "layernorm_affine_mx launch");
 }
 

@@ -404,18 +404,20 @@ def layernorm_mod_mx(x, eps, scale, shift, data, scales, fmt="e4m3", _eager=Fals
     return data, scales
 
 
-def layernorm_affine_mx(x, eps, weight, bias, data, scales, _eager=False):
-    """MXFP8 codes + tiled scales of LN(x) * weight + bias (norm3 before an MXFP8 cross_attn.q)."""
+def layernorm_affine_mx(x, eps, weight, bias, data, scales, fmt="e4m3", _eager=False):
+    """MXFP8 codes (E4M3, or E5M2 with fmt="e5m2") + tiled scales of LN(x) * weight + bias (norm3 before an MXFP8
+    cross_attn.q)."""
     if _tracing(_eager):
-        _op("layernorm_affine_mx")(x, float(eps), weight, bias, data, scales)
+        _op("layernorm_affine_mx")(x, float(eps), weight, bias, data, scales, fmt)
         return data, scales
     require_cuda(x, weight, bias, data, scales)
     _c(x, torch.float32), _c(weight, torch.float32), _c(bias, torch.float32)
     m, c = x.shape
     if data.shape != (m, c) or scales.numel() < (m + 127) // 128 * 128 * (c // 32):
         raise ValueError("layernorm_affine_mx: output buffers do not match x")
-    check(load().lbw_layernorm_affine_mx(ptr(x), m, c, ctypes.c_float(eps), ptr(weight), ptr(bias), ptr(data),
-                                         ptr(scales), stream_of(x.device)), "layernorm_affine_mx")
+    check(load().lbw_layernorm_affine_mx_fmt(ptr(x), m, c, ctypes.c_float(eps), ptr(weight), ptr(bias),
+                                             _fp8_fmt(fmt, "layernorm_affine_mx"), ptr(data), ptr(scales),
+                                             stream_of(x.device)), "layernorm_affine_mx")
     return data, scales
 
 
@@ -466,7 +468,7 @@ def mx_linear_gelu(a, a_s, w, w_s, bias, out, out_scales, fmt="e4m3", _eager=Fal
 
 def mx_linear_residual(a, a_s, w, w_s, bias, x, gate=None, film_scale=None, film_shift=None, fmt="e4m3",
                        _eager=False):
-    """x += bf16(bf16(a w^T) + bias) * gate (then the FiLM, E4M3 only), operands in fmt (e4m3 or e5m2)."""
+    """x += bf16(bf16(a w^T) + bias) * gate (then the optional FiLM), operands in fmt (e4m3 or e5m2)."""
     if _tracing(_eager):
         _op("mx_linear_residual")(a, a_s, w, w_s, bias, x, gate, film_scale, film_shift, fmt)
         return x
@@ -479,19 +481,20 @@ def mx_linear_residual(a, a_s, w, w_s, bias, x, gate=None, film_scale=None, film
                                                 _fp8_fmt(fmt, "mx_linear_residual"), ptr(x), ptr(gate),
                                                 stream_of(a.device)), "mx_linear_residual")
         return x
-    if fmt != "e4m3":
-        raise ValueError("mx_linear_residual: the FiLM epilogue takes E4M3 operands only")
+
     for t in (film_scale, film_shift):
         if t is None or t.shape != (m, n) or t.dtype != BF16 or not t.is_contiguous():
             raise ValueError("mx_linear_residual: FiLM tensors must both be contiguous bf16 [m, n]")
-    check(load().lbw_mx_linear_residual_film(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(x),
-                                             ptr(gate), ptr(film_scale), ptr(film_shift), stream_of(a.device)),
+    check(load().lbw_mx_linear_residual_film_fmt(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k,
+                                                 _fp8_fmt(fmt, "mx_linear_residual"), ptr(x), ptr(gate),
+                                                 ptr(film_scale), ptr(film_shift), stream_of(a.device)),
           "mx_linear_residual_film")
     return x
 
 
-def mx_qkv_proj(hq, hs, w_qkv, w_qkv_s, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, v_row_off=0):
-    """MXFP8 counterpart of qkv_proj: hq/hs the MXFP8 operand of the normed rows, w_qkv/w_qkv_s of [Wq; Wk; Wv]."""
+def mx_qkv_proj(hq, hs, w_qkv, w_qkv_s, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, v_row_off=0, fmt="e4m3"):
+    """MXFP8 counterpart of qkv_proj: hq/hs the MXFP8 operand of the normed rows, w_qkv/w_qkv_s of [Wq; Wk; Wv];
+    fmt: the codes' element format (e4m3 or e5m2)."""
     m, n, c = _mx_check(hq, hs, w_qkv, w_qkv_s)
     require_cuda(b_qkv, q_raw, k_raw, ss_q, ss_k, v_out)
     v2 = _rows(v_out)
@@ -500,31 +503,33 @@ def mx_qkv_proj(hq, hs, w_qkv, w_qkv_s, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, 
     if v2.shape[1] != c or v_row_off < 0 or v_row_off + m > v2.shape[0]:
         raise ValueError(f"mx_qkv_proj: rows {v_row_off}..{v_row_off + m} outside the V destination "
                          f"({v2.shape[0]} rows)")
-    check(load().lbw_mx_qkv_proj(ptr(hq), ptr(hs), ptr(w_qkv), ptr(w_qkv_s), ptr(b_qkv), m, c, ptr(q_raw), ptr(k_raw),
-                                 ptr(ss_q), ptr(ss_k), ptr(v2), v2.stride(0), v_row_off, stream_of(hq.device)),
-          "mx_qkv_proj")
+    check(load().lbw_mx_qkv_proj_fmt(ptr(hq), ptr(hs), ptr(w_qkv), ptr(w_qkv_s), ptr(b_qkv), m, c,
+                                     _fp8_fmt(fmt, "mx_qkv_proj"), ptr(q_raw), ptr(k_raw), ptr(ss_q), ptr(ss_k),
+                                     ptr(v2), v2.stride(0), v_row_off, stream_of(hq.device)), "mx_qkv_proj")
 
 
-def mx_linear_rowss(a, a_s, w, w_s, bias, out, ss):
+def mx_linear_rowss(a, a_s, w, w_s, bias, out, ss, fmt="e4m3"):
     m, n, k = _mx_check(a, a_s, w, w_s)
     require_cuda(bias, out, ss)
     if out.shape != (m, n) or out.dtype != BF16 or not out.is_contiguous() or ss.numel() < m:
         raise ValueError("mx_linear_rowss: shape mismatch")
-    check(load().lbw_mx_linear_rowss(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k, ptr(out), ptr(ss),
-                                     stream_of(a.device)), "mx_linear_rowss")
+    check(load().lbw_mx_linear_rowss_fmt(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), m, n, k,
+                                         _fp8_fmt(fmt, "mx_linear_rowss"), ptr(out), ptr(ss), stream_of(a.device)),
+          "mx_linear_rowss")
     return out
 
 
-def mx_linear_act(a, a_s, w, w_s, bias=None, addend=None, silu=False, out=None):
-    """MXFP8 counterpart of linear_act (camera-FiLM MLP layers)."""
+def mx_linear_act(a, a_s, w, w_s, bias=None, addend=None, silu=False, out=None, fmt="e4m3"):
+    """MXFP8 counterpart of linear_act (camera-FiLM MLP layers); fmt: e4m3 or e5m2."""
     m, n, k = _mx_check(a, a_s, w, w_s)
     require_cuda(bias, addend, out)
     if addend is not None and (addend.shape != (m, n) or addend.dtype != BF16 or not addend.is_contiguous()):
         raise ValueError("mx_linear_act: addend must be contiguous bf16 [m, n]")
     if out is None:
         out = torch.empty(m, n, dtype=BF16, device=a.device)
-    check(load().lbw_mx_linear_act(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), ptr(addend), int(bool(silu)), m, n,
-                                   k, ptr(out), stream_of(a.device)), "mx_linear_act")
+    check(load().lbw_mx_linear_act_fmt(ptr(a), ptr(a_s), ptr(w), ptr(w_s), ptr(bias), ptr(addend), int(bool(silu)), m,
+                                       n, k, _fp8_fmt(fmt, "mx_linear_act"), ptr(out), stream_of(a.device)),
+          "mx_linear_act")
     return out
 
 

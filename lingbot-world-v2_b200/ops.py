@@ -77,12 +77,12 @@ def _(x, eps, scale, shift, data, scales, fmt):
 
 @torch.library.custom_op("lbw::layernorm_affine_mx", mutates_args=("data", "scales"))
 def layernorm_affine_mx(x: torch.Tensor, eps: float, weight: torch.Tensor, bias: torch.Tensor, data: torch.Tensor,
-                        scales: torch.Tensor) -> None:
-    K.layernorm_affine_mx(x, eps, weight, bias, data, scales, _eager=True)
+                        scales: torch.Tensor, fmt: str) -> None:
+    K.layernorm_affine_mx(x, eps, weight, bias, data, scales, fmt=fmt, _eager=True)
 
 
 @layernorm_affine_mx.register_fake
-def _(x, eps, weight, bias, data, scales):
+def _(x, eps, weight, bias, data, scales, fmt):
     return None
 
 

@@ -91,10 +91,11 @@ def mx_matmul(x, w, b, fmt="e4m3"):
     return y if b is None else (y.float() + b.float()).to(torch.bfloat16)
 
 
-def block_linear(p, name, x, mx_linears=()):
-    """Block Linear `name` (e.g. "self_attn.q") on x: nn.Linear, or _mx_matmul when LINGBOT_LIN_MX quantises it."""
+def block_linear(p, name, x, mx_linears=(), fmt="e4m3"):
+    """Block Linear `name` (e.g. "self_attn.q") on x: nn.Linear, or _mx_matmul when LINGBOT_LIN_MX quantises it (in
+    the element format fmt of LINGBOT_MX_FP8)."""
     w, b = p[name + ".weight"], p.get(name + ".bias")
-    return mx_matmul(x, w, b) if name in mx_linears else linear(x, w, b)
+    return mx_matmul(x, w, b, fmt) if name in mx_linears else linear(x, w, b)
 
 
 def rms_norm(x, weight, eps):
@@ -137,13 +138,13 @@ def cross_dedup_bias(k, v, kc):
 # --------------------------------------------------------------------------------------------
 # block
 # --------------------------------------------------------------------------------------------
-def cross_kv(p, context, eps=1e-6, mx_linears=()):
+def cross_kv(p, context, eps=1e-6, mx_linears=(), mx_fmt="e4m3"):
     """Cross-attention K/V of the text context, filled on the first call (model_fast.py:2784-2798)."""
     C = context.shape[-1]
     H = C // HEAD_DIM
     ctx = context.reshape(-1, C).to(torch.bfloat16)
-    k = rms_norm(block_linear(p, "cross_attn.k", ctx, mx_linears), p["cross_attn.norm_k.weight"], eps)
-    v = block_linear(p, "cross_attn.v", ctx, mx_linears)
+    k = rms_norm(block_linear(p, "cross_attn.k", ctx, mx_linears, mx_fmt), p["cross_attn.norm_k.weight"], eps)
+    v = block_linear(p, "cross_attn.v", ctx, mx_linears, mx_fmt)
     return k.view(-1, H, HEAD_DIM), v.view(-1, H, HEAD_DIM)
 
 
@@ -151,10 +152,10 @@ def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, m
                   dedup_kc=None, return_all=False, mx_linears=(), mx_fmt="e4m3"):
     """One block. x [Lq, C] fp32; e0 [6, C] fp32; k_lead/v_lead lists of [L_i, H, d] bf16;
     ctx_k/ctx_v [T, H, d] bf16; cos/sin [Lq, 64] fp32; film = (scale, shift) [Lq, C] bf16; mx: MXFP8 FFN;
-    mx_linears: names of the other Linears in MXFP8 (LINGBOT_LIN_MX); mx_fmt: the FFN's element format ("e4m3",
-    or "e5m2" for LINGBOT_MX_FP8=float8_e5m2, kernels/ffn_mx.py:8,18).
+    mx_linears: names of the other Linears in MXFP8 (LINGBOT_LIN_MX); mx_fmt: the element format of every MX
+    matmul ("e4m3", or "e5m2" for LINGBOT_MX_FP8=float8_e5m2, kernels/ffn_mx.py:8,18).
     Returns x_out (and, with return_all, the intermediates)."""
-    lin = lambda name, t: block_linear(p, name, t, mx_linears)  # noqa: E731
+    lin = lambda name, t: block_linear(p, name, t, mx_linears, mx_fmt)  # noqa: E731
     Lq, C = x.shape
     H = C // HEAD_DIM
     e = (p["modulation"].reshape(6, C).float() + e0.float()).chunk(6, dim=0)
@@ -202,11 +203,11 @@ def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, m
     return x3
 
 
-def cam_film(p, c, mx_linears=()):
+def cam_film(p, c, mx_linears=(), mx_fmt="e4m3"):
     """CausalWanAttentionBlock.cam_film (model_fast.py:2882-2891): bf16 Linears (or _mx_matmul under
     LINGBOT_LIN_MX), SiLU on the bf16 hidden, the camera embedding added to layer 2's bf16 output.
     c [L, C] bf16 -> (scale, shift) bf16."""
-    lin = lambda name, t: block_linear(p, name, t, mx_linears)  # noqa: E731
+    lin = lambda name, t: block_linear(p, name, t, mx_linears, mx_fmt)  # noqa: E731
     h = F.silu(lin("cam_injector_layer1", c).float()).to(torch.bfloat16)
     h2 = (lin("cam_injector_layer2", h) + c).to(torch.bfloat16)
     return lin("cam_scale_layer", h2), lin("cam_shift_layer", h2)

@@ -265,14 +265,13 @@ def test_entry_points_validate_before_any_cuda_call(lib, case):
 
 
 def test_block_mx_format_options(monkeypatch):
-    """mx_fp8 (LINGBOT_MX_FP8): E4M3 by default, E5M2 for the fused MX FFN; refused where the kernels take E4M3 only
-    (LINGBOT_LIN_MX's Linears, the bf16-pipe variant) or for a name the reference does not accept."""
+    """mx_fp8 (LINGBOT_MX_FP8): E4M3 by default, E5M2 for the MX FFN and the LINGBOT_LIN_MX Linears; refused for the
+    bf16-pipe variant (E4M3 only) and for a name the reference does not accept."""
     import lbw_b200.block as B
     mk = lambda **kw: B.CausalWanAttentionBlock(256, 512, 2, cross_attn_norm=True, **kw)  # noqa: E731
     assert mk().mx_fmt == "e4m3"
     assert mk(mx_fp8="float8_e5m2").mx_fmt == "e5m2"
-    with pytest.raises(ValueError, match="E4M3 only"):
-        mk(mx_fp8="float8_e5m2", lin_mx=True)
+    assert mk(mx_fp8="float8_e5m2", lin_mx=True).mx_fmt == "e5m2"
     with pytest.raises(ValueError, match="E4M3 only"):
         mk(mx_fp8="float8_e5m2", mx_pipe="bf16")
     with pytest.raises(ValueError, match="mx_fp8"):
