@@ -223,6 +223,19 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
       tc_fence_before();
       mbar_arrive(&tempty_bar);  // the accumulator may be overwritten from here on
       aph ^= 1;
+      // Every epilogue of this GEMM starts from the accumulator rounded to bf16 (the bf16 matmul result of the
+      // reference's MX matmul): rounding it here, two values per register, halves what the epilogue warps hold
+      // while they work through the column slices (the rounding there is then exact).
+      uint32_t pk[HALF_COLS / 2];
+#pragma unroll
+      for (int i = 0; i < HALF_COLS / 2; ++i) pk[i] = pack_bf16(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+      auto slice = [&](int c, float (&v)[32]) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          v[2 * i] = __uint_as_float(pk[c * 16 + i] << 16);
+          v[2 * i + 1] = __uint_as_float(pk[c * 16 + i] & 0xFFFF0000u);
+        }
+      };
       float stat = 0.f;
       if constexpr (Epi::WARP_SMEM > 0) {
         // warp-cooperative epilogue (all lanes; rows >= M are skipped inside), staged past the operand ring
@@ -230,15 +243,21 @@ __global__ void __launch_bounds__(mxg::THREADS, 1)
 #pragma unroll
         for (int c = 0; c < HALF_COLS / 32; ++c) {
           const int col = col0 + c * 32;
-          if (col < N)
-            epi.chunk_warp(m_blk * BM + quarter * 32, lane, col, *reinterpret_cast<const float(*)[32]>(&r[c * 32]),
-                           M, sm);
+          if (col < N) {
+            float v[32];
+            slice(c, v);
+            epi.chunk_warp(m_blk * BM + quarter * 32, lane, col, v, M, sm);
+          }
         }
       } else if (row < M) {
 #pragma unroll
         for (int c = 0; c < HALF_COLS / 32; ++c) {
           const int col = col0 + c * 32;
-          if (col < N) stat += epi.chunk(row, col, *reinterpret_cast<const float(*)[32]>(&r[c * 32]));
+          if (col < N) {
+            float v[32];
+            slice(c, v);
+            stat += epi.chunk(row, col, v);
+          }
         }
         epi.tile_done(row, col0, stat);
       }
