@@ -96,6 +96,22 @@ int lbw_chunk_attention_gated(const void* q, long long ldq, int q_rows, int head
  * Replaces attention.py:963-990 cte_merge. */
 int lbw_attention_merge(const float* part_o, const float* part_ml, int n_slots, int q_rows, int heads, void* out,
                         long long ldo, void* stream);
+/* lbw_chunk_attention balanced over the SMs of the current device: a window is one head's pair of 128-row query
+ * tiles against every key (ceil(q_rows / 256) * heads of them); whole windows run in full waves, and the windows
+ * past the last full wave are cut into `pieces` key ranges (0: chosen here) that fill the SMs the last wave
+ * leaves idle, followed by a merge of those windows only (two launches on `stream`). part_o / part_ml hold
+ * ws_blocks blocks of [256][128] / [256][2] fp32; lbw_attention_tail_plan gives the n_tail * pieces needed
+ * (0 when nothing is cut: the workspace may then be NULL). gate_flag / gate_value / gate_chunk as in
+ * lbw_chunk_attention_gated (gate_chunk = n_chunks: no gate; a gated launch takes no key bias). Replaces the
+ * same call as lbw_chunk_attention (wan/modules/attention.py:1048-1058) and, gated, the per-chunk partials
+ * merged after the all-gather (attention.py:963-1045). */
+int lbw_attention_tail_plan(int q_rows, int heads, const int* chunk_rows, int n_chunks, int pieces, int* n_tail,
+                            int* pieces_used);
+int lbw_chunk_attention_tail(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                             const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                             const float* key_bias, float softmax_scale, void* out, long long ldo, int pieces,
+                             float* part_o, float* part_ml, long long ws_blocks, const unsigned int* gate_flag,
+                             unsigned int gate_value, int gate_chunk, void* stream);
 
 /* ---- tensor-core linear layers (bf16 x bf16 -> fp32 accumulate) ------------------------
  * All weights are nn.Linear layout [n_out, k_in] bf16; K must be a multiple of 64, N of 32. */

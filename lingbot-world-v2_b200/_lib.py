@@ -42,6 +42,9 @@ SIGNATURES = {
     "lbw_linear_rmsnorm_noalloc": ([_vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp], _i),
     "lbw_chunk_attention_partial": ([_vp, _ll, _i, _i, _vp, _vp, _vp, _i, _ll, _vp, _f, _i, _vp, _vp, _i, _vp], _i),
     "lbw_attention_merge": ([_vp, _vp, _i, _i, _i, _vp, _ll, _vp], _i),
+    "lbw_attention_tail_plan": ([_i, _i, _vp, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)], _i),
+    "lbw_chunk_attention_tail": ([_vp, _ll, _i, _i, _vp, _vp, _vp, _i, _ll, _vp, _f, _vp, _ll, _i, _vp, _vp, _ll,
+                                  _vp, ctypes.c_uint, _i, _vp], _i),
     "lbw_linear_act": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
     "lbw_layernorm_mod_mx": ([_vp, _i, _i, _f, _vp, _vp, _vp, _vp, _vp], _i),
     "lbw_mx_linear": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp], _i),
@@ -115,15 +118,16 @@ def last_error():
     return buf.value.decode(errors="replace")
 
 
-# Entry points called successfully (each enqueues one kernel of liblbw.so, except
-# lbw_linear_rmsnorm_noalloc, which enqueues two); bench.py reads this for its launch count.
+# Entry points called successfully (each enqueues one kernel of liblbw.so, except lbw_linear_rmsnorm_noalloc, which
+# enqueues two, and lbw_chunk_attention_tail, which enqueues two when it cuts windows); bench.py reads this for its
+# launch count.
 CALLS = [0]
 
 
 def check(rc, what, launches=1):
     """Raises on a non-zero status; on success counts `launches` kernels enqueued by the call."""
     if rc == LBW_OK:
-        if what not in ("device status", "lbw_init", "lbw_destroy"):
+        if what not in ("device status", "lbw_init", "lbw_destroy", "attention_tail_plan"):
             CALLS[0] += launches
         return
     msg = f"{what}: {last_error()} (status {rc})"

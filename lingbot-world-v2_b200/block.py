@@ -91,11 +91,18 @@ class Workspace:
                             torch.empty(chunk_rows, self.dim, dtype=BF16, device=self.h.device))
         return self._new_kv
 
-    def attn_parts(self, slots, heads):
-        """Split-KV workspace (fp32 partial outputs + (m, l)), grown on demand."""
-        if getattr(self, "_parts", None) is None or self._parts[0].shape[0] < slots:
-            self._parts = kernels.attention_workspace(slots, self.rows, heads, self.h.device)
-        return self._parts
+    def attn_tail(self, heads, chunk_rows):
+        """(workspace, pieces) of the self-attention's tail schedule over these key chunks (workspace None when no
+        window is cut), planned once per key-chunk shape."""
+        if getattr(self, "_tail", None) is None:
+            self._tail = {}
+        key = (heads, tuple(chunk_rows))
+        hit = self._tail.get(key)
+        if hit is None:
+            dev = self.h.device
+            _, pieces = kernels.attention_tail_plan(self.rows, heads, chunk_rows, dev)
+            hit = self._tail[key] = (kernels.attention_tail_workspace(self.rows, heads, chunk_rows, dev, pieces), pieces)
+        return hit
 
     def fits(self, rows, dim, ffn_dim, device):
         return (self.rows, self.dim, self.ffn_dim) == (rows, dim, ffn_dim) and self.h.device == device
@@ -293,23 +300,18 @@ class CausalWanAttentionBlock(nn.Module):
         gather runs on copy engines from a side stream while ONE attention launch covers the whole window:
         its CTAs reach the destination chunk last and wait in-kernel for the copy engines' completion flag
         (the reference attends cached chunks while the gather is in flight the same way,
-        model_fast.py:2033-2110). When the rank has few query rows the KV window is also split across CTAs so
-        that the GPU is filled."""
+        model_fast.py:2033-2110). The windows (one head's pair of 128-row query tiles against every key) that
+        the last full wave of CTAs leaves over are cut into key ranges, so that they fill the SMs that wave leaves
+        idle, and merged (kernels.chunk_attention_tail)."""
         C, H = self.dim, self.num_heads
         rows = [k.numel() // C for k in k_chunks]
-        n_tiles = kernels.n_kv_tiles(rows)
         k_dst, v_dst = k_chunks[-1], v_chunks[-1]
-        splits = kernels.pick_kv_splits(L, H, n_tiles)
+        tail_ws, pieces = ws.attn_tail(H, rows)
         pk = sp.peer_kv(k_dst.view(chunk_rows, C), L) if p > 1 else None
         if pk is None:
             if p > 1:
                 sp.gather_kv_inplace(k_dst.view(chunk_rows, C), v_dst.view(chunk_rows, C), L)
-            if splits == 1:
-                kernels.chunk_attention(ws.q, k_chunks, v_chunks, out=ws.attn)
-            else:
-                po, pml = ws.attn_parts(splits, H)
-                kernels.chunk_attention_partial(ws.q, k_chunks, v_chunks, splits, po, pml, 0)
-                kernels.attention_merge(po, pml, splits, ws.attn)
+            kernels.chunk_attention_tail(ws.q, k_chunks, v_chunks, tail_ws, out=ws.attn, pieces=pieces)
             return
         dev = ws.q.device
         comm = self._comm_streams.get(dev)
@@ -323,13 +325,8 @@ class CausalWanAttentionBlock(nn.Module):
         with torch.cuda.stream(comm):
             comm.wait_event(ready)
             pk.finish(k2d, v2d)
-        gate = (pk.gathered_flag, pk.epoch, len(k_chunks) - 1)
-        if splits == 1:
-            kernels.chunk_attention_gated(ws.q, k_chunks, v_chunks, *gate, out=ws.attn)
-        else:
-            po, pml = ws.attn_parts(splits, H)
-            kernels.chunk_attention_gated(ws.q, k_chunks, v_chunks, *gate, n_splits=splits, part_o=po, part_ml=pml)
-            kernels.attention_merge(po, pml, splits, ws.attn)
+        kernels.chunk_attention_tail(ws.q, k_chunks, v_chunks, tail_ws, out=ws.attn, pieces=pieces,
+                                     gate_flag_ptr=pk.gathered_flag, gate_value=pk.epoch, gate_chunk=len(k_chunks) - 1)
         main.wait_stream(comm)                   # the destination chunk is complete for the caller
 
     # ------------------------------------------------------------------ forward
@@ -498,4 +495,4 @@ class CausalWanAttentionBlock(nn.Module):
         return xf
 
 
-KERNELS_PER_BLOCK = 13
+KERNELS_PER_BLOCK = 13  # plus the merge of the self-attention's cut windows when its tail schedule cuts some

@@ -56,6 +56,19 @@ struct KVMaps {
   int n_tiles;  // 128-key tiles over all chunks (each chunk's last tile may be ragged)
 };
 
+// Work schedule of one launch.
+//   pieces == 0: grid (query-tile pairs, heads, KV splits); split z attends the key tiles [z n / Z, (z + 1) n / Z)
+//                of its window and, when a workspace is given, writes slot slot0 + z of [slot][row][head][128].
+//   pieces > 0:  1-D grid over windows w = head * qpairs + pair (a window is one head's pair of query tiles
+//                against every key). Blocks [0, n_dp) attend whole windows and write the output. The last n_tail
+//                windows (the final, partial wave of whole windows) are cut into `pieces` key ranges each: block
+//                n_dp + p * n_tail + t attends range p of window n_dp + t and writes its unnormalised rows to
+//                [p][t][256 rows][128] and (m, l) to [p][t][256][2], which attn_merge_tail_kernel combines. The
+//                pieces run after every whole window has been dispatched and fill the SMs the last wave leaves.
+struct AttnSched {
+  int qpairs, heads, n_dp, n_tail, pieces;
+};
+
 // Combines split-KV partials: out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, M = max_s m_s.
 // One warp per (row, head); each lane owns 4 of the 128 head dims.
 __global__ void attn_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int n_slots,
@@ -75,6 +88,34 @@ __global__ void attn_merge_kernel(const float* __restrict__ part_o, const float*
     L += w * ml.y;
     const float4 o = *reinterpret_cast<const float4*>(part_o + base * attn::D + lane * 4);
     acc[0] += w * o.x; acc[1] += w * o.y; acc[2] += w * o.z; acc[3] += w * o.w;
+  }
+  const float inv = 1.f / L;
+  uint2 pk = make_uint2(pack_bf16(acc[0] * inv, acc[1] * inv), pack_bf16(acc[2] * inv, acc[3] * inv));
+  *reinterpret_cast<uint2*>(out + row * ldo + (long long)head * attn::D + lane * 4) = pk;
+}
+
+// The same combination for the cut windows of a pieces > 0 schedule: one warp per (cut window, row).
+__global__ void attn_merge_tail_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                                       const AttnSched sc, int q_rows, __nv_bfloat16* __restrict__ out, long long ldo) {
+  constexpr int WR = attn::QT * attn::BM;  // rows of a window
+  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (long long)sc.n_tail * WR) return;
+  const int t = (int)(wid / WR), r = (int)(wid % WR);
+  const int w = sc.n_dp + t;
+  const int head = w / sc.qpairs;
+  const long long row = (long long)(w % sc.qpairs) * WR + r;
+  if (row >= q_rows) return;
+  float M = -INFINITY;
+  for (int p = 0; p < sc.pieces; ++p) M = fmaxf(M, part_ml[(((long long)p * sc.n_tail + t) * WR + r) * 2]);
+  float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int p = 0; p < sc.pieces; ++p) {
+    const long long base = ((long long)p * sc.n_tail + t) * WR + r;
+    const float2 ml = *reinterpret_cast<const float2*>(part_ml + base * 2);
+    const float wgt = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+    L += wgt * ml.y;
+    const float4 o = *reinterpret_cast<const float4*>(part_o + base * attn::D + lane * 4);
+    acc[0] += wgt * o.x; acc[1] += wgt * o.y; acc[2] += wgt * o.z; acc[3] += wgt * o.w;
   }
   const float inv = 1.f / L;
   uint2 pk = make_uint2(pack_bf16(acc[0] * inv, acc[1] * inv), pack_bf16(acc[2] * inv, acc[3] * inv));
@@ -116,8 +157,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     chunk_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KVMaps kv, int q_rows,
                       float scale_log2, const float* __restrict__ key_bias, __nv_bfloat16* __restrict__ out,
                       long long ldo, float* __restrict__ part_o, float* __restrict__ part_ml, int slot0,
-                      const unsigned int* gate_flag, unsigned int gate_value, int gate_chunk, long long gate_limit_ns,
-                      int* status) {
+                      const AttnSched sc, const unsigned int* gate_flag, unsigned int gate_value, int gate_chunk,
+                      long long gate_limit_ns, int* status) {
   using namespace attn;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -130,12 +171,31 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int q0 = blockIdx.x * (QT * BM);
+  // This CTA attends its window's 128-key tiles [g_begin, g_end) (see AttnSched).
+  int head, pair, g_begin, g_end;
+  long long part_row0 = -1;  // pieces > 0: first workspace row of this block's partial; -1: write the output
+  if (sc.pieces == 0) {
+    pair = blockIdx.x;
+    head = blockIdx.y;
+    g_begin = (int)((long long)blockIdx.z * kv.n_tiles / gridDim.z);
+    g_end = (int)((long long)(blockIdx.z + 1) * kv.n_tiles / gridDim.z);
+  } else {
+    int w = blockIdx.x;
+    g_begin = 0;
+    g_end = kv.n_tiles;
+    if (w >= sc.n_dp) {
+      const int t = (w - sc.n_dp) % sc.n_tail, p = (w - sc.n_dp) / sc.n_tail;
+      w = sc.n_dp + t;
+      g_begin = (int)((long long)p * kv.n_tiles / sc.pieces);
+      g_end = (int)((long long)(p + 1) * kv.n_tiles / sc.pieces);
+      part_row0 = ((long long)p * sc.n_tail + t) * (QT * BM);
+    }
+    head = w / sc.qpairs;
+    pair = w % sc.qpairs;
+  }
+  const bool to_part = sc.pieces == 0 ? part_o != nullptr : part_row0 >= 0;
+  const int q0 = pair * (QT * BM);
   const bool two = q0 + BM < q_rows;  // false when the block's second query tile lies past the last row
-  // KV split: this CTA attends the window's 128-key tiles [g_begin, g_end) (all of them when gridDim.z == 1).
-  const int g_begin = (int)((long long)blockIdx.z * kv.n_tiles / gridDim.z);
-  const int g_end = (int)((long long)(blockIdx.z + 1) * kv.n_tiles / gridDim.z);
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
@@ -435,12 +495,12 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     const int row = q0 + wg * BM + quarter * 32 + lane;
     if (!active) {
       // nothing to write: every row of this tile is past q_rows
-    } else if (part_o && ok && mbar_wait(&o_done, 0, ab, 0x49)) {
-      // split-KV partial: unnormalised O (fp32) and this row's (m, l), merged by attn_merge_kernel
+    } else if (to_part && ok && mbar_wait(&o_done, 0, ab, 0x49)) {
+      // split-KV partial: unnormalised O (fp32) and this row's (m, l), merged by attn_merge(_tail)_kernel
       tc_fence_after();
-      const int heads = gridDim.y;
-      const long long slot = slot0 + blockIdx.z;
-      float* orow = part_o + ((slot * q_rows + row) * heads + head) * (long long)D;
+      const long long prow = sc.pieces == 0 ? ((slot0 + (long long)blockIdx.z) * q_rows + row) * sc.heads + head
+                                            : part_row0 + wg * BM + quarter * 32 + lane;
+      float* orow = part_o + prow * (long long)D;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
         uint32_t r[32];
@@ -454,9 +514,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                                 __uint_as_float(r[4 * q + 3]));
         }
       }
-      if (row < q_rows)
-        *reinterpret_cast<float2*>(part_ml + ((slot * q_rows + row) * heads + head) * 2) = make_float2(m, l);
-    } else if (!part_o && ok && mbar_wait(&o_done, 0, ab, 0x48)) {
+      if (row < q_rows) *reinterpret_cast<float2*>(part_ml + prow * 2) = make_float2(m, l);
+    } else if (!to_part && ok && mbar_wait(&o_done, 0, ab, 0x48)) {
       tc_fence_after();
       const float inv = 1.f / l;
       __nv_bfloat16* orow = out + (long long)row * ldo + (long long)head * D;
@@ -498,11 +557,45 @@ static long long gate_timeout_ns() {
   return (long long)(s * 1e9);
 }
 
+// Per-piece cost of a cut window in key-tile periods (the block's prologue and pipeline fill, its partial write and
+// its share of the merge), used to choose the number of pieces: on B200 each further wave of pieces measured
+// ~35 us, about 18 periods (c4 window, 1,350 and 2,700 query rows, 2 to 16 pieces).
+#ifndef LBW_ATTN_PIECE_COST_TILES
+#define LBW_ATTN_PIECE_COST_TILES 18
+#endif
+
+// Tail schedule of n_windows whole windows of n_tiles key tiles each on `sms` SMs: the windows past the last
+// full wave are cut into `pieces` key ranges (0: the count that minimises the modelled time of the cut part,
+// waves of pieces x (n_tiles / pieces + LBW_ATTN_PIECE_COST_TILES)). n_tail = 0 when nothing is cut.
+static void tail_plan(long long n_windows, int n_tiles, int pieces, int sms, int* n_tail, int* pieces_out) {
+  const long long tail = n_windows % sms;
+  if (pieces == 0) {
+    double best = 1e300;
+    pieces = 1;
+    for (int k = 1; k <= 16 && k <= n_tiles; ++k) {
+      const double waves = (double)((tail * k + sms - 1) / sms);
+      const double cost = waves * ((double)n_tiles / k + LBW_ATTN_PIECE_COST_TILES);
+      if (cost < best - 1e-9) {
+        best = cost;
+        pieces = k;
+      }
+    }
+  }
+  if (tail == 0 || pieces <= 1) {
+    *n_tail = 0;
+    *pieces_out = 1;
+    return;
+  }
+  *n_tail = (int)tail;
+  *pieces_out = pieces;
+}
+
 static int launch_attention(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
                             const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
                             const float* key_bias, float softmax_scale, void* out, long long ldo, int n_splits,
                             float* part_o, float* part_ml, int slot0, const unsigned int* gate_flag,
-                            unsigned int gate_value, int gate_chunk, cudaStream_t s) {
+                            unsigned int gate_value, int gate_chunk, cudaStream_t s, int pieces = -1,
+                            long long ws_blocks = 0) {
   using namespace attn;
   if (!q || !k_chunks || !v_chunks || !chunk_rows) return set_error(LBW_ERR_INVALID, "chunk_attention: null pointer");
   if (!out && !part_o) return set_error(LBW_ERR_INVALID, "chunk_attention: null output");
@@ -516,7 +609,10 @@ static int launch_attention(const void* q, long long ldq, int q_rows, int heads,
   if (key_bias && !aligned(key_bias, 4)) return set_error(LBW_ERR_ALIGN, "chunk_attention: key_bias alignment");
   if (part_o && (!part_ml || !aligned(part_o, 16) || !aligned(part_ml, 8) || slot0 < 0))
     return set_error(LBW_ERR_INVALID, "chunk_attention: partial buffers missing or misaligned");
-  if (!part_o && n_splits != 1) return set_error(LBW_ERR_INVALID, "chunk_attention: KV splits need partial buffers");
+  if (!part_o && n_splits != 1 && pieces < 0)
+    return set_error(LBW_ERR_INVALID, "chunk_attention: KV splits need partial buffers");
+  if (pieces >= 0 && (!out || n_splits != 1 || slot0 != 0))
+    return set_error(LBW_ERR_INVALID, "chunk_attention: a tail schedule writes out (one split, slot 0)");
   if (gate_chunk < n_chunks && (!gate_flag || !aligned(gate_flag, 4)))
     return set_error(LBW_ERR_INVALID, "chunk_attention: gated chunks need a 4-byte aligned gate flag");
   if (gate_chunk < 0) gate_chunk = 0;
@@ -543,6 +639,20 @@ static int launch_attention(const void* q, long long ldq, int q_rows, int heads,
   kv.n_tiles = n_tiles;
   if (n_splits < 1 || n_splits > n_tiles)
     return set_error(LBW_ERR_SHAPE, "chunk_attention: %d KV splits for %d key tiles", n_splits, n_tiles);
+  AttnSched sc{(q_rows + QT * BM - 1) / (QT * BM), heads, 0, 0, 0};
+  dim3 grid(sc.qpairs, heads, n_splits);
+  if (pieces >= 0) {
+    if (pieces > n_tiles)
+      return set_error(LBW_ERR_SHAPE, "chunk_attention: %d pieces for %d key tiles", pieces, n_tiles);
+    const long long n_windows = (long long)sc.qpairs * heads;
+    tail_plan(n_windows, n_tiles, pieces, num_sms(), &sc.n_tail, &sc.pieces);
+    sc.n_dp = (int)(n_windows - sc.n_tail);
+    if (sc.n_tail > 0 && (!part_o || !part_ml || !aligned(part_o, 16) || !aligned(part_ml, 8) ||
+                          ws_blocks < (long long)sc.n_tail * sc.pieces))
+      return set_error(LBW_ERR_INVALID, "chunk_attention: the tail schedule needs %lld workspace blocks (%lld given)",
+                       (long long)sc.n_tail * sc.pieces, ws_blocks);
+    grid = dim3((unsigned)(sc.n_dp + (long long)sc.n_tail * sc.pieces));
+  }
   static bool attr[64][2] = {};  // per device and variant
   const int hb = key_bias ? 1 : 0;
   const int dix = device_index();
@@ -554,17 +664,24 @@ static int launch_attention(const void* q, long long ldq, int q_rows, int heads,
     if (err) return err;
     attr[dix][hb] = true;
   }
-  dim3 grid((q_rows + QT * BM - 1) / (QT * BM), heads, n_splits);
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
   const long long gate_ns = gate_chunk < n_chunks ? gate_timeout_ns() : 0;
   __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
   if (hb)
     chunk_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, key_bias, o, ldo, part_o,
-                                                              part_ml, slot0, gate_flag, gate_value, gate_chunk, gate_ns, st);
+                                                              part_ml, slot0, sc, gate_flag, gate_value, gate_chunk,
+                                                              gate_ns, st);
   else
     chunk_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(tmQ, kv, q_rows, scale_log2, nullptr, o, ldo, part_o,
-                                                               part_ml, slot0, gate_flag, gate_value, gate_chunk, gate_ns, st);
-  return cuda_check(cudaGetLastError(), "attention launch");
+                                                               part_ml, slot0, sc, gate_flag, gate_value, gate_chunk,
+                                                               gate_ns, st);
+  if ((err = cuda_check(cudaGetLastError(), "attention launch"))) return err;
+  if (sc.n_tail > 0) {
+    const long long threads = (long long)sc.n_tail * QT * BM * 32;
+    attn_merge_tail_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(part_o, part_ml, sc, q_rows, o, ldo);
+    err = cuda_check(cudaGetLastError(), "attention tail merge launch");
+  }
+  return err;
 }
 
 extern "C" {
@@ -600,6 +717,39 @@ int lbw_chunk_attention_gated(const void* q, long long ldq, int q_rows, int head
   return launch_attention(q, ldq, q_rows, heads, k_chunks, v_chunks, chunk_rows, n_chunks, ldkv, nullptr,
                           softmax_scale, out, ldo, n_splits, part_o, part_ml, slot0, gate_flag, gate_value, gate_chunk,
                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+int lbw_attention_tail_plan(int q_rows, int heads, const int* chunk_rows, int n_chunks, int pieces, int* n_tail,
+                            int* pieces_used) {
+  using namespace attn;
+  if (!chunk_rows || !n_tail || !pieces_used) return set_error(LBW_ERR_INVALID, "attention_tail_plan: null pointer");
+  if (q_rows <= 0 || heads <= 0 || n_chunks < 1 || n_chunks > MAX_CHUNKS || pieces < 0)
+    return set_error(LBW_ERR_SHAPE, "attention_tail_plan: bad shape");
+  int n_tiles = 0;
+  for (int c = 0; c < n_chunks; ++c) {
+    if (chunk_rows[c] <= 0) return set_error(LBW_ERR_SHAPE, "attention_tail_plan: chunk %d is empty", c);
+    n_tiles += (chunk_rows[c] + BN - 1) / BN;
+  }
+  if (pieces > n_tiles) return set_error(LBW_ERR_SHAPE, "attention_tail_plan: %d pieces for %d key tiles", pieces, n_tiles);
+  const long long n_windows = (long long)((q_rows + QT * BM - 1) / (QT * BM)) * heads;
+  tail_plan(n_windows, n_tiles, pieces, num_sms(), n_tail, pieces_used);
+  return LBW_OK;
+}
+
+int lbw_chunk_attention_tail(const void* q, long long ldq, int q_rows, int heads, const void* const* k_chunks,
+                             const void* const* v_chunks, const int* chunk_rows, int n_chunks, long long ldkv,
+                             const float* key_bias, float softmax_scale, void* out, long long ldo, int pieces,
+                             float* part_o, float* part_ml, long long ws_blocks, const unsigned int* gate_flag,
+                             unsigned int gate_value, int gate_chunk, void* stream) {
+  if (!out) return set_error(LBW_ERR_INVALID, "chunk_attention_tail: null output");
+  if (pieces < 0) return set_error(LBW_ERR_SHAPE, "chunk_attention_tail: pieces %d", pieces);
+  if (gate_chunk < 0 || gate_chunk > n_chunks)
+    return set_error(LBW_ERR_SHAPE, "chunk_attention_tail: gate chunk %d of %d", gate_chunk, n_chunks);
+  if (gate_chunk < n_chunks && key_bias)
+    return set_error(LBW_ERR_INVALID, "chunk_attention_tail: a gated launch takes no key bias");
+  return launch_attention(q, ldq, q_rows, heads, k_chunks, v_chunks, chunk_rows, n_chunks, ldkv, key_bias,
+                          softmax_scale, out, ldo, 1, part_o, part_ml, 0, gate_flag, gate_value, gate_chunk,
+                          reinterpret_cast<cudaStream_t>(stream), pieces, ws_blocks);
 }
 
 int lbw_attention_merge(const float* part_o, const float* part_ml, int n_slots, int q_rows, int heads, void* out,

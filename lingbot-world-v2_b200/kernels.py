@@ -156,6 +156,95 @@ def chunk_attention_gated(q, k_chunks, v_chunks, gate_flag_ptr, gate_value, gate
     return out
 
 
+_TAIL_PLANS = {}
+
+
+def attention_tail_plan(q_rows, heads, chunk_rows, device, pieces=0):
+    """(cut windows, pieces) of lbw_chunk_attention_tail on `device` (its SM count sets the waves); cached."""
+    device = torch.device(device)
+    key = (int(q_rows), int(heads), tuple(int(r) for r in chunk_rows), device.index, int(pieces))
+    hit = _TAIL_PLANS.get(key)
+    if hit is None:
+        n = len(chunk_rows)
+        rows = (ctypes.c_int * n)(*key[2])
+        n_tail, used = ctypes.c_int(0), ctypes.c_int(0)
+        with torch.cuda.device(device):
+            check(load().lbw_attention_tail_plan(key[0], key[1], rows, n, key[4], ctypes.byref(n_tail),
+                                                 ctypes.byref(used)), "attention_tail_plan")
+        hit = _TAIL_PLANS[key] = (n_tail.value, used.value)
+    return hit
+
+
+def attention_tail_workspace(q_rows, heads, chunk_rows, device, pieces=0):
+    """fp32 workspace (part_o [blocks, 256, 128], part_ml [blocks, 256, 2]) for chunk_attention_tail, or None
+    when nothing is cut."""
+    n_tail, used = attention_tail_plan(q_rows, heads, chunk_rows, device, pieces)
+    if n_tail == 0:
+        return None
+    blocks = n_tail * used
+    return (torch.empty(blocks, 256, HEAD_DIM, dtype=torch.float32, device=device),
+            torch.empty(blocks, 256, 2, dtype=torch.float32, device=device))
+
+
+def chunk_attention_tail(q, k_chunks, v_chunks, workspace, key_bias=None, out=None, pieces=0, gate_flag_ptr=None,
+                         gate_value=0, gate_chunk=None, softmax_scale=None, _eager=False):
+    """chunk_attention with the windows past the last full wave cut into key ranges (see lbw.h); `workspace`
+    from attention_tail_workspace with the same pieces. With gate_flag_ptr, chunks gate_chunk.. are waited
+    for in-kernel as in chunk_attention_gated."""
+    if _tracing(_eager) and gate_flag_ptr is None:
+        if out is None:
+            raise ValueError("chunk_attention_tail: pass out= when compiling")
+        scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(HEAD_DIM)
+        part_o, part_ml = workspace if workspace is not None else (None, None)
+        _op("chunk_attention_tail")(q, list(k_chunks), list(v_chunks), key_bias, float(scale), out, part_o, part_ml,
+                                    int(pieces))
+        return out
+    require_cuda(q, *k_chunks, *v_chunks, key_bias, out)
+    q2 = _rows(_c(q, BF16))
+    lq, cols = q2.shape
+    if cols % HEAD_DIM:
+        raise ValueError("head_dim must be 128")
+    heads = cols // HEAD_DIM
+    n = len(k_chunks)
+    if n != len(v_chunks) or n == 0:
+        raise ValueError("need the same, non-zero number of K and V chunks")
+    ks = [_rows(_c(k, BF16)) for k in k_chunks]
+    vs = [_rows(_c(v, BF16)) for v in v_chunks]
+    for k, v in zip(ks, vs):
+        if k.shape != v.shape or k.shape[1] != cols:
+            raise ValueError(f"chunk shape {tuple(k.shape)} / {tuple(v.shape)} does not match q width {cols}")
+    if out is None:
+        out = torch.empty(lq, cols, dtype=BF16, device=q.device)
+    o2 = _rows(_c(out, BF16))
+    if o2.shape[0] != lq or o2.shape[1] < cols:
+        raise ValueError("chunk_attention_tail: out does not match q")
+    part_o = part_ml = None
+    blocks = 0
+    if workspace is not None:
+        part_o, part_ml = workspace
+        require_cuda(part_o, part_ml)
+        _c(part_o, torch.float32), _c(part_ml, torch.float32)
+        if part_o.shape[1:] != (256, HEAD_DIM) or part_ml.shape[1:] != (256, 2) or part_o.shape[0] != part_ml.shape[0]:
+            raise ValueError("chunk_attention_tail: workspace must be [blocks, 256, 128] and [blocks, 256, 2] fp32")
+        blocks = part_o.shape[0]
+    if key_bias is not None:
+        key_bias = _c(key_bias, torch.float32)
+        if key_bias.numel() != sum(k.shape[0] for k in ks):
+            raise ValueError("key_bias needs one value per key")
+    kp = (ctypes.c_void_p * n)(*[k.data_ptr() for k in ks])
+    vp = (ctypes.c_void_p * n)(*[v.data_ptr() for v in vs])
+    rows = (ctypes.c_int * n)(*[k.shape[0] for k in ks])
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(HEAD_DIM)
+    gate_chunk = n if gate_flag_ptr is None else int(gate_chunk)
+    n_tail, _ = attention_tail_plan(lq, heads, [k.shape[0] for k in ks], q.device, pieces)
+    check(load().lbw_chunk_attention_tail(ptr(q2), q2.stride(0), lq, heads, kp, vp, rows, n, cols, ptr(key_bias),
+                                          ctypes.c_float(scale), ptr(o2), o2.stride(0), int(pieces), ptr(part_o),
+                                          ptr(part_ml), blocks, ctypes.c_void_p(gate_flag_ptr or 0),
+                                          ctypes.c_uint(gate_value), gate_chunk, stream_of(q.device)),
+          "chunk_attention_tail", launches=2 if n_tail else 1)
+    return out
+
+
 def attention_merge(part_o, part_ml, n_slots, out, _eager=False):
     if _tracing(_eager):
         _op("attention_merge")(part_o, part_ml, int(n_slots), out)

@@ -42,6 +42,21 @@ def _(q, k_chunks, v_chunks, n_splits, part_o, part_ml, slot0, key_bias, scale):
     return None
 
 
+@torch.library.custom_op("lbw::chunk_attention_tail", mutates_args=("out", "part_o", "part_ml"))
+def chunk_attention_tail(q: torch.Tensor, k_chunks: List[torch.Tensor], v_chunks: List[torch.Tensor],
+                         key_bias: Optional[torch.Tensor], scale: float, out: torch.Tensor,
+                         part_o: Optional[torch.Tensor], part_ml: Optional[torch.Tensor], pieces: int) -> None:
+    """chunk_attention with the windows past the last full wave cut into key ranges and merged (lbw.h)."""
+    ws = (part_o, part_ml) if part_o is not None else None
+    K.chunk_attention_tail(q, k_chunks, v_chunks, ws, key_bias=key_bias, out=out, pieces=pieces, softmax_scale=scale,
+                           _eager=True)
+
+
+@chunk_attention_tail.register_fake
+def _(q, k_chunks, v_chunks, key_bias, scale, out, part_o, part_ml, pieces):
+    return None
+
+
 @torch.library.custom_op("lbw::attention_merge", mutates_args=("out",))
 def attention_merge(part_o: torch.Tensor, part_ml: torch.Tensor, n_slots: int, out: torch.Tensor) -> None:
     K.attention_merge(part_o, part_ml, n_slots, out, _eager=True)
@@ -223,6 +238,6 @@ def _(a, a_s, w, w_s, bias, fmt):
     return a.new_empty((a.shape[0], w.shape[0]), dtype=BF16)
 
 
-OPS = ("chunk_attention", "chunk_attention_partial", "attention_merge", "layernorm_mod", "layernorm_mod_mx",
+OPS = ("chunk_attention", "chunk_attention_partial", "chunk_attention_tail", "attention_merge", "layernorm_mod", "layernorm_mod_mx",
        "layernorm_affine_mx", "qkv_proj", "rmsnorm_rope", "qk_rmsnorm_rope", "linear_residual", "linear_rowss", "linear_gelu",
        "mx_linear_gelu", "mx_linear_residual", "mx_quantize_into", "mx_quantize", "mx_linear")

@@ -179,12 +179,14 @@ def test_ffn_mx_c4_rows(cuda_dev):
     assert rel_l2(got, want) <= 1e-2, rel_l2(got, want)
 
 
-@pytest.mark.parametrize("q_rows,splits", [(10800, 1), (10800, 3), (1350, 0), (1350, 1)])
+@pytest.mark.parametrize("q_rows,splits", [(10800, 1), (10800, 3), (10800, "tail"), (1350, 0), (1350, 1),
+                                          (1350, "tail")])
 def test_attention_c4_window(cuda_dev, q_rows, splits):
     """The self-attention kernel over the c4 window (7 chunks x 10,800 keys, 40 heads) at the 1-GPU query count
     (a (43, 40) grid whose last CTA per head holds a lone 48-row tile) and at the 8-GPU per-rank count (1,350
-    rows: a lone 70-row tile), whole-window and split-KV (splits 0 = the block's automatic choice), against fp32
-    torch on the sampled rows of every head."""
+    rows: a lone 70-row tile), whole-window, split-KV (splits 0 = the automatic uniform split) and the block's
+    tail schedule (the windows past the last full wave cut into key ranges: heads 38-39 and the end of head 37
+    at 10,800 rows, heads 25-39 at 1,350), against fp32 torch on the sampled rows of every head."""
     import lbw_b200.kernels as K
     dev = cuda_dev
     H, C = 40, 5120
@@ -195,7 +197,11 @@ def test_attention_c4_window(cuda_dev, q_rows, splits):
     if splits == 0:
         splits = K.pick_kv_splits(q_rows, H, K.n_kv_tiles([10800] * 7))
     out = torch.empty(q_rows, C, dtype=BF, device=dev)
-    if splits == 1:
+    if splits == "tail":
+        n_tail, pieces = K.attention_tail_plan(q_rows, H, [10800] * 7, dev)
+        assert n_tail > 0 and pieces > 1
+        K.chunk_attention_tail(q, ks, vs, K.attention_tail_workspace(q_rows, H, [10800] * 7, dev), out=out)
+    elif splits == 1:
         K.chunk_attention(q, ks, vs, out=out)
     else:
         po, pml = K.attention_workspace(splits, q_rows, H, dev)

@@ -298,6 +298,55 @@ def test_chunk_attention_split_kv_and_merge(cuda_dev, splits):
     assert rel_l2(out2.view(300, 2, 128), ref) < 1e-2
 
 
+@pytest.mark.parametrize("pieces", [0, 2, 3, 7])
+def test_chunk_attention_tail_schedule(cuda_dev, pieces):
+    """The tail schedule over 300 query rows x 75 heads = 150 windows (a window: one head's pair of 128-row query
+    tiles against every key; here the second pair holds a lone 44-row tile): the windows of the full waves run
+    whole and write exactly what lbw_chunk_attention writes; the windows past the last full wave (2 of them on
+    148 SMs) are cut into `pieces` key ranges (0: the planned count) and merged, within fp32 rounding of the
+    whole-window result (bf16 rounding of P) and against the fp32 oracle."""
+    import lbw_b200.kernels as K
+    d = cuda_dev
+    heads, lq, rows = 75, 300, [200, 77, 500]
+    q, ks, vs = _attn_case(lq, rows, heads, 41, qscale=2.0)
+    qd, kd, vd = q.to(d), [k.to(d) for k in ks], [v.to(d) for v in vs]
+    whole = K.chunk_attention(qd, kd, vd)
+    n_tail, used = K.attention_tail_plan(lq, heads, rows, d, pieces)
+    assert n_tail == 150 % torch.cuda.get_device_properties(d).multi_processor_count
+    assert used == (pieces if pieces else used) and 1 < used <= 7
+    out = K.chunk_attention_tail(qd, kd, vd, K.attention_tail_workspace(lq, heads, rows, d, pieces), pieces=pieces)
+    torch.cuda.synchronize()
+    n_dp = 150 - n_tail
+    for w in range(150):
+        head, pair = divmod(w, 2)
+        r0, r1 = pair * 256, min(lq, pair * 256 + 256)
+        got, want = out[r0:r1, head * 128:(head + 1) * 128], whole[r0:r1, head * 128:(head + 1) * 128]
+        if w < n_dp:
+            assert torch.equal(got, want), w
+        else:
+            # P is rounded to bf16 against each piece's own running max, so the rounding differs from the whole
+            # window's (about 3e-3 of the output here)
+            assert rel_l2(got, want) < 5e-3, (w, rel_l2(got, want))
+            ref = ob.attention(q[r0:r1, head:head + 1], torch.cat(ks)[:, head:head + 1], torch.cat(vs)[:, head:head + 1])
+            assert rel_l2(got.cpu().view(r1 - r0, 1, 128), ref) < 1e-2
+
+
+def test_chunk_attention_tail_validation(cuda_dev):
+    """More pieces than key tiles, and a workspace smaller than the plan, are refused before any launch."""
+    import lbw_b200.kernels as K
+    d = cuda_dev
+    heads, lq, rows = 75, 300, [200, 77, 500]
+    q, ks, vs = _attn_case(lq, rows, heads, 43)
+    qd, kd, vd = q.to(d), [k.to(d) for k in ks], [v.to(d) for v in vs]
+    with pytest.raises(ValueError, match="pieces"):
+        K.attention_tail_plan(lq, heads, rows, d, 8)
+    po, pml = K.attention_tail_workspace(lq, heads, rows, d, 3)
+    with pytest.raises(ValueError, match="workspace blocks"):
+        K.chunk_attention_tail(qd, kd, vd, (po[:1], pml[:1]), pieces=3)
+    with pytest.raises(ValueError, match="workspace blocks"):
+        K.chunk_attention_tail(qd, kd, vd, None, pieces=3)
+
+
 def test_gated_attention_matches_ungated(cuda_dev):
     """With its gate already open, the gated kernel computes exactly what the ungated one does, in both output
     modes (direct and split-KV partials + merge); a gate chunk outside the window is rejected."""
@@ -316,6 +365,12 @@ def test_gated_attention_matches_ungated(cuda_dev):
     po2, pml2 = K.attention_workspace(3, 300, 2, d)
     K.chunk_attention_gated(q, ks, vs, flag.data_ptr(), 6, 1, n_splits=3, part_o=po2, part_ml=pml2)
     assert torch.equal(K.attention_merge(po2, pml2, 3, torch.empty_like(ref)), ref3)
+    # the tail schedule (here every window is cut: 4 windows), gated and ungated
+    wst = K.attention_tail_workspace(300, 2, [256, 200, 130], d, 3)
+    reft = K.chunk_attention_tail(q, ks, vs, wst, pieces=3)
+    outt = K.chunk_attention_tail(q, ks, vs, wst, pieces=3, gate_flag_ptr=flag.data_ptr(), gate_value=7, gate_chunk=2)
+    assert torch.equal(outt, reft)
+    assert rel_l2(reft, ref) < 5e-3
     with pytest.raises(ValueError, match="gate chunk"):
         K.chunk_attention_gated(q, ks, vs, flag.data_ptr(), 7, 3, out=out)
 

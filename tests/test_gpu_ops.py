@@ -118,6 +118,9 @@ def _opcheck_cases(d):
                                             torch.zeros(m, device=d))),
         "chunk_attention": (ops.chunk_attention, (q, [k], [v], None, 128 ** -0.5,
                                                   torch.empty(m, 256, dtype=BF, device=d))),
+        "chunk_attention_tail": (ops.chunk_attention_tail, (q, [k], [v], None, 128 ** -0.5,
+                                                            torch.empty(m, 256, dtype=BF, device=d),
+                                                            *K.attention_tail_workspace(m, 2, [300], d, 3), 3)),
         "rmsnorm_rope": (ops.rmsnorm_rope, (a, (a.float() ** 2).sum(1), r(c, dt=BF), 1e-6,
                                             torch.empty(m, c, dtype=BF, device=d), None, None, 0, 0, 0, 0, 0)),
         "qk_rmsnorm_rope": (ops.qk_rmsnorm_rope, (a, (a.float() ** 2).sum(1), r(c, dt=BF),
@@ -133,7 +136,7 @@ def _opcheck_cases(d):
 
 
 @pytest.mark.parametrize("name", ["layernorm_mod", "linear_residual", "linear_rowss", "chunk_attention",
-                                  "rmsnorm_rope", "qk_rmsnorm_rope", "mx_quantize", "mx_quantize_into",
+                                  "chunk_attention_tail", "rmsnorm_rope", "qk_rmsnorm_rope", "mx_quantize", "mx_quantize_into",
                                   "mx_linear"])
 def test_opcheck(cuda_dev, name):
     """torch.library.opcheck: each operator's schema (the tensors it declares it writes are the ones it writes, new
