@@ -31,7 +31,7 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-ATTN_TRAFFIC_C4_BYTES = 2114.584832e6 + 122.817024e6  # ncu dram bytes, one chunk_attn_kernel launch at c4
+ATTN_TRAFFIC_C4_BYTES = 2101.592576e6 + 137.902848e6  # ncu dram bytes, one chunk_attn_kernel launch at c4 (tail schedule)
 ATTN_KV_BYTES_C4 = 4.0 * 75600 * 5120
 
 CONFIGS = {
@@ -353,19 +353,17 @@ def run_sweep(args):
             rows = [lkv // n_chunks + (1 if i < lkv % n_chunks else 0) for i in range(n_chunks)]
             ks = [torch.randn(r, C, generator=g, device=dev, dtype=bf) for r in rows]
             vs = [torch.randn(r, C, generator=g, device=dev, dtype=bf) for r in rows]
-            splits = K.pick_kv_splits(lq, H, K.n_kv_tiles(rows))
-            parts = K.attention_workspace(splits, lq, H, dev) if splits > 1 else None
+            # the block's schedule: whole windows in full waves, the last partial wave cut into key ranges + merge
+            n_tail, pieces = K.attention_tail_plan(lq, H, rows, dev)
+            parts = K.attention_tail_workspace(lq, H, rows, dev)
 
             def run():
-                if parts is None:
-                    K.chunk_attention(q, ks, vs, out=out)
-                else:
-                    K.chunk_attention_partial(q, ks, vs, splits, *parts)
-                    K.attention_merge(*parts, splits, out)
+                K.chunk_attention_tail(q, ks, vs, parts, out=out)
             ms = timed(run)
             tf = 4.0 * lq * lkv * C / (ms / 1e3) / 1e12
-            print(json.dumps({"sweep": "chunk_attention", "q_rows": lq, "kv_rows": lkv, "heads": H, "kv_splits": splits,
-                              "ms": ms, "tflops": tf, "frac_of_peak": tf / peak, "peak": f"{src} bf16_tflops {peak}"}))
+            print(json.dumps({"sweep": "chunk_attention", "q_rows": lq, "kv_rows": lkv, "heads": H,
+                              "cut_windows": n_tail, "pieces": pieces, "ms": ms, "tflops": tf,
+                              "frac_of_peak": tf / peak, "peak": f"{src} bf16_tflops {peak}"}))
             del ks, vs, parts
     # block-scaled FFN GEMMs: MXFP8 E4M3 (the reference's default), E5M2 (its LINGBOT_MX_FP8 option) and MXFP4 E2M1;
     # the nominal dense rates are 2x (FP8) and 4x (FP4) the bf16 rate, so each point is also given against 2x / 4x
@@ -481,7 +479,8 @@ def run_sweep(args):
                 rec[f"ms_{tn}"] = timed(fn, reps=5)
             os.environ.pop("LBW_GEMM_TILE_N", None)
             print(json.dumps(rec))
-    # KV splits of the self-attention at the per-rank query rows of 8 / 4 GPUs (c4 window: 7 chunks x 10,800 keys)
+    # KV splits and tail pieces of the self-attention at the per-rank query rows of 8 / 4 GPUs (c4 window: 7 chunks x
+    # 10,800 keys)
     for lq in ((1350, 2700) if only == "tiles" else ()):
         q = torch.randn(lq, C, generator=g, device=dev, dtype=bf)
         out = torch.empty(lq, C, dtype=bf, device=dev)
@@ -500,6 +499,15 @@ def run_sweep(args):
                     K.attention_merge(*parts, sp_, out)
             run()
             rec[f"ms_s{sp_}"] = timed(run, reps=3)
+        # the block's tail schedule: the last partial wave of windows cut into `pieces` key ranges (0: planned)
+        rec["tail_plan"] = K.attention_tail_plan(lq, H, [10800] * 7, dev)
+        for pc in (0, 1, 2, 3, 4, 6, 8):
+            parts = K.attention_tail_workspace(lq, H, [10800] * 7, dev, pc)
+
+            def run_tail():
+                K.chunk_attention_tail(q, ks, vs, parts, out=out, pieces=pc)
+            run_tail()
+            rec[f"ms_tail{pc}"] = timed(run_tail, reps=3)
         print(json.dumps(rec))
         del ks, vs
     return 0
