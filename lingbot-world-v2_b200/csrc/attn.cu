@@ -27,6 +27,9 @@
 // MMAs of one CTA execute in issue order, and every tcgen05.commit covers all earlier MMAs:
 // when softmax i sees S_i(j+1) complete, PV_i(j) has completed too, so O_i is stable and P_i(j)
 // has been consumed.
+// Launch shapes (AttnSched): a grid of (query-tile pairs, heads, uniform KV splits), or the tail schedule the block
+// uses -- whole windows in full waves of CTAs, then the windows of the last, partial wave cut into key ranges that
+// fill the SMs it would leave idle, merged by attn_merge_tail_kernel.
 #include <math.h>
 
 #include "host_common.cuh"
