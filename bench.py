@@ -158,6 +158,8 @@ def cpu_oracle_step(cfg_name, rows_sample, threads, blocks=1, mx=False):
     v_lead = [r(chunk, H, 128, std=1.0).to(bf) for _ in range(c["n_lead"])]
     ctx_k, ctx_v = r(TEXT_LEN, H, 128, std=1.0).to(bf), r(TEXT_LEN, H, 128, std=1.0).to(bf)
     cos, sin = ob.rope_grid(ob.rope_freqs(), c["grid"], c["start_frame"])
+    # the reference's RoPE arithmetic for a chunk of this size (bf16 from 4,096 tokens, model_fast.py:1144-1148)
+    rope_dt = torch.bfloat16 if f * gh * gw >= 4096 else torch.float32
     film = (r(rows_sample, C, std=0.1).to(bf), r(rows_sample, C, std=0.1).to(bf))
     # the chunk's own K/V are computed from the sample rows; the rest of the destination chunk is cached data
     k_lead = k_lead + [r(chunk - rows_sample, H, 128, std=1.0).to(bf)]
@@ -165,7 +167,7 @@ def cpu_oracle_step(cfg_name, rows_sample, threads, blocks=1, mx=False):
     t0 = time.perf_counter()
     for _ in range(blocks):
         ob.block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos[:rows_sample], sin[:rows_sample], film=film,
-                         mx=mx)
+                         mx=mx, rope_dtype=rope_dt)
     return time.perf_counter() - t0
 
 
@@ -247,8 +249,10 @@ def block_parity(stack, args, c, dims, dev, world, rank, L_loc, ks0, vs0, ctx, c
     names = [n for n in B.MX_LINEAR_NAMES] if args.lin_mx else ()
     ck, cv = ob.cross_kv(p, ctx.cpu(), mx_linears=names)
     t0 = time.perf_counter()
+    import lbw_b200.rope as R
     r = ob.block_forward(p, x_full[idx], e0.cpu(), k_lead, v_lead, ck, cv, cos[idx], sin[idx],
-                         film=(fs_full[idx], ft_full[idx]), mx=True, return_all=True, mx_linears=names)
+                         film=(fs_full[idx], ft_full[idx]), mx=True, return_all=True, mx_linears=names,
+                         rope_dtype=R.ROPE_DTYPE)
     t_oracle = time.perf_counter() - t0
     n = len(own)
     got = xs.cpu()[torch.tensor(own)]
@@ -631,6 +635,10 @@ def main():
     import lbw_b200.rope as R
     import lbw_b200.sp as sp
 
+    # the reference's RoPE arithmetic for this chunk: its model forward switches to bf16 RoPE for chunks of 4,096 or
+    # more tokens (model_fast.py:1144-1148); the stack here is driven without the model, so set it the same way
+    R.set_bf16_rope_for_forward(CONFIGS[args.config]["grid"][0] * CONFIGS[args.config]["grid"][1]
+                                * CONFIGS[args.config]["grid"][2])
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -216,6 +216,21 @@ int lbw_qk_rmsnorm_rope(const void* q_raw, const float* ss_q, const void* gamma_
                         int q_row_off, const void* k_raw, const float* ss_k, const void* gamma_k, void* k_out,
                         long long ldk, int k_row_off, int m, int c, float eps, const float* rope_cos,
                         const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0, void* stream);
+/* The same two with the rotation's arithmetic chosen: LBW_ROPE_FP32 (what the two above do: fp32 tables, products
+ * and sums, one rounding to bf16) or LBW_ROPE_BF16, the reference's RoPE once a forward has seen a chunk of 4,096 or
+ * more tokens (model_fast.py:1144-1148 set_bf16_rope_for_forward -> mark_bf16_rope :1000-1003, then
+ * causal_rope_apply_rotation :933-979 with ROPE_DTYPE bf16 and the grids cast to bf16 :928-929): cos and sin
+ * rounded to bf16, each product and each sum of the rotation rounded to bf16. */
+#define LBW_ROPE_FP32 0
+#define LBW_ROPE_BF16 1
+int lbw_rmsnorm_rope_dt(const void* x, const float* ss, const void* gamma, int m, int c, float eps,
+                        const float* rope_cos, const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0,
+                        void* out, long long ldo, int out_row_off, int rope_dtype, void* stream);
+int lbw_qk_rmsnorm_rope_dt(const void* q_raw, const float* ss_q, const void* gamma_q, void* q_out, long long ldq,
+                           int q_row_off, const void* k_raw, const float* ss_k, const void* gamma_k, void* k_out,
+                           long long ldk, int k_row_off, int m, int c, float eps, const float* rope_cos,
+                           const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0, int rope_dtype,
+                           void* stream);
 
 /* ---- MXFP8 -------------------------------------------------------------------------------- */
 /* Quantise bf16 x [rows, k] (k % 128 == 0) to E4M3 data [rows, k] and E8M0 scales in the tiled

@@ -36,6 +36,9 @@ SIGNATURES = {
     "lbw_rmsnorm_rope": ([_vp, _vp, _vp, _i, _i, _f, _vp, _vp, _i, _i, _i, _i, _vp, _ll, _i, _vp], _i),
     "lbw_qk_rmsnorm_rope": ([_vp, _vp, _vp, _vp, _ll, _i, _vp, _vp, _vp, _vp, _ll, _i, _i, _i, _f, _vp, _vp, _i, _i,
                              _i, _i, _vp], _i),
+    "lbw_rmsnorm_rope_dt": ([_vp, _vp, _vp, _i, _i, _f, _vp, _vp, _i, _i, _i, _i, _vp, _ll, _i, _i, _vp], _i),
+    "lbw_qk_rmsnorm_rope_dt": ([_vp, _vp, _vp, _vp, _ll, _i, _vp, _vp, _vp, _vp, _ll, _i, _i, _i, _f, _vp, _vp, _i, _i,
+                                _i, _i, _i, _vp], _i),
     "lbw_mx_quantize": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
     "lbw_mx_quantize_fmt": ([_vp, _i, _i, _i, _vp, _vp, _vp, _vp], _i),
     "lbw_mx_linear_fmt": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),

@@ -427,7 +427,7 @@ class CausalWanAttentionBlock(nn.Module):
             kernels.qkv_proj(ws.h, pk["wqkv"], pk["bqkv"], ws.q_raw, ws.k_raw, ss_q, ss_k, v_dst, v_row_off=row0)
         mark("qkv")
         kernels.qk_rmsnorm_rope(ws.q_raw, ss_q, pk["gq"], ws.q, ws.k_raw, ss_k, pk["gk"], k_dst, eps, rp, grid,
-                                tok0=row0, k_row_off=row0)
+                                tok0=row0, k_row_off=row0, rope_bf16=rope.ROPE_DTYPE == torch.bfloat16)
         mark("qk_norm_rope")
         if kv_only:
             if p > 1:

@@ -118,7 +118,7 @@ __device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* __restrict
                                                  const __nv_bfloat16* __restrict__ gamma, int C, float eps,
                                                  const float* __restrict__ rcos, const float* __restrict__ rsin,
                                                  int n_frames, int gh, int gw, int tok0, __nv_bfloat16* __restrict__ out,
-                                                 long long ldo, int out_row_off, long long row) {
+                                                 long long ldo, int out_row_off, long long row, int rope_bf16) {
   const float r = 1.f / sqrtf(ss[row] / (float)C + eps);
   const int tok = tok0 + (int)row;
   const int f = tok / (gh * gw), hh = (tok / gw) % gh, ww = tok % gw;
@@ -139,10 +139,18 @@ __device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* __restrict
       for (int k = 0; k < 4; ++k) {
         const int p = p0 + k;
         const int idx = p < 22 ? f * 22 + p : (p < 43 ? base_h + hh * 21 + (p - 22) : base_w + ww * 21 + (p - 43));
-        const float c = rcos[idx], s = rsin[idx];
         const float re = y[2 * k], im = y[2 * k + 1];
-        y[2 * k] = __fsub_rn(__fmul_rn(re, c), __fmul_rn(im, s));
-        y[2 * k + 1] = __fadd_rn(__fmul_rn(re, s), __fmul_rn(im, c));
+        if (rope_bf16) {
+          // the reference's bf16 RoPE (model_fast.py:985-1003, :933-979 with ROPE_DTYPE bf16): bf16 cos / sin, and
+          // every product and the sum rounded to bf16 as torch's bf16 elementwise ops do
+          const float c = bf16_round(rcos[idx]), s = bf16_round(rsin[idx]);
+          y[2 * k] = bf16_round(__fsub_rn(bf16_round(__fmul_rn(re, c)), bf16_round(__fmul_rn(im, s))));
+          y[2 * k + 1] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(re, s)), bf16_round(__fmul_rn(im, c))));
+        } else {
+          const float c = rcos[idx], s = rsin[idx];
+          y[2 * k] = __fsub_rn(__fmul_rn(re, c), __fmul_rn(im, s));
+          y[2 * k + 1] = __fadd_rn(__fmul_rn(re, s), __fmul_rn(im, c));
+        }
       }
     }
     uint4 o = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
@@ -153,8 +161,9 @@ __device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* __restrict
 __global__ void __launch_bounds__(ROW_THREADS) rmsnorm_rope_kernel(
     const __nv_bfloat16* __restrict__ x, const float* __restrict__ ss, const __nv_bfloat16* __restrict__ gamma, int C,
     float eps, const float* __restrict__ rcos, const float* __restrict__ rsin, int n_frames, int gh, int gw, int tok0,
-    __nv_bfloat16* __restrict__ out, long long ldo, int out_row_off) {
-  rmsnorm_rope_row(x, ss, gamma, C, eps, rcos, rsin, n_frames, gh, gw, tok0, out, ldo, out_row_off, blockIdx.x);
+    __nv_bfloat16* __restrict__ out, long long ldo, int out_row_off, int rope_bf16) {
+  rmsnorm_rope_row(x, ss, gamma, C, eps, rcos, rsin, n_frames, gh, gw, tok0, out, ldo, out_row_off, blockIdx.x,
+                   rope_bf16);
 }
 
 // q and k of the same tokens in one launch (blocks 0..m-1: q rows, m..2m-1: k rows), as the reference's
@@ -171,10 +180,10 @@ struct QKRows {
 __global__ void __launch_bounds__(ROW_THREADS) qk_rmsnorm_rope_kernel(const __grid_constant__ QKRows t, int m, int C,
                                                                       float eps, const float* __restrict__ rcos,
                                                                       const float* __restrict__ rsin, int n_frames,
-                                                                      int gh, int gw, int tok0) {
+                                                                      int gh, int gw, int tok0, int rope_bf16) {
   const int w = blockIdx.x >= (unsigned)m;
   rmsnorm_rope_row(t.x[w], t.ss[w], t.gamma[w], C, eps, rcos, rsin, n_frames, gh, gw, tok0, t.out[w], t.ldo[w],
-                   t.out_row_off[w], (long long)blockIdx.x - (w ? m : 0));
+                   t.out_row_off[w], (long long)blockIdx.x - (w ? m : 0), rope_bf16);
 }
 
 // One thread per 32-value block; rows up to the next multiple of 128 get zero scales. FMT: MX_E4M3 / MX_E5M2
@@ -288,7 +297,16 @@ int lbw_layernorm_mod_mx_fmt(const float* x, int m, int c, float eps, const floa
 int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, int c, float eps,
                      const float* rope_cos, const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0,
                      void* out, long long ldo, int out_row_off, void* stream) {
+  return lbw_rmsnorm_rope_dt(x, ss, gamma, m, c, eps, rope_cos, rope_sin, rope_frames, grid_h, grid_w, tok0, out, ldo,
+                             out_row_off, LBW_ROPE_FP32, stream);
+}
+
+int lbw_rmsnorm_rope_dt(const void* x, const float* ss, const void* gamma, int m, int c, float eps,
+                        const float* rope_cos, const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0,
+                        void* out, long long ldo, int out_row_off, int rope_dtype, void* stream) {
   if (!x || !ss || !gamma || !out) return set_error(LBW_ERR_INVALID, "rmsnorm_rope: null pointer");
+  if (rope_dtype != LBW_ROPE_FP32 && rope_dtype != LBW_ROPE_BF16)
+    return set_error(LBW_ERR_INVALID, "rmsnorm_rope: rope dtype %d", rope_dtype);
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return set_error(LBW_ERR_INVALID, "rmsnorm_rope: cos/sin pair");
   if (m <= 0 || c <= 0 || c % 128 || c > RR_MAXIT * ROW_THREADS * 8)
     return set_error(LBW_ERR_SHAPE, "rmsnorm_rope: width %d must be a multiple of 128 and <= %d", c,
@@ -303,7 +321,7 @@ int lbw_rmsnorm_rope(const void* x, const float* ss, const void* gamma, int m, i
   rmsnorm_rope_kernel<<<m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), ss, reinterpret_cast<const __nv_bfloat16*>(gamma), c, eps, rope_cos,
       rope_sin, n_frames, grid_h > 0 ? grid_h : 1, grid_w > 0 ? grid_w : 1, tok0,
-      reinterpret_cast<__nv_bfloat16*>(out), ldo, out_row_off);
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, out_row_off, rope_dtype == LBW_ROPE_BF16);
   return cuda_check(cudaGetLastError(), "rmsnorm_rope launch");
 }
 
@@ -311,8 +329,20 @@ int lbw_qk_rmsnorm_rope(const void* q_raw, const float* ss_q, const void* gamma_
                         int q_row_off, const void* k_raw, const float* ss_k, const void* gamma_k, void* k_out,
                         long long ldk, int k_row_off, int m, int c, float eps, const float* rope_cos,
                         const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0, void* stream) {
+  return lbw_qk_rmsnorm_rope_dt(q_raw, ss_q, gamma_q, q_out, ldq, q_row_off, k_raw, ss_k, gamma_k, k_out, ldk,
+                                k_row_off, m, c, eps, rope_cos, rope_sin, rope_frames, grid_h, grid_w, tok0,
+                                LBW_ROPE_FP32, stream);
+}
+
+int lbw_qk_rmsnorm_rope_dt(const void* q_raw, const float* ss_q, const void* gamma_q, void* q_out, long long ldq,
+                           int q_row_off, const void* k_raw, const float* ss_k, const void* gamma_k, void* k_out,
+                           long long ldk, int k_row_off, int m, int c, float eps, const float* rope_cos,
+                           const float* rope_sin, int rope_frames, int grid_h, int grid_w, int tok0, int rope_dtype,
+                           void* stream) {
   if (!q_raw || !ss_q || !gamma_q || !q_out || !k_raw || !ss_k || !gamma_k || !k_out)
     return set_error(LBW_ERR_INVALID, "qk_rmsnorm_rope: null pointer");
+  if (rope_dtype != LBW_ROPE_FP32 && rope_dtype != LBW_ROPE_BF16)
+    return set_error(LBW_ERR_INVALID, "qk_rmsnorm_rope: rope dtype %d", rope_dtype);
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return set_error(LBW_ERR_INVALID, "qk_rmsnorm_rope: cos/sin pair");
   if (m <= 0 || c <= 0 || c % 128 || c > RR_MAXIT * ROW_THREADS * 8 || m > (1 << 30))
     return set_error(LBW_ERR_SHAPE, "qk_rmsnorm_rope: %d rows of width %d (a multiple of 128, <= %d)", m, c,
@@ -340,7 +370,8 @@ int lbw_qk_rmsnorm_rope(const void* q_raw, const float* ss_q, const void* gamma_
   t.out_row_off[1] = k_row_off;
   const int n_frames = rope_cos ? rope_frames : 0;
   qk_rmsnorm_rope_kernel<<<2 * m, ROW_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      t, m, c, eps, rope_cos, rope_sin, n_frames, grid_h > 0 ? grid_h : 1, grid_w > 0 ? grid_w : 1, tok0);
+      t, m, c, eps, rope_cos, rope_sin, n_frames, grid_h > 0 ? grid_h : 1, grid_w > 0 ? grid_w : 1, tok0,
+      rope_dtype == LBW_ROPE_BF16);
   return cuda_check(cudaGetLastError(), "qk_rmsnorm_rope launch");
 }
 

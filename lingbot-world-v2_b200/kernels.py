@@ -376,14 +376,17 @@ def layernorm_mod(x, eps, out, scale=None, shift=None, weight=None, bias=None, m
     return out
 
 
-def rmsnorm_rope(x, ss, gamma, eps, out, rope=None, grid=None, tok0=0, out_row_off=0, _eager=False):
-    """rope = (cos, sin, n_frames) from rope.rope_tables; grid = (f, h, w)."""
+def rmsnorm_rope(x, ss, gamma, eps, out, rope=None, grid=None, tok0=0, out_row_off=0, rope_bf16=False,
+                 _eager=False):
+    """rope = (cos, sin, n_frames) from rope.rope_tables; grid = (f, h, w). rope_bf16: the reference's bf16
+    rotation (lbw.h LBW_ROPE_BF16; rope.ROPE_DTYPE), else fp32."""
     if _tracing(_eager):
         if rope is not None:
             _op("rmsnorm_rope")(x, ss, gamma, float(eps), out, rope[0], rope[1], int(rope[2]), int(grid[1]),
-                                int(grid[2]), int(tok0), int(out_row_off))
+                                int(grid[2]), int(tok0), int(out_row_off), bool(rope_bf16))
         else:
-            _op("rmsnorm_rope")(x, ss, gamma, float(eps), out, None, None, 0, 0, 0, int(tok0), int(out_row_off))
+            _op("rmsnorm_rope")(x, ss, gamma, float(eps), out, None, None, 0, 0, 0, int(tok0), int(out_row_off),
+                                False)
         return out
     require_cuda(x, ss, gamma, out)
     m, c = x.shape
@@ -396,19 +399,21 @@ def rmsnorm_rope(x, ss, gamma, eps, out, rope=None, grid=None, tok0=0, out_row_o
     else:
         cos = sin = None
         nf = gh = gw = 0
-    check(load().lbw_rmsnorm_rope(ptr(x), ptr(ss), ptr(gamma), m, c, ctypes.c_float(eps), ptr(cos), ptr(sin), nf, gh,
-                                  gw, tok0, ptr(o2), o2.stride(0), out_row_off, stream_of(x.device)), "rmsnorm_rope")
+    check(load().lbw_rmsnorm_rope_dt(ptr(x), ptr(ss), ptr(gamma), m, c, ctypes.c_float(eps), ptr(cos), ptr(sin), nf,
+                                     gh, gw, tok0, ptr(o2), o2.stride(0), out_row_off, 1 if rope_bf16 else 0,
+                                     stream_of(x.device)), "rmsnorm_rope")
     return out
 
 
 def qk_rmsnorm_rope(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out, eps, rope, grid, tok0=0, q_row_off=0,
-                    k_row_off=0, _eager=False):
+                    k_row_off=0, rope_bf16=False, _eager=False):
     """rmsnorm_rope of q and k of the same tokens in one launch (lbw_qk_rmsnorm_rope, the reference's
-    qk_post.qk_norm_rope): q_out rows q_row_off.., k_out rows k_row_off.. get the normalised, rotated rows."""
+    qk_post.qk_norm_rope): q_out rows q_row_off.., k_out rows k_row_off.. get the normalised, rotated rows.
+    rope_bf16: the reference's bf16 rotation (rope.ROPE_DTYPE), else fp32."""
     if _tracing(_eager):
         _op("qk_rmsnorm_rope")(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out, float(eps), rope[0],
                                rope[1], int(rope[2]), int(grid[1]), int(grid[2]), int(tok0), int(q_row_off),
-                               int(k_row_off))
+                               int(k_row_off), bool(rope_bf16))
         return q_out, k_out
     require_cuda(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out)
     m, c = q_raw.shape
@@ -418,10 +423,10 @@ def qk_rmsnorm_rope(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out, ep
     if q_row_off < 0 or q_row_off + m > qo.shape[0] or k_row_off < 0 or k_row_off + m > ko.shape[0]:
         raise ValueError("qk_rmsnorm_rope: rows outside an output")
     cos, sin, nf = rope
-    check(load().lbw_qk_rmsnorm_rope(ptr(q_raw), ptr(ss_q), ptr(gamma_q), ptr(qo), qo.stride(0), q_row_off,
-                                     ptr(k_raw), ptr(ss_k), ptr(gamma_k), ptr(ko), ko.stride(0), k_row_off, m, c,
-                                     ctypes.c_float(eps), ptr(cos), ptr(sin), nf, int(grid[1]), int(grid[2]), tok0,
-                                     stream_of(q_raw.device)), "qk_rmsnorm_rope")
+    check(load().lbw_qk_rmsnorm_rope_dt(ptr(q_raw), ptr(ss_q), ptr(gamma_q), ptr(qo), qo.stride(0), q_row_off,
+                                        ptr(k_raw), ptr(ss_k), ptr(gamma_k), ptr(ko), ko.stride(0), k_row_off, m, c,
+                                        ctypes.c_float(eps), ptr(cos), ptr(sin), nf, int(grid[1]), int(grid[2]), tok0,
+                                        1 if rope_bf16 else 0, stream_of(q_raw.device)), "qk_rmsnorm_rope")
     return q_out, k_out
 
 

@@ -248,6 +248,7 @@ class CausalWanModel(nn.Module):
             raise ValueError("the B200 model serves the chunked KV cache (allocate_self_kv_chunks)")
         if self.model_type == "i2v" and y is None:
             raise ValueError("i2v needs the conditioning y")
+        rope.set_bf16_rope_for_forward(seq_len)   # the reference's switch to bf16 RoPE (model_fast.py:3348)
         u = torch.cat([x[0], y[0]], dim=0) if y is not None else x[0]
         grid = tuple(int(v) // p for v, p in zip(u.shape[1:], self.patch_size))
         L = grid[0] * grid[1] * grid[2]

@@ -115,14 +115,15 @@ def _(h, w_qkv, b_qkv, q_raw, k_raw, ss_q, ss_k, v_out, v_row_off):
 @torch.library.custom_op("lbw::rmsnorm_rope", mutates_args=("out",))
 def rmsnorm_rope(x: torch.Tensor, ss: torch.Tensor, gamma: torch.Tensor, eps: float, out: torch.Tensor,
                  cos: Optional[torch.Tensor], sin: Optional[torch.Tensor], n_frames: int, grid_h: int, grid_w: int,
-                 tok0: int, out_row_off: int) -> None:
+                 tok0: int, out_row_off: int, rope_bf16: bool) -> None:
     rope = (cos, sin, n_frames) if cos is not None else None
     grid = (n_frames, grid_h, grid_w) if cos is not None else None
-    K.rmsnorm_rope(x, ss, gamma, eps, out, rope=rope, grid=grid, tok0=tok0, out_row_off=out_row_off, _eager=True)
+    K.rmsnorm_rope(x, ss, gamma, eps, out, rope=rope, grid=grid, tok0=tok0, out_row_off=out_row_off,
+                   rope_bf16=rope_bf16, _eager=True)
 
 
 @rmsnorm_rope.register_fake
-def _(x, ss, gamma, eps, out, cos, sin, n_frames, grid_h, grid_w, tok0, out_row_off):
+def _(x, ss, gamma, eps, out, cos, sin, n_frames, grid_h, grid_w, tok0, out_row_off, rope_bf16):
     return None
 
 
@@ -130,15 +131,16 @@ def _(x, ss, gamma, eps, out, cos, sin, n_frames, grid_h, grid_w, tok0, out_row_
 def qk_rmsnorm_rope(q_raw: torch.Tensor, ss_q: torch.Tensor, gamma_q: torch.Tensor, q_out: torch.Tensor,
                     k_raw: torch.Tensor, ss_k: torch.Tensor, gamma_k: torch.Tensor, k_out: torch.Tensor, eps: float,
                     cos: torch.Tensor, sin: torch.Tensor, n_frames: int, grid_h: int, grid_w: int, tok0: int,
-                    q_row_off: int, k_row_off: int) -> None:
+                    q_row_off: int, k_row_off: int, rope_bf16: bool) -> None:
     """q and k RMSNorm + RoPE in one launch (kernels/qk_post.py qk_norm_rope)."""
     K.qk_rmsnorm_rope(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out, eps, (cos, sin, n_frames),
-                      (n_frames, grid_h, grid_w), tok0=tok0, q_row_off=q_row_off, k_row_off=k_row_off, _eager=True)
+                      (n_frames, grid_h, grid_w), tok0=tok0, q_row_off=q_row_off, k_row_off=k_row_off,
+                      rope_bf16=rope_bf16, _eager=True)
 
 
 @qk_rmsnorm_rope.register_fake
 def _(q_raw, ss_q, gamma_q, q_out, k_raw, ss_k, gamma_k, k_out, eps, cos, sin, n_frames, grid_h, grid_w, tok0,
-      q_row_off, k_row_off):
+      q_row_off, k_row_off, rope_bf16):
     return None
 
 

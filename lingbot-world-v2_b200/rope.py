@@ -13,6 +13,23 @@ import torch
 
 HEAD_DIM = 128
 
+# Arithmetic of the rotation, process-wide as in the reference (model_fast.py:985-1003): fp32 until a model forward
+# sees a chunk of 4,096 or more tokens, bf16 from then on (cos / sin rounded to bf16 and every product and sum of the
+# rotation rounded to bf16: lbw.h LBW_ROPE_BF16). The block reads it at each call.
+ROPE_DTYPE = torch.float32
+
+
+def mark_bf16_rope():
+    """bf16 RoPE for the rest of this process (model_fast.py:1000-1003)."""
+    global ROPE_DTYPE
+    ROPE_DTYPE = torch.bfloat16
+
+
+def set_bf16_rope_for_forward(seq_len):
+    """Called once per model forward with its seq_len, as the reference does (model_fast.py:1144-1148, :3348)."""
+    if seq_len >= 4096:
+        mark_bf16_rope()
+
 
 def rope_params(max_seq_len, dim, theta=10000):
     pos = torch.arange(max_seq_len).float()

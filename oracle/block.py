@@ -63,12 +63,15 @@ def rope_grid(freqs, grid, start_frame):
     return torch.cos(ang), torch.sin(ang)
 
 
-def rope_apply(x, cos, sin):
-    """x [L, H, d] bf16 -> rotated bf16 (fp32 math; interleaved (re, im) pairs)."""
+def rope_apply(x, cos, sin, dtype=torch.float32):
+    """x [L, H, d] bf16 -> rotated bf16 (interleaved (re, im) pairs), model_fast.py:933-979. dtype is the
+    reference's RoPE dtype (ROPE_DTYPE, :985-1003): fp32 math by default; bf16 once a model forward has seen a
+    chunk of 4,096 or more tokens (:1144-1148), when the grids are cast to bf16 (:928-929) and every product and sum
+    of the rotation is a bf16 op."""
     L, H, d = x.shape
-    xf = x.float().reshape(L, H, d // 2, 2)
+    xf = x.to(dtype).reshape(L, H, d // 2, 2)
     re, im = xf[..., 0], xf[..., 1]
-    c, s = cos.view(L, 1, -1), sin.view(L, 1, -1)
+    c, s = cos.to(dtype).view(L, 1, -1), sin.to(dtype).view(L, 1, -1)
     out = torch.stack([re * c - im * s, re * s + im * c], dim=-1)
     return out.reshape(L, H, d).to(x.dtype)
 
@@ -149,11 +152,12 @@ def cross_kv(p, context, eps=1e-6, mx_linears=(), mx_fmt="e4m3"):
 
 
 def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, mx=False, eps=1e-6,
-                  dedup_kc=None, return_all=False, mx_linears=(), mx_fmt="e4m3"):
+                  dedup_kc=None, return_all=False, mx_linears=(), mx_fmt="e4m3", rope_dtype=torch.float32):
     """One block. x [Lq, C] fp32; e0 [6, C] fp32; k_lead/v_lead lists of [L_i, H, d] bf16;
     ctx_k/ctx_v [T, H, d] bf16; cos/sin [Lq, 64] fp32; film = (scale, shift) [Lq, C] bf16; mx: MXFP8 FFN;
     mx_linears: names of the other Linears in MXFP8 (LINGBOT_LIN_MX); mx_fmt: the element format of every MX
-    matmul ("e4m3", or "e5m2" for LINGBOT_MX_FP8=float8_e5m2, kernels/ffn_mx.py:8,18).
+    matmul ("e4m3", or "e5m2" for LINGBOT_MX_FP8=float8_e5m2, kernels/ffn_mx.py:8,18); rope_dtype: the rotation's
+    arithmetic (rope_apply).
     Returns x_out (and, with return_all, the intermediates)."""
     lin = lambda name, t: block_linear(p, name, t, mx_linears, mx_fmt)  # noqa: E731
     Lq, C = x.shape
@@ -166,8 +170,8 @@ def block_forward(p, x, e0, k_lead, v_lead, ctx_k, ctx_v, cos, sin, film=None, m
     q = rms_norm(lin("self_attn.q", h), p["self_attn.norm_q.weight"], eps)
     k = rms_norm(lin("self_attn.k", h), p["self_attn.norm_k.weight"], eps)
     v = lin("self_attn.v", h).view(Lq, H, HEAD_DIM)
-    q = rope_apply(q.view(Lq, H, HEAD_DIM), cos, sin)
-    k = rope_apply(k.view(Lq, H, HEAD_DIM), cos, sin)
+    q = rope_apply(q.view(Lq, H, HEAD_DIM), cos, sin, rope_dtype)
+    k = rope_apply(k.view(Lq, H, HEAD_DIM), cos, sin, rope_dtype)
     ks = torch.cat(list(k_lead) + [k], dim=0)
     vs = torch.cat(list(v_lead) + [v], dim=0)
     attn = attention(q, ks, vs)

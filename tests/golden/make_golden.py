@@ -11,8 +11,9 @@ the destination-chunk K/V it writes and the outputs of self_attn / cross_attn / 
 the reference's cross_dedup_bias + cross_attention_dedup (wan/modules/attention.py:516-554) on a
 duplicated-context case, the reference's RoPE grids, its camera FiLM MLP, and one whole
 WanModelFast.forward (model_fast.py:3283-3935) of a 2-block i2v model with the camera condition, and the
-Wan 2.1 VAE decode (wan/modules/vae2_1.py) of a small latent. Inputs are NOT stored (except the small VAE
-latent): they are regenerated from the seed by oracle.inputs / oracle.vae; a checksum guards against drift.
+Wan 2.1 VAE decode (wan/modules/vae2_1.py) of a small latent, and the RoPE rotation in the reference's bf16 mode
+(`make_golden.py rope_bf16` writes that fixture alone). Inputs are NOT stored (except the small VAE latent and the
+RoPE rows): they are regenerated from the seed by oracle.inputs / oracle.vae; a checksum guards against drift.
 
 Nothing at test or bench time reads the reference; only the .pt files produced here are used.
 """
@@ -247,6 +248,30 @@ def run_vae():
                 checksum=sum(float(v.abs().sum()) for v in params.values()))
 
 
+ROPE_BF16 = dict(grid=(3, 5, 7), start_frame=9, heads=2, seed=8)
+
+
+def run_rope_bf16(mf):
+    """The reference's RoPE rotation in its bf16 mode (mark_bf16_rope, model_fast.py:1000-1003: what every forward
+    of a 4,096-token or larger chunk switches on) on seeded bf16 q rows: grids built in bf16 (:878-931) and
+    causal_rope_apply_rotation (:933-979) with ROPE_DTYPE bf16."""
+    f, h, w = ROPE_BF16["grid"]
+    L, H, d = f * h * w, ROPE_BF16["heads"], 128
+    g = torch.Generator().manual_seed(ROPE_BF16["seed"])
+    x = torch.randn(L, H, d, generator=g).to(torch.bfloat16)
+    freqs = torch.cat([mf.rope_params(1024, d - 4 * (d // 6)), mf.rope_params(1024, 2 * (d // 6)),
+                       mf.rope_params(1024, 2 * (d // 6))], dim=1)
+    cos_g, sin_g = mf._causal_rope_grids_build(freqs, torch.tensor([[f, h, w]]), "cpu", ROPE_BF16["start_frame"],
+                                               dtype=torch.bfloat16)
+    saved = mf.ROPE_DTYPE
+    mf.mark_bf16_rope()
+    try:
+        out = mf.causal_rope_apply_rotation(x.unsqueeze(0), [(f, h, w)], cos_g, sin_g)[0]
+    finally:
+        mf.ROPE_DTYPE = saved
+    return dict(case=ROPE_BF16, x=x, out=out.clone())
+
+
 def main():
     if not REF or not os.path.isdir(os.path.join(REF, "wan")):
         raise SystemExit("set LBW_REFERENCE to the reference checkout (the directory holding wan/)")
@@ -255,6 +280,10 @@ def main():
         import wan.modules.model_fast as mf
         import wan.modules.attention as attn_mod
         import wan.modules.chunked_kv_cache as ckv
+    if sys.argv[1:] == ["rope_bf16"]:       # only this fixture
+        torch.save(run_rope_bf16(mf), os.path.join(HERE, "rope_bf16.pt"))
+        print("rope_bf16 saved")
+        return
     torch.manual_seed(0)
     for name, case in CASES.items():
         res = run_block(mf, case)
@@ -272,6 +301,8 @@ def main():
     print("chunk_routing saved")
     torch.save(run_vae(), os.path.join(HERE, "vae_decode.pt"))
     print("vae_decode saved")
+    torch.save(run_rope_bf16(mf), os.path.join(HERE, "rope_bf16.pt"))
+    print("rope_bf16 saved")
 
 
 if __name__ == "__main__":

@@ -73,6 +73,28 @@ def test_block_mx_vs_oracle(cuda_dev, peaked, pipe):
     assert rel_l2(k.view(-1, case.heads, 128), r["k"]) <= 1e-2
 
 
+def test_block_bf16_rope_vs_oracle(cuda_dev, monkeypatch):
+    """With the reference's bf16 RoPE switched on (rope.ROPE_DTYPE, set by every model forward of a 4,096-token or
+    larger chunk), the block's K written into the destination chunk is closer to the oracle's bf16-RoPE K than to its
+    fp32-RoPE K (the kernel's rotation bits are pinned separately, test_rope_rotation_bits), and the block output
+    stays within the usual tolerance of the bf16-RoPE oracle."""
+    import lbw_b200.rope as R
+    monkeypatch.setattr(R, "ROPE_DTYPE", torch.bfloat16)
+    case = BlockCase(dim=512, ffn=1024, grid=(3, 6, 10), n_lead=3, text_len=64, start_frame=9, seed=25)
+    p, inp = make_case(case)
+    blk = _build(case, p, cuda_dev, ffn_mx=True)
+    x, k, v, _ = _run(blk, case, inp, cuda_dev)
+    cos, sin = ob.rope_grid(ob.rope_freqs(), case.grid, case.start_frame)
+    ck, cv = ob.cross_kv(p, inp["context"])
+    args = (p, inp["x"], inp["e0"], inp["k_lead"], inp["v_lead"], ck, cv, cos, sin)
+    rb = ob.block_forward(*args, film=inp["film"], mx=True, return_all=True, rope_dtype=torch.bfloat16)
+    rf = ob.block_forward(*args, film=inp["film"], mx=True, return_all=True)
+    kk = k.view(-1, case.heads, 128)
+    assert rel_l2(x, rb["x"]) <= 1e-2 and max_abs(x, rb["x"]) <= 5e-2
+    assert rel_l2(kk, rb["k"]) <= 1e-2
+    assert rel_l2(kk, rb["k"]) < rel_l2(kk, rf["k"])
+
+
 def test_block_mx_e5m2_vs_oracle(cuda_dev):
     """LINGBOT_MX_FP8=float8_e5m2 (kernels/ffn_mx.py:8,18): the block's fused MX FFN with E5M2 codes (LayerNorm ->
     codes, FFN-up + GELU -> codes, FFN-down) against the oracle with the E5M2 emulation, and measurably closer to it

@@ -243,6 +243,32 @@ def test_rmsnorm_rope(cuda_dev, grid, start, tok0, m, c):
     assert rel_l2(out[8:].view(m, -1, 128), ref) < 2e-3
 
 
+@pytest.mark.parametrize("grid,start,tok0,m,c", [((3, 4, 6), 6, 0, 72, 512), ((3, 30, 52), 18, 1170, 1170, 512),
+                                                   ((3, 45, 80), 18, 3600, 2700, 5120)])
+def test_rope_rotation_bits(cuda_dev, grid, start, tok0, m, c):
+    """The kernel's rotation, in both RoPE modes, is bit-identical to the oracle's rotation of the kernel's own
+    normalised rows (the same launch without RoPE): fp32 math, and the reference's bf16 mode (bf16 tables, every
+    product and sum rounded to bf16; the oracle's bf16 rotation is pinned to the reference by rope_bf16.pt). The last
+    case is a c4 shard: tokens 3,600.. of the 720p chunk, 40 heads."""
+    import lbw_b200.kernels as K
+    import lbw_b200.rope as R
+    g = _g(23)
+    d = cuda_dev
+    x = torch.randn(m, c, generator=g).to(BF).to(d)
+    gamma = (1 + 0.02 * torch.randn(c, generator=g)).to(BF).to(d)
+    ss = x.float().pow(2).sum(1)
+    cos, sin = R.rope_tables(R.rope_freqs(), grid, start, d)
+    y = torch.empty(m, c, dtype=BF, device=d)
+    K.rmsnorm_rope(x, ss, gamma, 1e-6, y)
+    gc, gs = ob.rope_grid(ob.rope_freqs(), grid, start)
+    for dt in (torch.float32, torch.bfloat16):
+        out = torch.empty(m, c, dtype=BF, device=d)
+        K.rmsnorm_rope(x, ss, gamma, 1e-6, out, rope=(cos, sin, grid[0]), grid=grid, tok0=tok0,
+                       rope_bf16=dt == torch.bfloat16)
+        ref = ob.rope_apply(y.cpu().view(m, c // 128, 128), gc[tok0:tok0 + m], gs[tok0:tok0 + m], dt)
+        assert torch.equal(out.cpu().view(m, -1, 128), ref), dt
+
+
 @pytest.mark.parametrize("grid,start,tok0,m,c", [((3, 4, 6), 6, 0, 72, 512), ((3, 30, 52), 18, 1170, 1170, 512)])
 def test_qk_rmsnorm_rope_equals_two_launches(cuda_dev, grid, start, tok0, m, c):
     """The fused q + k launch gives the bits of the two separate rmsnorm_rope launches (own gammas, row sums and
@@ -261,6 +287,11 @@ def test_qk_rmsnorm_rope_equals_two_launches(cuda_dev, grid, start, tok0, m, c):
     K.rmsnorm_rope(k, ssk, gk, 1e-6, k1, rope=rp, grid=grid, tok0=tok0, out_row_off=16)
     q2, k2 = torch.empty(m, c, dtype=BF, device=d), torch.full((m + 16, c), 3.0, dtype=BF, device=d)
     K.qk_rmsnorm_rope(q, ssq, gq, q2, k, ssk, gk, k2, 1e-6, rp, grid, tok0=tok0, k_row_off=16)
+    assert torch.equal(q1, q2) and torch.equal(k1, k2)
+    # the same with the reference's bf16 rotation
+    K.rmsnorm_rope(q, ssq, gq, 1e-6, q1, rope=rp, grid=grid, tok0=tok0, rope_bf16=True)
+    K.rmsnorm_rope(k, ssk, gk, 1e-6, k1, rope=rp, grid=grid, tok0=tok0, out_row_off=16, rope_bf16=True)
+    K.qk_rmsnorm_rope(q, ssq, gq, q2, k, ssk, gk, k2, 1e-6, rp, grid, tok0=tok0, k_row_off=16, rope_bf16=True)
     assert torch.equal(q1, q2) and torch.equal(k1, k2)
 
 

@@ -122,12 +122,12 @@ def _opcheck_cases(d):
                                                             torch.empty(m, 256, dtype=BF, device=d),
                                                             *K.attention_tail_workspace(m, 2, [300], d, 3), 3)),
         "rmsnorm_rope": (ops.rmsnorm_rope, (a, (a.float() ** 2).sum(1), r(c, dt=BF), 1e-6,
-                                            torch.empty(m, c, dtype=BF, device=d), None, None, 0, 0, 0, 0, 0)),
+                                            torch.empty(m, c, dtype=BF, device=d), None, None, 0, 0, 0, 0, 0, False)),
         "qk_rmsnorm_rope": (ops.qk_rmsnorm_rope, (a, (a.float() ** 2).sum(1), r(c, dt=BF),
                                                   torch.empty(m, c, dtype=BF, device=d), a.flip(0).contiguous(),
                                                   (a.float() ** 2).sum(1).flip(0).contiguous(), r(c, dt=BF),
                                                   torch.empty(m + 8, c, dtype=BF, device=d), 1e-6, *rope,
-                                                  9, 4, 6, 0, 0, 8)),
+                                                  9, 4, 6, 0, 0, 8, True)),
         "mx_quantize": (ops.mx_quantize, (a, "e4m3")),
         "mx_quantize_into": (ops.mx_quantize_into, (a, torch.empty_like(ad), torch.empty_like(as_), "e4m3")),
         "mx_linear": (ops.mx_linear, (ad, as_, wd, ws, b, "e4m3")),

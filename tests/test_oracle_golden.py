@@ -27,6 +27,35 @@ def test_block_matches_reference(name):
     assert rel_l2(r["k"], g["k_dest"]) < 1e-3 and rel_l2(r["v"], g["v_dest"]) < 1e-3
 
 
+def test_rope_bf16_matches_reference():
+    """The rotation in the reference's bf16 RoPE mode (what every forward of a chunk of 4,096 or more tokens switches
+    on): bf16 grids and bf16 products and sums, bit-identical to causal_rope_apply_rotation with ROPE_DTYPE bf16;
+    the fp32 rotation of the same rows differs."""
+    g = load_golden("rope_bf16")
+    f, h, w = g["case"]["grid"]
+    cos, sin = ob.rope_grid(ob.rope_freqs(), (f, h, w), g["case"]["start_frame"])
+    got = ob.rope_apply(g["x"], cos, sin, torch.bfloat16)
+    assert got.dtype == torch.bfloat16 and torch.equal(got, g["out"])
+    assert not torch.equal(ob.rope_apply(g["x"], cos, sin), g["out"])
+
+
+def test_rope_dtype_switch_follows_the_reference():
+    """lbw_b200.rope.ROPE_DTYPE: fp32 until a forward sees seq_len >= 4096, then bf16 for the rest of the process
+    (model_fast.py:1144-1148, :1000-1003)."""
+    import lbw_b200.rope as R
+    saved = R.ROPE_DTYPE
+    try:
+        R.ROPE_DTYPE = torch.float32
+        R.set_bf16_rope_for_forward(4095)
+        assert R.ROPE_DTYPE == torch.float32
+        R.set_bf16_rope_for_forward(4096)
+        assert R.ROPE_DTYPE == torch.bfloat16
+        R.set_bf16_rope_for_forward(100)
+        assert R.ROPE_DTYPE == torch.bfloat16
+    finally:
+        R.ROPE_DTYPE = saved
+
+
 def test_cross_dedup_matches_reference():
     g = load_golden("cross_dedup")
     bias = ob.cross_dedup_bias(g["ctx_k"], g["ctx_v"], g["kc"])
