@@ -340,10 +340,15 @@ struct EpiGeluMX {
     for (int e = 0; e < 32; e += 8) {
       uint4 bb = *reinterpret_cast<const uint4*>(bias + col + e);
       const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&bb);
+      // v is the MX GEMM's accumulator already rounded to bf16 (its epilogue pulls it as bf16 pairs); u = bf16(v + b)
+      // and GELU(u) rounded two values per conversion
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float u = bf16_round(bf16_round(v[e + q]) + __bfloat162float(bp[q]));
-        g[e + q] = bf16_round(gelu_tanh_fast(u));
+      for (int q = 0; q < 8; q += 2) {
+        const uint32_t up = pack_bf16(v[e + q] + __bfloat162float(bp[q]), v[e + q + 1] + __bfloat162float(bp[q + 1]));
+        const uint32_t gp = pack_bf16(gelu_tanh_fast(__uint_as_float(up << 16)),
+                                      gelu_tanh_fast(__uint_as_float(up & 0xFFFF0000u)));
+        g[e + q] = __uint_as_float(gp << 16);
+        g[e + q + 1] = __uint_as_float(gp & 0xFFFF0000u);
       }
     }
     __align__(16) uint8_t qb[32];
