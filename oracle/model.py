@@ -88,8 +88,11 @@ def block_params(sd, i):
     return {k[len(pre):]: v for k, v in sd.items() if k.startswith(pre)}
 
 
-def model_forward(sd, inp, case, chunk_routing):
-    """Returns (out [out_dim, F, H, W] fp32, per-layer destination K and V, per-layer context K and V)."""
+def model_forward(sd, inp, case, chunk_routing, seq_len=None, rope_dtype=None):
+    """Returns (out [out_dim, F, H, W] fp32, per-layer destination K and V, per-layer context K and V).
+    seq_len is the forward's seq_len (default: the chunk's tokens); from 4,096 on the reference switches its RoPE to
+    bf16 (model_fast.py:1144-1148, :3348), which rope_dtype overrides (the reference keeps bf16 for the rest of the
+    process once any forward has switched it)."""
     x_cat = torch.cat([inp["x"], inp["y"]], dim=0)
     tokens = patch_embed(sd, x_cat).float()
     ctx = text_embed(sd, inp["context"], case.text_len)
@@ -99,6 +102,8 @@ def model_forward(sd, inp, case, chunk_routing):
     L = case.lq
     start_frame = (case.chunk_index * L) // (grid[1] * grid[2])
     cos, sin = ob.rope_grid(ob.rope_freqs(), grid, start_frame)
+    if rope_dtype is None:
+        rope_dtype = torch.bfloat16 if (L if seq_len is None else seq_len) >= 4096 else torch.float32
     dest, leading = chunk_routing(case.chunk_index, case.n_chunks)
     x = tokens
     k_dest, v_dest, ctx_k, ctx_v = [], [], [], []
@@ -109,7 +114,8 @@ def model_forward(sd, inp, case, chunk_routing):
         lead = inp["cache"][i]
         k_lead = [lead[s][0] for s in leading]
         v_lead = [lead[s][1] for s in leading]
-        r = ob.block_forward(p, x, e0, k_lead, v_lead, ck, cv, cos, sin, film=film, return_all=True)
+        r = ob.block_forward(p, x, e0, k_lead, v_lead, ck, cv, cos, sin, film=film, return_all=True,
+                             rope_dtype=rope_dtype)
         x = r["x"]
         k_dest.append(r["k"].to(torch.bfloat16))
         v_dest.append(r["v"].to(torch.bfloat16))

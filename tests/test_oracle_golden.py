@@ -97,6 +97,10 @@ def test_model_forward_matches_reference():
     for i in range(case.layers):
         assert rel_l2(k_dest[i], g["k_dest"][i]) < 1e-2 and rel_l2(v_dest[i], g["v_dest"][i]) < 1e-2
         assert rel_l2(ctx_k[i], g["ctx_k"][i]) < 1e-2 and rel_l2(ctx_v[i], g["ctx_v"][i]) < 1e-2
+    # a forward called with seq_len >= 4096 rotates in bf16, as the reference's: the roped K differs, V does not
+    _, kb, vb, _, _ = om.model_forward(sd, inp, case, routing.chunk_routing, seq_len=4096)
+    _, kb2, _, _, _ = om.model_forward(sd, inp, case, routing.chunk_routing, rope_dtype=torch.bfloat16)
+    assert torch.equal(kb[0], kb2[0]) and not torch.equal(kb[0], k_dest[0]) and torch.equal(vb[0], v_dest[0])
 
 
 def test_oracle_vae_decode_vs_reference_golden():
