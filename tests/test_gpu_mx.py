@@ -262,6 +262,39 @@ def test_mx_linear_formats_vs_emulation(cuda_dev, fmt, m, n, k):
     assert rel_l2(out, ref) < 4e-3
 
 
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "e2m1"])
+def test_mx_wide_tiles_with_a_half_scale_block(cuda_dev, monkeypatch, fmt):
+    """256-wide tiles (forced with LBW_GEMM_TILE_N) where N = 640 is an odd number of 128-row weight blocks: the
+    last tile's second scale block does not exist (the kernel reuses the first one for those rows) and its columns
+    past N are dropped by every epilogue. The automatic choice runs 128-wide tiles at these shapes, so only the
+    override reaches this path."""
+    import lbw_b200.kernels as K
+    monkeypatch.setenv("LBW_GEMM_TILE_N", "256")
+    m, n, k = 300, 640, 768
+    a, w, b = _ab(m, n, k, 31)
+    d = cuda_dev
+    ad, as_, _ = K.mx_quantize(a.to(d), fmt=fmt)
+    wd, ws, _ = K.mx_quantize(w.to(d), fmt=fmt)
+    out = K.mx_linear(ad, as_, wd, ws, b.to(d), fmt=fmt)
+    y = omx.mx_linear(a, w, fmt)
+    assert rel_l2(out, (y.float() + b.float()).to(BF)) < 4e-3
+    if fmt == "e2m1":
+        return
+    g = torch.Generator().manual_seed(32)
+    x = torch.randn(m, n, generator=g)
+    gate = torch.randn(n, generator=g) * 0.1
+    xd = x.to(d)
+    K.mx_linear_residual(ad, as_, wd, ws, b.to(d), xd, gate=gate.to(d), fmt=fmt)
+    assert rel_l2(xd.cpu() - x, ob.mx_matmul(a, w, b, fmt).float() * gate) < 5e-3
+    oq, os_ = K.mx_buffers(m, n, d, fmt=fmt)
+    K.mx_linear_gelu(ad, as_, wd, ws, b.to(d), oq, os_, fmt=fmt)
+    u = (y.to(BF) + b).to(BF)
+    q, s = omx.quantize(F.gelu(u.float(), approximate="tanh").to(BF), fmt)
+    dt = torch.float8_e4m3fn if fmt == "e4m3" else torch.float8_e5m2
+    got = omx.dequantize(oq.cpu().view(dt), _untile(os_.cpu(), m, n))
+    assert rel_l2(got, omx.dequantize(q, s)) < (1e-2 if fmt == "e4m3" else 2e-2)
+
+
 def test_mx_formats_reject_bad_shapes(cuda_dev):
     import lbw_b200.kernels as K
     d = cuda_dev
