@@ -38,9 +38,11 @@ def _worker(rank, world, port, q, mode):
     sp.set_group(None)
     live = sp.Liveness(timeout_s=LIVE_S)
     rows = 4
-    t0 = time.monotonic()
+    t1 = None  # start of step 1: detection times are measured from here, not from start-up (step 0 included)
     try:
         for step in range(3):
+            if step == 1:
+                t1 = time.monotonic()
             if step == 1 and rank == world - 1:        # the failing rank, between steps 0 and 1
                 if mode == "error":
                     live.fail("injected: out of memory while preparing step 1")
@@ -67,10 +69,10 @@ def _worker(rank, world, port, q, mode):
         dist.destroy_process_group()
     except sp.PeerLost as e:
         sp.abort()
-        q.put((rank, ("PeerLost", e.ranks, str(e), time.monotonic() - t0)))
+        q.put((rank, ("PeerLost", e.ranks, str(e), time.monotonic() - (t1 if t1 is not None else 0.0))))
     except RuntimeError as e:
         sp.abort()
-        q.put((rank, ("RuntimeError", (), str(e), time.monotonic() - t0)))
+        q.put((rank, ("RuntimeError", (), str(e), time.monotonic() - (t1 if t1 is not None else 0.0))))
 
 
 def _run(mode, world):
