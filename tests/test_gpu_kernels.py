@@ -73,6 +73,36 @@ def test_linear_residual_gate_and_film(cuda_dev):
     assert rel_l2(xd2 - x.to(d), ob.linear(a, w, None).float()) < 5e-3
 
 
+@pytest.mark.parametrize("width", [128, 256])
+@pytest.mark.parametrize("m,n,k", [(300, 640, 512), (77, 96, 128), (200, 160, 256)])
+def test_bf16_gemm_epilogues_at_both_tile_widths(cuda_dev, monkeypatch, width, m, n, k):
+    """Each tile width (forced with LBW_GEMM_TILE_N) at N not a multiple of 256, so that the last tile is cut inside
+    its columns: the automatic choice picks one width per shape, and the shapes of the other tests are whole
+    256-wide tiles wherever 256 is chosen. The store, residual + FiLM and row-sum-of-squares epilogues."""
+    import lbw_b200.kernels as K
+    monkeypatch.setenv("LBW_GEMM_TILE_N", str(width))
+    g = _g(m + n + k + width)
+    a = torch.randn(m, k, generator=g).to(BF)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(BF)
+    b = (torch.randn(n, generator=g) * 0.05).to(BF)
+    x = torch.randn(m, n, generator=g)
+    gate = torch.randn(n, generator=g) * 0.1
+    fs, ft = (torch.randn(m, n, generator=g) * 0.1).to(BF), (torch.randn(m, n, generator=g) * 0.1).to(BF)
+    d = cuda_dev
+    y = ob.linear(a, w, b)
+    out = K.gemm_bf16(a.to(d), w.to(d), b.to(d))
+    assert rel_l2(out, y) < 4e-3
+    xd = x.to(d)
+    K.linear_residual(a.to(d), w.to(d), b.to(d), xd, gate=gate.to(d), film_scale=fs.to(d), film_shift=ft.to(d))
+    ref = (1.0 + fs) * (x + y.float() * gate) + ft
+    assert rel_l2(xd, ref) < 1e-4
+    out2 = torch.empty(m, n, dtype=BF, device=d)
+    ss = torch.empty(m, device=d)
+    K.linear_rowss(a.to(d), w.to(d), b.to(d), out2, ss)
+    assert rel_l2(out2, y) < 4e-3
+    assert rel_l2(ss, out2.float().pow(2).sum(1)) < 1e-5
+
+
 @pytest.mark.parametrize("qdq", [False, True])
 def test_linear_gelu(cuda_dev, qdq):
     import lbw_b200.kernels as K
